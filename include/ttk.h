@@ -1,0 +1,262 @@
+/* ttk: the C ABI of the B200 (sm_100a) kernel layer under tinytrain's
+ * Tensor / ops / nn / optim API.
+ *
+ * Plain pointers and sizes only. Every float* / int64_t* argument named as a
+ * tensor is DEVICE memory; `stream` is a cudaStream_t passed as void* (NULL =
+ * the legacy default stream). Every function returns TTK_OK (0) or a
+ * TTK_ERR_* code; ttk_last_error() gives the message of the last failure on
+ * the calling thread. Argument checks mirror the reference's
+ * std::invalid_argument throws and run before any launch.
+ *
+ * Tensors are row-major fp32 (the reference's only dtype, tensor.h:25).
+ * "accumulate" flags select out += result (the reference's grad +=
+ * semantics, ops.cpp:12-15) instead of out = result.
+ *
+ * The reference (seampm/tinytrain) has no FFI; each entry point names the
+ * reference function whose arithmetic it replaces.
+ */
+#ifndef TTK_H
+#define TTK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TTK_OK 0
+#define TTK_ERR_ARG 1     /* invalid argument (shape, range, null, alignment) */
+#define TTK_ERR_CUDA 2    /* CUDA runtime / driver failure */
+#define TTK_ERR_NCCL 3    /* collective library failure */
+#define TTK_ERR_DEVICE 4  /* a kernel reported an error through the status word */
+
+/* ------------------------------------------------------------------ runtime */
+
+const char* ttk_last_error(void);
+const char* ttk_version(void);
+/* Sets the calling thread's device and creates its stream-ordered memory pool. */
+int ttk_init(int device);
+int ttk_device_count(int* n);
+/* Reads and clears the device status word (bit 0: a bounded wait expired,
+ * bit 1: an out-of-range index was skipped). Synchronizes the device. */
+int ttk_device_status(unsigned* bits);
+int ttk_synchronize(void);
+
+/* Stream-ordered allocation from the device's pool (cached, never released to
+ * the driver until exit). The caching allocator under tt::Tensor storage. */
+int ttk_malloc(void** ptr, size_t bytes, void* stream);
+int ttk_free(void* ptr, void* stream);
+int ttk_pool_stats(size_t* reserved, size_t* used);
+int ttk_host_alloc(void** ptr, size_t bytes); /* pinned host memory */
+int ttk_host_free(void* ptr);
+
+int ttk_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+int ttk_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+int ttk_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+int ttk_memset(void* dst, int value, size_t bytes, void* stream);
+
+int ttk_stream_create(void** stream);
+int ttk_stream_destroy(void* stream);
+int ttk_stream_synchronize(void* stream);
+int ttk_event_create(void** event);
+int ttk_event_destroy(void* event);
+int ttk_event_record(void* event, void* stream);
+int ttk_stream_wait_event(void* stream, void* event);
+int ttk_event_elapsed_ms(void* start, void* end, float* ms);
+int ttk_event_synchronize(void* event);
+
+/* ------------------------------------------------------------ dense algebra */
+
+/* C[b] = alpha * op(A[b]) @ op(B[b]) + beta * C[b], fp32-accurate (3xTF32 on
+ * tcgen05). op(A) is A [M,K] (lda) when transA = 0, or A^T with A stored
+ * [K,M] when transA = 1; op(B) is B [K,N] (ldb) when transB = 0, or B^T with B
+ * stored [N,K] when transB = 1. stride* are the batch strides (elements).
+ * `workspace` (device, 16-byte aligned) holds the split operands and must be
+ * at least ttk_gemm_workspace_size(...) bytes.
+ * Replaces: sgemm + matmul fwd/bwd (ops.cpp:96-125, 661-697) and bmm
+ * (ops.cpp:699-742). */
+size_t ttk_gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
+                               int64_t K);
+int ttk_gemm(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+             const float* A, int64_t lda, int64_t strideA, const float* B, int64_t ldb,
+             int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC,
+             void* workspace, size_t workspace_bytes, void* stream);
+/* The operand split alone: dst[b][0|1][r][0..ld_pad) = hi | lo of
+ * src[b][r][0..cols) (ld, batch stride bstride), zero in [cols, ld_pad).
+ * ld_pad must be a multiple of 16 (32 for an operand read MN-major by
+ * ttk_gemm_presplit: A with transA = 1, B with transB = 0). */
+int ttk_split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+                   int64_t batch, float* dst, int64_t ld_pad, void* stream);
+/* GEMM on operands already split by ttk_split_tf32 (e.g. weights split once
+ * per optimizer step). a_split holds op(A)'s storage ([M,K] or [K,M]) with
+ * padded leading dimension lda_pad, likewise b_split. */
+int ttk_gemm_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                      float alpha, const float* a_split, int64_t lda_pad, const float* b_split,
+                      int64_t ldb_pad, float beta, float* C, int64_t ldc, int64_t strideC,
+                      void* stream);
+
+/* ------------------------------------------------------------ fused NN ops */
+
+/* y = x * rstd * w, rstd = (mean(x^2) + eps)^-1/2 per row; x, y [R,D], w [D],
+ * rstd [R] (saved for the backward). Replaces the 7-op composite rmsnorm
+ * (ops.cpp:932-942). */
+int ttk_rmsnorm_fwd(const float* x, const float* w, float* y, float* rstd, int64_t R, int64_t D,
+                    float eps, void* stream);
+/* dx (+)= rstd*w*dy - x*rstd^3/D*sum(dy*w*x); dw += sum_rows(dy*x*rstd).
+ * dx may be NULL. dw (when not NULL) is always accumulated; `workspace`
+ * (device) must hold ttk_rmsnorm_bwd_workspace_size(R, D) bytes. */
+size_t ttk_rmsnorm_bwd_workspace_size(int64_t R, int64_t D);
+int ttk_rmsnorm_bwd(const float* x, const float* w, const float* rstd, const float* dy, float* dx,
+                    int accumulate_dx, float* dw, int64_t R, int64_t D, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* y = silu(a) * b (model.cpp:149-151, ops.cpp:324); n elements. */
+int ttk_swiglu_fwd(const float* a, const float* b, float* y, int64_t n, void* stream);
+/* da (+)= dy*b*s*(1+a*(1-s)), db (+)= dy*silu(a) (ops.cpp:325-328, :256). */
+int ttk_swiglu_bwd(const float* a, const float* b, const float* dy, float* da, float* db,
+                   int accumulate, int64_t n, void* stream);
+
+/* Fused log_softmax + nll_loss (ops.cpp:840-930) over logits [N,C]:
+ * loss_sum[0] (+)= sum_i (lse_i - x[i,t_i]) accumulated in fp64 into
+ * loss_acc (device double), and, when dlogits is not NULL,
+ * dlogits = grad_scale * (softmax(x) - onehot(t)) (dlogits may alias logits).
+ * Targets out of [0, C) are rejected before launch. */
+int ttk_cross_entropy(const float* logits, const int64_t* targets, int64_t N, int64_t C,
+                      double* loss_acc, float* dlogits, float grad_scale, void* stream);
+/* loss_out[0] = (float)(loss_acc[0] * scale) (the mean of ops.cpp:911-912). */
+int ttk_loss_finalize(const double* loss_acc, float scale, float* loss_out, void* stream);
+
+/* Causal self-attention with RoPE, fused (model.cpp:127-141: rope(q), rope(k),
+ * softmax(q k^T * scale + causal mask) v). q, k, v, o are [B,T,H,hd] (the
+ * layout the projections produce; o is ready for the output projection);
+ * cos/sin [T, hd/2] are the model's RoPE tables (model.cpp:43-53); lse
+ * [B,H,T] is saved for the backward. hd in {32, 64, 128}. */
+int ttk_attention_fwd(const float* q, const float* k, const float* v, const float* cos_t,
+                      const float* sin_t, float* o, float* lse, int64_t B, int64_t T, int64_t H,
+                      int64_t hd, float scale, void* stream);
+/* dq, dk, dv (+)= gradients w.r.t. the pre-RoPE q, k and v. `workspace` must
+ * hold ttk_attention_bwd_workspace_size(B,T,H,hd) bytes. */
+size_t ttk_attention_bwd_workspace_size(int64_t B, int64_t T, int64_t H, int64_t hd);
+int ttk_attention_bwd(const float* q, const float* k, const float* v, const float* cos_t,
+                      const float* sin_t, const float* o, const float* lse, const float* dout,
+                      float* dq, float* dk, float* dv, int accumulate, int64_t B, int64_t T,
+                      int64_t H, int64_t hd, float scale, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* out[i,:] = W[idx[i],:] (ops.cpp:746-759); idx validated against V. */
+int ttk_embedding_fwd(const float* W, const int64_t* idx, float* out, int64_t N, int64_t D,
+                      int64_t V, void* stream);
+/* dW[idx[i],:] += dout[i,:] in ascending i per row, deterministic and
+ * bit-identical to the reference's sequential loop (ops.cpp:761-772).
+ * `workspace` must hold ttk_embedding_bwd_workspace_size(N) bytes. */
+size_t ttk_embedding_bwd_workspace_size(int64_t N);
+int ttk_embedding_bwd(const float* dout, const int64_t* idx, float* dW, int64_t N, int64_t D,
+                      int64_t V, void* workspace, size_t workspace_bytes, void* stream);
+/* Range check of ids on the device: *bad = number of ids outside [0, V). */
+int ttk_index_check(const int64_t* idx, int64_t n, int64_t V, int64_t* bad_host, void* stream);
+
+/* RoPE on x [B,T,H,D] with cos/sin [T,D/2] (ops.cpp:970-999) and its
+ * transpose rotation for the backward (ops.cpp:1011-1023). */
+int ttk_rope_fwd(const float* x, const float* cos_t, const float* sin_t, float* y, int64_t B,
+                 int64_t T, int64_t H, int64_t D, void* stream);
+int ttk_rope_bwd(const float* dy, const float* cos_t, const float* sin_t, float* dx,
+                 int accumulate, int64_t B, int64_t T, int64_t H, int64_t D, void* stream);
+
+/* Row softmax / log-softmax over the last dim of [R,C] (ops.cpp:777-896);
+ * backward: dx (+)= y*(dy - sum(dy*y)) resp. dy - exp(y)*sum(dy). */
+int ttk_softmax_fwd(const float* x, float* y, int64_t R, int64_t C, int log, void* stream);
+int ttk_softmax_bwd(const float* y, const float* dy, float* dx, int accumulate, int64_t R,
+                    int64_t C, int log, void* stream);
+
+/* --------------------------------------------------------------- optimizer */
+
+/* Sum of squares of a list of tensors, accumulated in fp64 into *acc
+ * (device double); the global grad norm for clipping. */
+int ttk_sumsq_multi(const float* const* ptrs, const int64_t* sizes, int n_tensors, double* acc,
+                    void* stream);
+/* One fused AdamW step over a list of tensors (optim.cpp:17-48: decoupled
+ * decay with lr before the moments, bias correction folded into lr_t, eps on
+ * the uncorrected sqrt(v)), with global-norm clipping folded in: the gradient
+ * is multiplied by min(1, max_norm / (sqrt(*sumsq) + 1e-6)) read on the
+ * device (max_norm <= 0 disables it) and by grad_scale (e.g. 1/world for an
+ * all-reduced sum). step is the 1-based step count. */
+int ttk_adamw_multi(float* const* params, const float* const* grads, float* const* m,
+                    float* const* v, const int64_t* sizes, int n_tensors, float lr, float beta1,
+                    float beta2, float eps, float weight_decay, int64_t step,
+                    const double* sumsq, float max_norm, float grad_scale, void* stream);
+/* SGD with momentum / L2 decay (optim.cpp:58-82) on one tensor. */
+int ttk_sgd(float* p, const float* g, float* vel, int64_t n, float lr, float momentum,
+            float weight_decay, void* stream);
+
+/* -------------------------------------------------- generic tensor kernels */
+
+/* Elementwise ops on up-to-8-D broadcast views. shape[] is the output shape;
+ * a_strides / b_strides are element strides of each input expressed in the
+ * output's index space (0 on broadcast dims). Binary ops: 0 add, 1 sub,
+ * 2 mul, 3 div (ops.cpp:139-266). */
+#define TTK_MAX_DIMS 8
+int ttk_binary(int op, const float* a, const int64_t* a_strides, const float* b,
+               const int64_t* b_strides, float* out, const int64_t* shape, int ndim,
+               void* stream);
+/* Gradient of a binary op w.r.t. one input, accumulated into grad (which has
+ * the output's shape when `reduce` is 0). which = 0: d/da, 1: d/db. */
+int ttk_binary_bwd(int op, int which, const float* a, const int64_t* a_strides, const float* b,
+                   const int64_t* b_strides, const float* dout, float* g_full,
+                   const int64_t* shape, int ndim, void* stream);
+/* Unary ops: 0 neg, 1 exp, 2 log, 3 sqrt, 4 tanh, 5 silu, 6 sin, 7 cos,
+ * 8 pow(p) (ops.cpp:268-363); y = f(x). */
+int ttk_unary(int op, const float* x, float* y, int64_t n, float p, void* stream);
+/* dx (+)= dy * f'(x) (the b_* rules of ops.cpp:314-363). */
+int ttk_unary_bwd(int op, const float* x, const float* dy, float* dx, int64_t n, float p,
+                  void* stream);
+/* out[o, i] (+)= sum_k in[o, k, i] over [outer, K, inner] (ops.cpp:367-439 sum). */
+int ttk_reduce_mid(const float* in, float* out, int64_t outer, int64_t K, int64_t inner,
+                   int accumulate, void* stream);
+/* *out (+)= sum of n elements (fp64 accumulate, like ops.cpp:441-460). */
+int ttk_sum_all(const float* in, int64_t n, float* out, int accumulate, void* stream);
+/* out = in viewed through (shape, in_strides) made contiguous; accumulate
+ * adds instead. Implements permute/transpose/expand copies
+ * (ops.cpp:534-629). scatter_add = 1 performs the reverse: out[in_view] +=
+ * in_contiguous (permute/expand backward). */
+int ttk_strided_copy(const float* in, const int64_t* in_strides, float* out,
+                     const int64_t* shape, int ndim, int accumulate, int scatter_add,
+                     void* stream);
+int ttk_fill(float* x, float v, int64_t n, void* stream);
+/* y (+)= alpha * x. */
+int ttk_axpy(float alpha, const float* x, float* y, int64_t n, void* stream);
+/* out[k] (+)= sum over the dims of `shape` whose bit is clear in keep_mask of
+ * g[...] (g contiguous with shape `shape`; out contiguous over the kept
+ * dims). The broadcast-gradient reduction (ops.cpp:35-61 bcast_add). */
+int ttk_reduce_to(const float* g, const int64_t* shape, int ndim, unsigned keep_mask, float* out,
+                  int accumulate, void* stream);
+/* mask[i] = (u_i >= p) ? 1 : 0 with u_i from the reference's xorshift64*
+ * stream for `seed` (ops.cpp:949-963), generated on the device by jumping
+ * the stream; see ttk_dropout_mask in generic_kernels.cu. */
+int ttk_dropout_mask(float* mask, int64_t n, float p, uint64_t seed, void* stream);
+
+/* ---------------------------------------------------------------- training */
+
+/* Counter-based N(0, std) init on the device (seeded; not the reference's
+ * sequential xorshift stream, which is generated on the host instead). */
+int ttk_init_normal(float* x, int64_t n, float std, uint64_t seed, void* stream);
+
+/* -------------------------------------------------------------- collectives */
+
+/* NCCL over NVLink / NVSwitch, one communicator per rank (one process per
+ * GPU). The library is loaded on first use. */
+int ttk_dist_unique_id(unsigned char out[128]);
+int ttk_dist_init(int rank, int world, const unsigned char id[128], void** comm);
+int ttk_dist_destroy(void* comm);
+/* In-place sum over ranks of n fp32 values. */
+int ttk_dist_allreduce_f32(void* comm, float* buf, int64_t n, void* stream);
+int ttk_dist_allreduce_f64(void* comm, double* buf, int64_t n, void* stream);
+/* Non-zero when the communicator reported an asynchronous error. */
+int ttk_dist_async_error(void* comm, int* err);
+int ttk_dist_abort(void* comm);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TTK_H */

@@ -1,0 +1,138 @@
+"""Generates the golden fixtures in tests/golden/ by running the tinytrain
+reference's own CPU library (oracle/_ref/libttref.so, built by
+`make -C oracle` from the reference sources) on seeded inputs.
+
+    python tests/golden/make_golden.py            # op + tiny-model fixtures
+    python tests/golden/make_golden.py --cfg0     # + the 30-step config-0 run (~11 min)
+
+Fixtures:
+  ops_small.npz   per-op inputs, outputs and gradients (matmul incl. ragged
+                  shapes, linear, bmm, rmsnorm, swiglu, softmax, cross-entropy,
+                  embedding with repeated ids, rope, attention, AdamW)
+  model_tiny.npz  a 2-layer model: weights, tokens, logits, loss, all grads,
+                  and 10 AdamW+clip steps of losses and final weights
+  train_cfg0.json the 13.3M default model (dim 256, 6 layers, 8 heads, ffn 768,
+                  vocab 32000), batch 16 x seq 128, 30 steps of AdamW (lr 3e-4,
+                  betas 0.9/0.95, wd 0.1, clip 1.0): per-step losses and grad
+                  norms; inputs are regenerated from the recorded seeds and
+                  checked by the recorded checksums
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
+sys.path.insert(0, HERE)
+
+from oracle import refbind as rb  # noqa: E402
+import inputs  # noqa: E402
+
+TINY = dict(vocab=64, dim=32, layers=2, heads=4, ffn=48, max_seq=16)
+CFG0 = dict(vocab=32000, dim=256, layers=6, heads=8, ffn=768, max_seq=256)
+
+
+def ops_small():
+    rng = np.random.default_rng(1234)
+    u = lambda *s: rng.uniform(-1, 1, s).astype(np.float32)
+    n = lambda *s: rng.standard_normal(s).astype(np.float32)
+    out = {}
+    for tag, (M, K, N) in {"a": (4, 5, 3), "b": (64, 48, 40), "c": (130, 70, 33),
+                           "d": (128, 256, 96)}.items():
+        A, B, G = u(M, K), u(K, N), u(M, N)
+        Cm, dA, dB = rb.matmul(A, B, G)
+        out.update({f"mm_{tag}_A": A, f"mm_{tag}_B": B, f"mm_{tag}_G": G, f"mm_{tag}_C": Cm,
+                    f"mm_{tag}_dA": dA, f"mm_{tag}_dB": dB})
+    X, W, G = u(96, 64), u(80, 64), u(96, 80)
+    Y, dX, dW = rb.linear(X, W, G)
+    out.update(lin_X=X, lin_W=W, lin_G=G, lin_Y=Y, lin_dX=dX, lin_dW=dW)
+    A, B, G = u(3, 17, 9), u(3, 9, 11), u(3, 17, 11)
+    Cm, dA, dB = rb.bmm(A, B, G)
+    out.update(bmm_A=A, bmm_B=B, bmm_G=G, bmm_C=Cm, bmm_dA=dA, bmm_dB=dB)
+    X, W, G = u(48, 256), u(256), u(48, 256)
+    Y, dX, dW = rb.rmsnorm(X, W, 1e-5, G)
+    out.update(rms_X=X, rms_W=W, rms_G=G, rms_Y=Y, rms_dX=dX, rms_dW=dW)
+    A, B, G = rng.uniform(-4, 4, (40, 96)).astype(np.float32), u(40, 96), u(40, 96)
+    Y, dA, dB = rb.swiglu(A, B, G)
+    out.update(swi_A=A, swi_B=B, swi_G=G, swi_Y=Y, swi_dA=dA, swi_dB=dB)
+    X, G = n(24, 77) * 3, u(24, 77)
+    Y, dX = rb.softmax(X, G)
+    out.update(sm_X=X, sm_G=G, sm_Y=Y, sm_dX=dX)
+    L = n(32, 1000) * 2
+    t = rng.integers(0, 1000, 32)
+    loss, dL = rb.cross_entropy(L, t)
+    out.update(ce_L=L, ce_t=t, ce_loss=np.float32(loss), ce_dL=dL)
+    W = n(50, 16)
+    idx = np.array([0, 3, 3, 49, 1, 3, 0, 7, 7, 7, 12], np.int64)
+    G = n(len(idx), 16)
+    o, dW = rb.embedding(W, idx, G)
+    out.update(emb_W=W, emb_idx=idx, emb_G=G, emb_out=o, emb_dW=dW)
+    X = n(2, 9, 3, 8)
+    cs, sn = rng.uniform(-1, 1, (9, 4)).astype(np.float32), rng.uniform(-1, 1, (9, 4)).astype(np.float32)
+    G = n(2, 9, 3, 8)
+    Y, dX = rb.rope(X, cs, sn, G)
+    out.update(rope_X=X, rope_cos=cs, rope_sin=sn, rope_G=G, rope_Y=Y, rope_dX=dX)
+    for tag, (B, T, H, hd) in {"a": (2, 16, 3, 8), "b": (1, 70, 2, 32), "c": (1, 128, 2, 64)}.items():
+        q, k, v, G = n(B, T, H, hd), n(B, T, H, hd), n(B, T, H, hd), n(B, T, H * hd)
+        O, dq, dk, dv = rb.attention(q, k, v, 10000.0, G)
+        out.update({f"att_{tag}_q": q, f"att_{tag}_k": k, f"att_{tag}_v": v, f"att_{tag}_G": G,
+                    f"att_{tag}_O": O, f"att_{tag}_dq": dq, f"att_{tag}_dk": dk,
+                    f"att_{tag}_dv": dv})
+    p, gs = n(1000), n(6, 1000)
+    out.update(adam_p=p, adam_g=gs, adam_out=rb.adamw(p, gs, 1e-2, 0.9, 0.95, 1e-8, 0.1))
+    np.savez_compressed(os.path.join(HERE, "ops_small.npz"), **out)
+
+
+def model_tiny():
+    c = rb.cfg(**TINY)
+    shapes = inputs.param_shapes(TINY["vocab"], TINY["dim"], TINY["layers"], TINY["heads"],
+                                 TINY["ffn"])
+    assert shapes == rb.param_shapes(c)
+    w = inputs.make_weights(shapes, seed=7, std=0.3)
+    B, T, steps = 2, 16, 10
+    idx, tgt = inputs.make_tokens(steps, B, T, TINY["vocab"], seed=8)
+    logits, loss, grads = rb.model_fwd_bwd(c, w, idx[0], tgt[0], B, T)
+    lrs = np.full(steps, 1e-2, np.float32)
+    losses, norms, wf = rb.train(c, w, idx, tgt, B, T, lrs, 0.9, 0.95, 1e-8, 0.1, 1.0)
+    np.savez_compressed(os.path.join(HERE, "model_tiny.npz"), weights=w, idx=idx, tgt=tgt,
+                        logits=logits, loss=np.float32(loss), grads=grads, lrs=lrs,
+                        losses=losses, norms=norms, final=wf,
+                        cfg=np.array([TINY[k] for k in ("vocab", "dim", "layers", "heads", "ffn",
+                                                         "max_seq")], np.int64))
+
+
+def train_cfg0(steps=30):
+    c = rb.cfg(**CFG0)
+    shapes = inputs.param_shapes(CFG0["vocab"], CFG0["dim"], CFG0["layers"], CFG0["heads"],
+                                 CFG0["ffn"])
+    w = inputs.make_weights(shapes, seed=42)
+    B, T = 16, 128
+    idx, tgt = inputs.make_tokens(steps, B, T, CFG0["vocab"], seed=43)
+    lrs = np.full(steps, 3e-4, np.float32)
+    t0 = time.time()
+    losses, norms, wf = rb.train(c, w, idx, tgt, B, T, lrs, 0.9, 0.95, 1e-8, 0.1, 1.0)
+    secs = time.time() - t0
+    rec = dict(cfg=CFG0, B=B, T=T, steps=steps, weight_seed=42, weight_std=0.02, token_seed=43,
+               lr=3e-4, betas=[0.9, 0.95], eps=1e-8, weight_decay=0.1, clip=1.0,
+               n_params=int(w.size), weight_checksum=inputs.checksum(w),
+               token_checksum=int(idx.sum() + tgt.sum()), losses=[float(x) for x in losses],
+               grad_norms=[float(x) for x in norms], final_checksum=inputs.checksum(wf),
+               cpu_seconds=secs, numpy=np.__version__)
+    with open(os.path.join(HERE, "train_cfg0.json"), "w") as f:
+        json.dump(rec, f, indent=1)
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--cfg0", action="store_true")
+    a = ap.parse_args()
+    ops_small()
+    model_tiny()
+    if a.cfg0:
+        train_cfg0()

@@ -1,0 +1,100 @@
+"""Parity of the tcgen05 3xTF32 GEMM (ttk_gemm) with the reference's sgemm.
+
+Small shapes: against fixtures the reference produced (tests/golden/
+ops_small.npz: matmul forward, dA = G B^T, dB = A^T G; Linear through the
+transpose; bmm). Sweep shapes (M, K, N) of the op-level benchmark: against an
+fp64 product on the same seeded U(-1, 1) inputs, for forward, dX and dW.
+Tolerance: max|err| / max|ref| <= 1e-4 (the per-op bound), the 3xTF32 path
+typically lands near 1e-6.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+def t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+@pytest.mark.parametrize("tag", ["a", "b", "c", "d"])
+def test_matmul_golden(cuda, golden_ops, tag):
+    from tinytrain_b200 import kernels as K
+    g = golden_ops
+    A, B, G = (t(g[f"mm_{tag}_{n}"], cuda) for n in "ABG")
+    C = K.gemm(A, B)
+    dA = K.gemm(G, B, transB=True)
+    dB = K.gemm(A, G, transA=True)
+    torch.cuda.synchronize()
+    assert rel_err(C.cpu().numpy(), g[f"mm_{tag}_C"]) < TOL
+    assert rel_err(dA.cpu().numpy(), g[f"mm_{tag}_dA"]) < TOL
+    assert rel_err(dB.cpu().numpy(), g[f"mm_{tag}_dB"]) < TOL
+
+
+def test_linear_golden(cuda, golden_ops):
+    from tinytrain_b200 import kernels as K
+    g = golden_ops
+    X, W, G = t(g["lin_X"], cuda), t(g["lin_W"], cuda), t(g["lin_G"], cuda)
+    Y = K.linear_fwd(X, W)
+    dX, dW = K.linear_bwd(X, W, G)
+    assert rel_err(Y.cpu().numpy(), g["lin_Y"]) < TOL
+    assert rel_err(dX.cpu().numpy(), g["lin_dX"]) < TOL
+    assert rel_err(dW.cpu().numpy(), g["lin_dW"]) < TOL
+
+
+def test_bmm_golden(cuda, golden_ops):
+    from tinytrain_b200 import kernels as K
+    g = golden_ops
+    A, B, G = t(g["bmm_A"], cuda), t(g["bmm_B"], cuda), t(g["bmm_G"], cuda)
+    C = K.gemm(A, B)
+    dA = K.gemm(G, B, transB=True)
+    dB = K.gemm(A, G, transA=True)
+    assert rel_err(C.cpu().numpy(), g["bmm_C"]) < TOL
+    assert rel_err(dA.cpu().numpy(), g["bmm_dA"]) < TOL
+    assert rel_err(dB.cpu().numpy(), g["bmm_dB"]) < TOL
+
+
+def test_accumulate_beta(cuda):
+    from tinytrain_b200 import kernels as K
+    gen = torch.Generator(device=cuda).manual_seed(5)
+    A = torch.rand(300, 200, device=cuda, generator=gen) * 2 - 1
+    B = torch.rand(200, 260, device=cuda, generator=gen) * 2 - 1
+    C0 = torch.rand(300, 260, device=cuda, generator=gen) * 2 - 1
+    C = C0.clone()
+    K.gemm(A, B, C_out=C, beta=1.0)
+    ref = C0.double() + A.double() @ B.double()
+    assert rel_err(C.cpu().numpy(), ref.cpu().numpy()) < TOL
+    C = C0.clone()
+    K.gemm(A, B, C_out=C, alpha=0.5, beta=-2.0)
+    ref = -2.0 * C0.double() + 0.5 * (A.double() @ B.double())
+    assert rel_err(C.cpu().numpy(), ref.cpu().numpy()) < TOL
+
+
+@pytest.mark.parametrize("M,K,N", [(2048, 256, 256), (2048, 256, 32000), (8192, 768, 2048),
+                                   (16384, 2048, 5632)])
+def test_sweep_shapes(cuda, M, K, N):
+    """Linear forward (X W^T), dX (dY W) and dW (dY^T X) at the sweep shapes."""
+    from tinytrain_b200 import kernels as Kn
+    gen = torch.Generator(device=cuda).manual_seed(M + K + N)
+    X = torch.rand(M, K, device=cuda, generator=gen) * 2 - 1
+    W = torch.rand(N, K, device=cuda, generator=gen) * 2 - 1
+    dY = torch.rand(M, N, device=cuda, generator=gen) * 2 - 1
+    Y = Kn.linear_fwd(X, W)
+    dX, dW = Kn.linear_bwd(X, W, dY)
+    Xd, Wd, dYd = X.double(), W.double(), dY.double()
+    for got, ref in ((Y, Xd @ Wd.T), (dX, dYd @ Wd), (dW, dYd.T @ Xd)):
+        err = (got.double() - ref).abs().max().item() / ref.abs().max().item()
+        assert err < TOL, err
+    from tinytrain_b200 import _ttk
+    assert _ttk.device_status() == 0
+
+
+def test_rejects_bad_args(cuda):
+    from tinytrain_b200 import _ttk
+    with pytest.raises(_ttk.TtkError):
+        _ttk.call("ttk_gemm", 0, 0, 1, 4, 4, 4, 1.0, None, 4, 16, None, 4, 16, 0.0, None, 4, 16,
+                  None, 0, None)

@@ -1,0 +1,600 @@
+// fp32-accurate GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+//   C[b] = alpha * op(A[b]) @ op(B[b]) + beta * C[b]      (row-major fp32)
+//
+// Replaces the reference's CPU sgemm (ops.cpp:96-125) under matmul
+// (ops.cpp:661-697: forward, dA = G @ B^T, dB = A^T @ G) and bmm
+// (ops.cpp:699-742). op(X) = X or X^T is taken by reading the operand
+// K-major or MN-major straight from its storage; no transposed copies.
+//
+// Precision: 3xTF32. Each operand is split once by split_tf32_kernel into
+// hi = rna_tf32(x) and lo = x - hi (both exactly representable where it
+// matters), stored as two planes; the MMA accumulates hi*hi + hi*lo + lo*hi in
+// an fp32 TMEM accumulator, which gives fp32-level accuracy (the dropped lo*lo
+// term is ~2^-22 relative).
+//
+// Kernel structure (persistent, one CTA per SM, 64 + 32*EPI_WARPS threads):
+//   warp 0      TMA producer: 4-stage ring of {A hi|lo, B hi|lo} K-slices
+//               (BK = 16 fp32 = 64 B rows), one TMA per operand per stage (hi
+//               and lo planes are one extra tensor dimension)
+//   warp 1      TMEM allocator + MMA issuer (one lane): 2 k-steps x 3 products
+//               of tcgen05.mma.kind::tf32 M128 x BN x K8 per stage; commit
+//               frees the stage. Each 256-wide K chunk accumulates into its own
+//               TMEM buffer (a ring of 512/BN buffers of BN columns)
+//   warps 2..   epilogue: drain each chunk buffer with tcgen05.ld into fp32
+//               registers (each thread: one row x 128 columns), free it, and
+//               store the finished tile with alpha/beta; the ring lets the
+//               MMAs of the next chunk / tile run while a chunk is drained
+// Loads never use .multicast::cluster.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ttk_common.cuh"
+#include "ttk_internal.h"
+
+namespace ttk {
+
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 16;  // fp32 elements per k-slice: 64 bytes = one SW64 row
+constexpr int STAGES = 4;
+constexpr int GROUP_M = 16;  // tile raster: bands of 16 M-tiles sweep N
+// K extent accumulated inside TMEM before the partial sum is promoted to the
+// epilogue's fp32 registers. The tensor-core accumulator rounds with a bias
+// (its error grows linearly with K), so long sums are built from 256-wide
+// chunks added with round-to-nearest FADD; error then grows like sqrt(K/256).
+constexpr int KCHUNK_BLOCKS = 16;
+
+template <int BN>
+struct Cfg {
+    static constexpr int A_PLANE = BM * BK * 4;
+    static constexpr int B_PLANE = BN * BK * 4;
+    static constexpr int A_BYTES = 2 * A_PLANE;  // hi | lo
+    static constexpr int B_BYTES = 2 * B_PLANE;
+    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int NBUF = 512 / BN;            // TMEM chunk buffers
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int EPI_WARPS = 4 * (BN / 128);  // each thread: 1 row x 128 columns
+    static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
+    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct Params {
+    int64_t M, N, K, batch;
+    int a_mn, b_mn;  // 1: operand is MN-major in its storage
+    float alpha, beta;
+    float* C;
+    int64_t ldc, strideC;
+    int num_m, num_n, num_k;
+    int64_t num_tiles;
+};
+
+__device__ __forceinline__ void tile_coords(const Params& p, int64_t t, int& b, int& m, int& n) {
+    int64_t per_batch = static_cast<int64_t>(p.num_m) * p.num_n;
+    b = static_cast<int>(t / per_batch);
+    int64_t r = t % per_batch;
+    int64_t band = static_cast<int64_t>(GROUP_M) * p.num_n;
+    int64_t g = r / band;
+    int first_m = static_cast<int>(g * GROUP_M);
+    int gsize = min(p.num_m - first_m, GROUP_M);
+    int64_t rr = r % band;
+    m = first_m + static_cast<int>(rr % gsize);
+    n = static_cast<int>(rr / gsize);
+}
+
+// Descriptor of one K=8 sub-slice (ks = 0, 1) of an operand tile plane.
+// K-major, 64B swizzle: rows of 64 B (16 fp32 of K), 8-row groups 512 B
+// apart (SBO); the k sub-slice is a 32 B offset inside the swizzled row.
+// MN-major (tf32 admits only the 128B-swizzle-with-32B-atoms layout):
+// 32-element (128 B) chunks of the M/N extent, BK k-rows of 128 B each, so
+// chunks are BK*128 B apart (LBO) and 4-row swizzle groups 512 B apart (SBO);
+// the k sub-slice (8 rows) is a 1024 B step.
+constexpr uint32_t kLayoutSW64 = 4;
+constexpr uint32_t kLayoutSW128Base32B = 1;
+__device__ __forceinline__ uint64_t operand_desc(uint32_t plane_addr, int mn_major, int ks) {
+    if (mn_major)
+        return umma_smem_desc(plane_addr + ks * 1024, BK * 128, 512, kLayoutSW128Base32B);
+    return umma_smem_desc(plane_addr + ks * 32, 16, 512, kLayoutSW64);
+}
+
+template <int BN>
+__global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
+    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b, const Params p) {
+    using CF = Cfg<BN>;
+    constexpr int NBUF = CF::NBUF;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * CF::STAGE_BYTES);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + STAGES;
+    uint64_t* cfull = bars + 2 * STAGES;
+    uint64_t* cempty = bars + 2 * STAGES + NBUF;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 2 * NBUF);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < NBUF; ++b) {
+            mbar_init(&cfull[b], 1);
+            mbar_init(&cempty[b], 32 * CF::EPI_WARPS);
+        }
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch_desc(&map_a);
+        tma_prefetch_desc(&map_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, CF::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int s = 0;
+            uint32_t ph = 0;
+            // Parity each stage was last armed with (-1: never), so that an
+            // abort can wait for copies still landing in shared memory.
+            int armed_ph[STAGES];
+#pragma unroll
+            for (int i = 0; i < STAGES; ++i)
+                armed_ph[i] = -1;
+            for (int64_t t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
+                int b, mt, nt;
+                tile_coords(p, t, b, mt, nt);
+                for (int kb = 0; kb < p.num_k; ++kb) {
+                    if (!mbar_wait(&empty[s], ph ^ 1, 1)) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    uint8_t* sa = smem + s * CF::STAGE_BYTES;
+                    uint8_t* sb = sa + CF::A_BYTES;
+                    mbar_arrive_expect_tx(&full[s], CF::STAGE_BYTES);
+                    const int k0 = kb * BK;
+                    if (p.a_mn)
+                        tma_load_5d(sa, &map_a, &full[s], 0, k0, mt * (BM / 32), 0, b);
+                    else
+                        tma_load_4d(sa, &map_a, &full[s], k0, mt * BM, 0, b);
+                    if (p.b_mn)
+                        tma_load_5d(sb, &map_b, &full[s], 0, k0, nt * (BN / 32), 0, b);
+                    else
+                        tma_load_4d(sb, &map_b, &full[s], k0, nt * BN, 0, b);
+                    armed_ph[s] = static_cast<int>(ph);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
+                }
+            }
+            // On abort, let armed copies land before the CTA's smem is released.
+            if (*abort_flag) {
+#pragma unroll
+                for (int i = 0; i < STAGES; ++i)
+                    if (armed_ph[i] >= 0)
+                        mbar_wait(&full[i], static_cast<uint32_t>(armed_ph[i]), 5);
+            }
+        }
+    } else if (warp == 1) {
+        // -------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_tf32(BM, BN, p.a_mn, p.b_mn);
+            int s = 0;
+            uint32_t ph = 0;
+            int64_t g = 0;  // chunk counter across this CTA's tiles
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < p.num_tiles && ok && !*abort_flag; t += gridDim.x) {
+                for (int kc = 0; kc < p.num_k && ok; kc += KCHUNK_BLOCKS, ++g) {
+                    const int buf = static_cast<int>(g % NBUF);
+                    const uint32_t cph = static_cast<uint32_t>((g / NBUF) & 1);
+                    if (!mbar_wait(&cempty[buf], cph ^ 1, 2)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + buf * BN;
+                    const int kend = min(p.num_k, kc + KCHUNK_BLOCKS);
+                    for (int kb = kc; kb < kend; ++kb) {
+                        if (!mbar_wait(&full[s], ph, 3)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sa = smem_u32(smem + s * CF::STAGE_BYTES);
+                        const uint32_t sb = sa + CF::A_BYTES;
+#pragma unroll
+                        for (int ks = 0; ks < BK / 8; ++ks) {
+                            const uint64_t a_hi = operand_desc(sa, p.a_mn, ks);
+                            const uint64_t a_lo = operand_desc(sa + CF::A_PLANE, p.a_mn, ks);
+                            const uint64_t b_hi = operand_desc(sb, p.b_mn, ks);
+                            const uint64_t b_lo = operand_desc(sb + CF::B_PLANE, p.b_mn, ks);
+                            const uint32_t acc = (kb > kc || ks > 0) ? 1u : 0u;
+                            mma_tf32(d_tmem, a_lo, b_hi, idesc, acc);
+                            mma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
+                            mma_tf32(d_tmem, a_hi, b_hi, idesc, 1u);
+                        }
+                        mma_commit(&empty[s]);
+                        if (++s == STAGES) {
+                            s = 0;
+                            ph ^= 1;
+                        }
+                    }
+                    // Fires once every MMA issued so far has retired, also on
+                    // abort, so TMEM is quiescent before the epilogue / dealloc.
+                    mma_commit(&cfull[buf]);
+                }
+            }
+            if (!ok)
+                *abort_flag = 1;
+        }
+    } else {
+        // ---------------------------------------------------------- epilogue
+        const int e = warp - 2;
+        const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+        const int col_base = (e >> 2) * 128;
+        const int row_in_tile = quarter * 32 + lane;
+        const bool vec_ok = ((p.ldc & 3) == 0) &&
+                            ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
+                            ((p.strideC & 3) == 0);
+        int64_t g = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+            float acc[128];
+#pragma unroll
+            for (int j = 0; j < 128; ++j)
+                acc[j] = 0.0f;
+            for (int kc = 0; kc < p.num_k; kc += KCHUNK_BLOCKS, ++g) {
+                const int buf = static_cast<int>(g % NBUF);
+                const uint32_t cph = static_cast<uint32_t>((g / NBUF) & 1);
+                if (*abort_flag || !mbar_wait(&cfull[buf], cph, 4)) {
+                    ok = false;
+                    *abort_flag = 1;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float v[32];
+                    tmem_ld_32x32b_x32(tmem_base + buf * BN + col_base + c * 32 +
+                                           (static_cast<uint32_t>(quarter * 32) << 16),
+                                       v);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        acc[c * 32 + j] += v[j];
+                }
+                tc_fence_before();
+                mbar_arrive(&cempty[buf]);
+            }
+            if (!ok)
+                break;
+            int b, mt, nt;
+            tile_coords(p, t, b, mt, nt);
+            const int64_t row = static_cast<int64_t>(mt) * BM + row_in_tile;
+            if (row >= p.M)
+                continue;
+            const int64_t col0 = static_cast<int64_t>(nt) * BN + col_base;
+            float* dst = p.C + b * p.strideC + row * p.ldc + col0;
+            if (vec_ok && col0 + 128 <= p.N) {
+#pragma unroll
+                for (int j = 0; j < 128; j += 4) {
+                    float4 o = make_float4(p.alpha * acc[j], p.alpha * acc[j + 1],
+                                           p.alpha * acc[j + 2], p.alpha * acc[j + 3]);
+                    if (p.beta != 0.0f) {
+                        const float4 ci = *reinterpret_cast<const float4*>(dst + j);
+                        o.x += p.beta * ci.x;
+                        o.y += p.beta * ci.y;
+                        o.z += p.beta * ci.z;
+                        o.w += p.beta * ci.w;
+                    }
+                    *reinterpret_cast<float4*>(dst + j) = o;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 128; ++j) {
+                    if (col0 + j < p.N) {
+                        float o = p.alpha * acc[j];
+                        if (p.beta != 0.0f)
+                            o += p.beta * dst[j];
+                        dst[j] = o;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, CF::TMEM_COLS);
+    }
+}
+
+// hi = rna_tf32(x), lo = x - hi, written as planes dst[b][0|1][r][0..ld_pad)
+// with zeros in the padding columns [cols, ld_pad).
+__global__ void split_tf32_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
+                                  int64_t ld, int64_t bstride, int64_t batch,
+                                  float* __restrict__ dst, int64_t ld_pad) {
+    const int64_t per_row = ld_pad / 4;  // float4 groups per padded row
+    const int64_t total = batch * rows * per_row;
+    const int64_t plane = rows * ld_pad;
+    const bool vec = ((ld & 3) == 0) && ((bstride & 3) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t g = i % per_row;
+        const int64_t r = (i / per_row) % rows;
+        const int64_t b = i / (per_row * rows);
+        const int64_t c0 = g * 4;
+        const float* s = src + b * bstride + r * ld + c0;
+        float x[4];
+        if (vec && c0 + 4 <= cols) {
+            float4 t = __ldg(reinterpret_cast<const float4*>(s));
+            x[0] = t.x, x[1] = t.y, x[2] = t.z, x[3] = t.w;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                x[j] = (c0 + j < cols) ? __ldg(s + j) : 0.0f;
+        }
+        float hi[4], lo[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            uint32_t h;
+            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x[j]));
+            hi[j] = __uint_as_float(h);
+            lo[j] = x[j] - hi[j];
+        }
+        float* d = dst + b * 2 * plane + r * ld_pad + c0;
+        *reinterpret_cast<float4*>(d) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<float4*>(d + plane) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+}
+
+__global__ void scale_kernel(float* C, int64_t batch, int64_t M, int64_t N, int64_t ldc,
+                             int64_t strideC, float beta) {
+    const int64_t total = batch * M * N;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t n = i % N, m = (i / N) % M, b = i / (M * N);
+        float* c = C + b * strideC + m * ldc + n;
+        *c = beta == 0.0f ? 0.0f : beta * *c;
+    }
+}
+
+}  // namespace gemm
+
+// ------------------------------------------------------------- host side --
+
+namespace {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+// Storage geometry of one split operand: rows x cols per batch, padded to
+// ld_pad (multiple of 16 floats), planes hi|lo.
+struct SplitGeom {
+    int64_t rows, cols, ld_pad;
+    size_t bytes(int64_t batch) const {
+        return static_cast<size_t>(batch) * 2 * rows * ld_pad * sizeof(float);
+    }
+};
+
+// K-major map: dims {cols(K), rows(M|N), plane, batch}, box {BK, tile, 2, 1},
+//               64B swizzle.
+// MN-major map: dims {32, rows(K), cols/32 chunks, plane, batch},
+//               box {32, BK, tile/32, 2, 1}, 128B swizzle with 32B atoms.
+int make_operand_map(CUtensorMap* map, const float* base, const SplitGeom& g, int64_t batch,
+                     int mn_major, int tile) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc)
+        return set_error(TTK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t plane = static_cast<cuuint64_t>(g.rows * g.ld_pad * 4);
+    CUresult r;
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    if (!mn_major) {
+        cuuint64_t dims[4] = {static_cast<cuuint64_t>(g.cols), static_cast<cuuint64_t>(g.rows), 2,
+                              static_cast<cuuint64_t>(batch)};
+        cuuint64_t strides[3] = {static_cast<cuuint64_t>(g.ld_pad * 4), plane, 2 * plane};
+        cuuint32_t box[4] = {gemm::BK, static_cast<cuuint32_t>(tile), 2, 1};
+        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    } else {
+        cuuint64_t dims[5] = {32, static_cast<cuuint64_t>(g.rows),
+                              static_cast<cuuint64_t>(g.ld_pad / 32), 2,
+                              static_cast<cuuint64_t>(batch)};
+        cuuint64_t strides[4] = {static_cast<cuuint64_t>(g.ld_pad * 4), 128, plane, 2 * plane};
+        cuuint32_t box[5] = {32, gemm::BK, static_cast<cuuint32_t>(tile / 32), 2, 1};
+        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(base), dims, strides,
+                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    }
+    if (r != CUDA_SUCCESS)
+        return set_error(TTK_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+    return TTK_OK;
+}
+
+int num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0)
+            n = 148;
+    }
+    return n;
+}
+
+template <int BN>
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, gemm::Params p,
+                cudaStream_t stream) {
+    using CF = gemm::Cfg<BN>;
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64)
+        return set_error(TTK_ERR_ARG, "gemm: device ordinal out of range");
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(gemm::gemm_tf32x3_kernel<BN>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 CF::SMEM_BYTES) != cudaSuccess)
+            return set_error(TTK_ERR_CUDA, "cudaFuncSetAttribute(gemm) failed");
+        attr_set[dev] = true;
+    }
+    p.num_n = static_cast<int>((p.N + BN - 1) / BN);
+    p.num_tiles = static_cast<int64_t>(p.num_m) * p.num_n * p.batch;
+    const int grid = static_cast<int>(std::min<int64_t>(p.num_tiles, num_sms()));
+    gemm::gemm_tf32x3_kernel<BN><<<grid, CF::NUM_THREADS, CF::SMEM_BYTES, stream>>>(ma, mb, p);
+    return check_launch("gemm_tf32x3_kernel");
+}
+
+struct GemmPlan {
+    SplitGeom ga, gb;
+    size_t off_b, total;
+};
+
+GemmPlan plan(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K) {
+    GemmPlan pl;
+    // op(A) = A [M,K] (K-major) or A^T with A stored [K,M] (MN-major).
+    // K-major rows are padded to 16 floats, MN-major rows to 32 (whole chunks).
+    pl.ga = transA ? SplitGeom{K, M, round_up(M, 32)} : SplitGeom{M, K, round_up(K, 16)};
+    // op(B) = B [K,N] (MN-major) or B^T with B stored [N,K] (K-major).
+    pl.gb = transB ? SplitGeom{N, K, round_up(K, 16)} : SplitGeom{K, N, round_up(N, 32)};
+    pl.off_b = static_cast<size_t>(round_up(static_cast<int64_t>(pl.ga.bytes(batch)), 256));
+    pl.total = pl.off_b + pl.gb.bytes(batch);
+    return pl;
+}
+
+}  // namespace
+
+size_t gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
+                           int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0)
+        return 0;
+    return plan(transA, transB, batch, M, N, K).total;
+}
+
+int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+               int64_t batch, float* dst, int64_t ld_pad, cudaStream_t stream) {
+    const int64_t total = batch * rows * (ld_pad / 4);
+    if (total == 0)
+        return TTK_OK;
+    const int threads = 256;
+    const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
+    gemm::split_tf32_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(
+        src, rows, cols, ld, bstride, batch, dst, ld_pad);
+    return check_launch("split_tf32_kernel");
+}
+
+int gemm_tf32x3(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                float alpha, const float* A, int64_t lda, int64_t strideA, const float* B,
+                int64_t ldb, int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC,
+                void* ws, size_t ws_bytes, cudaStream_t stream) {
+    if (M < 0 || N < 0 || K < 0 || batch < 0)
+        return set_error(TTK_ERR_ARG, "gemm: negative size");
+    if (M == 0 || N == 0 || batch == 0)
+        return TTK_OK;
+    if (!C || (K > 0 && (!A || !B)))
+        return set_error(TTK_ERR_ARG, "gemm: null pointer");
+    if (ldc < N)
+        return set_error(TTK_ERR_ARG, "gemm: ldc < N");
+    if (K == 0 || alpha == 0.0f) {
+        if (beta == 1.0f)
+            return TTK_OK;
+        const int64_t total = batch * M * N;
+        const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
+        gemm::scale_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(C, batch, M, N, ldc,
+                                                                         strideC, beta);
+        return check_launch("scale_kernel");
+    }
+    if (M > (1ll << 31) / 2 || N > (1ll << 31) / 2 || K > (1ll << 31) / 2)
+        return set_error(TTK_ERR_ARG, "gemm: dimension too large");
+    const GemmPlan pl = plan(transA, transB, batch, M, N, K);
+    if (!ws || ws_bytes < pl.total)
+        return set_error(TTK_ERR_ARG, "gemm: workspace too small");
+    if ((transA ? lda < M : lda < K) || (transB ? ldb < K : ldb < N))
+        return set_error(TTK_ERR_ARG, "gemm: leading dimension too small");
+    float* wa = static_cast<float*>(ws);
+    float* wb = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.off_b);
+    int rc = split_tf32(A, pl.ga.rows, pl.ga.cols, lda, strideA, batch, wa, pl.ga.ld_pad, stream);
+    if (rc)
+        return rc;
+    rc = split_tf32(B, pl.gb.rows, pl.gb.cols, ldb, strideB, batch, wb, pl.gb.ld_pad, stream);
+    if (rc)
+        return rc;
+    return gemm_tf32x3_presplit(transA, transB, batch, M, N, K, alpha, wa, pl.ga.ld_pad, wb,
+                                pl.gb.ld_pad, beta, C, ldc, strideC, stream);
+}
+
+int gemm_tf32x3_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                         float alpha, const float* a_split, int64_t lda_pad,
+                         const float* b_split, int64_t ldb_pad, float beta, float* C,
+                         int64_t ldc, int64_t strideC, cudaStream_t stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0)
+        return set_error(TTK_ERR_ARG, "gemm_presplit: sizes must be positive");
+    // K-major planes: leading dimension a multiple of 16; MN-major: of 32.
+    if ((reinterpret_cast<uintptr_t>(a_split) & 15) || (reinterpret_cast<uintptr_t>(b_split) & 15) ||
+        (lda_pad & (transA ? 31 : 15)) || (ldb_pad & (transB ? 15 : 31)))
+        return set_error(TTK_ERR_ARG, "gemm_presplit: split planes misaligned or badly padded");
+    SplitGeom ga = transA ? SplitGeom{K, M, lda_pad} : SplitGeom{M, K, lda_pad};
+    SplitGeom gb = transB ? SplitGeom{N, K, ldb_pad} : SplitGeom{K, N, ldb_pad};
+    if (ga.ld_pad < ga.cols || gb.ld_pad < gb.cols)
+        return set_error(TTK_ERR_ARG, "gemm_presplit: padded leading dimension too small");
+    gemm::Params p{};
+    p.M = M, p.N = N, p.K = K, p.batch = batch;
+    p.a_mn = transA ? 1 : 0;
+    p.b_mn = transB ? 0 : 1;
+    p.alpha = alpha, p.beta = beta;
+    p.C = C, p.ldc = ldc, p.strideC = strideC;
+    p.num_m = static_cast<int>((M + gemm::BM - 1) / gemm::BM);
+    p.num_k = static_cast<int>((K + gemm::BK - 1) / gemm::BK);
+    // BN = 256 unless the N extent is small or 256-wide tiles would leave most
+    // SMs idle.
+    const int64_t tiles256 = p.num_m * ((N + 255) / 256) * batch;
+    const bool use128 = N <= 128 || tiles256 < num_sms();
+    const int bn = use128 ? 128 : 256;
+    CUtensorMap ma, mb;
+    int rc = make_operand_map(&ma, a_split, ga, batch, p.a_mn, gemm::BM);
+    if (rc)
+        return rc;
+    rc = make_operand_map(&mb, b_split, gb, batch, p.b_mn, bn);
+    if (rc)
+        return rc;
+    return use128 ? launch_gemm<128>(ma, mb, p, stream) : launch_gemm<256>(ma, mb, p, stream);
+}
+
+}  // namespace ttk

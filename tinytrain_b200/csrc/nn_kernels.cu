@@ -1,0 +1,715 @@
+// Bandwidth-bound NN kernels: RMSNorm, SwiGLU, fused cross-entropy,
+// embedding gather / deterministic scatter-add, RoPE, row softmax.
+//
+// All are HBM-bound: float4 coalesced access, warp-shuffle reductions, one
+// read and one write of each tensor where the algorithm allows (the fused
+// cross-entropy keeps its 32000-wide row in registers between the reduction
+// and the gradient write).
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ttk_common.cuh"
+#include "ttk_internal.h"
+
+namespace ttk {
+namespace nn {
+
+// ------------------------------------------------------------- RMSNorm --
+// One warp per row (ops.cpp:932-942: r = (sum(x^2)/D + eps)^-1/2, y = x*r*w).
+__global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                   float* __restrict__ y, float* __restrict__ rstd, int64_t R,
+                                   int64_t D, float eps) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    const bool vec = (D & 3) == 0;
+    for (int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         row < R; row += warps) {
+        const float* xr = x + row * D;
+        float ss = 0.0f;
+        if (vec) {
+            for (int64_t c = lane * 4; c < D; c += 128) {
+                float4 v = *reinterpret_cast<const float4*>(xr + c);
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+            }
+        } else {
+            for (int64_t c = lane; c < D; c += 32)
+                ss += xr[c] * xr[c];
+        }
+        ss = warp_sum(ss);
+        const float r = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+        if (lane == 0 && rstd)
+            rstd[row] = r;
+        float* yr = y + row * D;
+        if (vec) {
+            for (int64_t c = lane * 4; c < D; c += 128) {
+                float4 v = *reinterpret_cast<const float4*>(xr + c);
+                float4 g = *reinterpret_cast<const float4*>(w + c);
+                float4 o = make_float4(v.x * r * g.x, v.y * r * g.y, v.z * r * g.z, v.w * r * g.w);
+                *reinterpret_cast<float4*>(yr + c) = o;
+            }
+        } else {
+            for (int64_t c = lane; c < D; c += 32)
+                yr[c] = xr[c] * r * w[c];
+        }
+    }
+}
+
+// dx = r*(dy*w) - x * r^3/D * sum(dy*w*x); dw partial per block (fixed order).
+// Block: 8 warps; block b owns rows [b*rpb, (b+1)*rpb); partial[b][D].
+__global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                   const float* __restrict__ rstd, const float* __restrict__ dy,
+                                   float* __restrict__ dx, int accumulate,
+                                   float* __restrict__ partial, int64_t R, int64_t D,
+                                   int64_t rpb) {
+    extern __shared__ float sdw[];  // [8][D]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t r0 = blockIdx.x * rpb;
+    const int64_t r1 = min(R, r0 + rpb);
+    for (int64_t c = threadIdx.x; c < 8 * D; c += blockDim.x)
+        sdw[c] = 0.0f;
+    __syncthreads();
+    float* mydw = sdw + warp * D;
+    for (int64_t row = r0 + warp; row < r1; row += 8) {
+        const float* xr = x + row * D;
+        const float* gr = dy + row * D;
+        const float r = rstd[row];
+        float dot = 0.0f;
+        for (int64_t c = lane; c < D; c += 32)
+            dot += gr[c] * w[c] * xr[c];
+        dot = warp_sum(dot);
+        const float k = r * r * r / static_cast<float>(D) * dot;
+        for (int64_t c = lane; c < D; c += 32) {
+            const float gx = gr[c];
+            const float xv = xr[c];
+            if (dx) {
+                float v = r * (gx * w[c]) - xv * k;
+                dx[row * D + c] = accumulate ? dx[row * D + c] + v : v;
+            }
+            mydw[c] += gx * xv * r;
+        }
+    }
+    __syncthreads();
+    if (partial) {
+        for (int64_t c = threadIdx.x; c < D; c += blockDim.x) {
+            float s = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                s += sdw[i * D + c];
+            partial[blockIdx.x * D + c] = s;
+        }
+    }
+}
+
+// dw[c] += sum_b partial[b][c], b ascending.
+__global__ void colsum_kernel(const float* __restrict__ partial, int64_t nb, int64_t D,
+                              float* __restrict__ out) {
+    for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < D;
+         c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        float s = 0.0f;
+        for (int64_t b = 0; b < nb; ++b)
+            s += partial[b * D + c];
+        out[c] += s;
+    }
+}
+
+// -------------------------------------------------------------- SwiGLU --
+__device__ __forceinline__ float silu_f(float a) { return a / (1.0f + expf(-a)); }
+
+__global__ void swiglu_fwd_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                  float* __restrict__ y, int64_t n) {
+    const int64_t n4 = n / 4;
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += stride) {
+        float4 av = reinterpret_cast<const float4*>(a)[i];
+        float4 bv = reinterpret_cast<const float4*>(b)[i];
+        reinterpret_cast<float4*>(y)[i] = make_float4(silu_f(av.x) * bv.x, silu_f(av.y) * bv.y,
+                                                      silu_f(av.z) * bv.z, silu_f(av.w) * bv.w);
+    }
+    for (int64_t i = n4 * 4 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += stride)
+        y[i] = silu_f(a[i]) * b[i];
+}
+
+__device__ __forceinline__ void swiglu_grad(float a, float b, float g, float& da, float& db) {
+    const float s = 1.0f / (1.0f + expf(-a));
+    da = (g * b) * (s * (1.0f + a * (1.0f - s)));
+    db = g * (a / (1.0f + expf(-a)));
+}
+
+__global__ void swiglu_bwd_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                  const float* __restrict__ dy, float* __restrict__ da,
+                                  float* __restrict__ db, int accumulate, int64_t n) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t n4 = n / 4;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += stride) {
+        float4 av = reinterpret_cast<const float4*>(a)[i];
+        float4 bv = reinterpret_cast<const float4*>(b)[i];
+        float4 gv = reinterpret_cast<const float4*>(dy)[i];
+        float4 oa, ob;
+        swiglu_grad(av.x, bv.x, gv.x, oa.x, ob.x);
+        swiglu_grad(av.y, bv.y, gv.y, oa.y, ob.y);
+        swiglu_grad(av.z, bv.z, gv.z, oa.z, ob.z);
+        swiglu_grad(av.w, bv.w, gv.w, oa.w, ob.w);
+        if (accumulate) {
+            float4 pa = reinterpret_cast<float4*>(da)[i];
+            float4 pb = reinterpret_cast<float4*>(db)[i];
+            oa.x += pa.x, oa.y += pa.y, oa.z += pa.z, oa.w += pa.w;
+            ob.x += pb.x, ob.y += pb.y, ob.z += pb.z, ob.w += pb.w;
+        }
+        reinterpret_cast<float4*>(da)[i] = oa;
+        reinterpret_cast<float4*>(db)[i] = ob;
+    }
+    for (int64_t i = n4 * 4 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += stride) {
+        float oa, ob;
+        swiglu_grad(a[i], b[i], dy[i], oa, ob);
+        da[i] = accumulate ? da[i] + oa : oa;
+        db[i] = accumulate ? db[i] + ob : ob;
+    }
+}
+
+// ------------------------------------------------------- cross-entropy --
+// One 1024-thread block per row; the row (C <= 32768) stays in registers
+// between the max / sum-exp reduction and the gradient write.
+constexpr int CE_THREADS = 1024;
+constexpr int CE_VEC = 8;  // float4 per thread -> 32768 floats per row
+
+template <bool IN_REGS>
+__global__ void __launch_bounds__(CE_THREADS, 1)
+    cross_entropy_kernel(const float* __restrict__ logits, const int64_t* __restrict__ targets,
+                         int64_t N, int64_t C, double* __restrict__ loss_acc,
+                         float* __restrict__ dlogits, float grad_scale) {
+    __shared__ float s_red[32];
+    __shared__ double s_redd[32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool vec = (C & 3) == 0;
+    for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
+        const float* xr = logits + row * C;
+        float v[IN_REGS ? CE_VEC * 4 : 1];
+        float m = -INFINITY;
+        if (IN_REGS) {
+#pragma unroll
+            for (int j = 0; j < CE_VEC; ++j) {
+                const int64_t c = (static_cast<int64_t>(j) * CE_THREADS + threadIdx.x) * 4;
+                float4 t4;
+                if (vec && c + 4 <= C) {
+                    t4 = __ldg(reinterpret_cast<const float4*>(xr + c));
+                } else {
+                    t4.x = c < C ? xr[c] : -INFINITY;
+                    t4.y = c + 1 < C ? xr[c + 1] : -INFINITY;
+                    t4.z = c + 2 < C ? xr[c + 2] : -INFINITY;
+                    t4.w = c + 3 < C ? xr[c + 3] : -INFINITY;
+                }
+                v[4 * j] = t4.x, v[4 * j + 1] = t4.y, v[4 * j + 2] = t4.z, v[4 * j + 3] = t4.w;
+                m = fmaxf(m, fmaxf(fmaxf(t4.x, t4.y), fmaxf(t4.z, t4.w)));
+            }
+        } else {
+            for (int64_t c = threadIdx.x; c < C; c += CE_THREADS)
+                m = fmaxf(m, xr[c]);
+        }
+        m = warp_max(m);
+        if (lane == 0)
+            s_red[warp] = m;
+        __syncthreads();
+        m = s_red[lane];
+        m = warp_max(m);
+        __syncthreads();
+        double s = 0.0;
+        if (IN_REGS) {
+#pragma unroll
+            for (int j = 0; j < CE_VEC * 4; ++j)
+                s += static_cast<double>(expf(v[j] - m));  // exp(-inf) = 0 for padding
+        } else {
+            for (int64_t c = threadIdx.x; c < C; c += CE_THREADS)
+                s += static_cast<double>(expf(xr[c] - m));
+        }
+        s = warp_sum_d(s);
+        if (lane == 0)
+            s_redd[warp] = s;
+        __syncthreads();
+        s = s_redd[lane];
+        s = warp_sum_d(s);
+        const float lse = m + static_cast<float>(log(s));
+        const int64_t t = targets[row];
+        const bool t_ok = t >= 0 && t < C;
+        if (threadIdx.x == 0) {
+            if (t_ok)
+                atomicAdd(loss_acc, static_cast<double>(-(xr[t] - lse)));
+            else
+                report(kErrBadIndex);
+        }
+        if (dlogits) {
+            float* dr = dlogits + row * C;
+            if (IN_REGS) {
+#pragma unroll
+                for (int j = 0; j < CE_VEC; ++j) {
+                    const int64_t c = (static_cast<int64_t>(j) * CE_THREADS + threadIdx.x) * 4;
+                    float o[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float p = expf(v[4 * j + q] - lse);
+                        o[q] = grad_scale * (c + q == t ? p - 1.0f : p);
+                    }
+                    if (vec && c + 4 <= C) {
+                        *reinterpret_cast<float4*>(dr + c) = make_float4(o[0], o[1], o[2], o[3]);
+                    } else {
+                        for (int q = 0; q < 4; ++q)
+                            if (c + q < C)
+                                dr[c + q] = o[q];
+                    }
+                }
+            } else {
+                for (int64_t c = threadIdx.x; c < C; c += CE_THREADS) {
+                    const float p = expf(xr[c] - lse);
+                    dr[c] = grad_scale * (c == t ? p - 1.0f : p);
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+__global__ void loss_finalize_kernel(const double* acc, float scale, float* out) {
+    out[0] = static_cast<float>(acc[0] * static_cast<double>(scale));
+}
+
+// ----------------------------------------------------------- embedding --
+__global__ void embedding_fwd_kernel(const float* __restrict__ W, const int64_t* __restrict__ idx,
+                                     float* __restrict__ out, int64_t N, int64_t D, int64_t V) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    const bool vec = (D & 3) == 0;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         i < N; i += warps) {
+        const int64_t t = idx[i];
+        if (t < 0 || t >= V) {
+            if (lane == 0)
+                report(kErrBadIndex);
+            continue;
+        }
+        const float* src = W + t * D;
+        float* dst = out + i * D;
+        if (vec) {
+            for (int64_t c = lane * 4; c < D; c += 128)
+                *reinterpret_cast<float4*>(dst + c) = *reinterpret_cast<const float4*>(src + c);
+        } else {
+            for (int64_t c = lane; c < D; c += 32)
+                dst[c] = src[c];
+        }
+    }
+}
+
+// Keys (id << 32 | position) sorted ascending give, per id, its positions in
+// ascending order: the reference's accumulation order (ops.cpp:766-771).
+__global__ void make_keys_kernel(const int64_t* __restrict__ idx, int64_t N, int64_t Npow2,
+                                 uint64_t* __restrict__ keys) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < Npow2;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        keys[i] = i < N ? (static_cast<uint64_t>(idx[i]) << 32) | static_cast<uint64_t>(i)
+                        : ~0ull;
+}
+
+// Bitonic sort of Npow2 keys held in shared memory by one block.
+__global__ void bitonic_smem_kernel(uint64_t* __restrict__ keys, int64_t Npow2) {
+    extern __shared__ uint64_t sk[];
+    for (int64_t i = threadIdx.x; i < Npow2; i += blockDim.x)
+        sk[i] = keys[i];
+    __syncthreads();
+    for (int64_t k = 2; k <= Npow2; k <<= 1) {
+        for (int64_t j = k >> 1; j > 0; j >>= 1) {
+            for (int64_t i = threadIdx.x; i < Npow2; i += blockDim.x) {
+                const int64_t p = i ^ j;
+                if (p > i) {
+                    const bool up = (i & k) == 0;
+                    const uint64_t a = sk[i], b = sk[p];
+                    if ((a > b) == up) {
+                        sk[i] = b;
+                        sk[p] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int64_t i = threadIdx.x; i < Npow2; i += blockDim.x)
+        keys[i] = sk[i];
+}
+
+// One compare-exchange pass (k, j) of a global-memory bitonic sort.
+__global__ void bitonic_global_kernel(uint64_t* __restrict__ keys, int64_t Npow2, int64_t k,
+                                      int64_t j) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < Npow2;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t p = i ^ j;
+        if (p > i) {
+            const bool up = (i & k) == 0;
+            const uint64_t a = keys[i], b = keys[p];
+            if ((a > b) == up) {
+                keys[i] = b;
+                keys[p] = a;
+            }
+        }
+    }
+}
+
+// One warp per sorted position; the warp that starts a run of equal ids adds
+// the run's gradient rows into dW[id] sequentially, in position order.
+__global__ void embedding_segment_kernel(const uint64_t* __restrict__ keys, int64_t N,
+                                         const float* __restrict__ dout, float* __restrict__ dW,
+                                         int64_t D, int64_t V) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t p = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         p < N; p += warps) {
+        const uint64_t id = keys[p] >> 32;
+        if (p > 0 && (keys[p - 1] >> 32) == id)
+            continue;
+        if (id >= static_cast<uint64_t>(V)) {
+            if (lane == 0)
+                report(kErrBadIndex);
+            continue;
+        }
+        int64_t end = p + 1;
+        while (end < N && (keys[end] >> 32) == id)
+            ++end;
+        float* drow = dW + static_cast<int64_t>(id) * D;
+        for (int64_t c = lane; c < D; c += 32) {
+            float acc = drow[c];
+            for (int64_t q = p; q < end; ++q) {
+                const int64_t pos = static_cast<int64_t>(keys[q] & 0xffffffffull);
+                acc += dout[pos * D + c];
+            }
+            drow[c] = acc;
+        }
+    }
+}
+
+__global__ void index_check_kernel(const int64_t* __restrict__ idx, int64_t n, int64_t V,
+                                   unsigned long long* __restrict__ bad) {
+    unsigned long long cnt = 0;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        cnt += (idx[i] < 0 || idx[i] >= V) ? 1 : 0;
+    if (cnt)
+        atomicAdd(bad, cnt);
+}
+
+// ---------------------------------------------------------------- RoPE --
+// x [B,T,H,D], cos/sin [T,D/2]; pair (d, d + D/2) rotated (ops.cpp:970-999).
+__global__ void rope_kernel(const float* __restrict__ x, const float* __restrict__ cs,
+                            const float* __restrict__ sn, float* __restrict__ y, int accumulate,
+                            int backward, int64_t B, int64_t T, int64_t H, int64_t D) {
+    const int64_t Dh = D / 2;
+    const int64_t total = B * T * H * Dh;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t d = i % Dh;
+        const int64_t bth = i / Dh;
+        const int64_t t = (bth / H) % T;
+        const int64_t base = bth * D;
+        const float x1 = x[base + d], x2 = x[base + Dh + d];
+        const float c = cs[t * Dh + d], s = sn[t * Dh + d];
+        float o1, o2;
+        if (!backward) {
+            o1 = x1 * c - x2 * s;
+            o2 = x1 * s + x2 * c;
+        } else {  // transpose rotation (ops.cpp:1020-1021)
+            o1 = x1 * c + x2 * s;
+            o2 = -x1 * s + x2 * c;
+        }
+        if (accumulate) {
+            y[base + d] += o1;
+            y[base + Dh + d] += o2;
+        } else {
+            y[base + d] = o1;
+            y[base + Dh + d] = o2;
+        }
+    }
+}
+
+// -------------------------------------------------------------- softmax --
+// One warp per row; two passes over the row (max; sum in double; write).
+__global__ void softmax_fwd_kernel(const float* __restrict__ x, float* __restrict__ y, int64_t R,
+                                   int64_t C, int log_out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         row < R; row += warps) {
+        const float* xr = x + row * C;
+        float* yr = y + row * C;
+        float m = -1e30f;  // the reference's initial max (ops.cpp:794)
+        for (int64_t c = lane; c < C; c += 32)
+            m = fmaxf(m, xr[c]);
+        m = warp_max(m);
+        double s = 0.0;
+        for (int64_t c = lane; c < C; c += 32)
+            s += static_cast<double>(expf(xr[c] - m));
+        s = warp_sum_d(s);
+        if (log_out) {
+            const float lse = m + static_cast<float>(log(s));
+            for (int64_t c = lane; c < C; c += 32)
+                yr[c] = xr[c] - lse;
+        } else {
+            const float inv = static_cast<float>(1.0 / s);
+            for (int64_t c = lane; c < C; c += 32)
+                yr[c] = expf(xr[c] - m) * inv;
+        }
+    }
+}
+
+// softmax: dx (+)= y*(dy - sum(dy*y)); log_softmax: dx (+)= dy - exp(y)*sum(dy).
+__global__ void softmax_bwd_kernel(const float* __restrict__ y, const float* __restrict__ dy,
+                                   float* __restrict__ dx, int accumulate, int64_t R, int64_t C,
+                                   int log_in) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    for (int64_t row = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+         row < R; row += warps) {
+        const float* yr = y + row * C;
+        const float* gr = dy + row * C;
+        float* dr = dx + row * C;
+        double s = 0.0;
+        for (int64_t c = lane; c < C; c += 32)
+            s += log_in ? static_cast<double>(gr[c])
+                        : static_cast<double>(gr[c]) * static_cast<double>(yr[c]);
+        s = warp_sum_d(s);
+        const float sf = static_cast<float>(s);
+        for (int64_t c = lane; c < C; c += 32) {
+            const float v = log_in ? gr[c] - expf(yr[c]) * sf : yr[c] * (gr[c] - sf);
+            dr[c] = accumulate ? dr[c] + v : v;
+        }
+    }
+}
+
+}  // namespace nn
+}  // namespace ttk
+
+using namespace ttk;
+using namespace ttk::nn;
+
+static inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+extern "C" {
+
+int ttk_rmsnorm_fwd(const float* x, const float* w, float* y, float* rstd, int64_t R, int64_t D,
+                    float eps, void* stream) {
+    if (R < 0 || D <= 0 || !x || !w || !y)
+        return set_error(TTK_ERR_ARG, "rmsnorm_fwd: bad arguments");
+    if (R == 0)
+        return TTK_OK;
+    if ((D & 3) == 0 && !(aligned16(x) && aligned16(w) && aligned16(y)))
+        return set_error(TTK_ERR_ARG, "rmsnorm_fwd: tensors must be 16-byte aligned");
+    rmsnorm_fwd_kernel<<<grid_for(R, 8), 256, 0, S(stream)>>>(x, w, y, rstd, R, D, eps);
+    return check_launch("rmsnorm_fwd_kernel");
+}
+
+static int64_t rms_blocks(int64_t R) { return std::min<int64_t>(std::max<int64_t>(R / 64, 1), 296); }
+
+size_t ttk_rmsnorm_bwd_workspace_size(int64_t R, int64_t D) {
+    return static_cast<size_t>(rms_blocks(R) * D) * sizeof(float);
+}
+
+int ttk_rmsnorm_bwd(const float* x, const float* w, const float* rstd, const float* dy, float* dx,
+                    int accumulate_dx, float* dw, int64_t R, int64_t D, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+    if (R < 0 || D <= 0 || !x || !w || !rstd || !dy)
+        return set_error(TTK_ERR_ARG, "rmsnorm_bwd: bad arguments");
+    if (R == 0)
+        return TTK_OK;
+    const int64_t nb = rms_blocks(R);
+    const int64_t rpb = (R + nb - 1) / nb;
+    float* partial = nullptr;
+    if (dw) {
+        if (!workspace || workspace_bytes < ttk_rmsnorm_bwd_workspace_size(R, D))
+            return set_error(TTK_ERR_ARG, "rmsnorm_bwd: workspace too small");
+        partial = static_cast<float*>(workspace);
+    }
+    const size_t smem = static_cast<size_t>(8 * D) * sizeof(float);
+    if (smem > 200 * 1024)
+        return set_error(TTK_ERR_ARG, "rmsnorm_bwd: D too large");
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(rmsnorm_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem));
+    rmsnorm_bwd_kernel<<<static_cast<int>(nb), 256, smem, S(stream)>>>(
+        x, w, rstd, dy, dx, accumulate_dx, partial, R, D, rpb);
+    int rc = check_launch("rmsnorm_bwd_kernel");
+    if (rc || !dw)
+        return rc;
+    colsum_kernel<<<grid_for(D, 256), 256, 0, S(stream)>>>(partial, nb, D, dw);
+    return check_launch("colsum_kernel");
+}
+
+int ttk_swiglu_fwd(const float* a, const float* b, float* y, int64_t n, void* stream) {
+    if (n < 0 || (n && (!a || !b || !y)))
+        return set_error(TTK_ERR_ARG, "swiglu_fwd: bad arguments");
+    if (!n)
+        return TTK_OK;
+    if (!(aligned16(a) && aligned16(b) && aligned16(y)))
+        return set_error(TTK_ERR_ARG, "swiglu_fwd: tensors must be 16-byte aligned");
+    swiglu_fwd_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, S(stream)>>>(a, b, y, n);
+    return check_launch("swiglu_fwd_kernel");
+}
+
+int ttk_swiglu_bwd(const float* a, const float* b, const float* dy, float* da, float* db,
+                   int accumulate, int64_t n, void* stream) {
+    if (n < 0 || (n && (!a || !b || !dy || !da || !db)))
+        return set_error(TTK_ERR_ARG, "swiglu_bwd: bad arguments");
+    if (!n)
+        return TTK_OK;
+    if (!(aligned16(a) && aligned16(b) && aligned16(dy) && aligned16(da) && aligned16(db)))
+        return set_error(TTK_ERR_ARG, "swiglu_bwd: tensors must be 16-byte aligned");
+    swiglu_bwd_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, S(stream)>>>(a, b, dy, da, db,
+                                                                       accumulate, n);
+    return check_launch("swiglu_bwd_kernel");
+}
+
+int ttk_cross_entropy(const float* logits, const int64_t* targets, int64_t N, int64_t C,
+                      double* loss_acc, float* dlogits, float grad_scale, void* stream) {
+    if (N < 0 || C <= 0 || !logits || !targets || !loss_acc)
+        return set_error(TTK_ERR_ARG, "cross_entropy: bad arguments");
+    if (!N)
+        return TTK_OK;
+    if ((C & 3) == 0 && !(aligned16(logits) && (!dlogits || aligned16(dlogits))))
+        return set_error(TTK_ERR_ARG, "cross_entropy: tensors must be 16-byte aligned");
+    const int grid = static_cast<int>(std::min<int64_t>(N, 148 * 2));
+    if (C <= static_cast<int64_t>(CE_THREADS) * CE_VEC * 4)
+        cross_entropy_kernel<true><<<grid, CE_THREADS, 0, S(stream)>>>(logits, targets, N, C,
+                                                                       loss_acc, dlogits,
+                                                                       grad_scale);
+    else
+        cross_entropy_kernel<false><<<grid, CE_THREADS, 0, S(stream)>>>(logits, targets, N, C,
+                                                                        loss_acc, dlogits,
+                                                                        grad_scale);
+    return check_launch("cross_entropy_kernel");
+}
+
+int ttk_loss_finalize(const double* loss_acc, float scale, float* loss_out, void* stream) {
+    loss_finalize_kernel<<<1, 1, 0, S(stream)>>>(loss_acc, scale, loss_out);
+    return check_launch("loss_finalize_kernel");
+}
+
+int ttk_embedding_fwd(const float* W, const int64_t* idx, float* out, int64_t N, int64_t D,
+                      int64_t V, void* stream) {
+    if (N < 0 || D <= 0 || V <= 0 || (N && (!W || !idx || !out)))
+        return set_error(TTK_ERR_ARG, "embedding_fwd: bad arguments");
+    if (!N)
+        return TTK_OK;
+    if ((D & 3) == 0 && !(aligned16(W) && aligned16(out)))
+        return set_error(TTK_ERR_ARG, "embedding_fwd: tensors must be 16-byte aligned");
+    embedding_fwd_kernel<<<grid_for(N, 8), 256, 0, S(stream)>>>(W, idx, out, N, D, V);
+    return check_launch("embedding_fwd_kernel");
+}
+
+static int64_t pow2_at_least(int64_t n) {
+    int64_t p = 1;
+    while (p < n)
+        p <<= 1;
+    return p;
+}
+
+size_t ttk_embedding_bwd_workspace_size(int64_t N) {
+    return static_cast<size_t>(pow2_at_least(std::max<int64_t>(N, 1))) * sizeof(uint64_t);
+}
+
+int ttk_embedding_bwd(const float* dout, const int64_t* idx, float* dW, int64_t N, int64_t D,
+                      int64_t V, void* workspace, size_t workspace_bytes, void* stream) {
+    if (N < 0 || D <= 0 || V <= 0 || (N && (!dout || !idx || !dW)))
+        return set_error(TTK_ERR_ARG, "embedding_bwd: bad arguments");
+    if (!N)
+        return TTK_OK;
+    if (N >= (1ll << 32) || V >= (1ll << 31))
+        return set_error(TTK_ERR_ARG, "embedding_bwd: N or V too large");
+    const int64_t np2 = pow2_at_least(N);
+    if (!workspace || workspace_bytes < static_cast<size_t>(np2) * sizeof(uint64_t))
+        return set_error(TTK_ERR_ARG, "embedding_bwd: workspace too small");
+    uint64_t* keys = static_cast<uint64_t*>(workspace);
+    make_keys_kernel<<<grid_for(np2, 256), 256, 0, S(stream)>>>(idx, N, np2, keys);
+    int rc = check_launch("make_keys_kernel");
+    if (rc)
+        return rc;
+    const size_t smem = static_cast<size_t>(np2) * sizeof(uint64_t);
+    if (smem <= 128 * 1024) {
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(bitonic_smem_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 static_cast<int>(smem));
+        bitonic_smem_kernel<<<1, 1024, smem, S(stream)>>>(keys, np2);
+        rc = check_launch("bitonic_smem_kernel");
+    } else {
+        for (int64_t k = 2; k <= np2 && !rc; k <<= 1)
+            for (int64_t j = k >> 1; j > 0 && !rc; j >>= 1) {
+                bitonic_global_kernel<<<grid_for(np2, 256), 256, 0, S(stream)>>>(keys, np2, k, j);
+                rc = check_launch("bitonic_global_kernel");
+            }
+    }
+    if (rc)
+        return rc;
+    embedding_segment_kernel<<<grid_for(N, 8), 256, 0, S(stream)>>>(keys, N, dout, dW, D, V);
+    return check_launch("embedding_segment_kernel");
+}
+
+int ttk_index_check(const int64_t* idx, int64_t n, int64_t V, int64_t* bad_host, void* stream) {
+    if (n <= 0) {
+        *bad_host = 0;
+        return TTK_OK;
+    }
+    unsigned long long* d = nullptr;
+    int rc = check_cuda(cudaMallocAsync(reinterpret_cast<void**>(&d), 8, S(stream)), "alloc");
+    if (rc)
+        return rc;
+    cudaMemsetAsync(d, 0, 8, S(stream));
+    index_check_kernel<<<grid_for(n, 256), 256, 0, S(stream)>>>(idx, n, V, d);
+    unsigned long long h = 0;
+    cudaMemcpyAsync(&h, d, 8, cudaMemcpyDeviceToHost, S(stream));
+    cudaFreeAsync(d, S(stream));
+    rc = check_cuda(cudaStreamSynchronize(S(stream)), "index_check");
+    *bad_host = static_cast<int64_t>(h);
+    return rc;
+}
+
+int ttk_rope_fwd(const float* x, const float* cos_t, const float* sin_t, float* y, int64_t B,
+                 int64_t T, int64_t H, int64_t D, void* stream) {
+    if (B < 0 || T < 0 || H < 0 || D <= 0 || (D & 1))
+        return set_error(TTK_ERR_ARG, "rope: head dim must be even");
+    const int64_t total = B * T * H * (D / 2);
+    if (!total)
+        return TTK_OK;
+    rope_kernel<<<grid_for(total, 256), 256, 0, S(stream)>>>(x, cos_t, sin_t, y, 0, 0, B, T, H, D);
+    return check_launch("rope_kernel");
+}
+
+int ttk_rope_bwd(const float* dy, const float* cos_t, const float* sin_t, float* dx,
+                 int accumulate, int64_t B, int64_t T, int64_t H, int64_t D, void* stream) {
+    if (B < 0 || T < 0 || H < 0 || D <= 0 || (D & 1))
+        return set_error(TTK_ERR_ARG, "rope: head dim must be even");
+    const int64_t total = B * T * H * (D / 2);
+    if (!total)
+        return TTK_OK;
+    rope_kernel<<<grid_for(total, 256), 256, 0, S(stream)>>>(dy, cos_t, sin_t, dx, accumulate, 1,
+                                                             B, T, H, D);
+    return check_launch("rope_kernel");
+}
+
+int ttk_softmax_fwd(const float* x, float* y, int64_t R, int64_t C, int log, void* stream) {
+    if (R < 0 || C <= 0)
+        return set_error(TTK_ERR_ARG, "softmax: bad shape");
+    if (!R)
+        return TTK_OK;
+    softmax_fwd_kernel<<<grid_for(R, 8), 256, 0, S(stream)>>>(x, y, R, C, log);
+    return check_launch("softmax_fwd_kernel");
+}
+
+int ttk_softmax_bwd(const float* y, const float* dy, float* dx, int accumulate, int64_t R,
+                    int64_t C, int log, void* stream) {
+    if (R < 0 || C <= 0)
+        return set_error(TTK_ERR_ARG, "softmax: bad shape");
+    if (!R)
+        return TTK_OK;
+    softmax_bwd_kernel<<<grid_for(R, 8), 256, 0, S(stream)>>>(y, dy, dx, accumulate, R, C, log);
+    return check_launch("softmax_bwd_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,233 @@
+// Runtime services of the ttk C ABI: error reporting, the device status
+// word, a stream-ordered caching allocator, copies, streams and events.
+//
+// Memory: each device's default cudaMemPool with an unbounded release
+// threshold, so freed blocks stay cached in the pool and later ttk_malloc
+// calls are served without a driver round trip (the B200-native replacement
+// for the reference's per-op std::vector allocate + zero-fill,
+// tensor.cpp:13-31).
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "ttk_common.cuh"
+#include "ttk_internal.h"
+
+namespace ttk {
+
+__device__ unsigned g_device_status = 0;
+
+namespace {
+thread_local std::string t_last_error;
+}
+
+int set_error(int code, const char* msg) {
+    t_last_error = msg ? msg : "";
+    return code;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess)
+        return TTK_OK;
+    t_last_error = std::string(what) + ": " + cudaGetErrorString(e);
+    return TTK_ERR_CUDA;
+}
+
+int check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+
+const char* last_error_cstr() { return t_last_error.c_str(); }
+
+}  // namespace ttk
+
+using namespace ttk;
+
+static inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+
+extern "C" {
+
+const char* ttk_last_error(void) { return last_error_cstr(); }
+
+const char* ttk_version(void) { return "ttk 0.1 sm_100a"; }
+
+int ttk_init(int device) {
+    int rc = check_cuda(cudaSetDevice(device), "cudaSetDevice");
+    if (rc)
+        return rc;
+    cudaMemPool_t pool;
+    rc = check_cuda(cudaDeviceGetDefaultMemPool(&pool, device), "cudaDeviceGetDefaultMemPool");
+    if (rc)
+        return rc;
+    uint64_t threshold = UINT64_MAX;
+    rc = check_cuda(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold),
+                    "cudaMemPoolSetAttribute");
+    if (rc)
+        return rc;
+    return check_cuda(cudaFree(nullptr), "context init");
+}
+
+int ttk_device_count(int* n) { return check_cuda(cudaGetDeviceCount(n), "cudaGetDeviceCount"); }
+
+int ttk_device_status(unsigned* bits) {
+    int rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    if (rc)
+        return rc;
+    unsigned v = 0, zero = 0;
+    rc = check_cuda(cudaMemcpyFromSymbol(&v, g_device_status, sizeof(v)), "read status");
+    if (rc)
+        return rc;
+    rc = check_cuda(cudaMemcpyToSymbol(g_device_status, &zero, sizeof(zero)), "clear status");
+    if (bits)
+        *bits = v;
+    return rc;
+}
+
+int ttk_synchronize(void) { return check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize"); }
+
+int ttk_malloc(void** ptr, size_t bytes, void* stream) {
+    if (!ptr)
+        return set_error(TTK_ERR_ARG, "ttk_malloc: null out pointer");
+    *ptr = nullptr;
+    if (bytes == 0)
+        return TTK_OK;
+    // 256-byte granularity keeps every allocation TMA- and vector-aligned.
+    bytes = (bytes + 255) & ~static_cast<size_t>(255);
+    return check_cuda(cudaMallocAsync(ptr, bytes, S(stream)), "cudaMallocAsync");
+}
+
+int ttk_free(void* ptr, void* stream) {
+    if (!ptr)
+        return TTK_OK;
+    return check_cuda(cudaFreeAsync(ptr, S(stream)), "cudaFreeAsync");
+}
+
+int ttk_pool_stats(size_t* reserved, size_t* used) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaMemPool_t pool;
+    int rc = check_cuda(cudaDeviceGetDefaultMemPool(&pool, dev), "cudaDeviceGetDefaultMemPool");
+    if (rc)
+        return rc;
+    uint64_t r = 0, u = 0;
+    cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &r);
+    cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemCurrent, &u);
+    if (reserved)
+        *reserved = r;
+    if (used)
+        *used = u;
+    return TTK_OK;
+}
+
+int ttk_host_alloc(void** ptr, size_t bytes) {
+    return check_cuda(cudaMallocHost(ptr, bytes ? bytes : 1), "cudaMallocHost");
+}
+
+int ttk_host_free(void* ptr) { return check_cuda(cudaFreeHost(ptr), "cudaFreeHost"); }
+
+int ttk_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream) {
+    if (!bytes)
+        return TTK_OK;
+    return check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, S(stream)),
+                      "memcpy h2d");
+}
+
+int ttk_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream) {
+    if (!bytes)
+        return TTK_OK;
+    int rc = check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, S(stream)),
+                        "memcpy d2h");
+    if (rc)
+        return rc;
+    return check_cuda(cudaStreamSynchronize(S(stream)), "memcpy d2h sync");
+}
+
+int ttk_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream) {
+    if (!bytes)
+        return TTK_OK;
+    return check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, S(stream)),
+                      "memcpy d2d");
+}
+
+int ttk_memset(void* dst, int value, size_t bytes, void* stream) {
+    if (!bytes)
+        return TTK_OK;
+    return check_cuda(cudaMemsetAsync(dst, value, bytes, S(stream)), "memset");
+}
+
+int ttk_stream_create(void** stream) {
+    cudaStream_t s;
+    int rc = check_cuda(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking), "stream create");
+    *stream = s;
+    return rc;
+}
+
+int ttk_stream_destroy(void* stream) {
+    return check_cuda(cudaStreamDestroy(S(stream)), "stream destroy");
+}
+
+int ttk_stream_synchronize(void* stream) {
+    return check_cuda(cudaStreamSynchronize(S(stream)), "stream synchronize");
+}
+
+int ttk_event_create(void** event) {
+    cudaEvent_t e;
+    int rc = check_cuda(cudaEventCreate(&e), "event create");
+    *event = e;
+    return rc;
+}
+
+int ttk_event_destroy(void* event) {
+    return check_cuda(cudaEventDestroy(static_cast<cudaEvent_t>(event)), "event destroy");
+}
+
+int ttk_event_record(void* event, void* stream) {
+    return check_cuda(cudaEventRecord(static_cast<cudaEvent_t>(event), S(stream)), "event record");
+}
+
+int ttk_stream_wait_event(void* stream, void* event) {
+    return check_cuda(cudaStreamWaitEvent(S(stream), static_cast<cudaEvent_t>(event), 0),
+                      "stream wait event");
+}
+
+int ttk_event_elapsed_ms(void* start, void* end, float* ms) {
+    return check_cuda(cudaEventElapsedTime(ms, static_cast<cudaEvent_t>(start),
+                                           static_cast<cudaEvent_t>(end)),
+                      "event elapsed");
+}
+
+int ttk_event_synchronize(void* event) {
+    return check_cuda(cudaEventSynchronize(static_cast<cudaEvent_t>(event)), "event sync");
+}
+
+// ------------------------------------------------------------------ GEMM --
+
+size_t ttk_gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
+                               int64_t K) {
+    return gemm_workspace_size(transA, transB, batch, M, N, K);
+}
+
+int ttk_gemm(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+             const float* A, int64_t lda, int64_t strideA, const float* B, int64_t ldb,
+             int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC,
+             void* workspace, size_t workspace_bytes, void* stream) {
+    return gemm_tf32x3(transA, transB, batch, M, N, K, alpha, A, lda, strideA, B, ldb, strideB,
+                       beta, C, ldc, strideC, workspace, workspace_bytes, S(stream));
+}
+
+int ttk_split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+                   int64_t batch, float* dst, int64_t ld_pad, void* stream) {
+    if (ld_pad % 16 || ld_pad < cols || rows < 0 || cols < 0 || batch < 0)
+        return set_error(TTK_ERR_ARG, "ttk_split_tf32: bad geometry");
+    return split_tf32(src, rows, cols, ld, bstride, batch, dst, ld_pad, S(stream));
+}
+
+int ttk_gemm_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                      float alpha, const float* a_split, int64_t lda_pad, const float* b_split,
+                      int64_t ldb_pad, float beta, float* C, int64_t ldc, int64_t strideC,
+                      void* stream) {
+    return gemm_tf32x3_presplit(transA, transB, batch, M, N, K, alpha, a_split, lda_pad, b_split,
+                                ldb_pad, beta, C, ldc, strideC, S(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,42 @@
+// Host-side internals shared by the ttk translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+#include "ttk.h"
+
+namespace ttk {
+
+// Records a message for ttk_last_error() and returns the code.
+int set_error(int code, const char* msg);
+// Converts a pending launch error into a status.
+int check_launch(const char* what);
+int check_cuda(cudaError_t e, const char* what);
+const char* last_error_cstr();
+
+inline int grid_for(int64_t n, int threads, int max_blocks = 148 * 16) {
+    int64_t b = (n + threads - 1) / threads;
+    if (b < 1)
+        b = 1;
+    return static_cast<int>(std::min<int64_t>(b, max_blocks));
+}
+
+// GEMM entry points (gemm_tf32x3.cu), shared with the C ABI wrappers.
+size_t gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
+                           int64_t K);
+int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+               int64_t batch, float* dst, int64_t ld_pad, cudaStream_t stream);
+int gemm_tf32x3(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                float alpha, const float* A, int64_t lda, int64_t strideA, const float* B,
+                int64_t ldb, int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC,
+                void* ws, size_t ws_bytes, cudaStream_t stream);
+int gemm_tf32x3_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                         float alpha, const float* a_split, int64_t lda_pad,
+                         const float* b_split, int64_t ldb_pad, float beta, float* C,
+                         int64_t ldc, int64_t strideC, cudaStream_t stream);
+
+}  // namespace ttk

@@ -207,7 +207,8 @@ int ttk_binary_bwd(int op, int which, const float* a, const int64_t* a_strides, 
 /* Unary ops: 0 neg, 1 exp, 2 log, 3 sqrt, 4 tanh, 5 silu, 6 sin, 7 cos,
  * 8 pow(p) (ops.cpp:268-363); y = f(x). */
 int ttk_unary(int op, const float* x, float* y, int64_t n, float p, void* stream);
-/* dx (+)= dy * f'(x) (the b_* rules of ops.cpp:314-363). */
+/* dx += dy * f'(x) (the b_* rules of ops.cpp:314-363; always accumulates,
+ * like the reference's backward closures). */
 int ttk_unary_bwd(int op, const float* x, const float* dy, float* dx, int64_t n, float p,
                   void* stream);
 /* out[o, i] (+)= sum_k in[o, k, i] over [outer, K, inner] (ops.cpp:367-439 sum). */
@@ -230,10 +231,6 @@ int ttk_axpy(float alpha, const float* x, float* y, int64_t n, void* stream);
  * dims). The broadcast-gradient reduction (ops.cpp:35-61 bcast_add). */
 int ttk_reduce_to(const float* g, const int64_t* shape, int ndim, unsigned keep_mask, float* out,
                   int accumulate, void* stream);
-/* mask[i] = (u_i >= p) ? 1 : 0 with u_i from the reference's xorshift64*
- * stream for `seed` (ops.cpp:949-963), generated on the device by jumping
- * the stream; see ttk_dropout_mask in generic_kernels.cu. */
-int ttk_dropout_mask(float* mask, int64_t n, float p, uint64_t seed, void* stream);
 
 /* ---------------------------------------------------------------- training */
 

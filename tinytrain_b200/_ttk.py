@@ -82,7 +82,7 @@ SIGS = {
     "ttk_strided_copy": (I32, [P, P, P, P, I32, I32, I32, P]),
     "ttk_fill": (I32, [P, F32, I64, P]),
     "ttk_axpy": (I32, [F32, P, P, I64, P]),
-    "ttk_dropout_mask": (I32, [P, I64, F32, U64, P]),
+    "ttk_reduce_to": (I32, [P, P, I32, C.c_uint, P, I32, P]),
     "ttk_init_normal": (I32, [P, I64, F32, U64, P]),
     "ttk_dist_unique_id": (I32, [P]),
     "ttk_dist_init": (I32, [I32, I32, P, P]),

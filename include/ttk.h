@@ -42,6 +42,8 @@ int ttk_device_count(int* n);
  * bit 1: an out-of-range index was skipped). Synchronizes the device. */
 int ttk_device_status(unsigned* bits);
 int ttk_synchronize(void);
+/* Number of kernels launched through this library so far (all streams). */
+int64_t ttk_launch_count(void);
 
 /* Stream-ordered allocation from the device's pool (cached, never released to
  * the driver until exit). The caching allocator under tt::Tensor storage. */
@@ -163,6 +165,18 @@ int ttk_rope_fwd(const float* x, const float* cos_t, const float* sin_t, float* 
 int ttk_rope_bwd(const float* dy, const float* cos_t, const float* sin_t, float* dx,
                  int accumulate, int64_t B, int64_t T, int64_t H, int64_t D, void* stream);
 
+/* nll_loss over log-probabilities [N,C] (ops.cpp:898-926): *loss =
+ * -sum_i lp[i,t_i] / N (fp64, i ascending); backward dlp[i,t_i] -= g[0]/N with
+ * the upstream gradient g read on the device. */
+int ttk_nll_fwd(const float* lp, const int64_t* targets, int64_t N, int64_t C, float* loss,
+                void* stream);
+int ttk_nll_bwd(const int64_t* targets, int64_t N, int64_t C, const float* g, float* dlp,
+                void* stream);
+/* Gradients of the RoPE tables (ops.cpp:1024-1048): dcos/dsin [T,D/2] +=
+ * sums over b, h (either may be NULL). */
+int ttk_rope_table_grad(const float* x, const float* dy, int64_t B, int64_t T, int64_t H,
+                        int64_t D, float* dcos, float* dsin, void* stream);
+
 /* Row softmax / log-softmax over the last dim of [R,C] (ops.cpp:777-896);
  * backward: dx (+)= y*(dy - sum(dy*y)) resp. dy - exp(y)*sum(dy). */
 int ttk_softmax_fwd(const float* x, float* y, int64_t R, int64_t C, int log, void* stream);
@@ -224,8 +238,11 @@ int ttk_strided_copy(const float* in, const int64_t* in_strides, float* out,
                      const int64_t* shape, int ndim, int accumulate, int scatter_add,
                      void* stream);
 int ttk_fill(float* x, float v, int64_t n, void* stream);
-/* y (+)= alpha * x. */
+/* y += alpha * x. */
 int ttk_axpy(float alpha, const float* x, float* y, int64_t n, void* stream);
+/* y (+)= alpha[0] * x with alpha a device scalar (an upstream gradient). */
+int ttk_axpy_dev(const float* alpha, const float* x, float* y, int64_t n, int accumulate,
+                 void* stream);
 /* out[k] (+)= sum over the dims of `shape` whose bit is clear in keep_mask of
  * g[...] (g contiguous with shape `shape`; out contiguous over the kept
  * dims). The broadcast-gradient reduction (ops.cpp:35-61 bcast_add). */

@@ -384,6 +384,15 @@ int64_t ref_param_shapes(const RefCfg* c, int64_t* shapes, int64_t cap) {
     }
 }
 
+// The reference's own initialization of GPTModel(cfg, seed) (model.cpp:14-54,
+// nn.cpp:14-44), flattened in parameters() order.
+int ref_init_params(const RefCfg* c, uint64_t seed, float* out) {
+    return guarded([&] {
+        tt::GPTModel m(to_cfg(c), seed);
+        store_params(m, out);
+    });
+}
+
 // logits = GPTModel::forward(idx, B, T) (model.cpp:87-160) with the given
 // flat parameters; optionally the loss and every parameter gradient of
 // cross_entropy(logits, targets).

@@ -210,6 +210,12 @@ def param_shapes(c: RefCfg):
     return out
 
 
+def init_params(c: RefCfg, seed: int):
+    out = np.empty(param_count(c), np.float32)
+    _check(lib().ref_init_params(C.byref(c), C.c_uint64(seed), _p(out)))
+    return out
+
+
 def model_fwd_bwd(c: RefCfg, params, idx, targets, B, T, want_grads=True):
     params, idx = _f(params), _i(idx)
     logits = np.empty((B * T, c.vocab), np.float32)

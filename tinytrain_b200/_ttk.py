@@ -27,6 +27,7 @@ SIGS = {
     "ttk_device_count": (I32, [P]),
     "ttk_device_status": (I32, [P]),
     "ttk_synchronize": (I32, []),
+    "ttk_launch_count": (I64, []),
     "ttk_malloc": (I32, [P, SZ, P]),
     "ttk_free": (I32, [P, P]),
     "ttk_pool_stats": (I32, [P, P]),
@@ -68,6 +69,10 @@ SIGS = {
     "ttk_index_check": (I32, [P, I64, I64, P, P]),
     "ttk_rope_fwd": (I32, [P, P, P, P, I64, I64, I64, I64, P]),
     "ttk_rope_bwd": (I32, [P, P, P, P, I32, I64, I64, I64, I64, P]),
+    "ttk_nll_fwd": (I32, [P, P, I64, I64, P, P]),
+    "ttk_nll_bwd": (I32, [P, I64, I64, P, P, P]),
+    "ttk_rope_table_grad": (I32, [P, P, I64, I64, I64, I64, P, P, P]),
+    "ttk_axpy_dev": (I32, [P, P, P, I64, I32, P]),
     "ttk_softmax_fwd": (I32, [P, P, I64, I64, I32, P]),
     "ttk_softmax_bwd": (I32, [P, P, P, I32, I64, I64, I32, P]),
     "ttk_sumsq_multi": (I32, [P, P, I32, P, P]),

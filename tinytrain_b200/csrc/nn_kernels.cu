@@ -483,6 +483,78 @@ __global__ void softmax_bwd_kernel(const float* __restrict__ y, const float* __r
     }
 }
 
+// ----------------------------------------------------------------- NLL --
+// loss = -sum_i lp[i, t_i] / N with a double accumulator in i order
+// (ops.cpp:905-912); one block, deterministic.
+__global__ void nll_fwd_kernel(const float* __restrict__ lp, const int64_t* __restrict__ t,
+                               int64_t N, int64_t C, float* __restrict__ out) {
+    __shared__ double sh[32];
+    double s = 0.0;
+    for (int64_t i = threadIdx.x; i < N; i += blockDim.x) {
+        const int64_t c = t[i];
+        if (c >= 0 && c < C)
+            s -= static_cast<double>(lp[i * C + c]);
+        else
+            report(kErrBadIndex);
+    }
+    s = warp_sum_d(s);
+    if ((threadIdx.x & 31) == 0)
+        sh[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        s = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.0;
+        s = warp_sum_d(s);
+        if (threadIdx.x == 0)
+            out[0] = static_cast<float>(s / static_cast<double>(N));
+    }
+}
+
+// dlp[i, t_i] -= g[0] / N (ops.cpp:918-923).
+__global__ void nll_bwd_kernel(const int64_t* __restrict__ t, int64_t N, int64_t C,
+                               const float* __restrict__ g, float* __restrict__ dlp) {
+    const float gv = g[0] / static_cast<float>(N);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < N;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t c = t[i];
+        if (c >= 0 && c < C)
+            dlp[i * C + c] -= gv;
+    }
+}
+
+// Gradients of the RoPE tables (ops.cpp:1024-1048): per (t, d), summed over
+// b and h in ascending order.
+__global__ void rope_table_grad_kernel(const float* __restrict__ x, const float* __restrict__ g,
+                                       int64_t B, int64_t T, int64_t H, int64_t D,
+                                       float* __restrict__ dcos, float* __restrict__ dsin) {
+    const int64_t Dh = D / 2;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < T * Dh;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t t = i / Dh, d = i % Dh;
+        float sc = 0.0f, ss = 0.0f;
+        for (int64_t b = 0; b < B; ++b)
+            for (int64_t h = 0; h < H; ++h) {
+                const int64_t base = ((b * T + t) * H + h) * D;
+                const float x1 = x[base + d], x2 = x[base + Dh + d];
+                const float g1 = g[base + d], g2 = g[base + Dh + d];
+                sc += g1 * x1 + g2 * x2;
+                ss += -g1 * x2 + g2 * x1;
+            }
+        if (dcos)
+            dcos[i] += sc;
+        if (dsin)
+            dsin[i] += ss;
+    }
+}
+
+// y (+)= alpha[0] * x with alpha read on the device.
+__global__ void axpy_dev_kernel(const float* __restrict__ alpha, const float* __restrict__ x,
+                                float* __restrict__ y, int64_t n, int accumulate) {
+    const float a = alpha[0];
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        y[i] = accumulate ? y[i] + a * x[i] : a * x[i];
+}
+
 }  // namespace nn
 }  // namespace ttk
 
@@ -710,6 +782,43 @@ int ttk_softmax_bwd(const float* y, const float* dy, float* dx, int accumulate, 
         return TTK_OK;
     softmax_bwd_kernel<<<grid_for(R, 8), 256, 0, S(stream)>>>(y, dy, dx, accumulate, R, C, log);
     return check_launch("softmax_bwd_kernel");
+}
+
+int ttk_nll_fwd(const float* lp, const int64_t* targets, int64_t N, int64_t C, float* loss,
+                void* stream) {
+    if (N <= 0 || C <= 0 || !lp || !targets || !loss)
+        return set_error(TTK_ERR_ARG, "nll_fwd: bad arguments");
+    nll_fwd_kernel<<<1, 1024, 0, S(stream)>>>(lp, targets, N, C, loss);
+    return check_launch("nll_fwd_kernel");
+}
+
+int ttk_nll_bwd(const int64_t* targets, int64_t N, int64_t C, const float* g, float* dlp,
+                void* stream) {
+    if (N <= 0 || C <= 0 || !targets || !g || !dlp)
+        return set_error(TTK_ERR_ARG, "nll_bwd: bad arguments");
+    nll_bwd_kernel<<<grid_for(N, 256), 256, 0, S(stream)>>>(targets, N, C, g, dlp);
+    return check_launch("nll_bwd_kernel");
+}
+
+int ttk_rope_table_grad(const float* x, const float* dy, int64_t B, int64_t T, int64_t H,
+                        int64_t D, float* dcos, float* dsin, void* stream) {
+    if (B < 0 || T < 0 || H < 0 || D <= 0 || (D & 1))
+        return set_error(TTK_ERR_ARG, "rope_table_grad: bad shape");
+    if (!B || !T || !H)
+        return TTK_OK;
+    rope_table_grad_kernel<<<grid_for(T * (D / 2), 256), 256, 0, S(stream)>>>(x, dy, B, T, H, D,
+                                                                             dcos, dsin);
+    return check_launch("rope_table_grad_kernel");
+}
+
+int ttk_axpy_dev(const float* alpha, const float* x, float* y, int64_t n, int accumulate,
+                 void* stream) {
+    if (n < 0 || (n && (!alpha || !x || !y)))
+        return set_error(TTK_ERR_ARG, "axpy_dev: bad arguments");
+    if (!n)
+        return TTK_OK;
+    axpy_dev_kernel<<<grid_for(n, 256), 256, 0, S(stream)>>>(alpha, x, y, n, accumulate);
+    return check_launch("axpy_dev_kernel");
 }
 
 }  // extern "C"

@@ -8,6 +8,7 @@
 // tensor.cpp:13-31).
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -35,7 +36,14 @@ int check_cuda(cudaError_t e, const char* what) {
     return TTK_ERR_CUDA;
 }
 
-int check_launch(const char* what) { return check_cuda(cudaGetLastError(), what); }
+// Kernel launches issued through this library (check_launch runs once after
+// every launch).
+std::atomic<int64_t> g_launches{0};
+
+int check_launch(const char* what) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return check_cuda(cudaGetLastError(), what);
+}
 
 const char* last_error_cstr() { return t_last_error.c_str(); }
 
@@ -50,6 +58,8 @@ extern "C" {
 const char* ttk_last_error(void) { return last_error_cstr(); }
 
 const char* ttk_version(void) { return "ttk 0.1 sm_100a"; }
+
+int64_t ttk_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int ttk_init(int device) {
     int rc = check_cuda(cudaSetDevice(device), "cudaSetDevice");

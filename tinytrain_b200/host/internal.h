@@ -1,0 +1,66 @@
+// Internals shared by the host translation units of libtinytrain.
+#pragma once
+
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "tinytrain/tensor.h"
+#include "ttk.h"
+
+namespace tt {
+namespace detail {
+
+using ImplPtr = std::shared_ptr<Tensor::Impl>;
+
+// Throws std::runtime_error carrying ttk_last_error() when rc != TTK_OK.
+inline void check(int rc, const char* what) {
+    if (rc != TTK_OK)
+        throw std::runtime_error(std::string(what) + ": " + ttk_last_error());
+}
+
+void* stream();
+void ensure_runtime();
+
+// Row-major strides of a shape.
+std::vector<int64_t> row_major(const std::vector<int64_t>& shape);
+int64_t numel_of(const std::vector<int64_t>& shape);
+
+// New tensor with an uninitialized device buffer of the given shape.
+Tensor make_out(const std::vector<int64_t>& shape, bool requires_grad);
+// View sharing `src`'s data buffer with another shape (same numel).
+Tensor make_view(const Tensor& src, const std::vector<int64_t>& shape, bool requires_grad);
+
+// Data of an impl materialized on the device (resolves lazy transposes).
+const float* dread(const ImplPtr& p);
+float* dwrite(const ImplPtr& p);
+
+// Gradient destination for an accumulation: returns the device pointer and
+// sets `overwrite` when the gradient is still logically zero, so the caller
+// may write instead of read-modify-write.
+float* grad_target(const ImplPtr& p, bool& overwrite);
+// Gradient for read-modify-write (materializes pending zeros).
+float* grad_rmw(const ImplPtr& p);
+// Upstream gradient of a node (null when nothing flowed into it).
+const float* grad_in(const ImplPtr& p);
+
+// Scratch device memory released (stream-ordered) when it goes out of scope.
+struct Scratch {
+    explicit Scratch(size_t bytes);
+    ~Scratch();
+    Scratch(const Scratch&) = delete;
+    Scratch& operator=(const Scratch&) = delete;
+    void* ptr = nullptr;
+    size_t bytes = 0;
+    template <class T>
+    T* as() const { return static_cast<T*>(ptr); }
+};
+
+// The reference's randn stream (xorshift64* + Box-Muller) on the host.
+void host_randn(float* out, int64_t n, uint64_t seed);
+
+// Materialize a lazy transpose into its own buffer.
+void materialize(const ImplPtr& p);
+
+}  // namespace detail
+}  // namespace tt

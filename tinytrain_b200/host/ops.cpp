@@ -1,0 +1,952 @@
+// Ops of the reference's ops.h on device tensors, with their reverse-mode
+// rules (the reference's ops.cpp of seampm/tinytrain is the model: argument
+// checks throw the same std::invalid_argument messages, and every backward
+// closure accumulates into its inputs' gradients). Every computation is a
+// ttk_* kernel call on the library stream.
+//
+// Gradient writes: a gradient buffer that is still logically zero is
+// overwritten instead of read-modified-written (grad_target), which saves a
+// memset and a read per first contribution.
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+
+#include "internal.h"
+#include "tinytrain/ops.h"
+#include "ttk.h"
+
+namespace tt {
+
+using namespace detail;
+
+namespace {
+
+// ------------------------------------------------------------- helpers --
+
+std::vector<int64_t> broadcast_shape(const std::vector<int64_t>& a,
+                                     const std::vector<int64_t>& b) {
+    int64_t ar = static_cast<int64_t>(a.size()), br = static_cast<int64_t>(b.size());
+    int64_t r = std::max(ar, br);
+    std::vector<int64_t> out(static_cast<size_t>(r));
+    for (int64_t i = 0; i < r; ++i) {
+        int64_t ad = (i < r - ar) ? 1 : a[static_cast<size_t>(i - (r - ar))];
+        int64_t bd = (i < r - br) ? 1 : b[static_cast<size_t>(i - (r - br))];
+        if (ad != bd && ad != 1 && bd != 1)
+            throw std::invalid_argument("broadcast: incompatible shapes");
+        out[static_cast<size_t>(i)] = std::max(ad, bd);
+    }
+    return out;
+}
+
+int64_t norm_dim(int64_t dim, int64_t rank) {
+    if (dim < 0)
+        dim += rank;
+    if (dim < 0 || dim >= rank)
+        throw std::invalid_argument("dim out of range");
+    return dim;
+}
+
+// Strides of `in` viewed in the index space of `out_shape` (trailing
+// alignment, 0 on broadcast dims).
+std::vector<int64_t> bcast_strides(const ImplPtr& in, const std::vector<int64_t>& out_shape) {
+    const int64_t r = static_cast<int64_t>(out_shape.size());
+    const int64_t ir = static_cast<int64_t>(in->shape.size());
+    std::vector<int64_t> st(static_cast<size_t>(r), 0);
+    for (int64_t d = 0; d < r; ++d) {
+        const int64_t di = d - (r - ir);
+        if (di >= 0 && in->shape[static_cast<size_t>(di)] != 1)
+            st[static_cast<size_t>(d)] = in->strides[static_cast<size_t>(di)];
+    }
+    return st;
+}
+
+// keep mask for reducing a gradient of shape out_shape back onto `in`.
+unsigned keep_mask(const ImplPtr& in, const std::vector<int64_t>& out_shape) {
+    const int64_t r = static_cast<int64_t>(out_shape.size());
+    const int64_t ir = static_cast<int64_t>(in->shape.size());
+    unsigned m = 0;
+    for (int64_t d = 0; d < r; ++d) {
+        const int64_t di = d - (r - ir);
+        if (di >= 0 && in->shape[static_cast<size_t>(di)] == out_shape[static_cast<size_t>(d)])
+            m |= 1u << d;
+    }
+    return m;
+}
+
+bool same_shape(const ImplPtr& a, const std::vector<int64_t>& s) { return a->shape == s; }
+
+// A constant-filled operand is read as one element with zero strides instead
+// of materializing it (e.g. the reference's full(scores.shape(), scale)).
+struct Operand {
+    const float* ptr;
+    std::vector<int64_t> strides;
+    std::shared_ptr<Scratch> holder;
+};
+
+Operand operand(const ImplPtr& p, const std::vector<int64_t>& out_shape) {
+    Operand o;
+    if (!p->transpose_of && p->data->pending_fill) {
+        o.holder = std::make_shared<Scratch>(16);
+        check(ttk_fill(o.holder->as<float>(), p->data->fill_value, 1, stream()), "const");
+        o.ptr = o.holder->as<float>();
+        o.strides.assign(out_shape.size(), 0);
+        return o;
+    }
+    o.ptr = dread(p);
+    o.strides = bcast_strides(p, out_shape);
+    return o;
+}
+
+// dst.grad += src (numel elements), overwriting a still-zero gradient.
+void accum_grad(const ImplPtr& dst, const float* src) {
+    bool ow = false;
+    float* g = grad_target(dst, ow);
+    if (ow)
+        check(ttk_memcpy_d2d(g, src, static_cast<size_t>(dst->numel) * 4, stream()), "grad copy");
+    else
+        check(ttk_axpy(1.0f, src, g, dst->numel, stream()), "grad axpy");
+}
+
+float* out_ptr(Tensor& t) { return t.impl()->data->device_for_overwrite(); }
+
+// --------------------------------------------------------- elementwise --
+
+Tensor elem_binary(const Tensor& a, const Tensor& b, int op) {
+    auto shape = broadcast_shape(a.shape(), b.shape());
+    Tensor out = make_out(shape, a.requires_grad() || b.requires_grad());
+    Operand oa = operand(a.impl(), shape), ob = operand(b.impl(), shape);
+    check(ttk_binary(op, oa.ptr, oa.strides.data(), ob.ptr, ob.strides.data(), out_ptr(out),
+                     shape.data(), static_cast<int>(shape.size()), stream()),
+          "binary");
+    if (out.requires_grad()) {
+        auto ao = a.impl(), bo = b.impl(), oo = out.impl();
+        oo->prev = {ao, bo};
+        oo->backward_fn = [ao, bo, oo, shape, op]() {
+            const float* g = grad_in(oo);
+            if (!g)
+                return;
+            for (int which = 0; which < 2; ++which) {
+                const ImplPtr& X = which ? bo : ao;
+                if (!X->requires_grad)
+                    continue;
+                const bool full = same_shape(X, shape);
+                if (full && (op == 0 || (op == 1 && which == 0))) {
+                    accum_grad(X, g);  // d(a+b)/da = d(a+b)/db = d(a-b)/da = 1
+                    continue;
+                }
+                Operand oa = operand(ao, shape), ob = operand(bo, shape);
+                Scratch tmp(static_cast<size_t>(oo->numel) * 4);
+                check(ttk_binary_bwd(op, which, oa.ptr, oa.strides.data(), ob.ptr,
+                                     ob.strides.data(), g, tmp.as<float>(), shape.data(),
+                                     static_cast<int>(shape.size()), stream()),
+                      "binary_bwd");
+                if (full)
+                    accum_grad(X, tmp.as<float>());
+                else
+                    check(ttk_reduce_to(tmp.as<float>(), shape.data(),
+                                        static_cast<int>(shape.size()), keep_mask(X, shape),
+                                        grad_rmw(X), 1, stream()),
+                          "reduce_to");
+            }
+        };
+    }
+    return out;
+}
+
+Tensor elem_unary(const Tensor& a, int op, float p = 0.0f) {
+    Tensor out = make_out(a.shape(), a.requires_grad());
+    check(ttk_unary(op, dread(a.impl()), out_ptr(out), a.numel(), p, stream()), "unary");
+    if (out.requires_grad()) {
+        auto ao = a.impl(), oo = out.impl();
+        oo->prev = {ao};
+        oo->backward_fn = [ao, oo, op, p]() {
+            const float* g = grad_in(oo);
+            if (!g || !ao->requires_grad)
+                return;
+            check(ttk_unary_bwd(op, dread(ao), g, grad_rmw(ao), ao->numel, p, stream()),
+                  "unary_bwd");
+        };
+    }
+    return out;
+}
+
+// Matrix operand of a GEMM: storage pointer, transposed flag, row length.
+struct MatOp {
+    ImplPtr base;   // tensor whose storage is read (the lazy transpose's source)
+    const float* ptr;
+    int trans;      // 1: the logical matrix is base^T
+};
+
+MatOp mat_operand(const ImplPtr& p) {
+    if (p->transpose_of && !p->data)
+        return {p->transpose_of, dread(p->transpose_of), 1};
+    return {p, dread(p), 0};
+}
+
+void gemm(int ta, int tb, int64_t batch, int64_t M, int64_t N, int64_t K, const float* A,
+          int64_t lda, int64_t sA, const float* B, int64_t ldb, int64_t sB, float beta, float* C,
+          int64_t ldc, int64_t sC) {
+    const size_t ws = ttk_gemm_workspace_size(ta, tb, batch, M, N, K);
+    Scratch w(ws);
+    check(ttk_gemm(ta, tb, batch, M, N, K, 1.0f, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, w.ptr,
+                   ws, stream()),
+          "gemm");
+}
+
+}  // namespace
+
+Tensor add(const Tensor& a, const Tensor& b) { return elem_binary(a, b, 0); }
+Tensor sub(const Tensor& a, const Tensor& b) { return elem_binary(a, b, 1); }
+Tensor mul(const Tensor& a, const Tensor& b) { return elem_binary(a, b, 2); }
+Tensor div(const Tensor& a, const Tensor& b) { return elem_binary(a, b, 3); }
+Tensor neg(const Tensor& a) { return elem_unary(a, 0); }
+
+Tensor exp(const Tensor& a) { return elem_unary(a, 1); }
+Tensor log(const Tensor& a) { return elem_unary(a, 2); }
+Tensor sqrt(const Tensor& a) { return elem_unary(a, 3); }
+Tensor tanh(const Tensor& a) { return elem_unary(a, 4); }
+Tensor silu(const Tensor& a) { return elem_unary(a, 5); }
+Tensor sin(const Tensor& a) { return elem_unary(a, 6); }
+Tensor cos(const Tensor& a) { return elem_unary(a, 7); }
+Tensor pow(const Tensor& a, float p) { return elem_unary(a, 8, p); }
+
+// ----------------------------------------------------------- reductions --
+
+Tensor sum(const Tensor& a, int64_t dim, bool keepdim) {
+    dim = norm_dim(dim, a.ndim());
+    std::vector<int64_t> oshape;
+    int64_t outer = 1, inner = 1;
+    for (int64_t d = 0; d < a.ndim(); ++d) {
+        if (d < dim)
+            outer *= a.dim(d);
+        if (d > dim)
+            inner *= a.dim(d);
+        if (d == dim) {
+            if (keepdim)
+                oshape.push_back(1);
+        } else {
+            oshape.push_back(a.dim(d));
+        }
+    }
+    if (oshape.empty())
+        oshape.push_back(1);
+    const int64_t K = a.dim(dim);
+    Tensor out = make_out(oshape, a.requires_grad());
+    check(ttk_reduce_mid(dread(a.impl()), out_ptr(out), outer, K, inner, 0, stream()), "sum");
+    if (out.requires_grad()) {
+        auto ao = a.impl(), oo = out.impl();
+        oo->prev = {ao};
+        oo->backward_fn = [ao, oo, outer, K, inner]() {
+            const float* g = grad_in(oo);
+            if (!g || !ao->requires_grad)
+                return;
+            const int64_t shp[3] = {outer, K, inner};
+            const int64_t st[3] = {inner, 0, 1};
+            check(ttk_strided_copy(g, st, grad_rmw(ao), shp, 3, 1, 0, stream()), "sum bwd");
+        };
+    }
+    return out;
+}
+
+Tensor sum_all(const Tensor& a) {
+    Tensor out = make_out({1}, a.requires_grad());
+    check(ttk_sum_all(dread(a.impl()), a.numel(), out_ptr(out), 0, stream()), "sum_all");
+    if (out.requires_grad()) {
+        auto ao = a.impl(), oo = out.impl();
+        oo->prev = {ao};
+        oo->backward_fn = [ao, oo]() {
+            const float* g = grad_in(oo);
+            if (!g || !ao->requires_grad)
+                return;
+            const int64_t shp[1] = {ao->numel};
+            const int64_t st[1] = {0};
+            check(ttk_strided_copy(g, st, grad_rmw(ao), shp, 1, 1, 0, stream()), "sum_all bwd");
+        };
+    }
+    return out;
+}
+
+Tensor mean(const Tensor& a) {
+    // The reference's mean is sum_all followed by a division by numel whose
+    // backward is og / numel (ops.cpp:462-479): the same as div by a constant.
+    return div(sum_all(a), full({1}, static_cast<float>(a.numel())));
+}
+
+// ---------------------------------------------------------------- shape --
+
+Tensor reshape(const Tensor& a, const std::vector<int64_t>& shape) {
+    int64_t n = 1;
+    int64_t infer = -1;
+    for (size_t i = 0; i < shape.size(); ++i) {
+        if (shape[i] == -1) {
+            if (infer != -1)
+                throw std::invalid_argument("reshape: only one -1 allowed");
+            infer = static_cast<int64_t>(i);
+        } else {
+            if (shape[i] <= 0)
+                throw std::invalid_argument("reshape: dims must be positive");
+            n *= shape[i];
+        }
+    }
+    std::vector<int64_t> out_shape = shape;
+    if (infer != -1) {
+        if (a.numel() % n != 0)
+            throw std::invalid_argument("reshape: incompatible size");
+        out_shape[static_cast<size_t>(infer)] = a.numel() / n;
+        n = a.numel();
+    }
+    if (n != a.numel() || out_shape.empty())
+        throw std::invalid_argument("reshape: incompatible size");
+    Tensor out = make_view(a, out_shape, a.requires_grad());
+    if (out.requires_grad()) {
+        auto ao = a.impl(), oo = out.impl();
+        oo->prev = {ao};
+        oo->backward_fn = [ao, oo]() {
+            const float* g = grad_in(oo);
+            if (!g || !ao->requires_grad)
+                return;
+            accum_grad(ao, g);
+        };
+    }
+    return out;
+}
+
+Tensor transpose(const Tensor& a, int64_t d0, int64_t d1) {
+    d0 = norm_dim(d0, a.ndim());
+    d1 = norm_dim(d1, a.ndim());
+    std::vector<int64_t> dims(static_cast<size_t>(a.ndim()));
+    for (int64_t d = 0; d < a.ndim(); ++d)
+        dims[static_cast<size_t>(d)] = d;
+    std::swap(dims[static_cast<size_t>(d0)], dims[static_cast<size_t>(d1)]);
+    return permute(a, dims);
+}
+
+Tensor permute(const Tensor& a, const std::vector<int64_t>& dims) {
+    const int64_t rank = a.ndim();
+    if (static_cast<int64_t>(dims.size()) != rank)
+        throw std::invalid_argument("permute: rank mismatch");
+    std::vector<int64_t> oshape(static_cast<size_t>(rank)), src(static_cast<size_t>(rank));
+    std::vector<bool> seen(static_cast<size_t>(rank), false);
+    for (int64_t d = 0; d < rank; ++d) {
+        const int64_t s = norm_dim(dims[static_cast<size_t>(d)], rank);
+        if (seen[static_cast<size_t>(s)])
+            throw std::invalid_argument("permute: repeated dim");
+        seen[static_cast<size_t>(s)] = true;
+        src[static_cast<size_t>(d)] = s;
+        oshape[static_cast<size_t>(d)] = a.dim(s);
+    }
+    auto ao = a.impl();
+    // Swap of the last two dims of a 2-D or 3-D tensor: lazy (read by
+    // matmul/bmm as a transposed operand, materialized only if needed).
+    const bool lazy = (rank == 2 || rank == 3) && src[static_cast<size_t>(rank - 1)] == rank - 2 &&
+                      src[static_cast<size_t>(rank - 2)] == rank - 1 && (rank == 2 || src[0] == 0) &&
+                      !ao->transpose_of;
+    Tensor out;
+    // Element strides of the source, listed in output dim order.
+    std::vector<int64_t> in_strides(static_cast<size_t>(rank));
+    for (int64_t d = 0; d < rank; ++d)
+        in_strides[static_cast<size_t>(d)] = ao->strides[static_cast<size_t>(src[static_cast<size_t>(d)])];
+    if (lazy) {
+        auto impl = std::make_shared<Tensor::Impl>();
+        impl->shape = oshape;
+        impl->strides = row_major(oshape);
+        impl->numel = a.numel();
+        impl->transpose_of = ao;
+        impl->requires_grad = a.requires_grad();
+        out = Tensor::from_impl(impl);
+    } else {
+        out = make_out(oshape, a.requires_grad());
+        check(ttk_strided_copy(dread(ao), in_strides.data(), out_ptr(out), oshape.data(),
+                               static_cast<int>(rank), 0, 0, stream()),
+              "permute");
+    }
+    if (out.requires_grad()) {
+        auto oo = out.impl();
+        oo->prev = {ao};
+        oo->backward_fn = [ao, oo, in_strides]() {
+            const float* g = grad_in(oo);
+            if (!g || !ao->requires_grad)
+                return;
+            // permute backward: scatter the gradient back through the same
+            // (bijective) index map.
+            check(ttk_strided_copy(g, in_strides.data(), grad_rmw(ao), oo->shape.data(),
+                                   static_cast<int>(oo->shape.size()), 1, 1, stream()),
+                  "permute bwd");
+        };
+    }
+    return out;
+}
+
+Tensor expand(const Tensor& a, const std::vector<int64_t>& shape) {
+    (void)broadcast_shape(a.shape(), shape);
+    const int64_t ar = a.ndim(), r = static_cast<int64_t>(shape.size());
+    if (r < ar)
+        throw std::invalid_argument("expand: incompatible shape");
+    for (int64_t i = 0; i < r; ++i) {
+        const int64_t ad = (i < r - ar) ? 1 : a.dim(i - (r - ar));
+        if (ad != 1 && ad != shape[static_cast<size_t>(i)])
+            throw std::invalid_argument("expand: incompatible shape");
+    }
+    Tensor out = make_out(shape, a.requires_grad());
+    auto ao = a.impl();
+    auto st = bcast_strides(ao, shape);
+    check(ttk_strided_copy(dread(ao), st.data(), out_ptr(out), shape.data(), static_cast<int>(r),
+                           0, 0, stream()),
+          "expand");
+    if (out.requires_grad()) {
+        auto oo = out.impl();
+        oo->prev = {ao};
+        oo->backward_fn = [ao, oo, shape]() {
+            const float* g = grad_in(oo);
+            if (!g || !ao->requires_grad)
+                return;
+            check(ttk_reduce_to(g, shape.data(), static_cast<int>(shape.size()),
+                                keep_mask(ao, shape), grad_rmw(ao), 1, stream()),
+                  "expand bwd");
+        };
+    }
+    return out;
+}
+
+Tensor squeeze(const Tensor& a, int64_t dim) {
+    dim = norm_dim(dim, a.ndim());
+    if (a.dim(dim) != 1)
+        throw std::invalid_argument("squeeze: dim size != 1");
+    std::vector<int64_t> oshape;
+    for (int64_t d = 0; d < a.ndim(); ++d)
+        if (d != dim)
+            oshape.push_back(a.dim(d));
+    if (oshape.empty())
+        oshape.push_back(1);
+    return reshape(a, oshape);
+}
+
+Tensor unsqueeze(const Tensor& a, int64_t dim) {
+    const int64_t rank = a.ndim() + 1;
+    if (dim < 0)
+        dim += rank;
+    if (dim < 0 || dim > a.ndim())
+        throw std::invalid_argument("unsqueeze: dim out of range");
+    std::vector<int64_t> oshape;
+    for (int64_t d = 0; d < a.ndim(); ++d) {
+        if (d == dim)
+            oshape.push_back(1);
+        oshape.push_back(a.dim(d));
+    }
+    if (dim == a.ndim())
+        oshape.push_back(1);
+    return reshape(a, oshape);
+}
+
+// ------------------------------------------------------- linear algebra --
+
+namespace {
+
+// C (batch x [M,N]) = op(A) op(B) and its backward, for matmul and bmm. A is
+// [M,K] (storage [K,M] when A.trans), B is [K,N] (storage [N,K] when B.trans).
+Tensor batched_matmul(const Tensor& a, const Tensor& b, int64_t Bt, int64_t M, int64_t K,
+                      int64_t N, std::vector<int64_t> oshape) {
+    Tensor out = make_out(oshape, a.requires_grad() || b.requires_grad());
+    MatOp A = mat_operand(a.impl()), Bm = mat_operand(b.impl());
+    const int64_t lda = A.trans ? M : K, ldb = Bm.trans ? K : N;
+    gemm(A.trans, Bm.trans, Bt, M, N, K, A.ptr, lda, M * K, Bm.ptr, ldb, K * N, 0.0f, out_ptr(out),
+         N, M * N);
+    if (out.requires_grad()) {
+        auto ao = a.impl(), bo = b.impl(), oo = out.impl();
+        oo->prev = {ao, bo};
+        oo->backward_fn = [ao, bo, oo, Bt, M, K, N]() {
+            const float* g = grad_in(oo);
+            if (!g)
+                return;
+            MatOp A = mat_operand(ao), Bm = mat_operand(bo);
+            const int64_t lda = A.trans ? M : K, ldb = Bm.trans ? K : N;
+            if (ao->requires_grad) {
+                // dA = g B^T. For a lazy transpose A = X^T the gradient goes
+                // straight into X: dX = B g^T.
+                bool ow = false;
+                if (!A.trans) {
+                    float* d = grad_target(ao, ow);
+                    gemm(0, Bm.trans ? 0 : 1, Bt, M, K, N, g, N, M * N, Bm.ptr, ldb, K * N,
+                         ow ? 0.0f : 1.0f, d, K, M * K);
+                } else if (A.base->requires_grad) {
+                    float* d = grad_target(A.base, ow);
+                    gemm(Bm.trans ? 1 : 0, 1, Bt, K, M, N, Bm.ptr, ldb, K * N, g, N, M * N,
+                         ow ? 0.0f : 1.0f, d, M, M * K);
+                }
+            }
+            if (bo->requires_grad) {
+                // dB = A^T g. For B = W^T: dW = g^T A.
+                bool ow = false;
+                if (!Bm.trans) {
+                    float* d = grad_target(bo, ow);
+                    gemm(A.trans ? 0 : 1, 0, Bt, K, N, M, A.ptr, lda, M * K, g, N, M * N,
+                         ow ? 0.0f : 1.0f, d, N, K * N);
+                } else if (Bm.base->requires_grad) {
+                    float* d = grad_target(Bm.base, ow);
+                    gemm(1, A.trans ? 1 : 0, Bt, N, K, M, g, N, M * N, A.ptr, lda, M * K,
+                         ow ? 0.0f : 1.0f, d, K, K * N);
+                }
+            }
+        };
+    }
+    return out;
+}
+
+}  // namespace
+
+Tensor matmul(const Tensor& a, const Tensor& b) {
+    if (a.ndim() != 2 || b.ndim() != 2)
+        throw std::invalid_argument("matmul: both inputs must be 2D");
+    const int64_t M = a.dim(0), K = a.dim(1), K2 = b.dim(0), N = b.dim(1);
+    if (K != K2)
+        throw std::invalid_argument("matmul: inner dims mismatch");
+    return batched_matmul(a, b, 1, M, K, N, {M, N});
+}
+
+Tensor bmm(const Tensor& a, const Tensor& b) {
+    if (a.ndim() != 3 || b.ndim() != 3)
+        throw std::invalid_argument("bmm: both inputs must be 3D");
+    const int64_t B = a.dim(0), M = a.dim(1), K = a.dim(2);
+    if (b.dim(0) != B || b.dim(1) != K)
+        throw std::invalid_argument("bmm: batch/inner dims mismatch");
+    const int64_t N = b.dim(2);
+    return batched_matmul(a, b, B, M, K, N, {B, M, N});
+}
+
+Tensor linear(const Tensor& x, const Tensor& weight) {
+    if (x.ndim() != 2 || weight.ndim() != 2)
+        throw std::invalid_argument("linear: x and weight must be 2D");
+    if (x.dim(1) != weight.dim(1))
+        throw std::invalid_argument("matmul: inner dims mismatch");
+    const int64_t R = x.dim(0), In = x.dim(1), Out = weight.dim(0);
+    Tensor out = make_out({R, Out}, x.requires_grad() || weight.requires_grad());
+    gemm(0, 1, 1, R, Out, In, dread(x.impl()), In, 0, dread(weight.impl()), In, 0, 0.0f,
+         out_ptr(out), Out, 0);
+    if (out.requires_grad()) {
+        auto xo = x.impl(), wo = weight.impl(), oo = out.impl();
+        oo->prev = {xo, wo};
+        oo->backward_fn = [xo, wo, oo, R, In, Out]() {
+            const float* g = grad_in(oo);
+            if (!g)
+                return;
+            if (xo->requires_grad) {  // dX = g W
+                bool ow = false;
+                float* d = grad_target(xo, ow);
+                gemm(0, 0, 1, R, In, Out, g, Out, 0, dread(wo), In, 0, ow ? 0.0f : 1.0f, d, In, 0);
+            }
+            if (wo->requires_grad) {  // dW = g^T X
+                bool ow = false;
+                float* d = grad_target(wo, ow);
+                gemm(1, 0, 1, Out, In, R, g, Out, 0, dread(xo), In, 0, ow ? 0.0f : 1.0f, d, In, 0);
+            }
+        };
+    }
+    return out;
+}
+
+// ---------------------------------------------------------- neural nets --
+
+DeviceIds::DeviceIds(const std::vector<int64_t>& host) : DeviceIds(host.data(),
+                                                                    static_cast<int64_t>(host.size())) {}
+
+DeviceIds::DeviceIds(const int64_t* host, int64_t n_) : n(n_) {
+    if (n <= 0)
+        return;
+    auto s = std::make_shared<Scratch>(static_cast<size_t>(n) * 8);
+    check(ttk_memcpy_h2d(s->ptr, host, static_cast<size_t>(n) * 8, stream()), "ids upload");
+    dev = s->as<int64_t>();
+    buf = std::shared_ptr<void>(s, s->ptr);
+}
+
+DeviceIds DeviceIds::borrow(const int64_t* d, int64_t n) {
+    DeviceIds ids;
+    ids.dev = d;
+    ids.n = n;
+    return ids;
+}
+
+const int64_t* DeviceIds::data() const { return dev; }
+
+Tensor embedding(const Tensor& weight, const std::vector<int64_t>& idx) {
+    const int64_t V = weight.dim(0);
+    for (int64_t t : idx)
+        if (t < 0 || t >= V)
+            throw std::invalid_argument("embedding: index out of range");
+    return embedding(weight, DeviceIds(idx));
+}
+
+Tensor embedding(const Tensor& weight, const DeviceIds& idx) {
+    if (weight.ndim() != 2)
+        throw std::invalid_argument("embedding: weight must be 2D");
+    const int64_t V = weight.dim(0), D = weight.dim(1), N = idx.size();
+    if (N <= 0)
+        throw std::invalid_argument("Tensor: dims must be positive");
+    Tensor out = make_out({N, D}, weight.requires_grad());
+    check(ttk_embedding_fwd(dread(weight.impl()), idx.data(), out_ptr(out), N, D, V, stream()),
+          "embedding");
+    if (out.requires_grad()) {
+        auto wo = weight.impl(), oo = out.impl();
+        oo->prev = {wo};
+        oo->backward_fn = [wo, oo, idx, N, D, V]() {
+            const float* g = grad_in(oo);
+            if (!g || !wo->requires_grad)
+                return;
+            const size_t ws = ttk_embedding_bwd_workspace_size(N);
+            Scratch w(ws);
+            check(ttk_embedding_bwd(g, idx.data(), grad_rmw(wo), N, D, V, w.ptr, ws, stream()),
+                  "embedding bwd");
+        };
+    }
+    return out;
+}
+
+namespace {
+
+Tensor softmax_impl(const Tensor& a, int64_t dim, int log) {
+    dim = norm_dim(dim, a.ndim());
+    if (dim != a.ndim() - 1) {
+        // Move `dim` last, apply, move it back (autograd flows through).
+        std::vector<int64_t> p(static_cast<size_t>(a.ndim()));
+        for (int64_t d = 0; d < a.ndim(); ++d)
+            p[static_cast<size_t>(d)] = d;
+        std::swap(p[static_cast<size_t>(dim)], p[static_cast<size_t>(a.ndim() - 1)]);
+        Tensor moved = permute(a, p);
+        Tensor r = softmax_impl(moved, -1, log);
+        return permute(r, p);
+    }
+    const int64_t C = a.dim(a.ndim() - 1), R = a.numel() / C;
+    Tensor out = make_out(a.shape(), a.requires_grad());
+    check(ttk_softmax_fwd(dread(a.impl()), out_ptr(out), R, C, log, stream()), "softmax");
+    if (out.requires_grad()) {
+        auto ao = a.impl(), oo = out.impl();
+        oo->prev = {ao};
+        oo->backward_fn = [ao, oo, R, C, log]() {
+            const float* g = grad_in(oo);
+            if (!g || !ao->requires_grad)
+                return;
+            bool ow = false;
+            float* d = grad_target(ao, ow);
+            check(ttk_softmax_bwd(dread(oo), g, d, ow ? 0 : 1, R, C, log, stream()),
+                  "softmax bwd");
+        };
+    }
+    return out;
+}
+
+void check_targets(const std::vector<int64_t>& targets, int64_t N, int64_t C, const char* who) {
+    if (static_cast<int64_t>(targets.size()) != N)
+        throw std::invalid_argument(std::string(who) + ": targets size mismatch");
+    for (int64_t t : targets)
+        if (t < 0 || t >= C)
+            throw std::invalid_argument(std::string(who) + ": target out of range");
+}
+
+}  // namespace
+
+Tensor softmax(const Tensor& a, int64_t dim) { return softmax_impl(a, dim, 0); }
+Tensor log_softmax(const Tensor& a, int64_t dim) { return softmax_impl(a, dim, 1); }
+
+Tensor nll_loss(const Tensor& log_probs, const std::vector<int64_t>& targets) {
+    if (log_probs.ndim() != 2)
+        throw std::invalid_argument("nll_loss: log_probs must be 2D");
+    const int64_t N = log_probs.dim(0), C = log_probs.dim(1);
+    check_targets(targets, N, C, "nll_loss");
+    DeviceIds ids(targets);
+    Tensor out = make_out({1}, log_probs.requires_grad());
+    check(ttk_nll_fwd(dread(log_probs.impl()), ids.data(), N, C, out_ptr(out), stream()), "nll");
+    if (out.requires_grad()) {
+        auto lo = log_probs.impl(), oo = out.impl();
+        oo->prev = {lo};
+        oo->backward_fn = [lo, oo, ids, N, C]() {
+            const float* g = grad_in(oo);
+            if (!g || !lo->requires_grad)
+                return;
+            check(ttk_nll_bwd(ids.data(), N, C, g, grad_rmw(lo), stream()), "nll bwd");
+        };
+    }
+    return out;
+}
+
+Tensor cross_entropy(const Tensor& logits, const std::vector<int64_t>& targets) {
+    if (logits.ndim() != 2)
+        throw std::invalid_argument("nll_loss: log_probs must be 2D");
+    check_targets(targets, logits.dim(0), logits.dim(1), "nll_loss");
+    return cross_entropy(logits, DeviceIds(targets));
+}
+
+Tensor cross_entropy(const Tensor& logits, const DeviceIds& targets) {
+    if (logits.ndim() != 2)
+        throw std::invalid_argument("nll_loss: log_probs must be 2D");
+    const int64_t N = logits.dim(0), C = logits.dim(1);
+    if (targets.size() != N)
+        throw std::invalid_argument("nll_loss: targets size mismatch");
+    Tensor out = make_out({1}, logits.requires_grad());
+    Scratch acc(8);
+    check(ttk_memset(acc.ptr, 0, 8, stream()), "ce zero");
+    // The gradient for d(loss) = 1 is produced in the same pass (the row is
+    // still in registers) and kept for the backward.
+    std::shared_ptr<Buffer> dlog;
+    if (logits.requires_grad())
+        dlog = std::make_shared<Buffer>(N * C);
+    const float inv_n = 1.0f / static_cast<float>(N);
+    check(ttk_cross_entropy(dread(logits.impl()), targets.data(), N, C, acc.as<double>(),
+                            dlog ? dlog->device_for_overwrite() : nullptr, inv_n, stream()),
+          "cross_entropy");
+    check(ttk_loss_finalize(acc.as<double>(), inv_n, out_ptr(out), stream()), "loss");
+    if (out.requires_grad()) {
+        auto lo = logits.impl(), oo = out.impl();
+        oo->prev = {lo};
+        oo->backward_fn = [lo, oo, dlog, N, C]() {
+            if (!oo->grad || !lo->requires_grad)
+                return;
+            Buffer& og = *oo->grad;
+            const bool unit = og.pending_fill && og.fill_value == 1.0f;
+            if (unit && (!lo->grad || (lo->grad->pending_fill && lo->grad->fill_value == 0.0f))) {
+                lo->grad = dlog;  // adopt the precomputed gradient, no copy
+                return;
+            }
+            bool ow = false;
+            float* d = grad_target(lo, ow);
+            if (unit) {
+                if (ow)
+                    check(ttk_memcpy_d2d(d, dlog->device(), static_cast<size_t>(N * C) * 4,
+                                         stream()),
+                          "ce grad copy");
+                else
+                    check(ttk_axpy(1.0f, dlog->device(), d, N * C, stream()), "ce grad");
+            } else {
+                check(ttk_axpy_dev(og.device(), dlog->device(), d, N * C, ow ? 0 : 1, stream()),
+                      "ce grad scale");
+            }
+        };
+    }
+    return out;
+}
+
+Tensor rmsnorm(const Tensor& a, const Tensor& weight, float eps) {
+    const int64_t D = a.dim(a.ndim() - 1);
+    if (weight.ndim() != 1 || weight.dim(0) != D)
+        throw std::invalid_argument("broadcast: incompatible shapes");
+    const int64_t R = a.numel() / D;
+    Tensor out = make_out(a.shape(), a.requires_grad() || weight.requires_grad());
+    auto rstd = std::make_shared<Buffer>(R);
+    check(ttk_rmsnorm_fwd(dread(a.impl()), dread(weight.impl()), out_ptr(out),
+                          rstd->device_for_overwrite(), R, D, eps, stream()),
+          "rmsnorm");
+    if (out.requires_grad()) {
+        auto ao = a.impl(), wo = weight.impl(), oo = out.impl();
+        oo->prev = {ao, wo};
+        oo->backward_fn = [ao, wo, oo, rstd, R, D]() {
+            const float* g = grad_in(oo);
+            if (!g)
+                return;
+            bool ow = false;
+            float* dx = ao->requires_grad ? grad_target(ao, ow) : nullptr;
+            float* dw = wo->requires_grad ? grad_rmw(wo) : nullptr;
+            const size_t ws = ttk_rmsnorm_bwd_workspace_size(R, D);
+            Scratch w(ws);
+            check(ttk_rmsnorm_bwd(dread(ao), dread(wo), rstd->device(), g, dx, ow ? 0 : 1, dw, R,
+                                  D, w.ptr, ws, stream()),
+                  "rmsnorm bwd");
+        };
+    }
+    return out;
+}
+
+Tensor dropout(const Tensor& a, float p, uint64_t seed) {
+    if (p <= 0.0f)
+        return a;
+    if (p >= 1.0f)
+        throw std::invalid_argument("dropout: p must be < 1");
+    // The reference's mask stream (xorshift64*, ops.cpp:949-963), generated on
+    // the host so that a given seed drops the same elements.
+    std::vector<float> m(static_cast<size_t>(a.numel()));
+    uint64_t s = seed ? seed : 0x9E3779B97F4A7C15ULL;
+    for (auto& x : m) {
+        s ^= s >> 12;
+        s ^= s << 25;
+        s ^= s >> 27;
+        const uint64_t r = s * 0x2545F4914F6CDD1DULL;
+        const double u = (r >> 11) * (1.0 / 9007199254740992.0);
+        x = (u >= p) ? 1.0f : 0.0f;
+    }
+    Tensor mask(a.shape(), false);
+    mask.copy_from_host(m.data());
+    const float scale = 1.0f / (1.0f - p);
+    return mul(mul(a, mask), full(a.shape(), scale));
+}
+
+Tensor rope(const Tensor& x, const Tensor& cos, const Tensor& sin) {
+    if (x.ndim() != 4 || cos.ndim() != 2 || sin.ndim() != 2)
+        throw std::invalid_argument("rope: rank mismatch");
+    const int64_t B = x.dim(0), T = x.dim(1), H = x.dim(2), D = x.dim(3);
+    if (D % 2 != 0)
+        throw std::invalid_argument("rope: head dim must be even");
+    const int64_t Dh = D / 2;
+    if (cos.dim(0) != T || cos.dim(1) != Dh || sin.dim(0) != T || sin.dim(1) != Dh)
+        throw std::invalid_argument("rope: cos/sin shape mismatch");
+    Tensor out = make_out(x.shape(), x.requires_grad());
+    check(ttk_rope_fwd(dread(x.impl()), dread(cos.impl()), dread(sin.impl()), out_ptr(out), B, T,
+                       H, D, stream()),
+          "rope");
+    if (out.requires_grad() || cos.requires_grad() || sin.requires_grad()) {
+        out.impl()->requires_grad = true;
+        auto xo = x.impl(), co = cos.impl(), so = sin.impl(), oo = out.impl();
+        oo->prev = {xo, co, so};
+        oo->backward_fn = [xo, co, so, oo, B, T, H, D]() {
+            const float* g = grad_in(oo);
+            if (!g)
+                return;
+            if (xo->requires_grad) {
+                bool ow = false;
+                float* d = grad_target(xo, ow);
+                check(ttk_rope_bwd(g, dread(co), dread(so), d, ow ? 0 : 1, B, T, H, D, stream()),
+                      "rope bwd");
+            }
+            if (co->requires_grad || so->requires_grad)
+                check(ttk_rope_table_grad(dread(xo), g, B, T, H, D,
+                                          co->requires_grad ? grad_rmw(co) : nullptr,
+                                          so->requires_grad ? grad_rmw(so) : nullptr, stream()),
+                      "rope table grad");
+        };
+    }
+    return out;
+}
+
+// ------------------------------------------------------------ fused ops --
+
+Tensor causal_attention(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& cos,
+                        const Tensor& sin) {
+    if (q.ndim() != 4 || q.shape() != k.shape() || q.shape() != v.shape())
+        throw std::invalid_argument("causal_attention: q, k, v must be [B,T,H,hd] alike");
+    const int64_t B = q.dim(0), T = q.dim(1), H = q.dim(2), hd = q.dim(3);
+    if (cos.ndim() != 2 || cos.dim(0) < T || cos.dim(1) != hd / 2 || sin.shape() != cos.shape())
+        throw std::invalid_argument("rope: cos/sin shape mismatch");
+    const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
+    const bool rg = q.requires_grad() || k.requires_grad() || v.requires_grad();
+    Tensor out = make_out({B, T, H * hd}, rg);
+    auto lse = std::make_shared<Buffer>(B * H * T);
+    check(ttk_attention_fwd(dread(q.impl()), dread(k.impl()), dread(v.impl()), dread(cos.impl()),
+                            dread(sin.impl()), out_ptr(out), lse->device_for_overwrite(), B, T, H,
+                            hd, scale, stream()),
+          "attention");
+    if (rg) {
+        auto qo = q.impl(), ko = k.impl(), vo = v.impl(), co = cos.impl(), so = sin.impl(),
+             oo = out.impl();
+        oo->prev = {qo, ko, vo};
+        oo->backward_fn = [qo, ko, vo, co, so, oo, lse, B, T, H, hd, scale]() {
+            const float* g = grad_in(oo);
+            if (!g)
+                return;
+            // Gradients that are not wanted go to scratch.
+            std::vector<std::unique_ptr<Scratch>> junk;
+            auto dst = [&](const ImplPtr& p, bool& ow) -> float* {
+                if (p->requires_grad)
+                    return grad_target(p, ow);
+                junk.emplace_back(new Scratch(static_cast<size_t>(p->numel) * 4));
+                ow = true;
+                return junk.back()->as<float>();
+            };
+            bool oq = false, ok = false, ov = false;
+            float* dq = dst(qo, oq);
+            float* dk = dst(ko, ok);
+            float* dv = dst(vo, ov);
+            const bool all_fresh = oq && ok && ov;
+            if (!all_fresh) {  // one accumulate flag covers all three
+                if (oq)
+                    check(ttk_memset(dq, 0, static_cast<size_t>(qo->numel) * 4, stream()), "zero");
+                if (ok)
+                    check(ttk_memset(dk, 0, static_cast<size_t>(ko->numel) * 4, stream()), "zero");
+                if (ov)
+                    check(ttk_memset(dv, 0, static_cast<size_t>(vo->numel) * 4, stream()), "zero");
+            }
+            const size_t ws = ttk_attention_bwd_workspace_size(B, T, H, hd);
+            Scratch w(ws);
+            check(ttk_attention_bwd(dread(qo), dread(ko), dread(vo), dread(co), dread(so),
+                                    dread(oo), lse->device(), g, dq, dk, dv, all_fresh ? 0 : 1, B,
+                                    T, H, hd, scale, w.ptr, ws, stream()),
+                  "attention bwd");
+        };
+    }
+    return out;
+}
+
+Tensor swiglu(const Tensor& a, const Tensor& b) {
+    if (a.shape() != b.shape())
+        throw std::invalid_argument("swiglu: shape mismatch");
+    Tensor out = make_out(a.shape(), a.requires_grad() || b.requires_grad());
+    check(ttk_swiglu_fwd(dread(a.impl()), dread(b.impl()), out_ptr(out), a.numel(), stream()),
+          "swiglu");
+    if (out.requires_grad()) {
+        auto ao = a.impl(), bo = b.impl(), oo = out.impl();
+        oo->prev = {ao, bo};
+        oo->backward_fn = [ao, bo, oo]() {
+            const float* g = grad_in(oo);
+            if (!g)
+                return;
+            std::unique_ptr<Scratch> ja, jb;
+            bool owa = true, owb = true;
+            float* da;
+            float* db;
+            if (ao->requires_grad) {
+                da = grad_target(ao, owa);
+            } else {
+                ja.reset(new Scratch(static_cast<size_t>(ao->numel) * 4));
+                da = ja->as<float>();
+            }
+            if (bo->requires_grad) {
+                db = grad_target(bo, owb);
+            } else {
+                jb.reset(new Scratch(static_cast<size_t>(bo->numel) * 4));
+                db = jb->as<float>();
+            }
+            if (owa != owb) {
+                if (owa)
+                    check(ttk_memset(da, 0, static_cast<size_t>(ao->numel) * 4, stream()), "zero");
+                if (owb)
+                    check(ttk_memset(db, 0, static_cast<size_t>(bo->numel) * 4, stream()), "zero");
+            }
+            check(ttk_swiglu_bwd(dread(ao), dread(bo), g, da, db, (owa && owb) ? 0 : 1, ao->numel,
+                                 stream()),
+                  "swiglu bwd");
+        };
+    }
+    return out;
+}
+
+float clip_grad_norm(const std::vector<Tensor*>& params, float max_norm) {
+    std::vector<const float*> ptrs;
+    std::vector<int64_t> sizes;
+    for (Tensor* p : params)
+        if (p->has_grad()) {
+            ptrs.push_back(p->device_grad());
+            sizes.push_back(p->numel());
+        }
+    Scratch acc(8);
+    check(ttk_memset(acc.ptr, 0, 8, stream()), "zero");
+    check(ttk_sumsq_multi(ptrs.data(), sizes.data(), static_cast<int>(ptrs.size()),
+                          acc.as<double>(), stream()),
+          "sumsq");
+    double ss = 0.0;
+    check(ttk_memcpy_d2h(&ss, acc.ptr, 8, stream()), "norm read");
+    const double total = std::sqrt(ss);
+    if (max_norm > 0.0f) {
+        const float coef = static_cast<float>(max_norm / (total + 1e-6));
+        if (coef < 1.0f) {
+            Scratch c(16);
+            check(ttk_fill(c.as<float>(), coef, 1, stream()), "coef");
+            const int64_t zero = 0, one = 1;
+            for (Tensor* p : params)
+                if (p->has_grad()) {
+                    const int64_t n = p->numel();
+                    float* g = p->impl()->grad->device();
+                    check(ttk_binary(2, g, &one, c.as<float>(), &zero, g, &n, 1, stream()),
+                          "clip scale");
+                    p->impl()->grad->host_valid = false;
+                }
+        }
+    }
+    return static_cast<float>(total);
+}
+
+}  // namespace tt

@@ -1,0 +1,385 @@
+// The training step of apps/train.cpp:212-256 (seampm/tinytrain) as a C ABI,
+// for a GPTModel held on the device, plus data parallelism.
+//
+// Gradients of all parameters live in one flat device arena, laid out in the
+// order backward finishes them (final norm, last block ... first block, the
+// tied embedding last). With a communicator, the arena is cut into buckets of
+// about bucket_bytes; during the last micro-batch's backward the autograd
+// engine reports each parameter whose gradient is final, and a bucket whose
+// parameters are all final is all-reduced on a separate comm stream while
+// backward continues. The compute stream waits for the last bucket before
+// the fused clip + AdamW kernel, which divides by world * n_micro.
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <unordered_map>
+
+#include "internal.h"
+#include "tinytrain/model.h"
+#include "tinytrain/optim.h"
+#include "tt_trainer.h"
+#include "ttk.h"
+
+extern "C" int64_t ttk_launch_count(void);
+
+namespace {
+
+thread_local std::string t_err;
+
+using namespace tt;
+using namespace tt::detail;
+
+struct Bucket {
+    int64_t offset = 0, count = 0;  // elements in the arena
+    int pending = 0;                // parameters not yet final this step
+    int total = 0;
+};
+
+struct Trainer {
+    GPTConfig cfg;
+    std::unique_ptr<GPTModel> model;
+    std::vector<Tensor*> params;
+    std::unique_ptr<AdamW> opt;
+    tt_adamw_config ocfg{3e-4f, 0.9f, 0.95f, 1e-8f, 0.1f, 1.0f};
+    float* arena = nullptr;
+    int64_t arena_n = 0;
+    std::vector<int64_t> param_offset;  // arena offset per parameter
+    float* loss_acc = nullptr;          // device: sum of micro-batch losses
+    float* loss_out = nullptr;          // device: step loss
+    // data parallelism
+    void* comm = nullptr;
+    int rank = 0, world = 1;
+    void* comm_stream = nullptr;
+    std::vector<Bucket> buckets;
+    std::unordered_map<Tensor::Impl*, int> bucket_of;
+    std::vector<void*> bucket_events;
+    void* done_event = nullptr;
+
+    ~Trainer() {
+        tt::set_grad_ready_hook(nullptr);
+        void* s = get_stream();
+        ttk_stream_synchronize(s);
+        if (comm)
+            ttk_dist_destroy(comm);
+        for (void* e : bucket_events)
+            ttk_event_destroy(e);
+        if (done_event)
+            ttk_event_destroy(done_event);
+        if (comm_stream)
+            ttk_stream_destroy(comm_stream);
+        opt.reset();
+        model.reset();
+        ttk_free(arena, s);
+        ttk_free(loss_acc, s);
+        ttk_free(loss_out, s);
+    }
+
+    void setup() {
+        params = model->parameters();
+        // Arena order: reverse of parameters(), which is the order in which
+        // backward completes them; the tied embedding (index 0) comes last.
+        std::vector<size_t> order;
+        for (size_t i = params.size(); i-- > 0;)
+            order.push_back(i);
+        param_offset.assign(params.size(), 0);
+        int64_t off = 0;
+        for (size_t i : order) {
+            param_offset[i] = off;
+            off += (params[i]->numel() + 63) / 64 * 64;  // 256-byte aligned slices
+        }
+        arena_n = off;
+        check(ttk_malloc(reinterpret_cast<void**>(&arena), static_cast<size_t>(arena_n) * 4,
+                         stream()),
+              "grad arena");
+        check(ttk_memset(arena, 0, static_cast<size_t>(arena_n) * 4, stream()), "grad arena");
+        for (size_t i = 0; i < params.size(); ++i) {
+            auto buf = std::make_shared<Buffer>(params[i]->numel());
+            buf->dev = arena + param_offset[i];
+            buf->external = true;
+            buf->fill(0.0f);
+            params[i]->impl()->grad = buf;
+        }
+        check(ttk_malloc(reinterpret_cast<void**>(&loss_acc), 16, stream()), "loss");
+        check(ttk_malloc(reinterpret_cast<void**>(&loss_out), 16, stream()), "loss");
+        opt.reset(new AdamW(params, ocfg.lr, ocfg.beta1, ocfg.beta2, ocfg.eps, ocfg.weight_decay));
+        opt->set_clip_norm(ocfg.clip_norm);
+    }
+
+    void zero_grads() {
+        // One memset of the arena; each parameter's gradient is then "fresh"
+        // (logically zero) so its first contribution overwrites.
+        for (Tensor* p : params)
+            p->impl()->grad->fill(0.0f);
+    }
+
+    void make_buckets(int64_t bucket_bytes) {
+        const int64_t cap = std::max<int64_t>(bucket_bytes / 4, 1 << 16);
+        std::vector<size_t> order;
+        for (size_t i = params.size(); i-- > 0;)
+            order.push_back(i);
+        buckets.clear();
+        bucket_of.clear();
+        Bucket cur;
+        cur.offset = 0;
+        for (size_t i : order) {
+            const int64_t span = (params[i]->numel() + 63) / 64 * 64;
+            if (cur.total > 0 && cur.count + span > cap) {
+                buckets.push_back(cur);
+                cur = Bucket();
+                cur.offset = param_offset[i];
+            }
+            cur.count += span;
+            cur.total += 1;
+            bucket_of[params[i]->impl().get()] = static_cast<int>(buckets.size());
+        }
+        if (cur.total > 0)
+            buckets.push_back(cur);
+        for (void* e : bucket_events)
+            ttk_event_destroy(e);
+        bucket_events.assign(buckets.size(), nullptr);
+        for (auto& e : bucket_events)
+            check(ttk_event_create(&e), "event");
+        if (!done_event)
+            check(ttk_event_create(&done_event), "event");
+    }
+
+    void launch_bucket(int b) {
+        Bucket& bk = buckets[static_cast<size_t>(b)];
+        check(ttk_event_record(bucket_events[static_cast<size_t>(b)], stream()), "record");
+        check(ttk_stream_wait_event(comm_stream, bucket_events[static_cast<size_t>(b)]), "wait");
+        check(ttk_dist_allreduce_f32(comm, arena + bk.offset, bk.count, comm_stream), "allreduce");
+    }
+
+    // Runs fwd+bwd over n_micro micro-batches; ids are device pointers.
+    void accumulate(const int64_t* idx, const int64_t* tgt, int64_t B, int64_t T,
+                    int64_t n_micro) {
+        check(ttk_memset(loss_acc, 0, 4, stream()), "loss zero");
+        const int64_t per = B * T;
+        for (int64_t m = 0; m < n_micro; ++m) {
+            const bool last = m + 1 == n_micro;
+            if (comm && last) {
+                for (auto& bk : buckets)
+                    bk.pending = bk.total;
+                tt::set_grad_ready_hook([this](const std::shared_ptr<Tensor::Impl>& p) {
+                    auto it = bucket_of.find(p.get());
+                    if (it == bucket_of.end())
+                        return;
+                    if (--buckets[static_cast<size_t>(it->second)].pending == 0)
+                        launch_bucket(it->second);
+                });
+            }
+            {
+                Tensor logits = model->forward(DeviceIds::borrow(idx + m * per, per), B, T);
+                Tensor loss = cross_entropy(logits, DeviceIds::borrow(tgt + m * per, per));
+                check(ttk_axpy(1.0f, loss.device_data(), loss_acc, 1, stream()), "loss acc");
+                loss.backward();
+            }
+            if (comm && last) {
+                tt::set_grad_ready_hook(nullptr);
+                // Any bucket whose parameters got no gradient this step.
+                for (size_t b = 0; b < buckets.size(); ++b)
+                    if (buckets[b].pending > 0)
+                        launch_bucket(static_cast<int>(b));
+                check(ttk_event_record(done_event, comm_stream), "record");
+                check(ttk_stream_wait_event(stream(), done_event), "wait");
+            }
+        }
+        // Step loss = mean over micro-batches (and ranks).
+        check(ttk_fill(loss_out, 0.0f, 1, stream()), "loss");
+        check(ttk_axpy(1.0f / static_cast<float>(n_micro), loss_acc, loss_out, 1, stream()), "loss");
+        if (comm) {
+            check(ttk_dist_allreduce_f32(comm, loss_out, 1, stream()), "loss allreduce");
+            const float inv = 1.0f / static_cast<float>(world);
+            check(ttk_fill(loss_acc, 0.0f, 1, stream()), "loss");
+            check(ttk_axpy(inv, loss_out, loss_acc, 1, stream()), "loss");
+            check(ttk_memcpy_d2d(loss_out, loss_acc, 4, stream()), "loss");
+        }
+    }
+
+    void optimizer_step(int64_t n_micro, float lr) {
+        opt->set_lr(lr);
+        opt->set_grad_scale(1.0f / static_cast<float>(n_micro * world));
+        opt->step();
+    }
+};
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        f();
+        return 0;
+    } catch (const std::exception& e) {
+        t_err = e.what();
+        return 1;
+    }
+}
+
+Trainer* T_(void* h) { return static_cast<Trainer*>(h); }
+
+}  // namespace
+
+extern "C" {
+
+const char* tt_last_error(void) { return t_err.c_str(); }
+
+int64_t tt_kernel_launches(void) { return ttk_launch_count(); }
+
+int tt_trainer_create(const tt_model_config* c, uint64_t seed, int host_init, void** handle) {
+    return guarded([&] {
+        auto tr = std::make_unique<Trainer>();
+        tr->cfg.vocab_size = c->vocab;
+        tr->cfg.dim = c->dim;
+        tr->cfg.n_layers = c->layers;
+        tr->cfg.n_heads = c->heads;
+        tr->cfg.n_kv_heads = c->heads;
+        tr->cfg.ffn_dim = c->ffn;
+        tr->cfg.max_seq_len = c->max_seq;
+        tr->cfg.norm_eps = c->norm_eps;
+        tr->cfg.rope_theta = c->rope_theta;
+        tr->model.reset(new GPTModel(tr->cfg, seed, host_init != 0));
+        tr->setup();
+        *handle = tr.release();
+    });
+}
+
+int tt_trainer_destroy(void* h) {
+    return guarded([&] { delete T_(h); });
+}
+
+int tt_trainer_set_stream(void* h, void* s) {
+    // The stream is process-wide; h may be NULL (call before creating).
+    return guarded([&] {
+        (void)h;
+        tt::set_stream(s);
+    });
+}
+
+int64_t tt_trainer_param_count(void* h) {
+    int64_t n = 0;
+    for (Tensor* p : T_(h)->params)
+        n += p->numel();
+    return n;
+}
+
+int tt_trainer_init_normal(void* h, float std, uint64_t seed) {
+    return guarded([&] { T_(h)->model->init_normal_(std, seed); });
+}
+
+int tt_trainer_set_params(void* h, const float* host, int64_t n) {
+    return guarded([&] {
+        if (n != tt_trainer_param_count(h))
+            throw std::invalid_argument("set_params: size mismatch");
+        int64_t off = 0;
+        for (Tensor* p : T_(h)->params) {
+            p->copy_from_host(host + off);
+            off += p->numel();
+        }
+    });
+}
+
+int tt_trainer_get_params(void* h, float* host, int64_t n) {
+    return guarded([&] {
+        if (n != tt_trainer_param_count(h))
+            throw std::invalid_argument("get_params: size mismatch");
+        int64_t off = 0;
+        for (Tensor* p : T_(h)->params) {
+            p->copy_to_host(host + off);
+            off += p->numel();
+        }
+    });
+}
+
+int tt_trainer_get_grads(void* h, float* host, int64_t n) {
+    return guarded([&] {
+        if (n != tt_trainer_param_count(h))
+            throw std::invalid_argument("get_grads: size mismatch");
+        int64_t off = 0;
+        for (Tensor* p : T_(h)->params) {
+            const float* g = p->grad_data();
+            std::memcpy(host + off, g, static_cast<size_t>(p->numel()) * 4);
+            off += p->numel();
+        }
+    });
+}
+
+int tt_trainer_set_optimizer(void* h, const tt_adamw_config* c) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        t->ocfg = *c;
+        t->opt.reset(new AdamW(t->params, c->lr, c->beta1, c->beta2, c->eps, c->weight_decay));
+        t->opt->set_clip_norm(c->clip_norm);
+    });
+}
+
+int tt_trainer_step_device(void* h, const int64_t* idx, const int64_t* targets, int64_t B,
+                           int64_t T, int64_t n_micro, float lr) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        if (B <= 0 || T <= 0 || n_micro <= 0)
+            throw std::invalid_argument("step: sizes must be positive");
+        t->zero_grads();
+        t->accumulate(idx, targets, B, T, n_micro);
+        t->optimizer_step(n_micro, lr);
+    });
+}
+
+int tt_trainer_step(void* h, const int64_t* idx, const int64_t* targets, int64_t B, int64_t T,
+                    int64_t n_micro, float lr, float* loss, float* grad_norm) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        const int64_t n = B * T * n_micro;
+        if (B <= 0 || T <= 0 || n_micro <= 0)
+            throw std::invalid_argument("step: sizes must be positive");
+        for (int64_t i = 0; i < n; ++i)
+            if (idx[i] < 0 || idx[i] >= t->cfg.vocab_size || targets[i] < 0 ||
+                targets[i] >= t->cfg.vocab_size)
+                throw std::invalid_argument("embedding: index out of range");
+        Scratch d(static_cast<size_t>(n) * 16);
+        check(ttk_memcpy_h2d(d.ptr, idx, static_cast<size_t>(n) * 8, stream()), "ids");
+        check(ttk_memcpy_h2d(d.as<int64_t>() + n, targets, static_cast<size_t>(n) * 8, stream()),
+              "ids");
+        t->zero_grads();
+        t->accumulate(d.as<int64_t>(), d.as<int64_t>() + n, B, T, n_micro);
+        t->optimizer_step(n_micro, lr);
+        if (loss)
+            check(ttk_memcpy_d2h(loss, t->loss_out, 4, stream()), "loss read");
+        if (grad_norm)
+            *grad_norm = t->ocfg.clip_norm > 0.0f ? t->opt->last_grad_norm() : 0.0f;
+    });
+}
+
+int tt_trainer_last_loss(void* h, float* loss) {
+    return guarded([&] { check(ttk_memcpy_d2h(loss, T_(h)->loss_out, 4, stream()), "loss read"); });
+}
+
+int tt_trainer_forward_backward(void* h, const int64_t* idx, const int64_t* targets, int64_t B,
+                                int64_t T, float* loss, float* logits) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        std::vector<int64_t> ix(idx, idx + B * T), tg(targets, targets + B * T);
+        t->zero_grads();
+        Tensor lg = t->model->forward(ix, B, T);
+        if (logits)
+            lg.copy_to_host(logits);
+        Tensor l = cross_entropy(lg, tg);
+        if (loss)
+            l.copy_to_host(loss);
+        l.backward();
+        tt::synchronize();
+    });
+}
+
+int tt_trainer_dist_init(void* h, int rank, int world, const unsigned char id[128],
+                         int64_t bucket_bytes) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        check(ttk_dist_init(rank, world, id, &t->comm), "dist init");
+        t->rank = rank;
+        t->world = world;
+        check(ttk_stream_create(&t->comm_stream), "comm stream");
+        t->make_buckets(bucket_bytes > 0 ? bucket_bytes : (64ll << 20));
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,173 @@
+"""Python front end of the trainer C ABI (include/tt_trainer.h).
+
+The training step itself runs in libtinytrain.so (C++20 tt:: API on device
+tensors, kernels in libttk.so). This module only marshals arguments, like the
+ctypes/cgo stub a host application in another language would write.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from . import _ttk
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libtinytrain.so")
+
+
+class ModelConfig(C.Structure):
+    _fields_ = [("vocab", C.c_int64), ("dim", C.c_int64), ("layers", C.c_int64),
+                ("heads", C.c_int64), ("ffn", C.c_int64), ("max_seq", C.c_int64),
+                ("norm_eps", C.c_float), ("rope_theta", C.c_float)]
+
+
+class AdamWConfig(C.Structure):
+    _fields_ = [("lr", C.c_float), ("beta1", C.c_float), ("beta2", C.c_float),
+                ("eps", C.c_float), ("weight_decay", C.c_float), ("clip_norm", C.c_float)]
+
+
+# Named model configurations (GPTConfig fields, model.h:15-26).
+CONFIGS = {
+    # the reference's default Llama (model.h defaults / train.cpp:40)
+    "llama-13m": dict(vocab=32000, dim=256, layers=6, heads=8, ffn=768, max_seq=256),
+    "llama-110m": dict(vocab=32000, dim=768, layers=12, heads=12, ffn=2048, max_seq=1024),
+    "llama-1b": dict(vocab=32000, dim=2048, layers=16, heads=16, ffn=5632, max_seq=2048),
+}
+
+_lib = None
+P, I64, F32, U64 = C.c_void_p, C.c_int64, C.c_float, C.c_uint64
+_SIGS = {
+    "tt_last_error": (C.c_char_p, []),
+    "tt_trainer_create": (C.c_int, [P, U64, C.c_int, P]),
+    "tt_trainer_destroy": (C.c_int, [P]),
+    "tt_trainer_set_stream": (C.c_int, [P, P]),
+    "tt_trainer_param_count": (I64, [P]),
+    "tt_trainer_init_normal": (C.c_int, [P, F32, U64]),
+    "tt_trainer_set_params": (C.c_int, [P, P, I64]),
+    "tt_trainer_get_params": (C.c_int, [P, P, I64]),
+    "tt_trainer_get_grads": (C.c_int, [P, P, I64]),
+    "tt_trainer_set_optimizer": (C.c_int, [P, P]),
+    "tt_trainer_step": (C.c_int, [P, P, P, I64, I64, I64, F32, P, P]),
+    "tt_trainer_step_device": (C.c_int, [P, P, P, I64, I64, I64, F32]),
+    "tt_trainer_last_loss": (C.c_int, [P, P]),
+    "tt_trainer_forward_backward": (C.c_int, [P, P, P, I64, I64, P, P]),
+    "tt_trainer_dist_init": (C.c_int, [P, C.c_int, C.c_int, P, I64]),
+    "tt_kernel_launches": (I64, []),
+}
+
+
+class TrainerError(RuntimeError):
+    pass
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        _ttk.lib()  # libttk.so first (RTLD_GLOBAL), then the C++ layer
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run `python -m tinytrain_b200.build`")
+        _lib = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)
+        for k, (r, a) in _SIGS.items():
+            f = getattr(_lib, k)
+            f.restype, f.argtypes = r, a
+    return _lib
+
+
+def _chk(rc, what):
+    if rc != 0:
+        raise TrainerError(f"{what}: {lib().tt_last_error().decode()}")
+
+
+def kernel_launches() -> int:
+    return int(lib().tt_kernel_launches())
+
+
+def set_stream(stream_handle: int):
+    _chk(lib().tt_trainer_set_stream(None, stream_handle), "set_stream")
+
+
+class Trainer:
+    """GPTModel + AdamW on one GPU (optionally one rank of a DP job)."""
+
+    def __init__(self, config, seed=42, host_init=True, norm_eps=1e-5, rope_theta=10000.0):
+        if isinstance(config, str):
+            config = CONFIGS[config]
+        self.cfg = dict(config)
+        mc = ModelConfig(self.cfg["vocab"], self.cfg["dim"], self.cfg["layers"], self.cfg["heads"],
+                         self.cfg["ffn"], self.cfg["max_seq"], norm_eps, rope_theta)
+        h = C.c_void_p()
+        _chk(lib().tt_trainer_create(C.byref(mc), seed, int(host_init), C.byref(h)), "create")
+        self.h = h
+        self.n_params = int(lib().tt_trainer_param_count(self.h))
+
+    def close(self):
+        if self.h:
+            _chk(lib().tt_trainer_destroy(self.h), "destroy")
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def init_normal(self, std=0.02, seed=0):
+        _chk(lib().tt_trainer_init_normal(self.h, std, seed), "init_normal")
+
+    def set_params(self, flat):
+        flat = np.ascontiguousarray(flat, np.float32)
+        _chk(lib().tt_trainer_set_params(self.h, flat.ctypes.data, flat.size), "set_params")
+
+    def get_params(self):
+        out = np.empty(self.n_params, np.float32)
+        _chk(lib().tt_trainer_get_params(self.h, out.ctypes.data, out.size), "get_params")
+        return out
+
+    def get_grads(self):
+        out = np.empty(self.n_params, np.float32)
+        _chk(lib().tt_trainer_get_grads(self.h, out.ctypes.data, out.size), "get_grads")
+        return out
+
+    def set_optimizer(self, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, clip=1.0):
+        c = AdamWConfig(lr, betas[0], betas[1], eps, weight_decay, clip)
+        _chk(lib().tt_trainer_set_optimizer(self.h, C.byref(c)), "set_optimizer")
+
+    def step(self, idx, targets, B, T, n_micro=1, lr=3e-4):
+        """Host ids (int64, n_micro*B*T); returns (loss, grad_norm)."""
+        idx = np.ascontiguousarray(idx, np.int64)
+        targets = np.ascontiguousarray(targets, np.int64)
+        loss, gn = C.c_float(0), C.c_float(0)
+        _chk(lib().tt_trainer_step(self.h, idx.ctypes.data, targets.ctypes.data, B, T, n_micro,
+                                   lr, C.byref(loss), C.byref(gn)), "step")
+        return loss.value, gn.value
+
+    def step_device(self, idx_ptr, tgt_ptr, B, T, n_micro=1, lr=3e-4):
+        _chk(lib().tt_trainer_step_device(self.h, idx_ptr, tgt_ptr, B, T, n_micro, lr),
+             "step_device")
+
+    def last_loss(self):
+        v = C.c_float(0)
+        _chk(lib().tt_trainer_last_loss(self.h, C.byref(v)), "last_loss")
+        return v.value
+
+    def forward_backward(self, idx, targets, B, T, want_logits=False):
+        idx = np.ascontiguousarray(idx, np.int64)
+        targets = np.ascontiguousarray(targets, np.int64)
+        loss = C.c_float(0)
+        logits = np.empty((B * T, self.cfg["vocab"]), np.float32) if want_logits else None
+        _chk(lib().tt_trainer_forward_backward(
+            self.h, idx.ctypes.data, targets.ctypes.data, B, T, C.byref(loss),
+            None if logits is None else logits.ctypes.data), "forward_backward")
+        return loss.value, logits
+
+    def dist_init(self, rank, world, uid: bytes, bucket_bytes=64 << 20):
+        buf = (C.c_ubyte * 128).from_buffer_copy(uid)
+        _chk(lib().tt_trainer_dist_init(self.h, rank, world, buf, bucket_bytes), "dist_init")
+
+
+def dist_unique_id() -> bytes:
+    buf = (C.c_ubyte * 128)()
+    _ttk.call("ttk_dist_unique_id", buf)
+    return bytes(buf)

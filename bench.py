@@ -1,0 +1,346 @@
+"""Training-throughput benchmark: tinytrain's training step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config llama-1b]
+    python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+    python bench.py --impl reference ...      # the reference's CPU build
+
+One step = one AdamW optimizer step over the global batch: n_micro
+micro-batches of 8 x 2048 tokens per rank (gradient accumulation), forward,
+fused cross-entropy, backward, bucketed NCCL gradient all-reduce overlapped
+with the last backward (N > 1), global-norm clipping folded into the fused
+AdamW kernel. Weights are fp32 ~ N(0, 0.02), tokens uniform in [0, 32000)
+(synthetic: no dataset). The global batch is fixed (256 x 2048 for llama-1b),
+so scaling is strong.
+
+value: tokens/s with the token ids already in HBM (tt_trainer_step_device),
+timed with CUDA events on the launching stream, max over ranks.
+e2e: the same through the public C ABI with host buffers (tt_trainer_step:
+host ids uploaded and the loss read back inside the timed region).
+roofline: the dominant kernel (the tcgen05 3xTF32 GEMM) timed live over the
+timed region (events around each launch); achieved = algorithmic FLOPs
+(2*M*N*K per GEMM) / kernel time.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "llama-1b": dict(model="llama-1b", vocab=32000, dim=2048, layers=16, heads=16, ffn=5632,
+                     max_seq=2048, global_batch=256, seq=2048, micro=8),
+    "llama-110m": dict(model="llama-110m", vocab=32000, dim=768, layers=12, heads=12, ffn=2048,
+                       max_seq=1024, global_batch=64, seq=1024, micro=16),
+    "llama-13m": dict(model="llama-13m", vocab=32000, dim=256, layers=6, heads=8, ffn=768,
+                      max_seq=256, global_batch=16, seq=128, micro=16),
+}
+# CPU sample of the reference per step (tokens), bounded to ~10-30 s of work.
+CPU_SAMPLE = {"llama-1b": (1, 16), "llama-110m": (1, 128), "llama-13m": (16, 128)}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return d["hbm_gbs"], d["bf16_tflops"], d["bf16_tflops_sustained"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def flops_per_token(w):
+    d, L, f, V, T = w["dim"], w["layers"], w["ffn"], w["vocab"], w["seq"]
+    linear = L * (4 * d * d + 3 * d * f) + d * V
+    return 6 * linear + 6 * T * d * L
+
+
+def n_params(w):
+    d, L, f, V = w["dim"], w["layers"], w["ffn"], w["vocab"]
+    return V * d + L * (2 * d + 4 * d * d + 3 * d * f) + d
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus):
+        self.gpus = gpus
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", ",".join(str(g) for g in self.gpus)],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax.append(float(p[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_reference_time(w, steps, warmup):
+    """Mean seconds per step of the reference's CPU build on a bounded sample."""
+    from oracle import refbind as rb
+    if not rb.available():
+        return None
+    B, T = CPU_SAMPLE[w["model"]]
+    c = rb.cfg(vocab=w["vocab"], dim=w["dim"], layers=w["layers"], heads=w["heads"],
+               ffn=w["ffn"], max_seq=max(w["max_seq"], T))
+    secs = rb.time_train(c, B, T, warmup, steps)
+    return secs, B * T
+
+
+def run_reference(args, w, rank, world):
+    """--impl reference: the reference's own CPU implementation (oracle/_ref,
+    the reference sources compiled unchanged), all host threads, rank 0 only."""
+    if rank != 0:
+        return
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
+    from oracle import refbind as rb
+    if not rb.available():
+        print(json.dumps({"impl": "reference",
+                          "unavailable": "oracle/_ref/libttref.so was not built"}))
+        return
+    B, T = CPU_SAMPLE[w["model"]]
+    t0 = time.time()
+    secs, ntok = cpu_reference_time(w, args.steps, args.warmup)
+    tps = ntok / secs
+    cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
+    sample = f"{B} x {T} tokens per step on the {w['model']} model (reference train step: " \
+             f"forward, cross-entropy, backward, clip, AdamW), {args.steps} timed steps"
+    print(json.dumps({
+        "impl": "reference", "metric": "train tokens/sec", "value": tps, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": secs * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": workload_config(w, world),
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "wall_s": time.time() - t0}))
+
+
+def workload_config(w, world):
+    return {"workload": f"{w['model']} training step: dim {w['dim']}, {w['layers']} layers, "
+                        f"{w['heads']} heads, ffn {w['ffn']}, vocab {w['vocab']}, tied "
+                        f"embeddings, global batch {w['global_batch']} x {w['seq']} tokens "
+                        f"in micro-batches of {w['micro']} x {w['seq']}, AdamW + clip 1.0",
+            "model": w["model"], "params": n_params(w), "global_batch": w["global_batch"],
+            "seq_len": w["seq"], "micro_batch": w["micro"], "parallelism": f"dp{world}",
+            "l2": "no flush: every step streams > 10 GB (weights, moments, activations) "
+                  "through a 126 MB L2"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="llama-1b", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    w = WORKLOADS[args.config]
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, w, rank, world)
+        return
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from tinytrain_b200 import _ttk
+    from tinytrain_b200 import trainer as trn
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    stream = torch.cuda.current_stream()
+    trn.set_stream(stream.cuda_stream)
+
+    if w["global_batch"] % (w["micro"] * world):
+        raise SystemExit("global batch must split into micro-batches across ranks")
+    n_micro = w["global_batch"] // (w["micro"] * world)
+    B, T = w["micro"], w["seq"]
+    tokens_rank = n_micro * B * T
+
+    cfgm = {k: w[k] for k in ("vocab", "dim", "layers", "heads", "ffn", "max_seq")}
+    tr = trn.Trainer(cfgm, seed=1234, host_init=False)
+    tr.init_normal(0.02, seed=1234)
+    tr.set_optimizer(lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, clip=1.0)
+    if world > 1:
+        uid = trn.dist_unique_id() if rank == 0 else b"\0" * 128
+        obj = [uid]
+        dist.broadcast_object_list(obj, src=0)
+        tr.dist_init(rank, world, obj[0], bucket_bytes=64 << 20)
+
+    # Synthetic tokens: each rank its own disjoint stream of windows.
+    g = np.random.default_rng(10_000 + rank)
+    n_sets = 4
+    host_idx = [g.integers(0, w["vocab"], tokens_rank, dtype=np.int64) for _ in range(n_sets)]
+    host_tgt = [g.integers(0, w["vocab"], tokens_rank, dtype=np.int64) for _ in range(n_sets)]
+    dev_idx = [torch.from_numpy(x).to(dev) for x in host_idx]
+    dev_tgt = [torch.from_numpy(x).to(dev) for x in host_tgt]
+    pin_idx = [torch.from_numpy(x).pin_memory() for x in host_idx]
+    pin_tgt = [torch.from_numpy(x).pin_memory() for x in host_tgt]
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up (device-resident ids)
+    for i in range(args.warmup):
+        tr.step_device(dev_idx[i % n_sets].data_ptr(), dev_tgt[i % n_sets].data_ptr(), B, T,
+                       n_micro, 3e-4)
+    barrier()
+
+    # ---- timed region: value
+    _ttk.call("ttk_profile_enable", 1)
+    l0 = trn.kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler([local] if world == 1 else list(range(world))) as clk:
+        barrier()
+        e0.record(stream)
+        for i in range(args.steps):
+            tr.step_device(dev_idx[i % n_sets].data_ptr(), dev_tgt[i % n_sets].data_ptr(), B, T,
+                           n_micro, 3e-4)
+        e1.record(stream)
+        barrier()
+    launches = trn.kernel_launches() - l0
+    gms, gfl, gl = C.c_double(0), C.c_double(0), C.c_int64(0)
+    _ttk.call("ttk_profile_enable", 0)
+    _ttk.call("ttk_profile_read", C.byref(gms), C.byref(gfl), C.byref(gl))
+    ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    loss_dev = tr.last_loss()
+    tokens_step = tokens_rank * world
+    value = tokens_step / (ms / 1e3)
+
+    # ---- e2e: public C ABI with host buffers (upload ids, read loss back)
+    ke = max(1, args.e2e_steps)
+    tr.step(pin_idx[0].numpy(), pin_tgt[0].numpy(), B, T, n_micro, 3e-4)  # warm path
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    loss_e2e = None
+    for i in range(ke):
+        loss_e2e, _ = tr.step(pin_idx[i % n_sets].numpy(), pin_tgt[i % n_sets].numpy(), B, T,
+                              n_micro, 3e-4)
+    f1.record(stream)
+    barrier()
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1)) / ke
+    e2e = tokens_step / (ms_e2e / 1e3)
+    status = _ttk.device_status()
+
+    if rank == 0:
+        hbm, bf16, bf16s, src = peaks()
+        gemm_tf = gfl.value / (gms.value / 1e3) / 1e12 if gms.value > 0 else 0.0
+        gemm_share = gms.value / (ms * args.steps) if ms > 0 else 0.0
+        line = {
+            "metric": "train tokens/sec", "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (N(0,0.02) weights, uniform tokens)",
+            "config": workload_config(w, world),
+            "roofline": {
+                "kernel": "gemm_tf32x3_kernel (tcgen05 3xTF32)", "bound": "tensor",
+                "achieved": gemm_tf, "peak": bf16s, "unit": "TFLOP/s",
+                "frac": gemm_tf / bf16s, "traffic": None,
+                "peak_source": f"{src} bf16 sustained (kernel timed inside a long step)",
+                "achieved_is": "algorithmic fp32 FLOP/s (2MNK per GEMM); each costs 3 TF32 "
+                               "MMAs at half the bf16 rate, so the 3xTF32 ceiling is peak/6",
+                "ceiling_3xtf32": bf16s / 6, "frac_of_3xtf32_ceiling": gemm_tf / (bf16s / 6),
+                "launches": gl.value, "share_of_step": gemm_share},
+            "mfu_fp32_equiv": value * flops_per_token(w) / 1e12 / world,
+            "gpu_launches": launches,
+            "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * tokens_rank * 8,
+                    "d2h_bytes_per_step": 4, "steps": ke},
+            "clocks": clk.summary(),
+            "loss": loss_dev, "loss_e2e": loss_e2e, "device_status": status,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                r = cpu_reference_time(w, 1, 0)
+            except Exception as ex:  # reported, never fatal
+                r = None
+                line["cpu_baseline_error"] = str(ex)[:200]
+            if r:
+                secs, ntok = r
+                Bc, Tc = CPU_SAMPLE[w["model"]]
+                line["cpu_baseline"] = {
+                    "value": ntok / secs, "unit": "tokens/s",
+                    "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
+                    "kind": "reference",
+                    "sample": f"one reference train step (forward, cross-entropy, backward, "
+                              f"clip, AdamW) of {Bc} x {Tc} tokens on the {w['model']} model, "
+                              f"{secs:.1f} s"}
+        print(json.dumps(line), flush=True)
+
+    tr.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -98,6 +98,14 @@ int ttk_gemm_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t 
                       int64_t ldb_pad, float beta, float* C, int64_t ldc, int64_t strideC,
                       void* stream);
 
+/* Live timing of the tcgen05 GEMM kernel on the calling thread: when enabled,
+ * each launch is bracketed by CUDA events on its stream; ttk_profile_read
+ * synchronizes, returns the summed kernel time (ms), the summed algorithmic
+ * FLOPs (2*M*N*K per GEMM) and the launch count since the last read, and
+ * resets them. Off by default. */
+int ttk_profile_enable(int on);
+int ttk_profile_read(double* gemm_ms, double* gemm_flops, int64_t* launches);
+
 /* ------------------------------------------------------------ fused NN ops */
 
 /* y = x * rstd * w, rstd = (mean(x^2) + eps)^-1/2 per row; x, y [R,D], w [D],

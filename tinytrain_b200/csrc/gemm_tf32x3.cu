@@ -30,6 +30,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 #include "ttk_common.cuh"
 #include "ttk_internal.h"
 
@@ -459,6 +461,32 @@ int num_sms() {
     return n;
 }
 
+// Optional live timing of the tcgen05 kernel (ttk_profile_enable): an event
+// pair around each launch, read back and summed by ttk_profile_read.
+struct ProfRec {
+    cudaEvent_t a, b;
+    double flops;
+};
+struct Profiler {
+    bool on = false;
+    std::vector<ProfRec> recs;
+    std::vector<cudaEvent_t> pool;
+    cudaEvent_t get() {
+        if (!pool.empty()) {
+            cudaEvent_t e = pool.back();
+            pool.pop_back();
+            return e;
+        }
+        cudaEvent_t e;
+        cudaEventCreate(&e);
+        return e;
+    }
+};
+Profiler& prof() {
+    static thread_local Profiler p;
+    return p;
+}
+
 template <int BN>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, gemm::Params p,
                 cudaStream_t stream) {
@@ -478,8 +506,21 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, gemm::Params p,
     p.num_n = static_cast<int>((p.N + BN - 1) / BN);
     p.num_tiles = static_cast<int64_t>(p.num_m) * p.num_n * p.batch;
     const int grid = static_cast<int>(std::min<int64_t>(p.num_tiles, num_sms()));
+    Profiler& pr = prof();
+    ProfRec rec{};
+    if (pr.on) {
+        rec.a = pr.get();
+        rec.b = pr.get();
+        rec.flops = 2.0 * static_cast<double>(p.M) * p.N * p.K * p.batch;
+        cudaEventRecord(rec.a, stream);
+    }
     gemm::gemm_tf32x3_kernel<BN><<<grid, CF::NUM_THREADS, CF::SMEM_BYTES, stream>>>(ma, mb, p);
-    return check_launch("gemm_tf32x3_kernel");
+    const int rc = check_launch("gemm_tf32x3_kernel");
+    if (pr.on) {
+        cudaEventRecord(rec.b, stream);
+        pr.recs.push_back(rec);
+    }
+    return rc;
 }
 
 struct GemmPlan {
@@ -500,6 +541,34 @@ GemmPlan plan(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64
 }
 
 }  // namespace
+
+int gemm_profile_enable(int on) {
+    prof().on = on != 0;
+    return TTK_OK;
+}
+
+int gemm_profile_read(double* ms, double* flops, int64_t* launches) {
+    Profiler& pr = prof();
+    double tms = 0.0, tfl = 0.0;
+    for (auto& r : pr.recs) {
+        float m = 0.0f;
+        if (cudaEventSynchronize(r.b) != cudaSuccess ||
+            cudaEventElapsedTime(&m, r.a, r.b) != cudaSuccess)
+            return set_error(TTK_ERR_CUDA, "profile: event read failed");
+        tms += m;
+        tfl += r.flops;
+        pr.pool.push_back(r.a);
+        pr.pool.push_back(r.b);
+    }
+    if (ms)
+        *ms = tms;
+    if (flops)
+        *flops = tfl;
+    if (launches)
+        *launches = static_cast<int64_t>(pr.recs.size());
+    pr.recs.clear();
+    return TTK_OK;
+}
 
 size_t gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
                            int64_t K) {

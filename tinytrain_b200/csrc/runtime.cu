@@ -212,6 +212,12 @@ int ttk_event_synchronize(void* event) {
 
 // ------------------------------------------------------------------ GEMM --
 
+int ttk_profile_enable(int on) { return gemm_profile_enable(on); }
+
+int ttk_profile_read(double* gemm_ms, double* gemm_flops, int64_t* launches) {
+    return gemm_profile_read(gemm_ms, gemm_flops, launches);
+}
+
 size_t ttk_gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
                                int64_t K) {
     return gemm_workspace_size(transA, transB, batch, M, N, K);

@@ -26,6 +26,8 @@ inline int grid_for(int64_t n, int threads, int max_blocks = 148 * 16) {
 }
 
 // GEMM entry points (gemm_tf32x3.cu), shared with the C ABI wrappers.
+int gemm_profile_enable(int on);
+int gemm_profile_read(double* ms, double* flops, int64_t* launches);
 size_t gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
                            int64_t K);
 int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,

@@ -32,8 +32,10 @@ Tensor make_out(const std::vector<int64_t>& shape, bool requires_grad);
 Tensor make_view(const Tensor& src, const std::vector<int64_t>& shape, bool requires_grad);
 
 // Data of an impl materialized on the device (resolves lazy transposes).
-const float* dread(const ImplPtr& p);
-float* dwrite(const ImplPtr& p);
+const float* dread(Tensor::Impl* p);
+float* dwrite(Tensor::Impl* p);
+inline const float* dread(const ImplPtr& p) { return dread(p.get()); }
+inline float* dwrite(const ImplPtr& p) { return dwrite(p.get()); }
 
 // Gradient destination for an accumulation: returns the device pointer and
 // sets `overwrite` when the gradient is still logically zero, so the caller
@@ -41,8 +43,10 @@ float* dwrite(const ImplPtr& p);
 float* grad_target(const ImplPtr& p, bool& overwrite);
 // Gradient for read-modify-write (materializes pending zeros).
 float* grad_rmw(const ImplPtr& p);
-// Upstream gradient of a node (null when nothing flowed into it).
-const float* grad_in(const ImplPtr& p);
+// Upstream gradient of a node (null when nothing flowed into it). Backward
+// closures refer to their own node by raw pointer: the node owns the
+// closure, so a shared_ptr capture would be a cycle and leak the graph.
+const float* grad_in(const Tensor::Impl* p);
 
 // Scratch device memory released (stream-ordered) when it goes out of scope.
 struct Scratch {
@@ -60,7 +64,8 @@ struct Scratch {
 void host_randn(float* out, int64_t n, uint64_t seed);
 
 // Materialize a lazy transpose into its own buffer.
-void materialize(const ImplPtr& p);
+void materialize(Tensor::Impl* p);
+inline void materialize(const ImplPtr& p) { materialize(p.get()); }
 
 }  // namespace detail
 }  // namespace tt

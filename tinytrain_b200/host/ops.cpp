@@ -119,7 +119,8 @@ Tensor elem_binary(const Tensor& a, const Tensor& b, int op) {
                      shape.data(), static_cast<int>(shape.size()), stream()),
           "binary");
     if (out.requires_grad()) {
-        auto ao = a.impl(), bo = b.impl(), oo = out.impl();
+        auto ao = a.impl(), bo = b.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao, bo};
         oo->backward_fn = [ao, bo, oo, shape, op]() {
             const float* g = grad_in(oo);
@@ -157,7 +158,8 @@ Tensor elem_unary(const Tensor& a, int op, float p = 0.0f) {
     Tensor out = make_out(a.shape(), a.requires_grad());
     check(ttk_unary(op, dread(a.impl()), out_ptr(out), a.numel(), p, stream()), "unary");
     if (out.requires_grad()) {
-        auto ao = a.impl(), oo = out.impl();
+        auto ao = a.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao};
         oo->backward_fn = [ao, oo, op, p]() {
             const float* g = grad_in(oo);
@@ -234,7 +236,8 @@ Tensor sum(const Tensor& a, int64_t dim, bool keepdim) {
     Tensor out = make_out(oshape, a.requires_grad());
     check(ttk_reduce_mid(dread(a.impl()), out_ptr(out), outer, K, inner, 0, stream()), "sum");
     if (out.requires_grad()) {
-        auto ao = a.impl(), oo = out.impl();
+        auto ao = a.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao};
         oo->backward_fn = [ao, oo, outer, K, inner]() {
             const float* g = grad_in(oo);
@@ -252,7 +255,8 @@ Tensor sum_all(const Tensor& a) {
     Tensor out = make_out({1}, a.requires_grad());
     check(ttk_sum_all(dread(a.impl()), a.numel(), out_ptr(out), 0, stream()), "sum_all");
     if (out.requires_grad()) {
-        auto ao = a.impl(), oo = out.impl();
+        auto ao = a.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao};
         oo->backward_fn = [ao, oo]() {
             const float* g = grad_in(oo);
@@ -299,7 +303,8 @@ Tensor reshape(const Tensor& a, const std::vector<int64_t>& shape) {
         throw std::invalid_argument("reshape: incompatible size");
     Tensor out = make_view(a, out_shape, a.requires_grad());
     if (out.requires_grad()) {
-        auto ao = a.impl(), oo = out.impl();
+        auto ao = a.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao};
         oo->backward_fn = [ao, oo]() {
             const float* g = grad_in(oo);
@@ -361,7 +366,7 @@ Tensor permute(const Tensor& a, const std::vector<int64_t>& dims) {
               "permute");
     }
     if (out.requires_grad()) {
-        auto oo = out.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao};
         oo->backward_fn = [ao, oo, in_strides]() {
             const float* g = grad_in(oo);
@@ -394,7 +399,7 @@ Tensor expand(const Tensor& a, const std::vector<int64_t>& shape) {
                            0, 0, stream()),
           "expand");
     if (out.requires_grad()) {
-        auto oo = out.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao};
         oo->backward_fn = [ao, oo, shape]() {
             const float* g = grad_in(oo);
@@ -452,7 +457,8 @@ Tensor batched_matmul(const Tensor& a, const Tensor& b, int64_t Bt, int64_t M, i
     gemm(A.trans, Bm.trans, Bt, M, N, K, A.ptr, lda, M * K, Bm.ptr, ldb, K * N, 0.0f, out_ptr(out),
          N, M * N);
     if (out.requires_grad()) {
-        auto ao = a.impl(), bo = b.impl(), oo = out.impl();
+        auto ao = a.impl(), bo = b.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao, bo};
         oo->backward_fn = [ao, bo, oo, Bt, M, K, N]() {
             const float* g = grad_in(oo);
@@ -523,7 +529,8 @@ Tensor linear(const Tensor& x, const Tensor& weight) {
     gemm(0, 1, 1, R, Out, In, dread(x.impl()), In, 0, dread(weight.impl()), In, 0, 0.0f,
          out_ptr(out), Out, 0);
     if (out.requires_grad()) {
-        auto xo = x.impl(), wo = weight.impl(), oo = out.impl();
+        auto xo = x.impl(), wo = weight.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {xo, wo};
         oo->backward_fn = [xo, wo, oo, R, In, Out]() {
             const float* g = grad_in(oo);
@@ -585,7 +592,8 @@ Tensor embedding(const Tensor& weight, const DeviceIds& idx) {
     check(ttk_embedding_fwd(dread(weight.impl()), idx.data(), out_ptr(out), N, D, V, stream()),
           "embedding");
     if (out.requires_grad()) {
-        auto wo = weight.impl(), oo = out.impl();
+        auto wo = weight.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {wo};
         oo->backward_fn = [wo, oo, idx, N, D, V]() {
             const float* g = grad_in(oo);
@@ -618,7 +626,8 @@ Tensor softmax_impl(const Tensor& a, int64_t dim, int log) {
     Tensor out = make_out(a.shape(), a.requires_grad());
     check(ttk_softmax_fwd(dread(a.impl()), out_ptr(out), R, C, log, stream()), "softmax");
     if (out.requires_grad()) {
-        auto ao = a.impl(), oo = out.impl();
+        auto ao = a.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao};
         oo->backward_fn = [ao, oo, R, C, log]() {
             const float* g = grad_in(oo);
@@ -655,7 +664,8 @@ Tensor nll_loss(const Tensor& log_probs, const std::vector<int64_t>& targets) {
     Tensor out = make_out({1}, log_probs.requires_grad());
     check(ttk_nll_fwd(dread(log_probs.impl()), ids.data(), N, C, out_ptr(out), stream()), "nll");
     if (out.requires_grad()) {
-        auto lo = log_probs.impl(), oo = out.impl();
+        auto lo = log_probs.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {lo};
         oo->backward_fn = [lo, oo, ids, N, C]() {
             const float* g = grad_in(oo);
@@ -694,7 +704,8 @@ Tensor cross_entropy(const Tensor& logits, const DeviceIds& targets) {
           "cross_entropy");
     check(ttk_loss_finalize(acc.as<double>(), inv_n, out_ptr(out), stream()), "loss");
     if (out.requires_grad()) {
-        auto lo = logits.impl(), oo = out.impl();
+        auto lo = logits.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {lo};
         oo->backward_fn = [lo, oo, dlog, N, C]() {
             if (!oo->grad || !lo->requires_grad)
@@ -734,7 +745,8 @@ Tensor rmsnorm(const Tensor& a, const Tensor& weight, float eps) {
                           rstd->device_for_overwrite(), R, D, eps, stream()),
           "rmsnorm");
     if (out.requires_grad()) {
-        auto ao = a.impl(), wo = weight.impl(), oo = out.impl();
+        auto ao = a.impl(), wo = weight.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao, wo};
         oo->backward_fn = [ao, wo, oo, rstd, R, D]() {
             const float* g = grad_in(oo);
@@ -791,7 +803,8 @@ Tensor rope(const Tensor& x, const Tensor& cos, const Tensor& sin) {
           "rope");
     if (out.requires_grad() || cos.requires_grad() || sin.requires_grad()) {
         out.impl()->requires_grad = true;
-        auto xo = x.impl(), co = cos.impl(), so = sin.impl(), oo = out.impl();
+        auto xo = x.impl(), co = cos.impl(), so = sin.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {xo, co, so};
         oo->backward_fn = [xo, co, so, oo, B, T, H, D]() {
             const float* g = grad_in(oo);
@@ -831,8 +844,8 @@ Tensor causal_attention(const Tensor& q, const Tensor& k, const Tensor& v, const
                             hd, scale, stream()),
           "attention");
     if (rg) {
-        auto qo = q.impl(), ko = k.impl(), vo = v.impl(), co = cos.impl(), so = sin.impl(),
-             oo = out.impl();
+        auto qo = q.impl(), ko = k.impl(), vo = v.impl(), co = cos.impl(), so = sin.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {qo, ko, vo};
         oo->backward_fn = [qo, ko, vo, co, so, oo, lse, B, T, H, hd, scale]() {
             const float* g = grad_in(oo);
@@ -878,7 +891,8 @@ Tensor swiglu(const Tensor& a, const Tensor& b) {
     check(ttk_swiglu_fwd(dread(a.impl()), dread(b.impl()), out_ptr(out), a.numel(), stream()),
           "swiglu");
     if (out.requires_grad()) {
-        auto ao = a.impl(), bo = b.impl(), oo = out.impl();
+        auto ao = a.impl(), bo = b.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {ao, bo};
         oo->backward_fn = [ao, bo, oo]() {
             const float* g = grad_in(oo);

@@ -167,7 +167,7 @@ Tensor make_view(const Tensor& src, const std::vector<int64_t>& shape, bool requ
     return Tensor::from_impl(impl);
 }
 
-void materialize(const ImplPtr& p) {
+void materialize(Tensor::Impl* p) {
     if (!p->transpose_of || p->data)
         return;
     const ImplPtr& base = p->transpose_of;
@@ -186,13 +186,13 @@ void materialize(const ImplPtr& p) {
     p->data = buf;
 }
 
-const float* dread(const ImplPtr& p) {
+const float* dread(Tensor::Impl* p) {
     if (p->transpose_of && !p->data)
         materialize(p);
     return p->data->device();
 }
 
-float* dwrite(const ImplPtr& p) {
+float* dwrite(Tensor::Impl* p) {
     if (p->transpose_of && !p->data)
         materialize(p);
     float* d = p->data->device();
@@ -226,7 +226,7 @@ float* grad_rmw(const ImplPtr& p) {
     return d;
 }
 
-const float* grad_in(const ImplPtr& p) {
+const float* grad_in(const Tensor::Impl* p) {
     if (!p->grad)
         return nullptr;
     return p->grad->device();

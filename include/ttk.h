@@ -84,6 +84,25 @@ int ttk_gemm(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_
              const float* A, int64_t lda, int64_t strideA, const float* B, int64_t ldb,
              int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC,
              void* workspace, size_t workspace_bytes, void* stream);
+/* ttk_gemm without a workspace argument, for callers that cannot allocate
+ * device memory: code running under another framework's fixed memory budget,
+ * paths that must not fail with out-of-memory after start-up, or host
+ * programs that own only their input and output buffers. No counterpart in
+ * the reference (its CPU sgemm needs no device scratch).
+ * The split operands go to a fixed scratch array compiled into libttk.so
+ * (ttk_gemm_noalloc_max_workspace() bytes, 32 MiB, held by every GPU that
+ * loads the library until exit); operands needing more scratch than that
+ * (see ttk_gemm_workspace_size) are rejected with TTK_ERR_ARG. No memory is
+ * allocated. The first call on each device looks up the array's device
+ * address; make that first call before any stream capture. All calls share
+ * the one array, so calls that overlap on the GPU (different streams, or
+ * different host threads, without ordering between them) race on it; the
+ * caller must serialize them. Inputs and outputs are as for ttk_gemm. */
+size_t ttk_gemm_noalloc_max_workspace(void);
+int ttk_gemm_noalloc(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                     float alpha, const float* A, int64_t lda, int64_t strideA, const float* B,
+                     int64_t ldb, int64_t strideB, float beta, float* C, int64_t ldc,
+                     int64_t strideC, void* stream);
 /* The operand split alone: dst[b][0|1][r][0..ld_pad) = hi | lo of
  * src[b][r][0..cols) (ld, batch stride bstride), zero in [cols, ld_pad).
  * ld_pad must be a multiple of 16 (32 for an operand read MN-major by

@@ -49,6 +49,9 @@ SIGS = {
     "ttk_gemm_workspace_size": (SZ, [I32, I32, I64, I64, I64, I64]),
     "ttk_gemm": (I32, [I32, I32, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, F32, P, I64,
                        I64, P, SZ, P]),
+    "ttk_gemm_noalloc_max_workspace": (SZ, []),
+    "ttk_gemm_noalloc": (I32, [I32, I32, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, F32, P,
+                               I64, I64, P]),
     "ttk_split_tf32": (I32, [P, I64, I64, I64, I64, I64, P, I64, P]),
     "ttk_gemm_presplit": (I32, [I32, I32, I64, I64, I64, I64, F32, P, I64, P, I64, F32, P, I64,
                                 I64, P]),

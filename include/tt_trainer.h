@@ -70,6 +70,14 @@ int tt_trainer_forward_backward(void* handle, const int64_t* idx, const int64_t*
  * about bucket_bytes during backward. */
 int tt_trainer_dist_init(void* handle, int rank, int world, const unsigned char id[128],
                          int64_t bucket_bytes);
+/* The gradient arena / bucket plan used by a data-parallel trainer (host
+ * only, no device needed): for n parameters of the given sizes in
+ * parameters() order, writes each one's arena offset (elements) and bucket
+ * id, and per bucket its offset and length (buckets ordered as backward
+ * finishes them; arrays sized n). */
+int tt_plan_buckets(const int64_t* sizes, int n, int64_t bucket_bytes, int64_t* offsets,
+                    int* bucket_of_param, int64_t* bucket_offset, int64_t* bucket_count,
+                    int* n_buckets);
 /* Number of CUDA kernels this library launched so far (all streams). */
 int64_t tt_kernel_launches(void);
 

@@ -145,6 +145,37 @@ double clip_grads(const std::vector<tt::Tensor*>& ps, float max_norm) {
     return total;
 }
 
+// The reference's backward closures capture their own node by shared_ptr
+// (e.g. ops.cpp:169-171), so every graph is a reference cycle and is never
+// freed; a multi-step run would exhaust host memory. After a step, walk the
+// graph from the loss and drop each node's closure and edges (both public
+// members of the reference's Tensor::Impl, tensor.h:21-32). Values already
+// computed are unaffected.
+void release_graph(const tt::Tensor& root) {
+    std::vector<std::shared_ptr<tt::Tensor::Impl>> stack{root.impl()}, seen;
+    std::vector<tt::Tensor::Impl*> visited;
+    while (!stack.empty()) {
+        auto n = stack.back();
+        stack.pop_back();
+        bool dup = false;
+        for (auto* v : visited)
+            if (v == n.get()) {
+                dup = true;
+                break;
+            }
+        if (dup)
+            continue;
+        visited.push_back(n.get());
+        seen.push_back(n);
+        for (auto& p : n->prev)
+            stack.push_back(p);
+    }
+    for (auto& n : seen) {
+        n->backward_fn = [] {};
+        n->prev.clear();
+    }
+}
+
 } // namespace
 
 extern "C" {
@@ -444,6 +475,7 @@ int ref_train(const RefCfg* c, float* params, const int64_t* idx, const int64_t*
                 grad_norms[s] = static_cast<float>(gn);
             opt.set_lr(lrs[s]);
             opt.step();
+            release_graph(l);
         }
         store_params(m, params);
     });
@@ -484,6 +516,7 @@ int ref_time_train(const RefCfg* c, int64_t B, int64_t T, int64_t warmup, int64_
             clip_grads(ps, 1.0f);
             opt.step();
             auto t1 = std::chrono::steady_clock::now();
+            release_graph(l);
             if (it >= warmup)
                 total += std::chrono::duration<double>(t1 - t0).count();
         }

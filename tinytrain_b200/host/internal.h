@@ -21,6 +21,9 @@ inline void check(int rc, const char* what) {
 
 void* stream();
 void ensure_runtime();
+// The library stream if the runtime is up, else null; never throws (for
+// destructors).
+void* stream_if_ready();
 
 // Row-major strides of a shape.
 std::vector<int64_t> row_major(const std::vector<int64_t>& shape);

@@ -32,11 +32,12 @@ AdamW::AdamW(const std::vector<Tensor*>& params, float lr, float beta1, float be
       weight_decay_(weight_decay), m_(params.size(), nullptr), v_(params.size(), nullptr) {}
 
 AdamW::~AdamW() {
+    void* s = stream_if_ready();
     for (float* p : m_)
-        ttk_free(p, get_stream());
+        ttk_free(p, s);
     for (float* p : v_)
-        ttk_free(p, get_stream());
-    ttk_free(sumsq_, get_stream());
+        ttk_free(p, s);
+    ttk_free(sumsq_, s);
 }
 
 void AdamW::zero_grad() {
@@ -94,8 +95,9 @@ SGD::SGD(const std::vector<Tensor*>& params, float lr, float momentum, float wei
       vel_(params.size(), nullptr) {}
 
 SGD::~SGD() {
+    void* s = stream_if_ready();
     for (float* p : vel_)
-        ttk_free(p, get_stream());
+        ttk_free(p, s);
 }
 
 void SGD::zero_grad() {

@@ -51,6 +51,8 @@ void* stream() {
     return g_stream;
 }
 
+void* stream_if_ready() { return g_stream; }
+
 std::vector<int64_t> row_major(const std::vector<int64_t>& shape) {
     std::vector<int64_t> st(shape.size());
     int64_t s = 1;
@@ -75,7 +77,7 @@ Scratch::Scratch(size_t b) : bytes(b) {
 
 Scratch::~Scratch() {
     if (ptr)
-        ttk_free(ptr, stream());
+        ttk_free(ptr, stream_if_ready());
 }
 
 }  // namespace detail

@@ -36,6 +36,37 @@ struct Bucket {
     int total = 0;
 };
 
+// Arena layout and bucket plan for parameters of the given sizes (in
+// parameters() order): parameter i gets arena offset offs[i]; parameters are
+// placed in reverse order (the order backward finishes them) on 64-element
+// (256-byte) boundaries; consecutive parameters are grouped into buckets of
+// at most cap elements (a larger parameter gets a bucket of its own).
+int64_t plan_arena(const std::vector<int64_t>& sizes, int64_t cap, std::vector<int64_t>& offs,
+                   std::vector<Bucket>& buckets, std::vector<int>& bucket_of_param) {
+    const size_t n = sizes.size();
+    offs.assign(n, 0);
+    bucket_of_param.assign(n, 0);
+    buckets.clear();
+    int64_t off = 0;
+    Bucket cur;
+    for (size_t k = n; k-- > 0;) {
+        const int64_t span = (sizes[k] + 63) / 64 * 64;
+        offs[k] = off;
+        if (cur.total > 0 && cur.count + span > cap) {
+            buckets.push_back(cur);
+            cur = Bucket();
+            cur.offset = off;
+        }
+        cur.count += span;
+        cur.total += 1;
+        bucket_of_param[k] = static_cast<int>(buckets.size());
+        off += span;
+    }
+    if (cur.total > 0)
+        buckets.push_back(cur);
+    return off;
+}
+
 struct Trainer {
     GPTConfig cfg;
     std::unique_ptr<GPTModel> model;
@@ -58,8 +89,9 @@ struct Trainer {
 
     ~Trainer() {
         tt::set_grad_ready_hook(nullptr);
-        void* s = get_stream();
-        ttk_stream_synchronize(s);
+        void* s = stream_if_ready();
+        if (s)
+            ttk_stream_synchronize(s);
         if (comm)
             ttk_dist_destroy(comm);
         for (void* e : bucket_events)
@@ -77,18 +109,12 @@ struct Trainer {
 
     void setup() {
         params = model->parameters();
-        // Arena order: reverse of parameters(), which is the order in which
-        // backward completes them; the tied embedding (index 0) comes last.
-        std::vector<size_t> order;
-        for (size_t i = params.size(); i-- > 0;)
-            order.push_back(i);
-        param_offset.assign(params.size(), 0);
-        int64_t off = 0;
-        for (size_t i : order) {
-            param_offset[i] = off;
-            off += (params[i]->numel() + 63) / 64 * 64;  // 256-byte aligned slices
-        }
-        arena_n = off;
+        std::vector<int64_t> sizes;
+        for (Tensor* p : params)
+            sizes.push_back(p->numel());
+        std::vector<Bucket> unused;
+        std::vector<int> unused_ids;
+        arena_n = plan_arena(sizes, INT64_MAX, param_offset, unused, unused_ids);
         check(ttk_malloc(reinterpret_cast<void**>(&arena), static_cast<size_t>(arena_n) * 4,
                          stream()),
               "grad arena");
@@ -115,26 +141,14 @@ struct Trainer {
 
     void make_buckets(int64_t bucket_bytes) {
         const int64_t cap = std::max<int64_t>(bucket_bytes / 4, 1 << 16);
-        std::vector<size_t> order;
-        for (size_t i = params.size(); i-- > 0;)
-            order.push_back(i);
-        buckets.clear();
+        std::vector<int64_t> sizes;
+        for (Tensor* p : params)
+            sizes.push_back(p->numel());
+        std::vector<int> ids;
+        plan_arena(sizes, cap, param_offset, buckets, ids);
         bucket_of.clear();
-        Bucket cur;
-        cur.offset = 0;
-        for (size_t i : order) {
-            const int64_t span = (params[i]->numel() + 63) / 64 * 64;
-            if (cur.total > 0 && cur.count + span > cap) {
-                buckets.push_back(cur);
-                cur = Bucket();
-                cur.offset = param_offset[i];
-            }
-            cur.count += span;
-            cur.total += 1;
-            bucket_of[params[i]->impl().get()] = static_cast<int>(buckets.size());
-        }
-        if (cur.total > 0)
-            buckets.push_back(cur);
+        for (size_t i = 0; i < params.size(); ++i)
+            bucket_of[params[i]->impl().get()] = ids[i];
         for (void* e : bucket_events)
             ttk_event_destroy(e);
         bucket_events.assign(buckets.size(), nullptr);
@@ -367,6 +381,26 @@ int tt_trainer_forward_backward(void* h, const int64_t* idx, const int64_t* targ
             l.copy_to_host(loss);
         l.backward();
         tt::synchronize();
+    });
+}
+
+int tt_plan_buckets(const int64_t* sizes, int n, int64_t bucket_bytes, int64_t* offsets,
+                    int* bucket_of_param, int64_t* bucket_offset, int64_t* bucket_count,
+                    int* n_buckets) {
+    return guarded([&] {
+        std::vector<int64_t> sz(sizes, sizes + n), offs;
+        std::vector<Bucket> bk;
+        std::vector<int> ids;
+        plan_arena(sz, std::max<int64_t>(bucket_bytes / 4, 1), offs, bk, ids);
+        for (int i = 0; i < n; ++i) {
+            offsets[i] = offs[static_cast<size_t>(i)];
+            bucket_of_param[i] = ids[static_cast<size_t>(i)];
+        }
+        for (size_t b = 0; b < bk.size(); ++b) {
+            bucket_offset[b] = bk[b].offset;
+            bucket_count[b] = bk[b].count;
+        }
+        *n_buckets = static_cast<int>(bk.size());
     });
 }
 

@@ -55,6 +55,7 @@ _SIGS = {
     "tt_trainer_forward_backward": (C.c_int, [P, P, P, I64, I64, P, P]),
     "tt_trainer_dist_init": (C.c_int, [P, C.c_int, C.c_int, P, I64]),
     "tt_kernel_launches": (I64, []),
+    "tt_plan_buckets": (C.c_int, [P, C.c_int, I64, P, P, P, P, P]),
 }
 
 
@@ -165,6 +166,21 @@ class Trainer:
     def dist_init(self, rank, world, uid: bytes, bucket_bytes=64 << 20):
         buf = (C.c_ubyte * 128).from_buffer_copy(uid)
         _chk(lib().tt_trainer_dist_init(self.h, rank, world, buf, bucket_bytes), "dist_init")
+
+
+def plan_buckets(sizes, bucket_bytes):
+    """(offsets, bucket_of_param, [(bucket_offset, bucket_len)]) of the DP
+    gradient arena for parameters of these sizes (host-only computation)."""
+    n = len(sizes)
+    sz = np.ascontiguousarray(sizes, np.int64)
+    offs = np.zeros(n, np.int64)
+    ids = np.zeros(n, np.int32)
+    boff = np.zeros(max(n, 1), np.int64)
+    bcnt = np.zeros(max(n, 1), np.int64)
+    nb = C.c_int(0)
+    _chk(lib().tt_plan_buckets(sz.ctypes.data, n, bucket_bytes, offs.ctypes.data, ids.ctypes.data,
+                               boff.ctypes.data, bcnt.ctypes.data, C.byref(nb)), "plan_buckets")
+    return offs, ids, list(zip(boff[:nb.value].tolist(), bcnt[:nb.value].tolist()))
 
 
 def dist_unique_id() -> bytes:

@@ -185,8 +185,13 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="override the config's global batch (sequences), e.g. one "
+                         "micro-batch per step for an ncu launch list")
     args = ap.parse_args()
-    w = WORKLOADS[args.config]
+    w = dict(WORKLOADS[args.config])
+    if args.global_batch:
+        w["global_batch"] = args.global_batch
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

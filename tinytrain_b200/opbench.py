@@ -1,0 +1,168 @@
+"""Op-level benchmark of the device kernels (one JSON line per op).
+
+    python -m tinytrain_b200.opbench                 # the whole sweep
+    python -m tinytrain_b200.opbench --only gemm --shape 16384,2048,5632
+    python -m tinytrain_b200.opbench --only ce --rows 16384
+
+Workloads (fp32, seeded):
+  gemm       matmul forward (X W^T), dX (dY W) and dW (dY^T X) at
+             (M, K, N) in {(2048,256,256), (2048,256,32000), (8192,768,2048),
+             (16384,2048,5632)}, inputs U(-1, 1)
+  rmsnorm / swiglu / ce
+             forward + backward at rows = batch * seq of the 13M, 110M and 1B
+             configs (2048, 65536 per 64x1024 step in 16-row micro-batches of
+             16384, 16384), d / F of the config, vocab 32000 for CE
+  attention  fused causal attention with RoPE, forward + backward, B 8, H 12,
+             hd 64, S in {128, 512, 1024, 2048}, inputs N(0, 1)
+Each line: median of `--iters` timed launches (CUDA events, after warm-up),
+the algorithmic work (FLOPs, or bytes that must cross HBM), achieved rate and
+fraction of the measured peak (MEASURED_PEAKS.json: bf16 burst for tensor
+work, HBM copy bandwidth for memory-bound kernels). The 3xTF32 GEMM's
+fp32-accurate ceiling is the bf16 peak / 6.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+
+import numpy as np
+import torch
+
+from . import _ttk, kernels as K
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GEMM_SHAPES = [(2048, 256, 256), (2048, 256, 32000), (8192, 768, 2048), (16384, 2048, 5632)]
+ROWS = [(2048, 256, 768), (16384, 768, 2048), (16384, 2048, 5632)]  # (rows, d, F)
+ATTN_S = [128, 512, 1024, 2048]
+
+
+def peaks():
+    try:
+        d = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def timed(fn, iters, warmup=3):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        b.synchronize()
+        ts.append(a.elapsed_time(b))
+    return statistics.median(ts)
+
+
+def emit(rec):
+    print(json.dumps(rec), flush=True)
+
+
+def bench_gemm(shapes, iters):
+    hbm, bf16, src = peaks()
+    s = torch.cuda.current_stream().cuda_stream
+    for (M, Kd, N) in shapes:
+        g = torch.Generator(device="cuda").manual_seed(M + Kd + N)
+        X = torch.rand(M, Kd, device="cuda", generator=g) * 2 - 1
+        W = torch.rand(N, Kd, device="cuda", generator=g) * 2 - 1
+        dY = torch.rand(M, N, device="cuda", generator=g) * 2 - 1
+        for name, (tA, tB, A, B, m, n, k) in {
+                "fwd": (0, 1, X, W, M, N, Kd), "dX": (0, 0, dY, W, M, Kd, N),
+                "dW": (1, 0, dY, X, N, Kd, M)}.items():
+            C = torch.empty(m, n, device="cuda")
+            wsn = _ttk.call("ttk_gemm_workspace_size", tA, tB, 1, m, n, k)
+            ws = torch.empty(wsn, dtype=torch.uint8, device="cuda")
+
+            def run():
+                _ttk.call("ttk_gemm", tA, tB, 1, m, n, k, 1.0, A.data_ptr(), A.shape[1], 0,
+                          B.data_ptr(), B.shape[1], 0, 0.0, C.data_ptr(), n, 0, ws.data_ptr(),
+                          wsn, s)
+            ms = timed(run, iters)
+            tf = 2 * m * n * k / ms / 1e9
+            emit({"op": "gemm", "pass": name, "M": m, "N": n, "K": k, "ms": ms,
+                  "tflops_fp32_accurate": tf, "peak_bf16": bf16, "peak_src": src,
+                  "frac_of_3xtf32_ceiling": tf / (bf16 / 6), "frac_of_bf16_peak": tf / bf16,
+                  "includes": "operand split (hi/lo) + tcgen05 kernel"})
+
+
+def bench_rows(rows, iters):
+    hbm, _, src = peaks()
+    for (R, D, F) in rows:
+        x = torch.rand(R, D, device="cuda") * 2 - 1
+        w = torch.rand(D, device="cuda")
+        dy = torch.rand(R, D, device="cuda") * 2 - 1
+        y, rstd = K.rmsnorm_fwd(x, w, 1e-5)
+        ms = timed(lambda: K.rmsnorm_fwd(x, w, 1e-5), iters)
+        emit({"op": "rmsnorm", "pass": "fwd", "rows": R, "d": D, "ms": ms,
+              "gbs": 8 * R * D / ms / 1e6, "frac_hbm": 8 * R * D / ms / 1e6 / hbm,
+              "peak_src": src})
+        dx, dw = torch.empty_like(x), torch.zeros_like(w)
+        ms = timed(lambda: K.rmsnorm_bwd(x, w, rstd, dy, dx=dx, dw=dw), iters)
+        emit({"op": "rmsnorm", "pass": "bwd", "rows": R, "d": D, "ms": ms,
+              "gbs": 12 * R * D / ms / 1e6, "frac_hbm": 12 * R * D / ms / 1e6 / hbm})
+        a = torch.rand(R, F, device="cuda") * 8 - 4
+        b = torch.rand(R, F, device="cuda") * 2 - 1
+        g = torch.rand(R, F, device="cuda") * 2 - 1
+        ms = timed(lambda: K.swiglu_fwd(a, b), iters)
+        emit({"op": "swiglu", "pass": "fwd", "rows": R, "F": F, "ms": ms,
+              "gbs": 12 * R * F / ms / 1e6, "frac_hbm": 12 * R * F / ms / 1e6 / hbm})
+        da, db = torch.empty_like(a), torch.empty_like(b)
+        ms = timed(lambda: K.swiglu_bwd(a, b, g, da=da, db=db), iters)
+        emit({"op": "swiglu", "pass": "bwd", "rows": R, "F": F, "ms": ms,
+              "gbs": 20 * R * F / ms / 1e6, "frac_hbm": 20 * R * F / ms / 1e6 / hbm})
+        V = 32000
+        L = torch.randn(R, V, device="cuda") * 3
+        t = torch.randint(0, V, (R,), device="cuda", dtype=torch.int64)
+        dL = torch.empty_like(L)
+        ms = timed(lambda: K.cross_entropy(L, t, dlogits=dL), iters)
+        emit({"op": "cross_entropy", "pass": "fwd+bwd fused", "rows": R, "vocab": V, "ms": ms,
+              "gbs": 8 * R * V / ms / 1e6, "frac_hbm": 8 * R * V / ms / 1e6 / hbm})
+        del L, dL
+
+
+def bench_attention(seqs, iters, B=8, H=12, hd=64):
+    _, bf16, src = peaks()
+    for S in seqs:
+        q, k, v, do = (torch.randn(B, S, H, hd, device="cuda") for _ in range(4))
+        cs, sn = K.rope_tables(S, hd, 10000.0, "cuda")
+        o, lse = K.attention_fwd(q, k, v, cs, sn)
+        ms_f = timed(lambda: K.attention_fwd(q, k, v, cs, sn), iters)
+        ms_b = timed(lambda: K.attention_bwd(q, k, v, cs, sn, o, lse, do), iters)
+        fl_f = 2 * B * H * S * S * hd  # causal half of 4*B*H*S^2*hd
+        fl_b = 2 * fl_f
+        emit({"op": "attention", "B": B, "H": H, "hd": hd, "S": S, "ms_fwd": ms_f,
+              "ms_bwd": ms_b, "tflops_fwd": fl_f / ms_f / 1e9, "tflops_bwd": fl_b / ms_b / 1e9,
+              "tflops_fwd_bwd": (fl_f + fl_b) / (ms_f + ms_b) / 1e9,
+              "engine": "fp32 FMA (CUDA cores)"})
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", choices=["gemm", "rows", "ce", "attention"], default=None)
+    ap.add_argument("--shape", default=None, help="M,K,N for --only gemm")
+    ap.add_argument("--rows", type=int, default=None)
+    ap.add_argument("--seq", type=int, default=None)
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args()
+    torch.cuda.set_device(0)
+    _ttk.call("ttk_init", 0)
+    shapes = [tuple(int(x) for x in a.shape.split(","))] if a.shape else GEMM_SHAPES
+    rows = [r for r in ROWS if a.rows is None or r[0] == a.rows] or ROWS
+    if a.only in (None, "gemm"):
+        bench_gemm(shapes, a.iters)
+    if a.only in (None, "rows", "ce"):
+        bench_rows(rows, a.iters)
+    if a.only in (None, "attention"):
+        bench_attention([a.seq] if a.seq else ATTN_S, a.iters)
+    assert _ttk.device_status() == 0
+
+
+if __name__ == "__main__":
+    main()

@@ -215,8 +215,12 @@ def main():
     stream = torch.cuda.current_stream()
     trn.set_stream(stream.cuda_stream)
 
-    if w["global_batch"] % (w["micro"] * world):
-        raise SystemExit("global batch must split into micro-batches across ranks")
+    if w["global_batch"] % world:
+        raise SystemExit("global batch must split evenly across ranks")
+    # Micro-batch: the config's, or the rank's whole share when that is smaller.
+    w["micro"] = min(w["micro"], w["global_batch"] // world)
+    if (w["global_batch"] // world) % w["micro"]:
+        raise SystemExit("rank share must split into whole micro-batches")
     n_micro = w["global_batch"] // (w["micro"] * world)
     B, T = w["micro"], w["seq"]
     tokens_rank = n_micro * B * T

@@ -38,6 +38,9 @@ const char* ttk_version(void);
 /* Sets the calling thread's device and creates its stream-ordered memory pool. */
 int ttk_init(int device);
 int ttk_device_count(int* n);
+/* The calling thread's current device (the one another runtime in the
+ * process, e.g. torch.cuda.set_device, made current; 0 by default). */
+int ttk_current_device(int* device);
 /* Reads and clears the device status word (bit 0: a bounded wait expired,
  * bit 1: an out-of-range index was skipped). Synchronizes the device. */
 int ttk_device_status(unsigned* bits);

@@ -25,6 +25,7 @@ SIGS = {
     "ttk_version": (C.c_char_p, []),
     "ttk_init": (I32, [I32]),
     "ttk_device_count": (I32, [P]),
+    "ttk_current_device": (I32, [P]),
     "ttk_device_status": (I32, [P]),
     "ttk_synchronize": (I32, []),
     "ttk_launch_count": (I64, []),

@@ -79,6 +79,8 @@ int ttk_init(int device) {
 
 int ttk_device_count(int* n) { return check_cuda(cudaGetDeviceCount(n), "cudaGetDeviceCount"); }
 
+int ttk_current_device(int* device) { return check_cuda(cudaGetDevice(device), "cudaGetDevice"); }
+
 int ttk_device_status(unsigned* bits) {
     int rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
     if (rc)

@@ -39,7 +39,10 @@ void ensure_runtime() {
         if (ttk_device_count(&n) != TTK_OK || n < 1)
             throw std::runtime_error(
                 "tinytrain: no CUDA device (the device kernels are the only implementation)");
+        // The device the calling thread already has current (selected by the
+        // application, e.g. one GPU per rank), device 0 otherwise.
         int dev = 0;
+        check(ttk_current_device(&dev), "current device");
         check(ttk_init(dev), "ttk_init");
         if (!g_stream_set)
             check(ttk_stream_create(&g_stream), "stream create");

@@ -305,6 +305,9 @@ def main():
         hbm, bf16, bf16s, src = peaks()
         gemm_tf = gfl.value / (gms.value / 1e3) / 1e12 if gms.value > 0 else 0.0
         gemm_share = gms.value / (ms * args.steps) if ms > 0 else 0.0
+        prec = "tf32x3" if _ttk.call("ttk_gemm_get_precision") == 1 else "bf16x3"
+        # Useful FMAs cost 3 MMAs: bf16 ones at the bf16 rate, tf32 ones at half.
+        ceil_div = 6.0 if prec == "tf32x3" else 3.0
         line = {
             "metric": "train tokens/sec", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -312,13 +315,14 @@ def main():
             "data": "synthetic (N(0,0.02) weights, uniform tokens)",
             "config": workload_config(w, world),
             "roofline": {
-                "kernel": "gemm_tf32x3_kernel (tcgen05 3xTF32)", "bound": "tensor",
+                "kernel": f"gemm_split3_kernel (tcgen05, {prec} split)", "bound": "tensor",
                 "achieved": gemm_tf, "peak": bf16s, "unit": "TFLOP/s",
                 "frac": gemm_tf / bf16s, "traffic": None,
                 "peak_source": f"{src} bf16 sustained (kernel timed inside a long step)",
-                "achieved_is": "algorithmic fp32 FLOP/s (2MNK per GEMM); each costs 3 TF32 "
-                               "MMAs at half the bf16 rate, so the 3xTF32 ceiling is peak/6",
-                "ceiling_3xtf32": bf16s / 6, "frac_of_3xtf32_ceiling": gemm_tf / (bf16s / 6),
+                "achieved_is": "algorithmic fp32 FLOP/s (2MNK per GEMM); each useful FMA "
+                               f"costs 3 MMAs, so the {prec} ceiling is peak/{int(ceil_div)}",
+                "ceiling_split3": bf16s / ceil_div,
+                "frac_of_split3_ceiling": gemm_tf / (bf16s / ceil_div),
                 "launches": gl.value, "share_of_step": gemm_share},
             "mfu_fp32_equiv": value * flops_per_token(w) / 1e12 / world,
             "gpu_launches": launches,

@@ -73,14 +73,22 @@ int ttk_event_synchronize(void* event);
 
 /* ------------------------------------------------------------ dense algebra */
 
-/* C[b] = alpha * op(A[b]) @ op(B[b]) + beta * C[b], fp32-accurate (3xTF32 on
- * tcgen05). op(A) is A [M,K] (lda) when transA = 0, or A^T with A stored
+/* C[b] = alpha * op(A[b]) @ op(B[b]) + beta * C[b] on the tcgen05 tensor
+ * cores, fp32-accurate through a three-term operand split (see
+ * ttk_gemm_set_precision). op(A) is A [M,K] (lda) when transA = 0, or A^T with A stored
  * [K,M] when transA = 1; op(B) is B [K,N] (ldb) when transB = 0, or B^T with B
  * stored [N,K] when transB = 1. stride* are the batch strides (elements).
  * `workspace` (device, 16-byte aligned) holds the split operands and must be
  * at least ttk_gemm_workspace_size(...) bytes.
  * Replaces: sgemm + matmul fwd/bwd (ops.cpp:96-125, 661-697) and bmm
  * (ops.cpp:699-742). */
+/* Split used by ttk_gemm (process-wide): 0 = bf16x3 (default; hi/lo bf16
+ * halves, three kind::f16 MMAs, ~4e-6 normalized error), 1 = tf32x3 (hi/lo
+ * TF32, three kind::tf32 MMAs, twice the tensor time). The environment
+ * variable TTK_GEMM_PRECISION=tf32x3 selects 1 at start-up. Workspace sizes
+ * depend on the choice. */
+int ttk_gemm_set_precision(int prec);
+int ttk_gemm_get_precision(void);
 size_t ttk_gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
                                int64_t K);
 int ttk_gemm(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
@@ -112,8 +120,8 @@ int ttk_gemm_noalloc(int transA, int transB, int64_t batch, int64_t M, int64_t N
  * ttk_gemm_presplit: A with transA = 1, B with transB = 0). */
 int ttk_split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
                    int64_t batch, float* dst, int64_t ld_pad, void* stream);
-/* GEMM on operands already split by ttk_split_tf32 (e.g. weights split once
- * per optimizer step). a_split holds op(A)'s storage ([M,K] or [K,M]) with
+/* GEMM on operands already split by ttk_split_tf32 (TF32 planes, always the
+ * tf32x3 kernel; e.g. weights split once per optimizer step). a_split holds op(A)'s storage ([M,K] or [K,M]) with
  * padded leading dimension lda_pad, likewise b_split. */
 int ttk_gemm_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
                       float alpha, const float* a_split, int64_t lda_pad, const float* b_split,

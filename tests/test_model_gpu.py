@@ -27,6 +27,16 @@ def tiny():
     return dict(np.load(os.path.join(GOLDEN, "model_tiny.npz")))
 
 
+@pytest.fixture(params=[0, 1], ids=["bf16x3", "tf32x3"])
+def gemm_prec(request, cuda):
+    """Runs a test under each GEMM operand split; restores the default."""
+    from tinytrain_b200 import _ttk
+    old = _ttk.call("ttk_gemm_get_precision")
+    _ttk.call("ttk_gemm_set_precision", request.param)
+    yield request.param
+    _ttk.call("ttk_gemm_set_precision", old)
+
+
 def _cfg(arr):
     v, d, l, h, f, ms = (int(x) for x in arr)
     return dict(vocab=v, dim=d, layers=l, heads=h, ffn=f, max_seq=ms)
@@ -44,7 +54,7 @@ def test_init_matches_reference(cuda):
     tr.close()
 
 
-def test_forward_backward_tiny(cuda, tiny):
+def test_forward_backward_tiny(cuda, tiny, gemm_prec):
     from tinytrain_b200.trainer import Trainer
     cfg = _cfg(tiny["cfg"])
     tr = Trainer(cfg, seed=1, host_init=False)
@@ -62,7 +72,7 @@ def test_forward_backward_tiny(cuda, tiny):
     tr.close()
 
 
-def test_train_tiny_10_steps(cuda, tiny):
+def test_train_tiny_10_steps(cuda, tiny, gemm_prec):
     from tinytrain_b200.trainer import Trainer
     cfg = _cfg(tiny["cfg"])
     tr = Trainer(cfg, seed=1, host_init=False)
@@ -80,7 +90,11 @@ def test_train_tiny_10_steps(cuda, tiny):
     assert abs(norms[0] - tiny["norms"][0]) <= 1e-4 * tiny["norms"][0]
     np.testing.assert_allclose(losses, tiny["losses"], rtol=0, atol=1e-3)
     np.testing.assert_allclose(norms, tiny["norms"], rtol=1e-3)
-    assert rel_err(tr.get_params(), tiny["final"]) < 1e-3
+    # AdamW moves every weight by about lr * m/sqrt(v), which is near +-1
+    # whatever the gradient's size, so a rounding-level difference in a tiny
+    # gradient can flip a step: weights are compared loosely for the bf16x3
+    # split (lr 1e-2, 10 steps), tightly for tf32x3.
+    assert rel_err(tr.get_params(), tiny["final"]) < (1e-3 if gemm_prec == 1 else 1e-2)
     tr.close()
 
 
@@ -105,7 +119,7 @@ def test_micro_batch_accumulation_equals_full_batch(cuda, tiny):
     assert rel_err(outs[1][2], outs[0][2]) < 1e-5
 
 
-def test_train_cfg0_30_steps(cuda):
+def test_train_cfg0_30_steps(cuda, gemm_prec):
     import inputs
     from tinytrain_b200.trainer import Trainer
     path = os.path.join(GOLDEN, "train_cfg0.json")

@@ -47,6 +47,8 @@ SIGS = {
     "ttk_stream_wait_event": (I32, [P, P]),
     "ttk_event_elapsed_ms": (I32, [P, P, P]),
     "ttk_event_synchronize": (I32, [P]),
+    "ttk_gemm_set_precision": (I32, [I32]),
+    "ttk_gemm_get_precision": (I32, []),
     "ttk_gemm_workspace_size": (SZ, [I32, I32, I64, I64, I64, I64]),
     "ttk_gemm": (I32, [I32, I32, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, F32, P, I64,
                        I64, P, SZ, P]),

@@ -82,7 +82,7 @@ int ttk_gemm_noalloc(int transA, int transB, int64_t batch, int64_t M, int64_t N
     }
     // The split kernels overwrite every byte of the scratch the GEMM reads
     // (padding included), so nothing left by an earlier call needs clearing.
-    return ttk::gemm_tf32x3(transA, transB, batch, M, N, K, alpha, A, lda, strideA, B, ldb,
+    return ttk::gemm_run(transA, transB, batch, M, N, K, alpha, A, lda, strideA, B, ldb,
                             strideB, beta, C, ldc, strideC, ws, kNoAllocScratchBytes,
                             static_cast<cudaStream_t>(stream));
 }

@@ -7,18 +7,24 @@
 // (ops.cpp:699-742). op(X) = X or X^T is taken by reading the operand
 // K-major or MN-major straight from its storage; no transposed copies.
 //
-// Precision: 3xTF32. Each operand is split once by split_tf32_kernel into
-// hi = rna_tf32(x) and lo = x - hi (both exactly representable where it
-// matters), stored as two planes; the MMA accumulates hi*hi + hi*lo + lo*hi in
-// an fp32 TMEM accumulator, which gives fp32-level accuracy (the dropped lo*lo
-// term is ~2^-22 relative).
+// Precision: a three-term split. Each operand is split once (split kernels)
+// into a high part and the rounded remainder, stored as two planes; the MMA
+// accumulates lo*hi + hi*lo + hi*hi in an fp32 TMEM accumulator:
+//   PREC_BF16X3 (default): hi = bf16_rn(x), lo = bf16_rn(x - hi), three
+//     tcgen05.mma.kind::f16 (bf16) products: ~2^-17 per product, ~4e-6
+//     normalized max error over any K (emulated and measured), at half the
+//     tensor-core time of the TF32 split.
+//   PREC_TF32X3: hi = rna_tf32(x), lo = x - hi, three kind::tf32 products:
+//     ~2^-21 per product.
+// Both smem layouts have 64-byte rows per k-slice (BK = 16 fp32 or 32 bf16),
+// so the pipeline geometry is shared.
 //
 // Kernel structure (persistent, one CTA per SM, 64 + 32*EPI_WARPS threads):
 //   warp 0      TMA producer: 4-stage ring of {A hi|lo, B hi|lo} K-slices
-//               (BK = 16 fp32 = 64 B rows), one TMA per operand per stage (hi
-//               and lo planes are one extra tensor dimension)
+//               (64 B rows), one TMA per operand per stage (hi and lo planes
+//               are one extra tensor dimension)
 //   warp 1      TMEM allocator + MMA issuer (one lane): 2 k-steps x 3 products
-//               of tcgen05.mma.kind::tf32 M128 x BN x K8 per stage; commit
+//               of tcgen05.mma M128 x BN x (K8 tf32 | K16 bf16) per stage; commit
 //               frees the stage. Each 256-wide K chunk accumulates into its own
 //               TMEM buffer (a ring of 512/BN buffers of BN columns)
 //   warps 2..   epilogue: drain each chunk buffer with tcgen05.ld into fp32
@@ -27,7 +33,10 @@
 //               MMAs of the next chunk / tile run while a chunk is drained
 // Loads never use .multicast::cluster.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <cstdlib>
+#include <string>
 #include <stdint.h>
 
 #include <vector>
@@ -40,19 +49,34 @@ namespace ttk {
 namespace gemm {
 
 constexpr int BM = 128;
-constexpr int BK = 16;  // fp32 elements per k-slice: 64 bytes = one SW64 row
+constexpr int ROW_BYTES = 64;  // one k-slice row of an operand tile (SW64)
 constexpr int STAGES = 4;
 constexpr int GROUP_M = 16;  // tile raster: bands of 16 M-tiles sweep N
 // K extent accumulated inside TMEM before the partial sum is promoted to the
 // epilogue's fp32 registers. The tensor-core accumulator rounds with a bias
 // (its error grows linearly with K), so long sums are built from 256-wide
 // chunks added with round-to-nearest FADD; error then grows like sqrt(K/256).
-constexpr int KCHUNK_BLOCKS = 16;
+constexpr int KCHUNK = 256;
+
+enum { PREC_BF16X3 = 0, PREC_TF32X3 = 1 };
+
+template <int PREC>
+struct Prec {
+    static constexpr int ELT = PREC == PREC_TF32X3 ? 4 : 2;  // bytes per split element
+    static constexpr int BK = ROW_BYTES / ELT;                // k per stage: 16 | 32
+    static constexpr int UK = PREC == PREC_TF32X3 ? 8 : 16;   // k per MMA instruction
+    static constexpr int KCHUNK_BLOCKS = KCHUNK / BK;
+    // MN-major smem layout: tf32 admits only 128B swizzle with 32B atoms
+    // (32 elements = 128 B per row); bf16 uses plain 64B swizzle (32
+    // elements = 64 B per row). Both: 32-element chunks of the M/N extent.
+    static constexpr uint32_t MN_LAYOUT = PREC == PREC_TF32X3 ? 1 : 4;
+    static constexpr int MN_ROW_BYTES = 32 * ELT;
+};
 
 template <int BN>
 struct Cfg {
-    static constexpr int A_PLANE = BM * BK * 4;
-    static constexpr int B_PLANE = BN * BK * 4;
+    static constexpr int A_PLANE = BM * ROW_BYTES;
+    static constexpr int B_PLANE = BN * ROW_BYTES;
     static constexpr int A_BYTES = 2 * A_PLANE;  // hi | lo
     static constexpr int B_BYTES = 2 * B_PLANE;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -86,26 +110,39 @@ __device__ __forceinline__ void tile_coords(const Params& p, int64_t t, int& b, 
     n = static_cast<int>(rr / gsize);
 }
 
-// Descriptor of one K=8 sub-slice (ks = 0, 1) of an operand tile plane.
-// K-major, 64B swizzle: rows of 64 B (16 fp32 of K), 8-row groups 512 B
-// apart (SBO); the k sub-slice is a 32 B offset inside the swizzled row.
-// MN-major (tf32 admits only the 128B-swizzle-with-32B-atoms layout):
-// 32-element (128 B) chunks of the M/N extent, BK k-rows of 128 B each, so
-// chunks are BK*128 B apart (LBO) and 4-row swizzle groups 512 B apart (SBO);
-// the k sub-slice (8 rows) is a 1024 B step.
+// Descriptor of one MMA k-step (ks = 0, 1) of an operand tile plane.
+// K-major, 64B swizzle: rows of 64 B, 8-row groups 512 B apart (SBO); one
+// k-step (8 tf32 | 16 bf16 = 32 B) is a 32 B offset inside the swizzled row.
+// MN-major: 32-element chunks of the M/N extent, BK k-rows each, so chunks are
+// BK*MN_ROW_BYTES = 2048 B apart (LBO); 8-row (bf16) / 4-row (tf32) swizzle
+// groups 512 B apart (SBO); one k-step is 1024 B further (8 rows of 128 B for
+// tf32, 16 rows of 64 B for bf16).
 constexpr uint32_t kLayoutSW64 = 4;
-constexpr uint32_t kLayoutSW128Base32B = 1;
+template <int PREC>
 __device__ __forceinline__ uint64_t operand_desc(uint32_t plane_addr, int mn_major, int ks) {
+    using P = Prec<PREC>;
     if (mn_major)
-        return umma_smem_desc(plane_addr + ks * 1024, BK * 128, 512, kLayoutSW128Base32B);
+        return umma_smem_desc(plane_addr + ks * 1024, P::BK * P::MN_ROW_BYTES, 512, P::MN_LAYOUT);
     return umma_smem_desc(plane_addr + ks * 32, 16, 512, kLayoutSW64);
 }
 
-template <int BN>
+template <int PREC>
+__device__ __forceinline__ void mma_split(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                          uint32_t acc) {
+    if (PREC == PREC_TF32X3)
+        mma_tf32(d, a, b, idesc, acc);
+    else
+        mma_bf16(d, a, b, idesc, acc);
+}
+
+template <int BN, int PREC>
 __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
-    gemm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_a,
+    gemm_split3_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b, const Params p) {
     using CF = Cfg<BN>;
+    using PR = Prec<PREC>;
+    constexpr int BK = PR::BK;
+    constexpr int KCHUNK_BLOCKS = PR::KCHUNK_BLOCKS;
     constexpr int NBUF = CF::NBUF;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -195,7 +232,8 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
     } else if (warp == 1) {
         // -------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc_tf32(BM, BN, p.a_mn, p.b_mn);
+            const uint32_t idesc = PREC == PREC_TF32X3 ? umma_idesc_tf32(BM, BN, p.a_mn, p.b_mn)
+                                                       : umma_idesc_bf16(BM, BN, p.a_mn, p.b_mn);
             int s = 0;
             uint32_t ph = 0;
             int64_t g = 0;  // chunk counter across this CTA's tiles
@@ -220,15 +258,15 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
                         const uint32_t sa = smem_u32(smem + s * CF::STAGE_BYTES);
                         const uint32_t sb = sa + CF::A_BYTES;
 #pragma unroll
-                        for (int ks = 0; ks < BK / 8; ++ks) {
-                            const uint64_t a_hi = operand_desc(sa, p.a_mn, ks);
-                            const uint64_t a_lo = operand_desc(sa + CF::A_PLANE, p.a_mn, ks);
-                            const uint64_t b_hi = operand_desc(sb, p.b_mn, ks);
-                            const uint64_t b_lo = operand_desc(sb + CF::B_PLANE, p.b_mn, ks);
+                        for (int ks = 0; ks < BK / PR::UK; ++ks) {
+                            const uint64_t a_hi = operand_desc<PREC>(sa, p.a_mn, ks);
+                            const uint64_t a_lo = operand_desc<PREC>(sa + CF::A_PLANE, p.a_mn, ks);
+                            const uint64_t b_hi = operand_desc<PREC>(sb, p.b_mn, ks);
+                            const uint64_t b_lo = operand_desc<PREC>(sb + CF::B_PLANE, p.b_mn, ks);
                             const uint32_t acc = (kb > kc || ks > 0) ? 1u : 0u;
-                            mma_tf32(d_tmem, a_lo, b_hi, idesc, acc);
-                            mma_tf32(d_tmem, a_hi, b_lo, idesc, 1u);
-                            mma_tf32(d_tmem, a_hi, b_hi, idesc, 1u);
+                            mma_split<PREC>(d_tmem, a_lo, b_hi, idesc, acc);
+                            mma_split<PREC>(d_tmem, a_hi, b_lo, idesc, 1u);
+                            mma_split<PREC>(d_tmem, a_hi, b_hi, idesc, 1u);
                         }
                         mma_commit(&empty[s]);
                         if (++s == STAGES) {
@@ -328,12 +366,27 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
     }
 }
 
-// hi = rna_tf32(x), lo = x - hi, written as planes dst[b][0|1][r][0..ld_pad)
-// with zeros in the padding columns [cols, ld_pad).
-__global__ void split_tf32_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
-                                  int64_t ld, int64_t bstride, int64_t batch,
-                                  float* __restrict__ dst, int64_t ld_pad) {
-    const int64_t per_row = ld_pad / 4;  // float4 groups per padded row
+// Split of src (rows x cols per batch, leading dim ld) into planes
+// dst[b][0|1][r][0..ld_pad) = hi | lo, zeros in the padding [cols, ld_pad):
+//   float dst: hi = rna_tf32(x), lo = x - hi (exact in fp32)
+//   bf16 dst:  hi = bf16_rn(x), lo = bf16_rn(x - hi)
+__device__ __forceinline__ void split_one(float x, float& hi, float& lo) {
+    uint32_t h;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+    hi = __uint_as_float(h);
+    lo = x - hi;
+}
+
+__device__ __forceinline__ void split_one(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+    hi = __float2bfloat16_rn(x);
+    lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+}
+
+template <class T>
+__global__ void split_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
+                             int64_t ld, int64_t bstride, int64_t batch, T* __restrict__ dst,
+                             int64_t ld_pad) {
+    const int64_t per_row = ld_pad / 4;  // 4-element groups per padded row
     const int64_t total = batch * rows * per_row;
     const int64_t plane = rows * ld_pad;
     const bool vec = ((ld & 3) == 0) && ((bstride & 3) == 0) &&
@@ -354,17 +407,18 @@ __global__ void split_tf32_kernel(const float* __restrict__ src, int64_t rows, i
             for (int j = 0; j < 4; ++j)
                 x[j] = (c0 + j < cols) ? __ldg(s + j) : 0.0f;
         }
-        float hi[4], lo[4];
+        T hi[4], lo[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            uint32_t h;
-            asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x[j]));
-            hi[j] = __uint_as_float(h);
-            lo[j] = x[j] - hi[j];
+        for (int j = 0; j < 4; ++j)
+            split_one(x[j], hi[j], lo[j]);
+        T* d = dst + b * 2 * plane + r * ld_pad + c0;
+        if (sizeof(T) == 4) {
+            *reinterpret_cast<float4*>(d) = *reinterpret_cast<const float4*>(hi);
+            *reinterpret_cast<float4*>(d + plane) = *reinterpret_cast<const float4*>(lo);
+        } else {
+            *reinterpret_cast<uint2*>(d) = *reinterpret_cast<const uint2*>(hi);
+            *reinterpret_cast<uint2*>(d + plane) = *reinterpret_cast<const uint2*>(lo);
         }
-        float* d = dst + b * 2 * plane + r * ld_pad + c0;
-        *reinterpret_cast<float4*>(d) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<float4*>(d + plane) = make_float4(lo[0], lo[1], lo[2], lo[3]);
     }
 }
 
@@ -406,42 +460,51 @@ EncodeTiledFn encode_fn() {
 inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 // Storage geometry of one split operand: rows x cols per batch, padded to
-// ld_pad (multiple of 16 floats), planes hi|lo.
+// ld_pad elements, planes hi|lo of elt-byte elements.
 struct SplitGeom {
     int64_t rows, cols, ld_pad;
+    int elt;
     size_t bytes(int64_t batch) const {
-        return static_cast<size_t>(batch) * 2 * rows * ld_pad * sizeof(float);
+        return static_cast<size_t>(batch) * 2 * rows * ld_pad * elt;
     }
 };
 
 // K-major map: dims {cols(K), rows(M|N), plane, batch}, box {BK, tile, 2, 1},
-//               64B swizzle.
+//               64B swizzle (64-byte rows).
 // MN-major map: dims {32, rows(K), cols/32 chunks, plane, batch},
-//               box {32, BK, tile/32, 2, 1}, 128B swizzle with 32B atoms.
-int make_operand_map(CUtensorMap* map, const float* base, const SplitGeom& g, int64_t batch,
+//               box {32, BK, tile/32, 2, 1}: tf32 128B swizzle with 32B atoms
+//               (128-byte rows), bf16 64B swizzle (64-byte rows).
+template <int PREC>
+int make_operand_map(CUtensorMap* map, const void* base, const SplitGeom& g, int64_t batch,
                      int mn_major, int tile) {
+    using PR = gemm::Prec<PREC>;
     EncodeTiledFn enc = encode_fn();
     if (!enc)
         return set_error(TTK_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-    const cuuint64_t plane = static_cast<cuuint64_t>(g.rows * g.ld_pad * 4);
+    const CUtensorMapDataType dt = PREC == gemm::PREC_TF32X3 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                              : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const cuuint64_t plane = static_cast<cuuint64_t>(g.rows * g.ld_pad * PR::ELT);
     CUresult r;
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     if (!mn_major) {
         cuuint64_t dims[4] = {static_cast<cuuint64_t>(g.cols), static_cast<cuuint64_t>(g.rows), 2,
                               static_cast<cuuint64_t>(batch)};
-        cuuint64_t strides[3] = {static_cast<cuuint64_t>(g.ld_pad * 4), plane, 2 * plane};
-        cuuint32_t box[4] = {gemm::BK, static_cast<cuuint32_t>(tile), 2, 1};
-        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float*>(base), dims, strides,
-                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+        cuuint64_t strides[3] = {static_cast<cuuint64_t>(g.ld_pad * PR::ELT), plane, 2 * plane};
+        cuuint32_t box[4] = {PR::BK, static_cast<cuuint32_t>(tile), 2, 1};
+        r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else {
         cuuint64_t dims[5] = {32, static_cast<cuuint64_t>(g.rows),
                               static_cast<cuuint64_t>(g.ld_pad / 32), 2,
                               static_cast<cuuint64_t>(batch)};
-        cuuint64_t strides[4] = {static_cast<cuuint64_t>(g.ld_pad * 4), 128, plane, 2 * plane};
-        cuuint32_t box[5] = {32, gemm::BK, static_cast<cuuint32_t>(tile / 32), 2, 1};
-        r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(base), dims, strides,
-                box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B,
+        cuuint64_t strides[4] = {static_cast<cuuint64_t>(g.ld_pad * PR::ELT),
+                                 static_cast<cuuint64_t>(32 * PR::ELT), plane, 2 * plane};
+        cuuint32_t box[5] = {32, PR::BK, static_cast<cuuint32_t>(tile / 32), 2, 1};
+        r = enc(map, dt, 5, const_cast<void*>(base), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE,
+                PREC == gemm::PREC_TF32X3 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                          : CU_TENSOR_MAP_SWIZZLE_64B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     }
     if (r != CUDA_SUCCESS)
@@ -487,7 +550,7 @@ Profiler& prof() {
     return p;
 }
 
-template <int BN>
+template <int BN, int PREC>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, gemm::Params p,
                 cudaStream_t stream) {
     using CF = gemm::Cfg<BN>;
@@ -497,7 +560,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, gemm::Params p,
     if (dev < 0 || dev >= 64)
         return set_error(TTK_ERR_ARG, "gemm: device ordinal out of range");
     if (!attr_set[dev]) {
-        if (cudaFuncSetAttribute(gemm::gemm_tf32x3_kernel<BN>,
+        if (cudaFuncSetAttribute(gemm::gemm_split3_kernel<BN, PREC>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  CF::SMEM_BYTES) != cudaSuccess)
             return set_error(TTK_ERR_CUDA, "cudaFuncSetAttribute(gemm) failed");
@@ -514,8 +577,8 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, gemm::Params p,
         rec.flops = 2.0 * static_cast<double>(p.M) * p.N * p.K * p.batch;
         cudaEventRecord(rec.a, stream);
     }
-    gemm::gemm_tf32x3_kernel<BN><<<grid, CF::NUM_THREADS, CF::SMEM_BYTES, stream>>>(ma, mb, p);
-    const int rc = check_launch("gemm_tf32x3_kernel");
+    gemm::gemm_split3_kernel<BN, PREC><<<grid, CF::NUM_THREADS, CF::SMEM_BYTES, stream>>>(ma, mb, p);
+    const int rc = check_launch("gemm_split3_kernel");
     if (pr.on) {
         cudaEventRecord(rec.b, stream);
         pr.recs.push_back(rec);
@@ -528,13 +591,14 @@ struct GemmPlan {
     size_t off_b, total;
 };
 
-GemmPlan plan(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K) {
+GemmPlan plan(int prec, int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K) {
     GemmPlan pl;
+    const int elt = prec == gemm::PREC_TF32X3 ? 4 : 2;
     // op(A) = A [M,K] (K-major) or A^T with A stored [K,M] (MN-major).
-    // K-major rows are padded to 16 floats, MN-major rows to 32 (whole chunks).
-    pl.ga = transA ? SplitGeom{K, M, round_up(M, 32)} : SplitGeom{M, K, round_up(K, 16)};
+    // K-major rows are padded to 16 elements, MN-major rows to 32 (whole chunks).
+    pl.ga = transA ? SplitGeom{K, M, round_up(M, 32), elt} : SplitGeom{M, K, round_up(K, 16), elt};
     // op(B) = B [K,N] (MN-major) or B^T with B stored [N,K] (K-major).
-    pl.gb = transB ? SplitGeom{N, K, round_up(K, 16)} : SplitGeom{K, N, round_up(N, 32)};
+    pl.gb = transB ? SplitGeom{N, K, round_up(K, 16), elt} : SplitGeom{K, N, round_up(N, 32), elt};
     pl.off_b = static_cast<size_t>(round_up(static_cast<int64_t>(pl.ga.bytes(batch)), 256));
     pl.total = pl.off_b + pl.gb.bytes(batch);
     return pl;
@@ -570,29 +634,107 @@ int gemm_profile_read(double* ms, double* flops, int64_t* launches) {
     return TTK_OK;
 }
 
-size_t gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
-                           int64_t K) {
-    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0)
-        return 0;
-    return plan(transA, transB, batch, M, N, K).total;
+namespace {
+
+// Process-wide precision of ttk_gemm (TTK_GEMM_PRECISION=tf32x3 selects the
+// TF32 split; default bf16x3).
+int g_prec = -1;
+
+int current_prec() {
+    if (g_prec < 0) {
+        const char* e = std::getenv("TTK_GEMM_PRECISION");
+        g_prec = (e && (std::string(e) == "tf32x3" || std::string(e) == "1"))
+                     ? gemm::PREC_TF32X3
+                     : gemm::PREC_BF16X3;
+    }
+    return g_prec;
 }
 
-int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
-               int64_t batch, float* dst, int64_t ld_pad, cudaStream_t stream) {
+template <int PREC>
+int launch_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+                 int64_t batch, void* dst, int64_t ld_pad, cudaStream_t stream) {
     const int64_t total = batch * rows * (ld_pad / 4);
     if (total == 0)
         return TTK_OK;
     const int threads = 256;
     const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
-    gemm::split_tf32_kernel<<<static_cast<int>(blocks), threads, 0, stream>>>(
-        src, rows, cols, ld, bstride, batch, dst, ld_pad);
-    return check_launch("split_tf32_kernel");
+    if (PREC == gemm::PREC_TF32X3)
+        gemm::split_kernel<float><<<static_cast<int>(blocks), threads, 0, stream>>>(
+            src, rows, cols, ld, bstride, batch, static_cast<float*>(dst), ld_pad);
+    else
+        gemm::split_kernel<__nv_bfloat16><<<static_cast<int>(blocks), threads, 0, stream>>>(
+            src, rows, cols, ld, bstride, batch, static_cast<__nv_bfloat16*>(dst), ld_pad);
+    return check_launch("split_kernel");
 }
 
-int gemm_tf32x3(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
-                float alpha, const float* A, int64_t lda, int64_t strideA, const float* B,
-                int64_t ldb, int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC,
-                void* ws, size_t ws_bytes, cudaStream_t stream) {
+template <int PREC>
+int run_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                 float alpha, const void* a_split, int64_t lda_pad, const void* b_split,
+                 int64_t ldb_pad, float beta, float* C, int64_t ldc, int64_t strideC,
+                 cudaStream_t stream) {
+    using PR = gemm::Prec<PREC>;
+    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0)
+        return set_error(TTK_ERR_ARG, "gemm_presplit: sizes must be positive");
+    // K-major planes: leading dimension a multiple of 16; MN-major: of 32.
+    if ((reinterpret_cast<uintptr_t>(a_split) & 15) || (reinterpret_cast<uintptr_t>(b_split) & 15) ||
+        (lda_pad & (transA ? 31 : 15)) || (ldb_pad & (transB ? 15 : 31)))
+        return set_error(TTK_ERR_ARG, "gemm_presplit: split planes misaligned or badly padded");
+    SplitGeom ga = transA ? SplitGeom{K, M, lda_pad, PR::ELT} : SplitGeom{M, K, lda_pad, PR::ELT};
+    SplitGeom gb = transB ? SplitGeom{N, K, ldb_pad, PR::ELT} : SplitGeom{K, N, ldb_pad, PR::ELT};
+    if (ga.ld_pad < ga.cols || gb.ld_pad < gb.cols)
+        return set_error(TTK_ERR_ARG, "gemm_presplit: padded leading dimension too small");
+    gemm::Params p{};
+    p.M = M, p.N = N, p.K = K, p.batch = batch;
+    p.a_mn = transA ? 1 : 0;
+    p.b_mn = transB ? 0 : 1;
+    p.alpha = alpha, p.beta = beta;
+    p.C = C, p.ldc = ldc, p.strideC = strideC;
+    p.num_m = static_cast<int>((M + gemm::BM - 1) / gemm::BM);
+    p.num_k = static_cast<int>((K + PR::BK - 1) / PR::BK);
+    // BN = 256 unless the N extent is small or 256-wide tiles would leave most
+    // SMs idle.
+    const int64_t tiles256 = p.num_m * ((N + 255) / 256) * batch;
+    const bool use128 = N <= 128 || tiles256 < num_sms();
+    const int bn = use128 ? 128 : 256;
+    CUtensorMap ma, mb;
+    int rc = make_operand_map<PREC>(&ma, a_split, ga, batch, p.a_mn, gemm::BM);
+    if (rc)
+        return rc;
+    rc = make_operand_map<PREC>(&mb, b_split, gb, batch, p.b_mn, bn);
+    if (rc)
+        return rc;
+    return use128 ? launch_gemm<128, PREC>(ma, mb, p, stream)
+                  : launch_gemm<256, PREC>(ma, mb, p, stream);
+}
+
+}  // namespace
+
+int gemm_set_precision(int prec) {
+    if (prec != gemm::PREC_BF16X3 && prec != gemm::PREC_TF32X3)
+        return set_error(TTK_ERR_ARG, "gemm precision must be 0 (bf16x3) or 1 (tf32x3)");
+    g_prec = prec;
+    return TTK_OK;
+}
+
+int gemm_get_precision() { return current_prec(); }
+
+size_t gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
+                           int64_t K) {
+    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0)
+        return 0;
+    return plan(current_prec(), transA, transB, batch, M, N, K).total;
+}
+
+int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+               int64_t batch, float* dst, int64_t ld_pad, cudaStream_t stream) {
+    return launch_split<gemm::PREC_TF32X3>(src, rows, cols, ld, bstride, batch, dst, ld_pad,
+                                           stream);
+}
+
+int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+             const float* A, int64_t lda, int64_t strideA, const float* B, int64_t ldb,
+             int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC, void* ws,
+             size_t ws_bytes, cudaStream_t stream) {
     if (M < 0 || N < 0 || K < 0 || batch < 0)
         return set_error(TTK_ERR_ARG, "gemm: negative size");
     if (M == 0 || N == 0 || batch == 0)
@@ -612,58 +754,45 @@ int gemm_tf32x3(int transA, int transB, int64_t batch, int64_t M, int64_t N, int
     }
     if (M > (1ll << 31) / 2 || N > (1ll << 31) / 2 || K > (1ll << 31) / 2)
         return set_error(TTK_ERR_ARG, "gemm: dimension too large");
-    const GemmPlan pl = plan(transA, transB, batch, M, N, K);
+    const int prec = current_prec();
+    const GemmPlan pl = plan(prec, transA, transB, batch, M, N, K);
     if (!ws || ws_bytes < pl.total)
         return set_error(TTK_ERR_ARG, "gemm: workspace too small");
     if ((transA ? lda < M : lda < K) || (transB ? ldb < K : ldb < N))
         return set_error(TTK_ERR_ARG, "gemm: leading dimension too small");
-    float* wa = static_cast<float*>(ws);
-    float* wb = reinterpret_cast<float*>(static_cast<char*>(ws) + pl.off_b);
-    int rc = split_tf32(A, pl.ga.rows, pl.ga.cols, lda, strideA, batch, wa, pl.ga.ld_pad, stream);
+    void* wa = ws;
+    void* wb = static_cast<char*>(ws) + pl.off_b;
+    if (prec == gemm::PREC_TF32X3) {
+        int rc = launch_split<gemm::PREC_TF32X3>(A, pl.ga.rows, pl.ga.cols, lda, strideA, batch,
+                                                 wa, pl.ga.ld_pad, stream);
+        if (!rc)
+            rc = launch_split<gemm::PREC_TF32X3>(B, pl.gb.rows, pl.gb.cols, ldb, strideB, batch,
+                                                 wb, pl.gb.ld_pad, stream);
+        if (rc)
+            return rc;
+        return run_presplit<gemm::PREC_TF32X3>(transA, transB, batch, M, N, K, alpha, wa,
+                                               pl.ga.ld_pad, wb, pl.gb.ld_pad, beta, C, ldc,
+                                               strideC, stream);
+    }
+    int rc = launch_split<gemm::PREC_BF16X3>(A, pl.ga.rows, pl.ga.cols, lda, strideA, batch, wa,
+                                             pl.ga.ld_pad, stream);
+    if (!rc)
+        rc = launch_split<gemm::PREC_BF16X3>(B, pl.gb.rows, pl.gb.cols, ldb, strideB, batch, wb,
+                                             pl.gb.ld_pad, stream);
     if (rc)
         return rc;
-    rc = split_tf32(B, pl.gb.rows, pl.gb.cols, ldb, strideB, batch, wb, pl.gb.ld_pad, stream);
-    if (rc)
-        return rc;
-    return gemm_tf32x3_presplit(transA, transB, batch, M, N, K, alpha, wa, pl.ga.ld_pad, wb,
-                                pl.gb.ld_pad, beta, C, ldc, strideC, stream);
+    return run_presplit<gemm::PREC_BF16X3>(transA, transB, batch, M, N, K, alpha, wa,
+                                           pl.ga.ld_pad, wb, pl.gb.ld_pad, beta, C, ldc, strideC,
+                                           stream);
 }
 
 int gemm_tf32x3_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
                          float alpha, const float* a_split, int64_t lda_pad,
                          const float* b_split, int64_t ldb_pad, float beta, float* C,
                          int64_t ldc, int64_t strideC, cudaStream_t stream) {
-    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0)
-        return set_error(TTK_ERR_ARG, "gemm_presplit: sizes must be positive");
-    // K-major planes: leading dimension a multiple of 16; MN-major: of 32.
-    if ((reinterpret_cast<uintptr_t>(a_split) & 15) || (reinterpret_cast<uintptr_t>(b_split) & 15) ||
-        (lda_pad & (transA ? 31 : 15)) || (ldb_pad & (transB ? 15 : 31)))
-        return set_error(TTK_ERR_ARG, "gemm_presplit: split planes misaligned or badly padded");
-    SplitGeom ga = transA ? SplitGeom{K, M, lda_pad} : SplitGeom{M, K, lda_pad};
-    SplitGeom gb = transB ? SplitGeom{N, K, ldb_pad} : SplitGeom{K, N, ldb_pad};
-    if (ga.ld_pad < ga.cols || gb.ld_pad < gb.cols)
-        return set_error(TTK_ERR_ARG, "gemm_presplit: padded leading dimension too small");
-    gemm::Params p{};
-    p.M = M, p.N = N, p.K = K, p.batch = batch;
-    p.a_mn = transA ? 1 : 0;
-    p.b_mn = transB ? 0 : 1;
-    p.alpha = alpha, p.beta = beta;
-    p.C = C, p.ldc = ldc, p.strideC = strideC;
-    p.num_m = static_cast<int>((M + gemm::BM - 1) / gemm::BM);
-    p.num_k = static_cast<int>((K + gemm::BK - 1) / gemm::BK);
-    // BN = 256 unless the N extent is small or 256-wide tiles would leave most
-    // SMs idle.
-    const int64_t tiles256 = p.num_m * ((N + 255) / 256) * batch;
-    const bool use128 = N <= 128 || tiles256 < num_sms();
-    const int bn = use128 ? 128 : 256;
-    CUtensorMap ma, mb;
-    int rc = make_operand_map(&ma, a_split, ga, batch, p.a_mn, gemm::BM);
-    if (rc)
-        return rc;
-    rc = make_operand_map(&mb, b_split, gb, batch, p.b_mn, bn);
-    if (rc)
-        return rc;
-    return use128 ? launch_gemm<128>(ma, mb, p, stream) : launch_gemm<256>(ma, mb, p, stream);
+    return run_presplit<gemm::PREC_TF32X3>(transA, transB, batch, M, N, K, alpha, a_split,
+                                           lda_pad, b_split, ldb_pad, beta, C, ldc, strideC,
+                                           stream);
 }
 
 }  // namespace ttk

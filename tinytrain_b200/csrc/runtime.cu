@@ -214,6 +214,10 @@ int ttk_event_synchronize(void* event) {
 
 // ------------------------------------------------------------------ GEMM --
 
+int ttk_gemm_set_precision(int prec) { return gemm_set_precision(prec); }
+
+int ttk_gemm_get_precision(void) { return gemm_get_precision(); }
+
 int ttk_profile_enable(int on) { return gemm_profile_enable(on); }
 
 int ttk_profile_read(double* gemm_ms, double* gemm_flops, int64_t* launches) {
@@ -229,7 +233,7 @@ int ttk_gemm(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_
              const float* A, int64_t lda, int64_t strideA, const float* B, int64_t ldb,
              int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC,
              void* workspace, size_t workspace_bytes, void* stream) {
-    return gemm_tf32x3(transA, transB, batch, M, N, K, alpha, A, lda, strideA, B, ldb, strideB,
+    return gemm_run(transA, transB, batch, M, N, K, alpha, A, lda, strideA, B, ldb, strideB,
                        beta, C, ldc, strideC, workspace, workspace_bytes, S(stream));
 }
 

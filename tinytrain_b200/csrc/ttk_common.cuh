@@ -162,6 +162,17 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
         : "memory");
 }
 
+// D[tmem] (+)= A x B^T, kind::f16 with bf16 operands, one CTA.
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive on an mbarrier once every tcgen05 op issued so far by this thread
 // has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
@@ -216,6 +227,17 @@ __host__ __device__ constexpr uint32_t umma_idesc_tf32(int M, int N, int a_mn, i
            | (2u << 10)                           // B format: TF32
            | (static_cast<uint32_t>(a_mn) << 15)  // A major
            | (static_cast<uint32_t>(b_mn) << 16)  // B major
+           | (static_cast<uint32_t>(N >> 3) << 17)
+           | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Instruction descriptor, kind::f16 with bf16 A/B and an fp32 accumulator.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int a_mn, int b_mn) {
+    return (1u << 4)                              // D format: F32
+           | (1u << 7)                            // A format: BF16
+           | (1u << 10)                           // B format: BF16
+           | (static_cast<uint32_t>(a_mn) << 15)
+           | (static_cast<uint32_t>(b_mn) << 16)
            | (static_cast<uint32_t>(N >> 3) << 17)
            | (static_cast<uint32_t>(M >> 4) << 24);
 }

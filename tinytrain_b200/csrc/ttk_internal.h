@@ -25,17 +25,19 @@ inline int grid_for(int64_t n, int threads, int max_blocks = 148 * 16) {
     return static_cast<int>(std::min<int64_t>(b, max_blocks));
 }
 
-// GEMM entry points (gemm_tf32x3.cu), shared with the C ABI wrappers.
+// GEMM entry points (gemm_split3.cu), shared with the C ABI wrappers.
 int gemm_profile_enable(int on);
 int gemm_profile_read(double* ms, double* flops, int64_t* launches);
 size_t gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
                            int64_t K);
 int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
                int64_t batch, float* dst, int64_t ld_pad, cudaStream_t stream);
-int gemm_tf32x3(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
-                float alpha, const float* A, int64_t lda, int64_t strideA, const float* B,
-                int64_t ldb, int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC,
-                void* ws, size_t ws_bytes, cudaStream_t stream);
+int gemm_set_precision(int prec);
+int gemm_get_precision();
+int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
+             const float* A, int64_t lda, int64_t strideA, const float* B, int64_t ldb,
+             int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC, void* ws,
+             size_t ws_bytes, cudaStream_t stream);
 int gemm_tf32x3_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
                          float alpha, const float* a_split, int64_t lda_pad,
                          const float* b_split, int64_t ldb_pad, float beta, float* C,

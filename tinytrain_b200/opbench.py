@@ -86,9 +86,11 @@ def bench_gemm(shapes, iters):
                           wsn, s)
             ms = timed(run, iters)
             tf = 2 * m * n * k / ms / 1e9
-            emit({"op": "gemm", "pass": name, "M": m, "N": n, "K": k, "ms": ms,
+            prec = "tf32x3" if _ttk.call("ttk_gemm_get_precision") == 1 else "bf16x3"
+            div = 6 if prec == "tf32x3" else 3
+            emit({"op": "gemm", "pass": name, "M": m, "N": n, "K": k, "ms": ms, "split": prec,
                   "tflops_fp32_accurate": tf, "peak_bf16": bf16, "peak_src": src,
-                  "frac_of_3xtf32_ceiling": tf / (bf16 / 6), "frac_of_bf16_peak": tf / bf16,
+                  "frac_of_split3_ceiling": tf / (bf16 / div), "frac_of_bf16_peak": tf / bf16,
                   "includes": "operand split (hi/lo) + tcgen05 kernel"})
 
 

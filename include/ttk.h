@@ -171,10 +171,14 @@ int ttk_loss_finalize(const double* loss_acc, float scale, float* loss_out, void
  * softmax(q k^T * scale + causal mask) v). q, k, v, o are [B,T,H,hd] (the
  * layout the projections produce; o is ready for the output projection);
  * cos/sin [T, hd/2] are the model's RoPE tables (model.cpp:43-53); lse
- * [B,H,T] is saved for the backward. hd in {32, 64, 128}. */
+ * [B,H,T] is saved for the backward. hd in {32, 64, 128}. `workspace` must
+ * hold ttk_attention_fwd_workspace_size(B,T,H,hd) bytes (the split
+ * operands). */
+size_t ttk_attention_fwd_workspace_size(int64_t B, int64_t T, int64_t H, int64_t hd);
 int ttk_attention_fwd(const float* q, const float* k, const float* v, const float* cos_t,
                       const float* sin_t, float* o, float* lse, int64_t B, int64_t T, int64_t H,
-                      int64_t hd, float scale, void* stream);
+                      int64_t hd, float scale, void* workspace, size_t workspace_bytes,
+                      void* stream);
 /* dq, dk, dv (+)= gradients w.r.t. the pre-RoPE q, k and v. `workspace` must
  * hold ttk_attention_bwd_workspace_size(B,T,H,hd) bytes. */
 size_t ttk_attention_bwd_workspace_size(int64_t B, int64_t T, int64_t H, int64_t hd);
@@ -183,6 +187,12 @@ int ttk_attention_bwd(const float* q, const float* k, const float* v, const floa
                       float* dq, float* dk, float* dv, int accumulate, int64_t B, int64_t T,
                       int64_t H, int64_t hd, float scale, void* workspace,
                       size_t workspace_bytes, void* stream);
+/* Attention engine (process-wide): 0 = tensor cores (mma.sync m16n8k16 with
+ * the bf16x3 operand split; default), 1 = fp32 FMA kernels. The environment
+ * variable TTK_ATTENTION=fma selects 1 at start-up. Workspace sizes depend on
+ * the choice. */
+int ttk_attention_set_impl(int impl);
+int ttk_attention_get_impl(void);
 
 /* out[i,:] = W[idx[i],:] (ops.cpp:746-759); idx validated against V. */
 int ttk_embedding_fwd(const float* W, const int64_t* idx, float* out, int64_t N, int64_t D,

@@ -162,8 +162,18 @@ def test_softmax_golden(cuda, golden_ops):
     assert rel_err(n(dx), g["sm_dX"]) < TOL
 
 
+@pytest.fixture(params=[0, 1], ids=["tensorcore", "fma"])
+def attn_impl(request, cuda):
+    """Runs a test under each attention engine; restores the default."""
+    from tinytrain_b200 import _ttk
+    old = _ttk.call("ttk_attention_get_impl")
+    _ttk.call("ttk_attention_set_impl", request.param)
+    yield request.param
+    _ttk.call("ttk_attention_set_impl", old)
+
+
 @pytest.mark.parametrize("tag", ["a", "b", "c"])
-def test_attention_golden(cuda, golden_ops, tag):
+def test_attention_golden(cuda, golden_ops, tag, attn_impl):
     from tinytrain_b200 import kernels as K
     g = golden_ops
     q, k, v, go = (t(g[f"att_{tag}_{s}"], cuda) for s in ("q", "k", "v", "G"))
@@ -180,8 +190,9 @@ def test_attention_golden(cuda, golden_ops, tag):
     assert status_ok()
 
 
-@pytest.mark.parametrize("B,T,H,hd", [(2, 128, 8, 32), (1, 200, 2, 64), (1, 512, 2, 128)])
-def test_attention_sizes(cuda, B, T, H, hd):
+@pytest.mark.parametrize("B,T,H,hd", [(2, 128, 8, 32), (1, 200, 2, 64), (1, 512, 2, 128),
+                                     (1, 70, 3, 32), (1, 333, 1, 128)])
+def test_attention_sizes(cuda, B, T, H, hd, attn_impl):
     from oracle import restate as rs
     from tinytrain_b200 import kernels as K
     rng = np.random.default_rng(B * T * H + hd)

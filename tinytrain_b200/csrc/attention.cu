@@ -22,6 +22,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+#include <string>
+
 #include "ttk_common.cuh"
 #include "ttk_internal.h"
 
@@ -518,11 +521,41 @@ static int attn_check(const void* q, const void* k, const void* v, const void* c
     return TTK_OK;
 }
 
+namespace {
+// 0: tensor cores (mma.sync, bf16x3 split; default), 1: fp32 FMA kernels.
+// TTK_ATTENTION=fma selects 1 at start-up.
+int g_attn_impl = -1;
+int attn_impl() {
+    if (g_attn_impl < 0) {
+        const char* e = std::getenv("TTK_ATTENTION");
+        g_attn_impl = (e && std::string(e) == "fma") ? 1 : 0;
+    }
+    return g_attn_impl;
+}
+inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+}  // namespace
+
 extern "C" {
+
+int ttk_attention_set_impl(int impl) {
+    if (impl != 0 && impl != 1)
+        return set_error(TTK_ERR_ARG, "attention impl must be 0 (tensor cores) or 1 (fp32 FMA)");
+    g_attn_impl = impl;
+    return TTK_OK;
+}
+
+int ttk_attention_get_impl(void) { return attn_impl(); }
+
+size_t ttk_attention_fwd_workspace_size(int64_t B, int64_t T, int64_t H, int64_t hd) {
+    if (attn_impl() == 1)
+        return 0;
+    return static_cast<size_t>(B * T * H * hd) * 6 * 2;  // q, k, v as bf16 hi|lo
+}
 
 int ttk_attention_fwd(const float* q, const float* k, const float* v, const float* cos_t,
                       const float* sin_t, float* o, float* lse, int64_t B, int64_t T, int64_t H,
-                      int64_t hd, float scale, void* stream) {
+                      int64_t hd, float scale, void* workspace, size_t workspace_bytes,
+                      void* stream) {
     int rc = attn_check(q, k, v, cos_t, sin_t, B, T, H, hd);
     if (rc)
         return rc;
@@ -530,6 +563,12 @@ int ttk_attention_fwd(const float* q, const float* k, const float* v, const floa
         return TTK_OK;
     if (!o || !lse)
         return set_error(TTK_ERR_ARG, "attention_fwd: null output");
+    if (attn_impl() == 0) {
+        if (!workspace || workspace_bytes < ttk_attention_fwd_workspace_size(B, T, H, hd))
+            return set_error(TTK_ERR_ARG, "attention_fwd: workspace too small");
+        return attention_mma_forward(static_cast<int>(hd), q, k, v, cos_t, sin_t, o, lse, B, T,
+                                     H, scale, workspace, S(stream));
+    }
     switch (hd) {
         case 32: return launch_fwd<32>(q, k, v, cos_t, sin_t, o, lse, B, T, H, scale, S(stream));
         case 64: return launch_fwd<64>(q, k, v, cos_t, sin_t, o, lse, B, T, H, scale, S(stream));
@@ -538,8 +577,10 @@ int ttk_attention_fwd(const float* q, const float* k, const float* v, const floa
 }
 
 size_t ttk_attention_bwd_workspace_size(int64_t B, int64_t T, int64_t H, int64_t hd) {
-    (void)hd;
-    return static_cast<size_t>(B * T * H) * sizeof(float);
+    const size_t dv = align256(static_cast<size_t>(B * T * H) * sizeof(float));
+    if (attn_impl() == 1)
+        return dv;
+    return dv + static_cast<size_t>(B * T * H * hd) * 8 * 2;  // q, k, v, dO as bf16 hi|lo
 }
 
 int ttk_attention_bwd(const float* q, const float* k, const float* v, const float* cos_t,
@@ -556,6 +597,10 @@ int ttk_attention_bwd(const float* q, const float* k, const float* v, const floa
         return set_error(TTK_ERR_ARG, "attention_bwd: null pointer");
     if (!workspace || workspace_bytes < ttk_attention_bwd_workspace_size(B, T, H, hd))
         return set_error(TTK_ERR_ARG, "attention_bwd: workspace too small");
+    if (attn_impl() == 0)
+        return attention_mma_backward(static_cast<int>(hd), q, k, v, cos_t, sin_t, o, lse, dout,
+                                      dq, dk, dv, accumulate, B, T, H, scale, workspace,
+                                      S(stream));
     float* Dv = static_cast<float*>(workspace);
     switch (hd) {
         case 32:

@@ -43,4 +43,15 @@ int gemm_tf32x3_presplit(int transA, int transB, int64_t batch, int64_t M, int64
                          const float* b_split, int64_t ldb_pad, float beta, float* C,
                          int64_t ldc, int64_t strideC, cudaStream_t stream);
 
+// Tensor-core attention (attention_mma.cu); ws sized by the C ABI's
+// workspace functions.
+int attention_mma_forward(int hd, const float* q, const float* k, const float* v,
+                          const float* cs, const float* sn, float* o, float* lse, int64_t B,
+                          int64_t T, int64_t H, float scale, void* ws, cudaStream_t st);
+int attention_mma_backward(int hd, const float* q, const float* k, const float* v,
+                           const float* cs, const float* sn, const float* o, const float* lse,
+                           const float* dout, float* dq, float* dk, float* dv, int accumulate,
+                           int64_t B, int64_t T, int64_t H, float scale, void* ws,
+                           cudaStream_t st);
+
 }  // namespace ttk

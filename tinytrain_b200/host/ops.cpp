@@ -839,10 +839,15 @@ Tensor causal_attention(const Tensor& q, const Tensor& k, const Tensor& v, const
     const bool rg = q.requires_grad() || k.requires_grad() || v.requires_grad();
     Tensor out = make_out({B, T, H * hd}, rg);
     auto lse = std::make_shared<Buffer>(B * H * T);
-    check(ttk_attention_fwd(dread(q.impl()), dread(k.impl()), dread(v.impl()), dread(cos.impl()),
-                            dread(sin.impl()), out_ptr(out), lse->device_for_overwrite(), B, T, H,
-                            hd, scale, stream()),
-          "attention");
+    {
+        const size_t ws = ttk_attention_fwd_workspace_size(B, T, H, hd);
+        Scratch w(ws);
+        check(ttk_attention_fwd(dread(q.impl()), dread(k.impl()), dread(v.impl()),
+                                dread(cos.impl()), dread(sin.impl()), out_ptr(out),
+                                lse->device_for_overwrite(), B, T, H, hd, scale, w.ptr, ws,
+                                stream()),
+              "attention");
+    }
     if (rg) {
         auto qo = q.impl(), ko = k.impl(), vo = v.impl(), co = cos.impl(), so = sin.impl();
         Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle

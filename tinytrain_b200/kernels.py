@@ -169,8 +169,9 @@ def attention_fwd(q, k, v, cos, sin, scale=None):
     scale = float(hd) ** -0.5 if scale is None else scale
     o = torch.empty_like(q)
     lse = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
+    ws = workspace(call("ttk_attention_fwd_workspace_size", B, T, H, hd), q.device)
     call("ttk_attention_fwd", _p(q), _p(k), _p(v), _p(cos), _p(sin), _p(o), _p(lse), B, T, H, hd,
-         scale, _s())
+         scale, _p(ws), ws.numel(), _s())
     return o, lse
 
 

@@ -130,6 +130,8 @@ def bench_rows(rows, iters):
 
 
 def bench_attention(seqs, iters, B=8, H=12, hd=64):
+    """Forward + backward; fwd FLOPs 2*B*H*S^2*hd (causal half of 4*B*H*S^2*hd),
+    backward counted as 2x forward (dQ, dK, dV; recomputation not credited)."""
     _, bf16, src = peaks()
     for S in seqs:
         q, k, v, do = (torch.randn(B, S, H, hd, device="cuda") for _ in range(4))
@@ -139,10 +141,11 @@ def bench_attention(seqs, iters, B=8, H=12, hd=64):
         ms_b = timed(lambda: K.attention_bwd(q, k, v, cs, sn, o, lse, do), iters)
         fl_f = 2 * B * H * S * S * hd  # causal half of 4*B*H*S^2*hd
         fl_b = 2 * fl_f
+        eng = ("fp32 FMA (CUDA cores)" if _ttk.call("ttk_attention_get_impl") == 1 else
+               "mma.sync m16n8k16 bf16x3 split")
         emit({"op": "attention", "B": B, "H": H, "hd": hd, "S": S, "ms_fwd": ms_f,
               "ms_bwd": ms_b, "tflops_fwd": fl_f / ms_f / 1e9, "tflops_bwd": fl_b / ms_b / 1e9,
-              "tflops_fwd_bwd": (fl_f + fl_b) / (ms_f + ms_b) / 1e9,
-              "engine": "fp32 FMA (CUDA cores)"})
+              "tflops_fwd_bwd": (fl_f + fl_b) / (ms_f + ms_b) / 1e9, "engine": eng})
 
 
 def main():
@@ -152,6 +155,7 @@ def main():
     ap.add_argument("--rows", type=int, default=None)
     ap.add_argument("--seq", type=int, default=None)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--hd", type=int, default=64)
     a = ap.parse_args()
     torch.cuda.set_device(0)
     _ttk.call("ttk_init", 0)
@@ -162,7 +166,8 @@ def main():
     if a.only in (None, "rows", "ce"):
         bench_rows(rows, a.iters)
     if a.only in (None, "attention"):
-        bench_attention([a.seq] if a.seq else ATTN_S, a.iters)
+        bench_attention([a.seq] if a.seq else ATTN_S, a.iters,
+                        H=12 if a.hd == 64 else 2048 // a.hd, hd=a.hd)
     assert _ttk.device_status() == 0
 
 

@@ -30,22 +30,66 @@ namespace fa {
 
 // ------------------------------------------------------------ primitives --
 
+// Not volatile: a pure register-to-register op, free for the compiler to
+// schedule between independent accumulators.
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// Three-term product into c: lo*hi + hi*lo + hi*hi.
-__device__ __forceinline__ void mma3(float (&c)[4], const uint32_t (&ah)[4],
-                                     const uint32_t (&al)[4], uint32_t bh0, uint32_t bh1,
-                                     uint32_t bl0, uint32_t bl1) {
-    mma16816(c, al, bh0, bh1);
-    mma16816(c, ah, bl0, bl1);
-    mma16816(c, ah, bh0, bh1);
+// Three-term products c[j0 + 2p + {0,1}] += A * B_p for NP pairs of n8 tiles
+// (B_p as loaded by frag_b_rows / frag_b_cols: [0],[1] the first tile, [2],[3]
+// the second), in pass-major order: every lo*hi term, then every hi*lo, then
+// every hi*hi. Each accumulator still sums its terms smallest first, and
+// consecutive MMAs go to different accumulators, so the tensor pipe is not
+// held up by the latency of a dependent MMA.
+template <int NP, int N>
+__device__ __forceinline__ void mma3_pairs(float (&c)[N][4], int j0, const uint32_t (&ah)[4],
+                                           const uint32_t (&al)[4], const uint32_t (&bh)[NP][4],
+                                           const uint32_t (&bl)[NP][4]) {
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+        mma16816(c[j0 + 2 * p], al, bh[p][0], bh[p][1]);
+        mma16816(c[j0 + 2 * p + 1], al, bh[p][2], bh[p][3]);
+    }
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+        mma16816(c[j0 + 2 * p], ah, bl[p][0], bl[p][1]);
+        mma16816(c[j0 + 2 * p + 1], ah, bl[p][2], bl[p][3]);
+    }
+#pragma unroll
+    for (int p = 0; p < NP; ++p) {
+        mma16816(c[j0 + 2 * p], ah, bh[p][0], bh[p][1]);
+        mma16816(c[j0 + 2 * p + 1], ah, bh[p][2], bh[p][3]);
+    }
+}
+
+// Two mma3_pairs groups (different A, B and accumulators) interleaved pass by
+// pass: 4*NP independent accumulators per pass.
+template <int NP, int N1, int N2>
+__device__ __forceinline__ void mma3_dual(float (&c1)[N1][4], int j1, const uint32_t (&a1h)[4],
+                                          const uint32_t (&a1l)[4], const uint32_t (&b1h)[NP][4],
+                                          const uint32_t (&b1l)[NP][4], float (&c2)[N2][4], int j2,
+                                          const uint32_t (&a2h)[4], const uint32_t (&a2l)[4],
+                                          const uint32_t (&b2h)[NP][4],
+                                          const uint32_t (&b2l)[NP][4]) {
+#pragma unroll
+    for (int pass = 0; pass < 3; ++pass) {
+#pragma unroll
+        for (int p = 0; p < NP; ++p) {
+            const uint32_t(&x1)[4] = pass == 0 ? a1l : a1h;
+            const uint32_t(&x2)[4] = pass == 0 ? a2l : a2h;
+            const uint32_t(&y1)[4] = pass == 1 ? b1l[p] : b1h[p];
+            const uint32_t(&y2)[4] = pass == 1 ? b2l[p] : b2h[p];
+            mma16816(c1[j1 + 2 * p], x1, y1[0], y1[1]);
+            mma16816(c1[j1 + 2 * p + 1], x1, y1[2], y1[3]);
+            mma16816(c2[j2 + 2 * p], x2, y2[0], y2[1]);
+            mma16816(c2[j2 + 2 * p + 1], x2, y2[2], y2[3]);
+        }
+    }
 }
 
 __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
@@ -246,14 +290,13 @@ __global__ void __launch_bounds__(FWD_THREADS) attn_fwd_mma(
                 uint32_t ah[4], al[4];
                 frag_a<HD>(ah, sQh, warp * 16, kk);
                 frag_a<HD>(al, sQl, warp * 16, kk);
+                uint32_t bh[4][4], bl[4][4];  // all 64 keys: 8 n8 tiles
 #pragma unroll
-                for (int nt = 0; nt < 8; nt += 2) {
-                    uint32_t bh4[4], bl4[4];
-                    frag_b_rows<HD>(bh4, sKh, nt * 8, kk);
-                    frag_b_rows<HD>(bl4, sKl, nt * 8, kk);
-                    mma3(s[nt], ah, al, bh4[0], bh4[1], bl4[0], bl4[1]);
-                    mma3(s[nt + 1], ah, al, bh4[2], bh4[3], bl4[2], bl4[3]);
+                for (int p = 0; p < 4; ++p) {
+                    frag_b_rows<HD>(bh[p], sKh, p * 16, kk);
+                    frag_b_rows<HD>(bl[p], sKl, p * 16, kk);
                 }
+                mma3_pairs<4>(s, 0, ah, al, bh, bl);
             }
             // mask (causal / past T) and online softmax; q was pre-scaled
             float mx0 = -INFINITY, mx1 = -INFINITY;
@@ -307,13 +350,16 @@ __global__ void __launch_bounds__(FWD_THREADS) attn_fwd_mma(
                 split2(s[2 * c][2], s[2 * c][3], ph[1], pl[1]);
                 split2(s[2 * c + 1][0], s[2 * c + 1][1], ph[2], pl[2]);
                 split2(s[2 * c + 1][2], s[2 * c + 1][3], ph[3], pl[3]);
+                constexpr int NP = NO >= 8 ? 4 : NO / 2;  // tile pairs per batch
 #pragma unroll
-                for (int j = 0; j < NO; j += 2) {
-                    uint32_t bh4[4], bl4[4];
-                    frag_b_cols<HD>(bh4, sVh, c * 16, j * 8);
-                    frag_b_cols<HD>(bl4, sVl, c * 16, j * 8);
-                    mma3(acc[j], ph, pl, bh4[0], bh4[1], bl4[0], bl4[1]);
-                    mma3(acc[j + 1], ph, pl, bh4[2], bh4[3], bl4[2], bl4[3]);
+                for (int j = 0; j < NO; j += 2 * NP) {
+                    uint32_t bh[NP][4], bl[NP][4];
+#pragma unroll
+                    for (int p = 0; p < NP; ++p) {
+                        frag_b_cols<HD>(bh[p], sVh, c * 16, (j + 2 * p) * 8);
+                        frag_b_cols<HD>(bl[p], sVl, c * 16, (j + 2 * p) * 8);
+                    }
+                    mma3_pairs<NP>(acc, j, ph, pl, bh, bl);
                 }
             }
         }
@@ -512,15 +558,12 @@ __global__ void __launch_bounds__(BWD_THREADS) attn_bwd_mma_dkv(
                 frag_a<HD>(avl, sVl, warp * 16, kk);
 #pragma unroll
                 for (int nt = 0; nt < NQ; nt += 2) {
-                    uint32_t bq[4], bql[4], bd[4], bdl[4];
-                    frag_b_rows<HD>(bq, sQh, nt * 8, kk);
-                    frag_b_rows<HD>(bql, sQl, nt * 8, kk);
-                    frag_b_rows<HD>(bd, sDh, nt * 8, kk);
-                    frag_b_rows<HD>(bdl, sDl, nt * 8, kk);
-                    mma3(sT[nt], akh, akl, bq[0], bq[1], bql[0], bql[1]);
-                    mma3(sT[nt + 1], akh, akl, bq[2], bq[3], bql[2], bql[3]);
-                    mma3(pT[nt], avh, avl, bd[0], bd[1], bdl[0], bdl[1]);
-                    mma3(pT[nt + 1], avh, avl, bd[2], bd[3], bdl[2], bdl[3]);
+                    uint32_t bq[1][4], bql[1][4], bd[1][4], bdl[1][4];
+                    frag_b_rows<HD>(bq[0], sQh, nt * 8, kk);
+                    frag_b_rows<HD>(bql[0], sQl, nt * 8, kk);
+                    frag_b_rows<HD>(bd[0], sDh, nt * 8, kk);
+                    frag_b_rows<HD>(bdl[0], sDl, nt * 8, kk);
+                    mma3_dual<1>(sT, nt, akh, akl, bq, bql, pT, nt, avh, avl, bd, bdl);
                 }
             }
             // P^T = exp(S^T - lse[q]) on live (key <= q < T) entries; dS^T =
@@ -552,15 +595,12 @@ __global__ void __launch_bounds__(BWD_THREADS) attn_bwd_mma_dkv(
                 split2(pT[2 * c + 1][2], pT[2 * c + 1][3], sh[3], sl[3]);
 #pragma unroll
                 for (int j = 0; j < NO; j += 2) {
-                    uint32_t bd[4], bdl[4], bq[4], bql[4];
-                    frag_b_cols<HD>(bd, sDh, c * 16, j * 8);
-                    frag_b_cols<HD>(bdl, sDl, c * 16, j * 8);
-                    frag_b_cols<HD>(bq, sQh, c * 16, j * 8);
-                    frag_b_cols<HD>(bql, sQl, c * 16, j * 8);
-                    mma3(dV[j], ph, pl, bd[0], bd[1], bdl[0], bdl[1]);
-                    mma3(dV[j + 1], ph, pl, bd[2], bd[3], bdl[2], bdl[3]);
-                    mma3(dK[j], sh, sl, bq[0], bq[1], bql[0], bql[1]);
-                    mma3(dK[j + 1], sh, sl, bq[2], bq[3], bql[2], bql[3]);
+                    uint32_t bd[1][4], bdl[1][4], bq[1][4], bql[1][4];
+                    frag_b_cols<HD>(bd[0], sDh, c * 16, j * 8);
+                    frag_b_cols<HD>(bdl[0], sDl, c * 16, j * 8);
+                    frag_b_cols<HD>(bq[0], sQh, c * 16, j * 8);
+                    frag_b_cols<HD>(bql[0], sQl, c * 16, j * 8);
+                    mma3_dual<1>(dV, j, ph, pl, bd, bdl, dK, j, sh, sl, bq, bql);
                 }
             }
         }
@@ -655,18 +695,16 @@ __global__ void __launch_bounds__(BWD_THREADS) attn_bwd_mma_dq(
                 frag_a<HD>(aql, sQl, warp * 16, kk);
                 frag_a<HD>(ad, sDh, warp * 16, kk);
                 frag_a<HD>(adl, sDl, warp * 16, kk);
+                constexpr int NP = NK / 2;  // all key tiles of the block at once
+                uint32_t bk[NP][4], bkl[NP][4], bv[NP][4], bvl[NP][4];
 #pragma unroll
-                for (int nt = 0; nt < NK; nt += 2) {
-                    uint32_t bk[4], bkl[4], bv[4], bvl[4];
-                    frag_b_rows<HD>(bk, sKh, nt * 8, kk);
-                    frag_b_rows<HD>(bkl, sKl, nt * 8, kk);
-                    frag_b_rows<HD>(bv, sVh, nt * 8, kk);
-                    frag_b_rows<HD>(bvl, sVl, nt * 8, kk);
-                    mma3(s[nt], aq, aql, bk[0], bk[1], bkl[0], bkl[1]);
-                    mma3(s[nt + 1], aq, aql, bk[2], bk[3], bkl[2], bkl[3]);
-                    mma3(dp[nt], ad, adl, bv[0], bv[1], bvl[0], bvl[1]);
-                    mma3(dp[nt + 1], ad, adl, bv[2], bv[3], bvl[2], bvl[3]);
+                for (int p = 0; p < NP; ++p) {
+                    frag_b_rows<HD>(bk[p], sKh, p * 16, kk);
+                    frag_b_rows<HD>(bkl[p], sKl, p * 16, kk);
+                    frag_b_rows<HD>(bv[p], sVh, p * 16, kk);
+                    frag_b_rows<HD>(bvl[p], sVl, p * 16, kk);
                 }
+                mma3_dual<NP>(s, 0, aq, aql, bk, bkl, dp, 0, ad, adl, bv, bvl);
             }
 #pragma unroll
             for (int nt = 0; nt < NK; ++nt) {
@@ -686,13 +724,16 @@ __global__ void __launch_bounds__(BWD_THREADS) attn_bwd_mma_dq(
                 split2(s[2 * c][2], s[2 * c][3], sh[1], sl[1]);
                 split2(s[2 * c + 1][0], s[2 * c + 1][1], sh[2], sl[2]);
                 split2(s[2 * c + 1][2], s[2 * c + 1][3], sh[3], sl[3]);
+                constexpr int NP = NO >= 8 ? 4 : NO / 2;
 #pragma unroll
-                for (int j = 0; j < NO; j += 2) {
-                    uint32_t bk[4], bkl[4];
-                    frag_b_cols<HD>(bk, sKh, c * 16, j * 8);
-                    frag_b_cols<HD>(bkl, sKl, c * 16, j * 8);
-                    mma3(dQ[j], sh, sl, bk[0], bk[1], bkl[0], bkl[1]);
-                    mma3(dQ[j + 1], sh, sl, bk[2], bk[3], bkl[2], bkl[3]);
+                for (int j = 0; j < NO; j += 2 * NP) {
+                    uint32_t bk[NP][4], bkl[NP][4];
+#pragma unroll
+                    for (int p = 0; p < NP; ++p) {
+                        frag_b_cols<HD>(bk[p], sKh, c * 16, (j + 2 * p) * 8);
+                        frag_b_cols<HD>(bkl[p], sKl, c * 16, (j + 2 * p) * 8);
+                    }
+                    mma3_pairs<NP>(dQ, j, sh, sl, bk, bkl);
                 }
             }
         }

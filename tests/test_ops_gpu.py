@@ -162,7 +162,7 @@ def test_softmax_golden(cuda, golden_ops):
     assert rel_err(n(dx), g["sm_dX"]) < TOL
 
 
-@pytest.fixture(params=[0, 1], ids=["tensorcore", "fma"])
+@pytest.fixture(params=[0, 1, 2], ids=["tensorcore", "fma", "mma"])
 def attn_impl(request, cuda):
     """Runs a test under each attention engine; restores the default."""
     from tinytrain_b200 import _ttk

@@ -522,13 +522,14 @@ static int attn_check(const void* q, const void* k, const void* v, const void* c
 }
 
 namespace {
-// 0: tensor cores (mma.sync, bf16x3 split; default), 1: fp32 FMA kernels.
-// TTK_ATTENTION=fma selects 1 at start-up.
+// 0: tensor cores, tcgen05 forward where the head dim allows (64, 128) and
+//    mma.sync otherwise (default); 1: fp32 FMA kernels; 2: mma.sync only.
+// TTK_ATTENTION=fma | mma selects 1 | 2 at start-up.
 int g_attn_impl = -1;
 int attn_impl() {
     if (g_attn_impl < 0) {
         const char* e = std::getenv("TTK_ATTENTION");
-        g_attn_impl = (e && std::string(e) == "fma") ? 1 : 0;
+        g_attn_impl = (e && std::string(e) == "fma") ? 1 : (e && std::string(e) == "mma") ? 2 : 0;
     }
     return g_attn_impl;
 }
@@ -538,8 +539,9 @@ inline size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 extern "C" {
 
 int ttk_attention_set_impl(int impl) {
-    if (impl != 0 && impl != 1)
-        return set_error(TTK_ERR_ARG, "attention impl must be 0 (tensor cores) or 1 (fp32 FMA)");
+    if (impl < 0 || impl > 2)
+        return set_error(TTK_ERR_ARG,
+                         "attention impl must be 0 (tensor cores), 1 (fp32 FMA) or 2 (mma.sync)");
     g_attn_impl = impl;
     return TTK_OK;
 }
@@ -563,11 +565,12 @@ int ttk_attention_fwd(const float* q, const float* k, const float* v, const floa
         return TTK_OK;
     if (!o || !lse)
         return set_error(TTK_ERR_ARG, "attention_fwd: null output");
-    if (attn_impl() == 0) {
+    if (attn_impl() != 1) {
         if (!workspace || workspace_bytes < ttk_attention_fwd_workspace_size(B, T, H, hd))
             return set_error(TTK_ERR_ARG, "attention_fwd: workspace too small");
+        const bool tc = attn_impl() == 0 && attention_tc_supported(static_cast<int>(hd));
         return attention_mma_forward(static_cast<int>(hd), q, k, v, cos_t, sin_t, o, lse, B, T,
-                                     H, scale, workspace, S(stream));
+                                     H, scale, workspace, tc, S(stream));
     }
     switch (hd) {
         case 32: return launch_fwd<32>(q, k, v, cos_t, sin_t, o, lse, B, T, H, scale, S(stream));
@@ -597,7 +600,7 @@ int ttk_attention_bwd(const float* q, const float* k, const float* v, const floa
         return set_error(TTK_ERR_ARG, "attention_bwd: null pointer");
     if (!workspace || workspace_bytes < ttk_attention_bwd_workspace_size(B, T, H, hd))
         return set_error(TTK_ERR_ARG, "attention_bwd: workspace too small");
-    if (attn_impl() == 0)
+    if (attn_impl() != 1)
         return attention_mma_backward(static_cast<int>(hd), q, k, v, cos_t, sin_t, o, lse, dout,
                                       dq, dk, dv, accumulate, B, T, H, scale, workspace,
                                       S(stream));

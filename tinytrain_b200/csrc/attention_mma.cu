@@ -760,7 +760,7 @@ inline int launch_split(const float* x, const float* cs, const float* sn, int ro
 
 template <int HD>
 int fwd(const float* q, const float* k, const float* v, const float* cs, const float* sn,
-        float* o, float* lse, int64_t B, int64_t T, int64_t H, float scale, SplitBufs s,
+        float* o, float* lse, int64_t B, int64_t T, int64_t H, float scale, SplitBufs s, bool tc,
         cudaStream_t st) {
     int rc = launch_split(q, cs, sn, 1, scale, s.qh, s.ql, B, T, H, HD, st);
     if (!rc)
@@ -769,6 +769,8 @@ int fwd(const float* q, const float* k, const float* v, const float* cs, const f
         rc = launch_split(v, cs, sn, 0, 1.0f, s.vh, s.vl, B, T, H, HD, st);
     if (rc)
         return rc;
+    if (tc)
+        return attention_tc_forward_core(HD, s.qh, s.kh, s.vh, o, lse, B, T, H, st);
     const int smem = FwdSmem<HD>::BYTES;
     cudaFuncSetAttribute(attn_fwd_mma<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     dim3 grid(static_cast<unsigned>((T + FWD_BQ - 1) / FWD_BQ), static_cast<unsigned>(B * H));
@@ -820,14 +822,15 @@ namespace ttk {
 
 int attention_mma_forward(int hd, const float* q, const float* k, const float* v,
                           const float* cs, const float* sn, float* o, float* lse, int64_t B,
-                          int64_t T, int64_t H, float scale, void* ws, cudaStream_t st) {
+                          int64_t T, int64_t H, float scale, void* ws, bool tc,
+                          cudaStream_t st) {
     const int64_t n = B * T * H * hd;
     __nv_bfloat16* w = static_cast<__nv_bfloat16*>(ws);
     fa::SplitBufs s{w, w + n, w + 2 * n, w + 3 * n, w + 4 * n, w + 5 * n, nullptr, nullptr};
     switch (hd) {
-        case 32: return fa::fwd<32>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, st);
-        case 64: return fa::fwd<64>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, st);
-        default: return fa::fwd<128>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, st);
+        case 32: return fa::fwd<32>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, false, st);
+        case 64: return fa::fwd<64>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st);
+        default: return fa::fwd<128>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st);
     }
 }
 

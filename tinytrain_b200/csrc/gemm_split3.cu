@@ -437,13 +437,6 @@ __global__ void scale_kernel(float* C, int64_t batch, int64_t M, int64_t N, int6
 
 // ------------------------------------------------------------- host side --
 
-namespace {
-
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
 EncodeTiledFn encode_fn() {
     static EncodeTiledFn fn = nullptr;
     if (!fn) {
@@ -456,6 +449,8 @@ EncodeTiledFn encode_fn() {
     }
     return fn;
 }
+
+namespace {
 
 inline int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 

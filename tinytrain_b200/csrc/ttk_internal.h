@@ -1,6 +1,8 @@
 // Host-side internals shared by the ttk translation units.
 #pragma once
 
+#include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -17,6 +19,14 @@ int set_error(int code, const char* msg);
 int check_launch(const char* what);
 int check_cuda(cudaError_t e, const char* what);
 const char* last_error_cstr();
+
+// cuTensorMapEncodeTiled, resolved once through the runtime's driver entry
+// point query (null if unavailable).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn();
 
 inline int grid_for(int64_t n, int threads, int max_blocks = 148 * 16) {
     int64_t b = (n + threads - 1) / threads;
@@ -47,11 +57,19 @@ int gemm_tf32x3_presplit(int transA, int transB, int64_t batch, int64_t M, int64
 // workspace functions.
 int attention_mma_forward(int hd, const float* q, const float* k, const float* v,
                           const float* cs, const float* sn, float* o, float* lse, int64_t B,
-                          int64_t T, int64_t H, float scale, void* ws, cudaStream_t st);
+                          int64_t T, int64_t H, float scale, void* ws, bool tc,
+                          cudaStream_t st);
 int attention_mma_backward(int hd, const float* q, const float* k, const float* v,
                            const float* cs, const float* sn, const float* o, const float* lse,
                            const float* dout, float* dq, float* dk, float* dv, int accumulate,
                            int64_t B, int64_t T, int64_t H, float scale, void* ws,
                            cudaStream_t st);
+
+// tcgen05 attention forward (attention_tc.cu) over split planes written by
+// the mma.sync path's split pass; head dims 64 and 128.
+bool attention_tc_supported(int hd);
+int attention_tc_forward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat16* kh,
+                              const __nv_bfloat16* vh, float* o, float* lse, int64_t B, int64_t T,
+                              int64_t H, cudaStream_t st);
 
 }  // namespace ttk

@@ -188,8 +188,9 @@ int ttk_attention_bwd(const float* q, const float* k, const float* v, const floa
                       int64_t H, int64_t hd, float scale, void* workspace,
                       size_t workspace_bytes, void* stream);
 /* Attention engine (process-wide), all fp32-accurate:
- *   0 = tensor cores (default): tcgen05 forward for head dims 64 and 128,
- *       mma.sync m16n8k16 elsewhere, both with the bf16x3 operand split;
+ *   0 = tensor cores (default): tcgen05 forward and backward for head dims
+ *       64 and 128, mma.sync m16n8k16 elsewhere, both with the bf16x3
+ *       operand split;
  *   1 = fp32 FMA kernels;
  *   2 = mma.sync m16n8k16 kernels only.
  * The environment variable TTK_ATTENTION=fma | mma selects 1 | 2 at start-up.

@@ -191,7 +191,8 @@ def test_attention_golden(cuda, golden_ops, tag, attn_impl):
 
 
 @pytest.mark.parametrize("B,T,H,hd", [(2, 128, 8, 32), (1, 200, 2, 64), (1, 512, 2, 128),
-                                     (1, 70, 3, 32), (1, 333, 1, 128)])
+                                     (1, 70, 3, 32), (1, 333, 1, 128), (2, 1000, 2, 64),
+                                     (1, 2048, 1, 128)])
 def test_attention_sizes(cuda, B, T, H, hd, attn_impl):
     from oracle import restate as rs
     from tinytrain_b200 import kernels as K
@@ -207,6 +208,26 @@ def test_attention_sizes(cuda, B, T, H, hd, attn_impl):
     assert rel_err(n(dq), dqr) < TOL
     assert rel_err(n(dk), dkr) < TOL
     assert rel_err(n(dv), dvr) < TOL
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_attention_bwd_accumulates(cuda, hd, attn_impl):
+    """accumulate = 1 adds the gradients into dq, dk, dv (the autograd engine's
+    += into existing grads, ops.cpp ensure_grad + accumulation)."""
+    from tinytrain_b200 import kernels as K
+    B, T, H = 1, 300, 2
+    rng = np.random.default_rng(hd)
+    q, k, v, go = (t(rng.standard_normal((B, T, H, hd)).astype(np.float32), cuda)
+                   for _ in range(4))
+    cs, sn = K.rope_tables(T, hd, 10000.0, cuda)
+    o, lse = K.attention_fwd(q, k, v, cs, sn)
+    dq, dk, dv = K.attention_bwd(q, k, v, cs, sn, o, lse, go)
+    base = [torch.randn_like(x) for x in (dq, dk, dv)]
+    acc = [x.clone() for x in base]
+    K.attention_bwd(q, k, v, cs, sn, o, lse, go, out=acc, accumulate=True)
+    for a, b0, g in zip(acc, base, (dq, dk, dv)):
+        assert rel_err(n(a), n(b0) + n(g)) < 1e-6
+    assert status_ok()
 
 
 def test_adamw_golden(cuda, golden_ops):

@@ -600,10 +600,12 @@ int ttk_attention_bwd(const float* q, const float* k, const float* v, const floa
         return set_error(TTK_ERR_ARG, "attention_bwd: null pointer");
     if (!workspace || workspace_bytes < ttk_attention_bwd_workspace_size(B, T, H, hd))
         return set_error(TTK_ERR_ARG, "attention_bwd: workspace too small");
-    if (attn_impl() != 1)
+    if (attn_impl() != 1) {
+        const bool tc = attn_impl() == 0 && attention_tc_supported(static_cast<int>(hd));
         return attention_mma_backward(static_cast<int>(hd), q, k, v, cos_t, sin_t, o, lse, dout,
-                                      dq, dk, dv, accumulate, B, T, H, scale, workspace,
+                                      dq, dk, dv, accumulate, B, T, H, scale, workspace, tc,
                                       S(stream));
+    }
     float* Dv = static_cast<float*>(workspace);
     switch (hd) {
         case 32:

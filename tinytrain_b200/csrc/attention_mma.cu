@@ -783,7 +783,7 @@ template <int HD>
 int bwd(const float* q, const float* k, const float* v, const float* cs, const float* sn,
         const float* o, const float* lse, const float* dout, float* dq, float* dk, float* dv,
         int accumulate, int64_t B, int64_t T, int64_t H, float scale, SplitBufs s, float* Dv,
-        cudaStream_t st) {
+        bool tc, cudaStream_t st) {
     int rc = launch_split(q, cs, sn, 1, scale, s.qh, s.ql, B, T, H, HD, st);
     if (!rc)
         rc = launch_split(k, cs, sn, 1, 1.0f, s.kh, s.kl, B, T, H, HD, st);
@@ -797,6 +797,9 @@ int bwd(const float* q, const float* k, const float* v, const float* cs, const f
     rc = check_launch("attn_rowdot_kernel");
     if (rc)
         return rc;
+    if (tc)
+        return attention_tc_backward_core(HD, s.qh, s.kh, s.vh, s.dh, lse, Dv, cs, sn, dq, dk, dv,
+                                          accumulate, B, T, H, scale, st);
     int smem = DkvSmem<HD>::BYTES;
     cudaFuncSetAttribute(attn_bwd_mma_dkv<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     dim3 g1(static_cast<unsigned>((T + DKV_BK - 1) / DKV_BK), static_cast<unsigned>(B * H));
@@ -837,7 +840,7 @@ int attention_mma_forward(int hd, const float* q, const float* k, const float* v
 int attention_mma_backward(int hd, const float* q, const float* k, const float* v,
                            const float* cs, const float* sn, const float* o, const float* lse,
                            const float* dout, float* dq, float* dk, float* dv, int accumulate,
-                           int64_t B, int64_t T, int64_t H, float scale, void* ws,
+                           int64_t B, int64_t T, int64_t H, float scale, void* ws, bool tc,
                            cudaStream_t st) {
     const int64_t n = B * T * H * hd;
     float* Dv = static_cast<float*>(ws);
@@ -847,13 +850,13 @@ int attention_mma_backward(int hd, const float* q, const float* k, const float* 
     switch (hd) {
         case 32:
             return fa::bwd<32>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                               scale, s, Dv, st);
+                               scale, s, Dv, false, st);
         case 64:
             return fa::bwd<64>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                               scale, s, Dv, st);
+                               scale, s, Dv, tc, st);
         default:
             return fa::bwd<128>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                                scale, s, Dv, st);
+                                scale, s, Dv, tc, st);
     }
 }
 

@@ -62,14 +62,19 @@ int attention_mma_forward(int hd, const float* q, const float* k, const float* v
 int attention_mma_backward(int hd, const float* q, const float* k, const float* v,
                            const float* cs, const float* sn, const float* o, const float* lse,
                            const float* dout, float* dq, float* dk, float* dv, int accumulate,
-                           int64_t B, int64_t T, int64_t H, float scale, void* ws,
+                           int64_t B, int64_t T, int64_t H, float scale, void* ws, bool tc,
                            cudaStream_t st);
 
-// tcgen05 attention forward (attention_tc.cu) over split planes written by
-// the mma.sync path's split pass; head dims 64 and 128.
+// tcgen05 attention forward / backward (attention_tc.cu) over split planes
+// written by the mma.sync path's split pass; head dims 64 and 128.
 bool attention_tc_supported(int hd);
 int attention_tc_forward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat16* kh,
                               const __nv_bfloat16* vh, float* o, float* lse, int64_t B, int64_t T,
                               int64_t H, cudaStream_t st);
+int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat16* kh,
+                               const __nv_bfloat16* vh, const __nv_bfloat16* dh,
+                               const float* lse, const float* Dv, const float* cs,
+                               const float* sn, float* dq, float* dk, float* dv, int accumulate,
+                               int64_t B, int64_t T, int64_t H, float scale, cudaStream_t st);
 
 }  // namespace ttk

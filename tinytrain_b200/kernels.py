@@ -175,13 +175,15 @@ def attention_fwd(q, k, v, cos, sin, scale=None):
     return o, lse
 
 
-def attention_bwd(q, k, v, cos, sin, o, lse, do, scale=None):
+def attention_bwd(q, k, v, cos, sin, o, lse, do, scale=None, out=None, accumulate=False):
+    """dq, dk, dv; with `out` = (dq, dk, dv) writes (or, with accumulate, adds) into them."""
     B, T, H, hd = q.shape
     scale = float(hd) ** -0.5 if scale is None else scale
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dq, dk, dv = out if out is not None else (torch.empty_like(q), torch.empty_like(k),
+                                               torch.empty_like(v))
     ws = workspace(call("ttk_attention_bwd_workspace_size", B, T, H, hd), q.device)
     call("ttk_attention_bwd", _p(q), _p(k), _p(v), _p(cos), _p(sin), _p(o), _p(lse), _p(do),
-         _p(dq), _p(dk), _p(dv), 0, B, T, H, hd, scale, _p(ws), ws.numel(), _s())
+         _p(dq), _p(dk), _p(dv), int(accumulate), B, T, H, hd, scale, _p(ws), ws.numel(), _s())
     return dq, dk, dv
 
 

@@ -141,7 +141,7 @@ def bench_attention(seqs, iters, B=8, H=12, hd=64):
         ms_b = timed(lambda: K.attention_bwd(q, k, v, cs, sn, o, lse, do), iters)
         fl_f = 2 * B * H * S * S * hd  # causal half of 4*B*H*S^2*hd
         fl_b = 2 * fl_f
-        eng = {0: ("tcgen05 fwd + mma.sync bwd, bf16x3 split" if hd in (64, 128) else
+        eng = {0: ("tcgen05 fwd + bwd, bf16x3 split" if hd in (64, 128) else
                    "mma.sync m16n8k16 bf16x3 split"),
                1: "fp32 FMA (CUDA cores)",
                2: "mma.sync m16n8k16 bf16x3 split"}[_ttk.call("ttk_attention_get_impl")]

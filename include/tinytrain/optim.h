@@ -31,6 +31,11 @@ public:
     // Norm measured by the last step() with clipping on (reads the device).
     float last_grad_norm() const;
     int64_t step_count() const { return step_; }
+    // Optimizer state for checkpoints: first (which = 0) or second (1) moment
+    // of parameter i on the device, allocated zeroed if it does not exist yet;
+    // and the step counter behind the bias correction.
+    float* moment(size_t i, int which);
+    void set_step_count(int64_t t) { step_ = t; }
 
 private:
     std::vector<Tensor*> params_;

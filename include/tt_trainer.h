@@ -65,6 +65,44 @@ int tt_trainer_last_loss(void* handle, float* loss);
 int tt_trainer_forward_backward(void* handle, const int64_t* idx, const int64_t* targets,
                                 int64_t B, int64_t T, float* loss, float* logits);
 
+/* ---- data feed (apps/train.cpp:162-174, 225-232) ----
+ * A token stream is the int32 token file written by apps/prepare_data.cpp
+ * (raw little-endian int32), held in device memory for the whole run. */
+int tt_tokens_from_file(const char* path, void** tokens);
+int tt_tokens_from_host(const int32_t* host, int64_t n, void** tokens);
+int64_t tt_tokens_count(void* tokens);
+int tt_tokens_destroy(void* tokens);
+/* The reference's window sampler: `count` draws of its xorshift64* Rng
+ * (apps/train.cpp:145-153; the state starts at the seed, apps/train.cpp uses
+ * seed + 999, and 0 stands for 0x9E3779B97F4A7C15), each start = next() %
+ * (ntok - T - 1). *rng_state advances, so consecutive calls continue the
+ * stream exactly as consecutive training steps do. Host only. */
+int tt_sample_windows(uint64_t* rng_state, int64_t ntok, int64_t T, int64_t count,
+                      int64_t* starts);
+/* One optimizer step on windows of a device token stream: `starts` (host)
+ * holds the n_micro*B window starts of this rank (for data parallelism, rank
+ * r takes draws [r*n_micro*B, (r+1)*n_micro*B) of the global batch); only
+ * they cross to the device, where a gather kernel builds ids and targets.
+ * loss / grad_norm as in tt_trainer_step (either may be NULL). */
+int tt_trainer_step_tokens(void* handle, void* tokens, const int64_t* starts, int64_t B,
+                           int64_t T, int64_t n_micro, float lr, float* loss, float* grad_norm);
+
+/* The learning-rate schedule of apps/train.cpp:214-222: linear warmup over
+ * `warmup` steps, then cosine decay to 10% of base_lr at total_steps (float
+ * arithmetic in the reference's order). The result is the lr argument of the
+ * step functions, i.e. a scalar argument of the fused AdamW kernel. */
+float tt_lr_at(float base_lr, int64_t step, int64_t warmup, int64_t total_steps);
+
+/* ---- checkpoints ----
+ * <dir>/model.safetensors + config.json exactly as GPTModel::save_checkpoint
+ * writes them (model.cpp:162-227; the reference's load_checkpoint reads them),
+ * plus <dir>/optimizer.safetensors with AdamW's moments ("m.<i>", "v.<i>",
+ * parameters() order) and its step count, so that a run resumes bit for bit
+ * (the reference restores weights only). tt_trainer_load restores the
+ * optimizer state when the file is present. */
+int tt_trainer_save(void* handle, const char* dir);
+int tt_trainer_load(void* handle, const char* dir);
+
 /* Data parallelism: join an NCCL communicator (id from rank 0's
  * ttk_dist_unique_id, shared out of band) and reduce gradients in buckets of
  * about bucket_bytes during backward. */

@@ -217,6 +217,19 @@ int ttk_rope_fwd(const float* x, const float* cos_t, const float* sin_t, float* 
 int ttk_rope_bwd(const float* dy, const float* cos_t, const float* sin_t, float* dx,
                  int accumulate, int64_t B, int64_t T, int64_t H, int64_t D, void* stream);
 
+/* The reference's dropout mask (ops.cpp:944-968): mask[i] = 1.0f when the
+ * (i+1)-th output r of its xorshift64* stream (seed 0 -> 0x9E3779B97F4A7C15)
+ * gives (r >> 11) * 2^-53 >= p, else 0.0f; bit-identical to the sequential
+ * loop at any n (each thread jumps ahead to its chunk of the stream). */
+int ttk_dropout_mask(float* mask, int64_t n, float p, uint64_t seed, void* stream);
+
+/* Training windows from a device-resident int32 token stream
+ * (apps/train.cpp:225-232): for w < count, idx[w*T + t] = tokens[starts[w] + t]
+ * and targets[w*T + t] = tokens[starts[w] + t + 1], widened to int64. starts
+ * (device) must satisfy starts[w] + T < token count (checked by the caller). */
+int ttk_gather_windows(const int32_t* tokens, const int64_t* starts, int64_t count, int64_t T,
+                       int64_t* idx, int64_t* targets, void* stream);
+
 /* nll_loss over log-probabilities [N,C] (ops.cpp:898-926): *loss =
  * -sum_i lp[i,t_i] / N (fp64, i ascending); backward dlp[i,t_i] -= g[0]/N with
  * the upstream gradient g read on the device. */

@@ -304,6 +304,18 @@ int ref_rope(int64_t B, int64_t T, int64_t H, int64_t D, const float* X, const f
     });
 }
 
+// The reference's dropout mask for n elements (ops.cpp:944-968): dropout of
+// a tensor of ones, whose output is mask / (1 - p); mask[i] = (out[i] != 0).
+int ref_dropout_mask(int64_t n, float p, uint64_t seed, float* mask) {
+    return guarded([&] {
+        tt::Tensor ones = tt::full({n}, 1.0f);
+        tt::Tensor y = tt::dropout(ones, p, seed);
+        const float* d = y.data();
+        for (int64_t i = 0; i < n; ++i)
+            mask[i] = d[i] != 0.0f ? 1.0f : 0.0f;
+    });
+}
+
 // y = softmax(x [R,C], -1) (ops.cpp:777-838).
 int ref_softmax(int64_t R, int64_t C, const float* X, const float* G, float* Y, float* dX) {
     return guarded([&] {
@@ -420,6 +432,16 @@ int64_t ref_param_shapes(const RefCfg* c, int64_t* shapes, int64_t cap) {
 int ref_init_params(const RefCfg* c, uint64_t seed, float* out) {
     return guarded([&] {
         tt::GPTModel m(to_cfg(c), seed);
+        store_params(m, out);
+    });
+}
+
+// Parameters of a GPTModel after the reference's load_checkpoint(dir)
+// (model.cpp:229-280), flat in parameters() order.
+int ref_load_checkpoint(const RefCfg* c, const char* dir, float* out) {
+    return guarded([&] {
+        tt::GPTModel m(to_cfg(c), 1);
+        m.load_checkpoint(dir);
         store_params(m, out);
     });
 }

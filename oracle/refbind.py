@@ -158,6 +158,13 @@ def rope(X, cos, sin, G=None):
     return (Y, dX) if G is not None else Y
 
 
+def dropout_mask(n, p, seed):
+    """Mask of the reference's dropout (ops.cpp:944-968) for n elements."""
+    m = np.empty(n, np.float32)
+    _check(lib().ref_dropout_mask(C.c_int64(n), C.c_float(p), C.c_uint64(seed), _p(m)))
+    return m
+
+
 def softmax(X, G=None):
     X = _f(X)
     R, Cn = X.shape
@@ -213,6 +220,13 @@ def param_shapes(c: RefCfg):
 def init_params(c: RefCfg, seed: int):
     out = np.empty(param_count(c), np.float32)
     _check(lib().ref_init_params(C.byref(c), C.c_uint64(seed), _p(out)))
+    return out
+
+
+def load_checkpoint(c: RefCfg, path: str):
+    """Flat parameters after the reference's GPTModel::load_checkpoint(path)."""
+    out = np.empty(param_count(c), np.float32)
+    _check(lib().ref_load_checkpoint(C.byref(c), os.fsencode(path), _p(out)))
     return out
 
 

@@ -197,6 +197,36 @@ def clip_grad_norm(grads, max_norm):
     return total
 
 
+_M64 = (1 << 64) - 1
+
+
+def xorshift_stream(seed, n):
+    """n outputs of the xorshift64* generator shared by tensor.cpp's Rng, the
+    dropout mask (ops.cpp:949-963) and apps/train.cpp:145-153 (seed 0 ->
+    0x9E3779B97F4A7C15). Pure Python: small n only."""
+    s = seed if seed else 0x9E3779B97F4A7C15
+    out = []
+    for _ in range(n):
+        s ^= s >> 12
+        s ^= (s << 25) & _M64
+        s ^= s >> 27
+        out.append((s * 0x2545F4914F6CDD1D) & _M64)
+    return out
+
+
+def dropout_mask(n, p, seed):
+    """ops.cpp:949-963: element i kept when ((r_i >> 11) * 2^-53) >= p."""
+    r = xorshift_stream(seed, n)
+    return np.array([1.0 if (x >> 11) * (1.0 / 9007199254740992.0) >= float(np.float32(p)) else 0.0
+                     for x in r], np.float32)
+
+
+def sample_windows(seed, ntok, T, count):
+    """apps/train.cpp:225-232: `count` window starts rng.next() % (ntok - T - 1)
+    from Rng(seed); returns (starts, next seed state is not exposed)."""
+    return [x % (ntok - T - 1) for x in xorshift_stream(seed, count)]
+
+
 def lr_scale(gstep, warmup, total_steps):
     """apps/train.cpp:214-222: linear warmup then cosine to 10% of peak."""
     if gstep < warmup:

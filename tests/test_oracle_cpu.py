@@ -101,6 +101,23 @@ def test_lr_schedule():
     assert abs(rs.lr_scale(1000, 100, 1000) - 0.1) < 1e-6
 
 
+@pytest.mark.parametrize("n,p,seed", [(1, 0.5, 0), (97, 0.1, 7), (5000, 0.3, 12345),
+                                      (2048, 0.9, (1 << 63) + 5)])
+def test_dropout_mask_restatement_bitexact(n, p, seed):
+    """The restated mask stream equals the reference's dropout (ops.cpp:944-968)."""
+    from oracle import refbind as rb
+    if not rb.available():
+        pytest.skip("oracle/_ref not built (needs the reference sources)")
+    assert np.array_equal(rs.dropout_mask(n, p, seed), rb.dropout_mask(n, p, seed))
+
+
+def test_window_sampler_uses_the_shared_generator():
+    """apps/train.cpp's Rng is the dropout generator: the first window start
+    is the first output modulo the window range."""
+    r = rs.xorshift_stream(1041, 3)
+    assert rs.sample_windows(1041, 20000, 64, 3) == [x % (20000 - 64 - 1) for x in r]
+
+
 def test_clip_rule():
     gs = [np.full(4, 3.0, np.float32), np.full(9, 1.0, np.float32)]
     total = rs.clip_grad_norm(gs, 1.0)

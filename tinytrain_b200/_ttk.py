@@ -79,6 +79,8 @@ SIGS = {
     "ttk_embedding_bwd": (I32, [P, P, P, I64, I64, I64, P, SZ, P]),
     "ttk_index_check": (I32, [P, I64, I64, P, P]),
     "ttk_rope_fwd": (I32, [P, P, P, P, I64, I64, I64, I64, P]),
+    "ttk_dropout_mask": (I32, [P, I64, F32, U64, P]),
+    "ttk_gather_windows": (I32, [P, P, I64, I64, P, P, P]),
     "ttk_rope_bwd": (I32, [P, P, P, P, I32, I64, I64, I64, I64, P]),
     "ttk_nll_fwd": (I32, [P, P, I64, I64, P, P]),
     "ttk_nll_bwd": (I32, [P, I64, I64, P, P, P]),

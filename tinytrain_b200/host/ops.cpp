@@ -771,19 +771,9 @@ Tensor dropout(const Tensor& a, float p, uint64_t seed) {
     if (p >= 1.0f)
         throw std::invalid_argument("dropout: p must be < 1");
     // The reference's mask stream (xorshift64*, ops.cpp:949-963), generated on
-    // the host so that a given seed drops the same elements.
-    std::vector<float> m(static_cast<size_t>(a.numel()));
-    uint64_t s = seed ? seed : 0x9E3779B97F4A7C15ULL;
-    for (auto& x : m) {
-        s ^= s >> 12;
-        s ^= s << 25;
-        s ^= s >> 27;
-        const uint64_t r = s * 0x2545F4914F6CDD1DULL;
-        const double u = (r >> 11) * (1.0 / 9007199254740992.0);
-        x = (u >= p) ? 1.0f : 0.0f;
-    }
-    Tensor mask(a.shape(), false);
-    mask.copy_from_host(m.data());
+    // the device bit for bit, so that a given seed drops the same elements.
+    Tensor mask = make_out(a.shape(), false);
+    check(ttk_dropout_mask(out_ptr(mask), mask.numel(), p, seed, stream()), "dropout");
     const float scale = 1.0f / (1.0f - p);
     return mul(mul(a, mask), full(a.shape(), scale));
 }

@@ -4,6 +4,7 @@
 // multi-tensor sum-of-squares kernel; moments are allocated lazily per
 // parameter on its first step with a gradient, as in the reference.
 #include <cmath>
+#include <stdexcept>
 
 #include "internal.h"
 #include "tinytrain/optim.h"
@@ -80,6 +81,16 @@ void AdamW::step() {
                           static_cast<int>(ps.size()), lr_, beta1_, beta2_, eps_, weight_decay_,
                           step_, ss, clip_, grad_scale_, stream()),
           "adamw");
+}
+
+float* AdamW::moment(size_t i, int which) {
+    if (i >= params_.size())
+        throw std::out_of_range("AdamW::moment: parameter index");
+    if (!m_[i]) {
+        m_[i] = zeroed(params_[i]->numel());
+        v_[i] = zeroed(params_[i]->numel());
+    }
+    return which == 0 ? m_[i] : v_[i];
 }
 
 float AdamW::last_grad_norm() const {

@@ -10,7 +10,11 @@
 // backward continues. The compute stream waits for the last bucket before
 // the fused clip + AdamW kernel, which divides by world * n_micro.
 #include <cmath>
+#include <cstdio>
 #include <cstring>
+#include <filesystem>
+#include <fstream>
+#include <map>
 #include <memory>
 #include <string>
 #include <unordered_map>
@@ -218,6 +222,85 @@ struct Trainer {
     }
 };
 
+// A token stream resident in device memory (int32, apps/prepare_data.cpp's
+// file format), plus a pinned staging buffer for window starts.
+struct Tokens {
+    int32_t* dev = nullptr;
+    int64_t n = 0;
+    ~Tokens() { ttk_free(dev, stream_if_ready()); }
+};
+
+Tokens* make_tokens(const int32_t* host, int64_t n) {
+    if (n < 2)
+        throw std::invalid_argument("tokens: need at least 2 tokens");
+    ensure_runtime();
+    auto t = std::make_unique<Tokens>();
+    t->n = n;
+    check(ttk_malloc(reinterpret_cast<void**>(&t->dev), static_cast<size_t>(n) * 4, stream()),
+          "tokens");
+    check(ttk_memcpy_h2d(t->dev, host, static_cast<size_t>(n) * 4, stream()), "tokens upload");
+    check(ttk_stream_synchronize(stream()), "tokens upload");
+    return t.release();
+}
+
+uint64_t xorshift_next(uint64_t& s) {  // apps/train.cpp:145-153
+    s ^= s >> 12;
+    s ^= s << 25;
+    s ^= s >> 27;
+    return s * 0x2545F4914F6CDD1DULL;
+}
+
+// safetensors writer / reader for flat float32 tensors (the format of
+// model.safetensors: 8-byte header length, JSON header, payloads).
+void write_safetensors(const std::string& path,
+                       const std::vector<std::pair<std::string, std::pair<int64_t, const float*>>>&
+                           tensors,
+                       const std::string& metadata_json) {
+    std::map<std::string, std::string> entries;
+    int64_t off = 0;
+    for (auto& [name, t] : tensors) {
+        entries[name] = "{\"data_offsets\":[" + std::to_string(off) + "," +
+                        std::to_string(off + t.first * 4) + "],\"dtype\":\"F32\",\"shape\":[" +
+                        std::to_string(t.first) + "]}";
+        off += t.first * 4;
+    }
+    std::string header = "{\"__metadata__\":" + metadata_json;
+    for (auto& [k, v] : entries)
+        header += ",\"" + k + "\":" + v;
+    header += "}";
+    std::ofstream f(path, std::ios::binary);
+    if (!f)
+        throw std::runtime_error("save: cannot open " + path);
+    const uint64_t hlen = header.size();
+    f.write(reinterpret_cast<const char*>(&hlen), 8);
+    f.write(header.data(), static_cast<std::streamsize>(header.size()));
+    for (auto& [name, t] : tensors)
+        f.write(reinterpret_cast<const char*>(t.second), static_cast<std::streamsize>(t.first * 4));
+    if (!f)
+        throw std::runtime_error("save: write failed for " + path);
+}
+
+// Reads the header of a safetensors file; returns it and the payload start.
+std::string read_header(std::ifstream& f, const std::string& path) {
+    uint64_t hlen = 0;
+    f.read(reinterpret_cast<char*>(&hlen), 8);
+    if (!f || hlen > (1ull << 30))
+        throw std::runtime_error("load: bad header in " + path);
+    std::string h(static_cast<size_t>(hlen), '\0');
+    f.read(h.data(), static_cast<std::streamsize>(hlen));
+    return h;
+}
+
+// Offsets of tensor `name` in a header written by write_safetensors.
+bool find_tensor(const std::string& h, const std::string& name, uint64_t& beg, uint64_t& end) {
+    const size_t at = h.find("\"" + name + "\":{");
+    if (at == std::string::npos)
+        return false;
+    const size_t p = h.find("\"data_offsets\":[", at);
+    return p != std::string::npos &&
+           std::sscanf(h.c_str() + p, "\"data_offsets\":[%lu,%lu]", &beg, &end) == 2;
+}
+
 template <class F>
 int guarded(F&& f) {
     try {
@@ -381,6 +464,150 @@ int tt_trainer_forward_backward(void* h, const int64_t* idx, const int64_t* targ
             l.copy_to_host(loss);
         l.backward();
         tt::synchronize();
+    });
+}
+
+int tt_tokens_from_host(const int32_t* host, int64_t n, void** tokens) {
+    return guarded([&] {
+        if (!host || !tokens)
+            throw std::invalid_argument("tokens: null pointer");
+        *tokens = make_tokens(host, n);
+    });
+}
+
+int tt_tokens_from_file(const char* path, void** tokens) {
+    return guarded([&] {
+        std::ifstream f(path, std::ios::binary | std::ios::ate);
+        if (!f)
+            throw std::runtime_error(std::string("tokens: cannot open ") + path);
+        const int64_t nbytes = f.tellg();
+        f.seekg(0);
+        std::vector<int32_t> tok(static_cast<size_t>(nbytes / 4));
+        f.read(reinterpret_cast<char*>(tok.data()), static_cast<std::streamsize>(tok.size() * 4));
+        if (!f)
+            throw std::runtime_error(std::string("tokens: read failed for ") + path);
+        *tokens = make_tokens(tok.data(), static_cast<int64_t>(tok.size()));
+    });
+}
+
+int64_t tt_tokens_count(void* tokens) { return tokens ? static_cast<Tokens*>(tokens)->n : 0; }
+
+int tt_tokens_destroy(void* tokens) {
+    return guarded([&] { delete static_cast<Tokens*>(tokens); });
+}
+
+int tt_sample_windows(uint64_t* rng_state, int64_t ntok, int64_t T, int64_t count,
+                      int64_t* starts) {
+    return guarded([&] {
+        if (!rng_state || (count > 0 && !starts) || T <= 0 || ntok - T - 1 <= 0)
+            throw std::invalid_argument("sample_windows: need ntok > T + 1");
+        uint64_t s = *rng_state ? *rng_state : 0x9E3779B97F4A7C15ULL;
+        const uint64_t range = static_cast<uint64_t>(ntok - T - 1);
+        for (int64_t i = 0; i < count; ++i)
+            starts[i] = static_cast<int64_t>(xorshift_next(s) % range);
+        *rng_state = s;
+    });
+}
+
+int tt_trainer_step_tokens(void* h, void* tokens, const int64_t* starts, int64_t B, int64_t T,
+                           int64_t n_micro, float lr, float* loss, float* grad_norm) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        Tokens* tk = static_cast<Tokens*>(tokens);
+        if (!tk || !starts || B <= 0 || T <= 0 || n_micro <= 0)
+            throw std::invalid_argument("step_tokens: bad arguments");
+        const int64_t w = B * n_micro;
+        for (int64_t i = 0; i < w; ++i)
+            if (starts[i] < 0 || starts[i] + T >= tk->n)
+                throw std::invalid_argument("step_tokens: window out of range");
+        // ids and targets for every micro-batch, then the window starts
+        Scratch d(static_cast<size_t>(w * T) * 16 + static_cast<size_t>(w) * 8);
+        int64_t* idx = d.as<int64_t>();
+        int64_t* tgt = idx + w * T;
+        int64_t* st = tgt + w * T;
+        check(ttk_memcpy_h2d(st, starts, static_cast<size_t>(w) * 8, stream()), "starts");
+        check(ttk_gather_windows(tk->dev, st, w, T, idx, tgt, stream()), "gather windows");
+        t->zero_grads();
+        t->accumulate(idx, tgt, B, T, n_micro);
+        t->optimizer_step(n_micro, lr);
+        if (loss)
+            check(ttk_memcpy_d2h(loss, t->loss_out, 4, stream()), "loss read");
+        if (grad_norm)
+            *grad_norm = t->ocfg.clip_norm > 0.0f ? t->opt->last_grad_norm() : 0.0f;
+    });
+}
+
+float tt_lr_at(float base_lr, int64_t gstep, int64_t warmup, int64_t total_steps) {
+    // apps/train.cpp:214-222, the same float expression order
+    float lr_scale;
+    if (gstep < warmup) {
+        lr_scale = static_cast<float>(gstep + 1) / static_cast<float>(warmup);
+    } else {
+        const float prog = static_cast<float>(gstep - warmup) /
+                           static_cast<float>(std::max<int64_t>(total_steps - warmup, 1));
+        lr_scale = 0.1f + 0.9f * 0.5f * (1.0f + std::cos(3.14159265f * prog));
+    }
+    return base_lr * lr_scale;
+}
+
+int tt_trainer_save(void* h, const char* dir) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        t->model->save_checkpoint(dir);
+        // optimizer moments (host copies) and step count
+        const size_t np = t->params.size();
+        std::vector<std::vector<float>> host(2 * np);
+        std::vector<std::pair<std::string, std::pair<int64_t, const float*>>> ts;
+        for (size_t i = 0; i < np; ++i) {
+            const int64_t n = t->params[i]->numel();
+            for (int which = 0; which < 2; ++which) {
+                auto& hb = host[2 * i + static_cast<size_t>(which)];
+                hb.resize(static_cast<size_t>(n));
+                check(ttk_memcpy_d2h(hb.data(), t->opt->moment(i, which),
+                                     static_cast<size_t>(n) * 4, stream()),
+                      "save: moments");
+                ts.push_back({(which ? "v." : "m.") + std::to_string(i), {n, hb.data()}});
+            }
+        }
+        const std::string meta = "{\"step\":\"" + std::to_string(t->opt->step_count()) + "\"}";
+        write_safetensors(std::string(dir) + "/optimizer.safetensors", ts, meta);
+    });
+}
+
+int tt_trainer_load(void* h, const char* dir) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        t->model->load_checkpoint(dir);
+        const std::string path = std::string(dir) + "/optimizer.safetensors";
+        std::ifstream f(path, std::ios::binary);
+        if (!f)
+            return;  // weights-only checkpoint (e.g. written by the reference)
+        const std::string hdr = read_header(f, path);
+        const uint64_t base = 8 + hdr.size();
+        int64_t step = 0;
+        const size_t sp = hdr.find("\"step\":\"");
+        if (sp == std::string::npos || std::sscanf(hdr.c_str() + sp, "\"step\":\"%ld", &step) != 1)
+            throw std::runtime_error("load: optimizer step missing in " + path);
+        std::vector<float> buf;
+        for (size_t i = 0; i < t->params.size(); ++i) {
+            const int64_t n = t->params[i]->numel();
+            for (int which = 0; which < 2; ++which) {
+                uint64_t beg = 0, end = 0;
+                const std::string name = (which ? "v." : "m.") + std::to_string(i);
+                if (!find_tensor(hdr, name, beg, end) || end - beg != static_cast<uint64_t>(n) * 4)
+                    throw std::runtime_error("load: optimizer tensor " + name + " missing or resized");
+                buf.resize(static_cast<size_t>(n));
+                f.seekg(static_cast<std::streamoff>(base + beg), std::ios::beg);
+                f.read(reinterpret_cast<char*>(buf.data()), static_cast<std::streamsize>(n * 4));
+                if (!f)
+                    throw std::runtime_error("load: read failed for " + name);
+                check(ttk_memcpy_h2d(t->opt->moment(i, which), buf.data(),
+                                     static_cast<size_t>(n) * 4, stream()),
+                      "load: moments");
+            }
+        }
+        check(ttk_stream_synchronize(stream()), "load");
+        t->opt->set_step_count(step);
     });
 }
 

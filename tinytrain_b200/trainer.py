@@ -56,6 +56,15 @@ _SIGS = {
     "tt_trainer_dist_init": (C.c_int, [P, C.c_int, C.c_int, P, I64]),
     "tt_kernel_launches": (I64, []),
     "tt_plan_buckets": (C.c_int, [P, C.c_int, I64, P, P, P, P, P]),
+    "tt_tokens_from_file": (C.c_int, [C.c_char_p, P]),
+    "tt_tokens_from_host": (C.c_int, [P, I64, P]),
+    "tt_tokens_count": (I64, [P]),
+    "tt_tokens_destroy": (C.c_int, [P]),
+    "tt_sample_windows": (C.c_int, [P, I64, I64, I64, P]),
+    "tt_trainer_step_tokens": (C.c_int, [P, P, P, I64, I64, I64, F32, P, P]),
+    "tt_lr_at": (F32, [F32, I64, I64, I64]),
+    "tt_trainer_save": (C.c_int, [P, C.c_char_p]),
+    "tt_trainer_load": (C.c_int, [P, C.c_char_p]),
 }
 
 
@@ -166,6 +175,69 @@ class Trainer:
     def dist_init(self, rank, world, uid: bytes, bucket_bytes=64 << 20):
         buf = (C.c_ubyte * 128).from_buffer_copy(uid)
         _chk(lib().tt_trainer_dist_init(self.h, rank, world, buf, bucket_bytes), "dist_init")
+
+    def step_tokens(self, tokens: "TokenStream", starts, B, T, n_micro=1, lr=3e-4):
+        """One step on windows of a device token stream; `starts` are this
+        rank's n_micro*B window starts. Returns (loss, grad_norm)."""
+        st = np.ascontiguousarray(starts, np.int64)
+        loss, gn = C.c_float(0), C.c_float(0)
+        _chk(lib().tt_trainer_step_tokens(self.h, tokens.h, st.ctypes.data, B, T, n_micro, lr,
+                                          C.byref(loss), C.byref(gn)), "step_tokens")
+        return loss.value, gn.value
+
+    def save(self, path):
+        _chk(lib().tt_trainer_save(self.h, os.fsencode(path)), "save")
+
+    def load(self, path):
+        _chk(lib().tt_trainer_load(self.h, os.fsencode(path)), "load")
+
+
+class TokenStream:
+    """An int32 token stream held in device memory (apps/prepare_data.cpp's
+    file format), from a file path or a host array."""
+
+    def __init__(self, path=None, host=None):
+        h = C.c_void_p()
+        if path is not None:
+            _chk(lib().tt_tokens_from_file(os.fsencode(path), C.byref(h)), "tokens")
+        else:
+            self._host = np.ascontiguousarray(host, np.int32)
+            _chk(lib().tt_tokens_from_host(self._host.ctypes.data, self._host.size, C.byref(h)),
+                 "tokens")
+        self.h = h.value
+
+    def __len__(self):
+        return int(lib().tt_tokens_count(self.h))
+
+    def close(self):
+        if self.h:
+            lib().tt_tokens_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class WindowSampler:
+    """The reference's window sampler (apps/train.cpp:145-153, 225-232): its
+    xorshift64* stream seeded with `seed` (train.cpp passes seed + 999)."""
+
+    def __init__(self, seed):
+        self.state = C.c_uint64(seed)
+
+    def draw(self, ntok, T, count):
+        out = np.empty(count, np.int64)
+        _chk(lib().tt_sample_windows(C.byref(self.state), ntok, T, count, out.ctypes.data),
+             "sample_windows")
+        return out
+
+
+def lr_at(base_lr, step, warmup, total_steps) -> float:
+    """apps/train.cpp:214-222 learning rate for global step `step`."""
+    return float(lib().tt_lr_at(base_lr, step, warmup, total_steps))
 
 
 def plan_buckets(sizes, bucket_bytes):

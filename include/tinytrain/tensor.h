@@ -45,6 +45,14 @@ struct Buffer {
     float fill_value = 0.0f;
     bool external = false;       // dev points into memory owned elsewhere
     uint64_t version = 0;        // bumped on every device-side write
+    // Cached three-term split of the contents as a GEMM operand (ttk_gemm_split
+    // layout; device memory owned by the buffer), valid while split_version ==
+    // version and the key (offset, batch, rows, cols, ld, batch stride,
+    // precision) matches: a tensor read by several GEMMs is split once.
+    void* split_dev = nullptr;
+    size_t split_bytes = 0;
+    uint64_t split_version = ~0ull;
+    int64_t split_key[7] = {};
 
     float* device();             // make the device copy current, return it
     float* device_for_overwrite();  // caller overwrites everything: skip uploads

@@ -114,6 +114,24 @@ int ttk_gemm_noalloc(int transA, int transB, int64_t batch, int64_t M, int64_t N
                      float alpha, const float* A, int64_t lda, int64_t strideA, const float* B,
                      int64_t ldb, int64_t strideB, float beta, float* C, int64_t ldc,
                      int64_t strideC, void* stream);
+/* Operand splits that a caller keeps and reuses across the GEMMs reading the
+ * same tensor (matmul forward, dA and dB of ops.cpp:661-697 read each operand
+ * twice; weights are read by every micro-batch until the optimizer writes
+ * them). In the current precision (bf16 planes for bf16x3, fp32 for tf32x3),
+ * layout [batch][hi|lo][rows][round_up(cols, 32)]: one split serves K-major
+ * and MN-major reads alike. ttk_gemm_split writes the split of src
+ * [batch][rows][cols] (leading dimension ld, batch stride bstride) into dst
+ * (16-byte aligned, ttk_gemm_split_bytes long); ttk_gemm_splits runs
+ * C = alpha op(A) op(B) + beta C on two splits holding op(A)'s storage
+ * (transA ? [K,M] : [M,K]) and op(B)'s (transB ? [N,K] : [K,N]). A split is
+ * valid only for the precision it was made in. */
+size_t ttk_gemm_split_bytes(int64_t batch, int64_t rows, int64_t cols);
+int ttk_gemm_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+                   int64_t batch, void* dst, void* stream);
+int ttk_gemm_splits(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                    float alpha, const void* a_split, const void* b_split, float beta, float* C,
+                    int64_t ldc, int64_t strideC, void* stream);
+
 /* The operand split alone: dst[b][0|1][r][0..ld_pad) = hi | lo of
  * src[b][r][0..cols) (ld, batch stride bstride), zero in [cols, ld_pad).
  * ld_pad must be a multiple of 16 (32 for an operand read MN-major by

@@ -56,6 +56,9 @@ SIGS = {
     "ttk_gemm_noalloc": (I32, [I32, I32, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, F32, P,
                                I64, I64, P]),
     "ttk_split_tf32": (I32, [P, I64, I64, I64, I64, I64, P, I64, P]),
+    "ttk_gemm_split_bytes": (C.c_size_t, [I64, I64, I64]),
+    "ttk_gemm_split": (I32, [P, I64, I64, I64, I64, I64, P, P]),
+    "ttk_gemm_splits": (I32, [I32, I32, I64, I64, I64, I64, F32, P, P, F32, P, I64, I64, P]),
     "ttk_gemm_presplit": (I32, [I32, I32, I64, I64, I64, I64, F32, P, I64, P, I64, F32, P, I64,
                                 I64, P]),
     "ttk_profile_enable": (I32, [I32]),

@@ -583,7 +583,9 @@ size_t ttk_attention_bwd_workspace_size(int64_t B, int64_t T, int64_t H, int64_t
     const size_t dv = align256(static_cast<size_t>(B * T * H) * sizeof(float));
     if (attn_impl() == 1)
         return dv;
-    return dv + static_cast<size_t>(B * T * H * hd) * 8 * 2;  // q, k, v, dO as bf16 hi|lo
+    // q, k, v, dO as bf16 hi|lo, then the (lse, D) table of the tcgen05 path
+    return dv + static_cast<size_t>(B * T * H * hd) * 8 * 2 +
+           align256(static_cast<size_t>(B * H * ((T + 31) / 32 * 32)) * 8);
 }
 
 int ttk_attention_bwd(const float* q, const float* k, const float* v, const float* cos_t,

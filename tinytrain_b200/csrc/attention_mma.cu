@@ -394,10 +394,13 @@ __global__ void __launch_bounds__(FWD_THREADS) attn_fwd_mma(
 namespace ttk {
 namespace fa {
 
-// D[bh][t] = sum_d dO[t][d] * O[t][d] (fp32, [B,T,H,HD] inputs).
+// D[bh][t] = sum_d dO[t][d] * O[t][d] (fp32, [B,T,H,HD] inputs); with `ld`,
+// also the table ld[bh][t] = (lse[bh][t] * log2 e, D[bh][t]) with rows padded
+// to T32 (the padding is zeroed beforehand).
 __global__ void attn_rowdot_kernel(const float* __restrict__ o, const float* __restrict__ dout,
                                    float* __restrict__ Dv, int64_t B, int64_t T, int64_t H,
-                                   int64_t HD) {
+                                   int64_t HD, const float* __restrict__ lse,
+                                   float* __restrict__ ld, int64_t T32) {
     const int lane = threadIdx.x & 31;
     const int64_t rows = B * T * H;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -412,6 +415,11 @@ __global__ void attn_rowdot_kernel(const float* __restrict__ o, const float* __r
         if (lane == 0) {
             const int64_t h = r % H, t = (r / H) % T, b = r / (H * T);
             Dv[(b * H + h) * T + t] = s;
+            if (ld) {
+                float* e = ld + ((b * H + h) * T32 + t) * 2;
+                e[0] = lse[(b * H + h) * T + t] * 1.4426950408889634f;
+                e[1] = s;
+            }
         }
     }
 }
@@ -783,7 +791,7 @@ template <int HD>
 int bwd(const float* q, const float* k, const float* v, const float* cs, const float* sn,
         const float* o, const float* lse, const float* dout, float* dq, float* dk, float* dv,
         int accumulate, int64_t B, int64_t T, int64_t H, float scale, SplitBufs s, float* Dv,
-        bool tc, cudaStream_t st) {
+        float* ld, bool tc, cudaStream_t st) {
     int rc = launch_split(q, cs, sn, 1, scale, s.qh, s.ql, B, T, H, HD, st);
     if (!rc)
         rc = launch_split(k, cs, sn, 1, 1.0f, s.kh, s.kl, B, T, H, HD, st);
@@ -793,13 +801,21 @@ int bwd(const float* q, const float* k, const float* v, const float* cs, const f
         rc = launch_split(dout, cs, sn, 0, 1.0f, s.dh, s.dl, B, T, H, HD, st);
     if (rc)
         return rc;
-    attn_rowdot_kernel<<<grid_for(B * T * H, 8), 256, 0, st>>>(o, dout, Dv, B, T, H, HD);
+    const int64_t T32 = (T + 31) / 32 * 32;
+    if (tc) {
+        rc = check_cuda(cudaMemsetAsync(ld, 0, static_cast<size_t>(B * H * T32) * 8, st),
+                        "attention_bwd: ld table");
+        if (rc)
+            return rc;
+    }
+    attn_rowdot_kernel<<<grid_for(B * T * H, 8), 256, 0, st>>>(o, dout, Dv, B, T, H, HD, lse,
+                                                                tc ? ld : nullptr, T32);
     rc = check_launch("attn_rowdot_kernel");
     if (rc)
         return rc;
     if (tc)
-        return attention_tc_backward_core(HD, s.qh, s.kh, s.vh, s.dh, lse, Dv, cs, sn, dq, dk, dv,
-                                          accumulate, B, T, H, scale, st);
+        return attention_tc_backward_core(HD, s.qh, s.kh, s.vh, s.dh, lse, Dv, ld, T32, cs, sn,
+                                          dq, dk, dv, accumulate, B, T, H, scale, st);
     int smem = DkvSmem<HD>::BYTES;
     cudaFuncSetAttribute(attn_bwd_mma_dkv<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     dim3 g1(static_cast<unsigned>((T + DKV_BK - 1) / DKV_BK), static_cast<unsigned>(B * H));
@@ -847,16 +863,17 @@ int attention_mma_backward(int hd, const float* q, const float* k, const float* 
     __nv_bfloat16* w = reinterpret_cast<__nv_bfloat16*>(
         static_cast<char*>(ws) + ((B * T * H * 4 + 255) / 256) * 256);
     fa::SplitBufs s{w, w + n, w + 2 * n, w + 3 * n, w + 4 * n, w + 5 * n, w + 6 * n, w + 7 * n};
+    float* ld = reinterpret_cast<float*>(w + 8 * n);  // 256-byte aligned: n*16 bytes before it
     switch (hd) {
         case 32:
             return fa::bwd<32>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                               scale, s, Dv, false, st);
+                               scale, s, Dv, ld, false, st);
         case 64:
             return fa::bwd<64>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                               scale, s, Dv, tc, st);
+                               scale, s, Dv, ld, tc, st);
         default:
             return fa::bwd<128>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                                scale, s, Dv, tc, st);
+                                scale, s, Dv, ld, tc, st);
     }
 }
 

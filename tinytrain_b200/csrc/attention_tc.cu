@@ -433,38 +433,55 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ------------------------------------------------------------ backward --
 // Both backward kernels take the split planes of q (rotated, pre-scaled), k
-// (rotated), v and dO, lse [B,H,T] and D = rowsum(dO * O) [B,H,T], and write
-// fp32 gradients in [B,T,H,HD] with the RoPE transpose rotation applied to
-// dq and dk. The small operands produced by the softmax warps (dS for dQ;
-// P^T and dS^T for dV, dK) are fed to the tensor core from TMEM (A operand,
-// row m in lane m, bf16 pairs packed per 32-bit column), which leaves shared
-// memory for 3-slot rings of the streamed tiles.
+// (rotated), v and dO, and write fp32 gradients in [B,T,H,HD] with the RoPE
+// transpose rotation applied to dq and dk. Streamed blocks are 32 rows (keys
+// for dQ, queries for dK/dV). Per block the tensor core computes the score
+// block S (S^T) and dP (dP^T) into one of NBUF TMEM buffers; a softmax warp
+// group reads them and writes the bf16 hi|lo split of dS (of P^T and dS^T)
+// back over the same columns, where the accumulation MMAs take it as their A
+// operand (row m in lane m, bf16 pairs packed per 32-bit column). Two softmax
+// groups of four warps take alternate blocks (one thread per row, all 32
+// columns), and the MMA warp issues the scores of block j before the
+// accumulation of block j - LOOKAHEAD, so the tensor core never waits on the
+// softmax of the block it just produced. dQ, dK and dV accumulate in TMEM
+// over every block.
 // Column ownership in the epilogues: with HH = HD/2 and QW = HD/4, the thread
-// of half h holds columns [h*QW, h*QW + QW) and [HH + h*QW, HH + h*QW + QW),
+// of group g holds columns [g*QW, g*QW + QW) and [HH + g*QW, HH + g*QW + QW),
 // so each RoPE pair (d, d + HH) lives in one thread.
 
-constexpr int BWD_BLK = 32;   // streamed rows (keys for dQ, queries for dK/dV) per block
-constexpr int DQ_CHUNK = 8;   // key blocks summed in TMEM per fold (256 keys)
-constexpr int RING = 3;
+constexpr int BWD_BLK = 32;
+constexpr int NBUF = 4;  // score buffers in TMEM (64 columns each)
+constexpr int GROUP_THREADS = 128;
+// Ring depths and lookahead (blocks between a score MMA and its accumulation
+// MMA, below NBUF). A ring slot is held from its tile's first MMA to its last;
+// each ring leaves about two blocks between a slot's release and its reuse,
+// so the copy into it hides behind the tensor core's work.
+//   dQ:     K held from S_j to dQ_j (lookahead 2) -> 4 slots; V freed after
+//           dP_j -> 2 slots
+//   dK, dV: Q_i and dO_i held from S^T_i to the accumulation (lookahead 1)
+//           -> 3 slots each
+constexpr int DQ_R1 = 4, DQ_R2 = 2, DQ_LOOKAHEAD = 2;
+constexpr int DKV_R1 = 3, DKV_R2 = 3, DKV_LOOKAHEAD = 1;
+static_assert(DKV_R1 == DKV_R2, "the dK/dV kernel indexes both rings with one slot");
+static_assert(DQ_LOOKAHEAD < NBUF && DKV_LOOKAHEAD < NBUF, "a score buffer is reused after its "
+              "accumulation MMA was issued");
+constexpr int LD_BYTES = BWD_BLK * 8;  // (lse * log2 e, D) pairs of one query block
 
-template <int HD>
+template <int HD, int R1, int R2>
 struct BwdCfg {
     static constexpr int NCH = HD / 32;
-    static constexpr int BIG_PLANE = NCH * BQ * 64;       // 128-row tile plane
+    static constexpr int BIG_PLANE = NCH * BQ * 64;         // 128-row tile plane
     static constexpr int BIG_BYTES = 2 * BIG_PLANE;
     static constexpr int SMALL_PLANE = NCH * BWD_BLK * 64;  // 32-row tile plane
     static constexpr int SMALL_BYTES = 2 * SMALL_PLANE;
-    static constexpr int OFF_BIG1 = BIG_BYTES;               // second resident tile
-    static constexpr int OFF_R1 = 2 * BIG_BYTES;             // ring 1 (K | Q)
-    static constexpr int OFF_R2 = OFF_R1 + RING * SMALL_BYTES;  // ring 2 (V | dO)
-    static constexpr int OFF_BAR = OFF_R2 + RING * SMALL_BYTES;
+    static constexpr int OFF_BIG1 = BIG_BYTES;                  // second resident tile
+    static constexpr int OFF_R1 = 2 * BIG_BYTES;                // ring 1 (K | Q)
+    static constexpr int OFF_R2 = OFF_R1 + R1 * SMALL_BYTES;  // ring 2 (V | dO)
+    static constexpr int OFF_LD = OFF_R2 + R2 * SMALL_BYTES;  // ring 1's (lse, D) blocks
+    static constexpr int OFF_BAR = OFF_LD + R1 * LD_BYTES;
     static constexpr int NBARS = 32;
     static constexpr int BYTES = OFF_BAR + 8 * NBARS + 16 + 1024;
-    static constexpr int S_COL = 0;     // 2 x 32: S (dQ) | S^T (dK/dV)
-    static constexpr int DP_COL = 64;   // 2 x 32: dP | dP^T
-    static constexpr int A1_COL = 128;  // dS | P^T: hi 16 cols, lo 16 cols
-    static constexpr int A2_COL = 160;  // dS^T: hi 16, lo 16
-    static constexpr int ACC_COL = 256;  // dQ: 2 chunk buffers x HD | dV (HD), dK (HD)
+    static constexpr int ACC_COL = NBUF * 64;  // dQ (HD) | dV (HD), dK (HD)
     static constexpr int TMEM_COLS = 512;
     static_assert(ACC_COL + 2 * HD <= TMEM_COLS, "TMEM budget");
     static_assert(BYTES <= 232448, "shared memory budget");
@@ -476,34 +493,22 @@ __device__ __forceinline__ uint64_t small_mn_desc(uint32_t plane, int ks) {
     return umma_smem_desc(plane + ks * 1024, BWD_BLK * 64, 512, kSW64);
 }
 
-// p and dS for 16 scores of one row / column set, split into packed bf16 hi|lo.
-__device__ __forceinline__ void split16(const float (&x)[16], uint32_t (&hi)[8],
-                                        uint32_t (&lo)[8]) {
-#pragma unroll
-    for (int e = 0; e < 16; e += 2) {
-        const __nv_bfloat16 h0 = __float2bfloat16_rn(x[e]), h1 = __float2bfloat16_rn(x[e + 1]);
-        hi[e / 2] = pack_bf16x2(h0, h1);
-        lo[e / 2] = pack_bf16x2(__float2bfloat16_rn(x[e] - __bfloat162float(h0)),
-                                __float2bfloat16_rn(x[e + 1] - __bfloat162float(h1)));
-    }
-}
-
 // Load this thread's 2*QW accumulator columns (see column ownership above).
 template <int HD>
-__device__ __forceinline__ void load_owned(uint32_t taddr, int half, float (&v)[HD / 2]) {
+__device__ __forceinline__ void load_owned(uint32_t taddr, int grp, float (&v)[HD / 2]) {
     constexpr int QW = HD / 4, HH = HD / 2;
     if constexpr (QW == 32) {
         float a[32], b[32];
-        tmem_ld_32x32b_x32(taddr + half * QW, a);
-        tmem_ld_32x32b_x32(taddr + HH + half * QW, b);
+        tmem_ld_32x32b_x32(taddr + grp * QW, a);
+        tmem_ld_32x32b_x32(taddr + HH + grp * QW, b);
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 32; ++e)
             v[e] = a[e], v[QW + e] = b[e];
     } else {
         float a[16], b[16];
-        tmem_ld_32x32b_x16(taddr + half * QW, a);
-        tmem_ld_32x32b_x16(taddr + HH + half * QW, b);
+        tmem_ld_32x32b_x16(taddr + grp * QW, a);
+        tmem_ld_32x32b_x16(taddr + HH + grp * QW, b);
         tmem_ld_wait();
 #pragma unroll
         for (int e = 0; e < 16; ++e)
@@ -517,21 +522,23 @@ template <int HD>
 __device__ __forceinline__ void store_owned(const float (&g)[HD / 2], float* __restrict__ row,
                                             int64_t t, const float* __restrict__ cs,
                                             const float* __restrict__ sn, bool rope, float scale,
-                                            int half, int accumulate) {
+                                            int grp, int accumulate) {
     constexpr int QW = HD / 4, HH = HD / 2;
 #pragma unroll
     for (int e = 0; e < QW; e += 4) {
-        const int d = half * QW + e;
+        const int d = grp * QW + e;
         float a[4], b[4];
+        float4 c4 = make_float4(1.f, 1.f, 1.f, 1.f), s4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (rope) {
+            c4 = __ldg(reinterpret_cast<const float4*>(cs + t * HH + d));
+            s4 = __ldg(reinterpret_cast<const float4*>(sn + t * HH + d));
+        }
+        const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            float g1 = g[e + u] * scale, g2 = g[QW + e + u] * scale;
-            if (rope) {
-                const float c = cs[t * HH + d + u], s = sn[t * HH + d + u];
-                const float r1 = g1 * c + g2 * s, r2 = -g1 * s + g2 * c;
-                g1 = r1, g2 = r2;
-            }
-            a[u] = g1, b[u] = g2;
+            const float g1 = g[e + u] * scale, g2 = g[QW + e + u] * scale;
+            a[u] = rope ? g1 * cc[u] + g2 * ss[u] : g1;
+            b[u] = rope ? -g1 * ss[u] + g2 * cc[u] : g2;
         }
         float4* p1 = reinterpret_cast<float4*>(row + d);
         float4* p2 = reinterpret_cast<float4*>(row + HH + d);
@@ -545,10 +552,18 @@ __device__ __forceinline__ void store_owned(const float (&g)[HD / 2], float* __r
     }
 }
 
+// Packed bf16 hi|lo of 32 values: hi[i], lo[i] hold elements 2i, 2i+1.
+__device__ __forceinline__ void split32(const float (&x)[32], uint32_t (&hi)[16],
+                                        uint32_t (&lo)[16]) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+        split_pair_bf16(x[2 * i], x[2 * i + 1], hi[i], lo[i]);
+}
+
 // dQ: CTA = 128 query rows of one (b, h); key blocks of 32 up to the diagonal.
-//   S_j = Q K_j^T, dP_j = dO V_j^T (TMEM, double-buffered), dS_j = P (dP - D)
-//   written to TMEM by the softmax warps, dQ += dS_j K_j into a TMEM chunk
-//   buffer; every 8 blocks the chunk is folded into fp32 registers.
+//   S_j = Q K_j^T (buffer cols [0,32)), dP_j = dO V_j^T ([32,64)); the
+//   softmax group writes dS_j = P (dP - D) split over S_j's columns
+//   (hi [0,16), lo [16,32)); dQ += dS_j K_j.
 template <int HD>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_bwd_dq_tc(const __grid_constant__ CUtensorMap map_q,
@@ -558,7 +573,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    const float* __restrict__ Dv, const float* __restrict__ cs,
                    const float* __restrict__ sn, float* __restrict__ dq, int accumulate,
                    float scale, int64_t T, int H) {
-    using CF = BwdCfg<HD>;
+    using CF = BwdCfg<HD, DQ_R1, DQ_R2>;
     constexpr int HH = HD / 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -566,15 +581,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CF::OFF_BAR);
     uint64_t* a_full = bars;
     uint64_t* kfull = bars + 1;
-    uint64_t* kempty = kfull + RING;
-    uint64_t* vfull = kempty + RING;
-    uint64_t* vempty = vfull + RING;
-    uint64_t* sd_full = vempty + RING;  // [2]
-    uint64_t* ds_full = sd_full + 2;
-    uint64_t* ds_free = ds_full + 1;
-    uint64_t* c_full = ds_free + 1;  // [2]
-    uint64_t* c_free = c_full + 2;   // [2]
-    uint64_t* done = c_free + 2;
+    uint64_t* kempty = kfull + DQ_R1;
+    uint64_t* vfull = kempty + DQ_R1;
+    uint64_t* vempty = vfull + DQ_R2;
+    uint64_t* sd_full = vempty + DQ_R2;  // [NBUF]
+    uint64_t* ds_full = sd_full + NBUF;  // [NBUF]
+    uint64_t* done = ds_full + NBUF;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + CF::NBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -588,19 +600,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(a_full, 1);
-        for (int i = 0; i < RING; ++i) {
+        for (int i = 0; i < DQ_R1; ++i) {
             mbar_init(&kfull[i], 1);
             mbar_init(&kempty[i], 1);
+        }
+        for (int i = 0; i < DQ_R2; ++i) {
             mbar_init(&vfull[i], 1);
             mbar_init(&vempty[i], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NBUF; ++b) {
             mbar_init(&sd_full[b], 1);
-            mbar_init(&c_full[b], 1);
-            mbar_init(&c_free[b], SOFTMAX_THREADS);
+            mbar_init(&ds_full[b], GROUP_THREADS);
         }
-        mbar_init(ds_full, SOFTMAX_THREADS);
-        mbar_init(ds_free, 1);
         mbar_init(done, 1);
         *abort_flag = 0;
         fence_barrier_init();
@@ -624,45 +635,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
         if (lane == 0) {
-            int karmed[RING], varmed[RING];
+            int karmed[DQ_R1], varmed[DQ_R2];
 #pragma unroll
-            for (int i = 0; i < RING; ++i)
-                karmed[i] = varmed[i] = -1;
+            for (int i = 0; i < DQ_R1; ++i)
+                karmed[i] = -1;
+#pragma unroll
+            for (int i = 0; i < DQ_R2; ++i)
+                varmed[i] = -1;
             mbar_arrive_expect_tx(a_full, 2 * CF::BIG_BYTES);
             tma_load_5d(smem, &map_q, a_full, 0, static_cast<int>(q0), 0, static_cast<int>(bh), 0);
             tma_load_5d(smem + CF::OFF_BIG1, &map_do, a_full, 0, static_cast<int>(q0), 0,
                         static_cast<int>(bh), 0);
             bool ok = true;
             for (int j = 0; j < nblk && ok; ++j) {
-                const int slot = j % RING;
-                const uint32_t ph = static_cast<uint32_t>((j / RING) & 1);
-                if (*abort_flag || !mbar_wait(&kempty[slot], ph ^ 1, 41)) {
+                const int ks_ = j % DQ_R1, vs_ = j % DQ_R2;
+                const uint32_t kph = static_cast<uint32_t>((j / DQ_R1) & 1);
+                const uint32_t vph = static_cast<uint32_t>((j / DQ_R2) & 1);
+                if (*abort_flag || !mbar_wait(&kempty[ks_], kph ^ 1, 41)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&kfull[slot], CF::SMALL_BYTES);
-                tma_load_5d(smem + CF::OFF_R1 + slot * CF::SMALL_BYTES, &map_k, &kfull[slot], 0,
+                mbar_arrive_expect_tx(&kfull[ks_], CF::SMALL_BYTES);
+                tma_load_5d(smem + CF::OFF_R1 + ks_ * CF::SMALL_BYTES, &map_k, &kfull[ks_], 0,
                             j * BWD_BLK, 0, static_cast<int>(bh), 0);
-                karmed[slot] = static_cast<int>(ph);
-                if (*abort_flag || !mbar_wait(&vempty[slot], ph ^ 1, 42)) {
+                karmed[ks_] = static_cast<int>(kph);
+                if (*abort_flag || !mbar_wait(&vempty[vs_], vph ^ 1, 42)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&vfull[slot], CF::SMALL_BYTES);
-                tma_load_5d(smem + CF::OFF_R2 + slot * CF::SMALL_BYTES, &map_v, &vfull[slot], 0,
+                mbar_arrive_expect_tx(&vfull[vs_], CF::SMALL_BYTES);
+                tma_load_5d(smem + CF::OFF_R2 + vs_ * CF::SMALL_BYTES, &map_v, &vfull[vs_], 0,
                             j * BWD_BLK, 0, static_cast<int>(bh), 0);
-                varmed[slot] = static_cast<int>(ph);
+                varmed[vs_] = static_cast<int>(vph);
             }
             if (!ok) {
                 *abort_flag = 1;
                 mbar_wait(a_full, 0, 46);
 #pragma unroll
-                for (int i = 0; i < RING; ++i) {
+                for (int i = 0; i < DQ_R1; ++i)
                     if (karmed[i] >= 0)
                         mbar_wait(&kfull[i], static_cast<uint32_t>(karmed[i]), 46);
+#pragma unroll
+                for (int i = 0; i < DQ_R2; ++i)
                     if (varmed[i] >= 0)
                         mbar_wait(&vfull[i], static_cast<uint32_t>(varmed[i]), 46);
-                }
             }
         }
     } else if (warp == 1) {
@@ -670,148 +686,121 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) {
             constexpr uint32_t idesc_sd = umma_idesc_bf16(BQ, BWD_BLK, 0, 0);
             constexpr uint32_t idesc_q = umma_idesc_bf16(BQ, HD, 0, 1);
-            const uint32_t sQ = s_base, sDO = s_base + CF::OFF_BIG1;
+            const uint64_t qh0 = kmajor_desc(s_base, BQ, 0);
+            const uint64_t ql0 = kmajor_desc(s_base + CF::BIG_PLANE, BQ, 0);
+            const uint64_t oh0 = kmajor_desc(s_base + CF::OFF_BIG1, BQ, 0);
+            const uint64_t ol0 = kmajor_desc(s_base + CF::OFF_BIG1 + CF::BIG_PLANE, BQ, 0);
+            const uint32_t dQ = tmem + CF::ACC_COL;
             bool ok = mbar_wait(a_full, 0, 43);
             auto issue_dq = [&](int i) -> bool {
-                const int c = i / DQ_CHUNK;
-                const bool first = (i % DQ_CHUNK) == 0;
-                if (first && c >= 2 &&
-                    (*abort_flag || !mbar_wait(&c_free[c & 1], ((c - 2) >> 1) & 1, 44)))
-                    return false;
-                if (*abort_flag || !mbar_wait(ds_full, i & 1, 45))
+                const int b = i % NBUF;
+                if (*abort_flag || !mbar_wait(&ds_full[b], (i / NBUF) & 1, 45))
                     return false;
                 tc_fence_after();
-                const uint32_t d = tmem + CF::ACC_COL + (c & 1) * HD;
-                const uint32_t sK = s_base + CF::OFF_R1 + (i % RING) * CF::SMALL_BYTES;
+                const uint32_t sK = s_base + CF::OFF_R1 + (i % DQ_R1) * CF::SMALL_BYTES;
+                const uint64_t kh = small_mn_desc(sK, 0), kl = small_mn_desc(sK + CF::SMALL_PLANE, 0);
+                const uint32_t a = tmem + b * 64;
 #pragma unroll
                 for (int ks = 0; ks < BWD_BLK / 16; ++ks) {
-                    const uint32_t a_hi = tmem + CF::A1_COL + ks * 8;
-                    const uint32_t a_lo = tmem + CF::A1_COL + 16 + ks * 8;
-                    const uint64_t b_hi = small_mn_desc(sK, ks);
-                    const uint64_t b_lo = small_mn_desc(sK + CF::SMALL_PLANE, ks);
-                    mma_bf16_ta(d, a_lo, b_hi, idesc_q, (first && ks == 0) ? 0u : 1u);
-                    mma_bf16_ta(d, a_hi, b_lo, idesc_q, 1u);
-                    mma_bf16_ta(d, a_hi, b_hi, idesc_q, 1u);
+                    const uint64_t bh_ = desc_add(kh, ks * 1024), bl_ = desc_add(kl, ks * 1024);
+                    mma_bf16_ta(dQ, a + 16 + ks * 8, bh_, idesc_q, (i == 0 && ks == 0) ? 0u : 1u);
+                    mma_bf16_ta(dQ, a + ks * 8, bl_, idesc_q, 1u);
+                    mma_bf16_ta(dQ, a + ks * 8, bh_, idesc_q, 1u);
                 }
-                mma_commit(ds_free);
-                mma_commit(&kempty[i % RING]);
-                if ((i % DQ_CHUNK) == DQ_CHUNK - 1 || i == nblk - 1)
-                    mma_commit(&c_full[c & 1]);
+                mma_commit(&kempty[i % DQ_R1]);
                 return true;
             };
             for (int j = 0; j < nblk && ok; ++j) {
-                const int slot = j % RING;
-                const uint32_t ph = static_cast<uint32_t>((j / RING) & 1);
-                if (*abort_flag || !mbar_wait(&kfull[slot], ph, 47) ||
-                    !mbar_wait(&vfull[slot], ph, 48)) {
+                const int ks_ = j % DQ_R1, vs_ = j % DQ_R2;
+                if (*abort_flag || !mbar_wait(&kfull[ks_], (j / DQ_R1) & 1, 47) ||
+                    !mbar_wait(&vfull[vs_], (j / DQ_R2) & 1, 48)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t sK = s_base + CF::OFF_R1 + slot * CF::SMALL_BYTES;
-                const uint32_t sV = s_base + CF::OFF_R2 + slot * CF::SMALL_BYTES;
-                const uint32_t ds = tmem + CF::S_COL + (j & 1) * BWD_BLK;
-                const uint32_t dp = tmem + CF::DP_COL + (j & 1) * BWD_BLK;
+                const uint32_t sK = s_base + CF::OFF_R1 + ks_ * CF::SMALL_BYTES;
+                const uint32_t sV = s_base + CF::OFF_R2 + vs_ * CF::SMALL_BYTES;
+                const uint64_t kh0 = kmajor_desc(sK, BWD_BLK, 0);
+                const uint64_t kl0 = kmajor_desc(sK + CF::SMALL_PLANE, BWD_BLK, 0);
+                const uint64_t vh0 = kmajor_desc(sV, BWD_BLK, 0);
+                const uint64_t vl0 = kmajor_desc(sV + CF::SMALL_PLANE, BWD_BLK, 0);
+                const uint32_t ds = tmem + (j % NBUF) * 64, dp = ds + 32;
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ++ks) {
-                    const uint64_t qh_ = kmajor_desc(sQ, BQ, ks);
-                    const uint64_t ql_ = kmajor_desc(sQ + CF::BIG_PLANE, BQ, ks);
-                    const uint64_t kh_ = kmajor_desc(sK, BWD_BLK, ks);
-                    const uint64_t kl_ = kmajor_desc(sK + CF::SMALL_PLANE, BWD_BLK, ks);
+                    const uint32_t ob = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
+                    const uint32_t sb = (ks >> 1) * (BWD_BLK * 64) + (ks & 1) * 32;
                     const uint32_t acc = ks > 0 ? 1u : 0u;
-                    mma_bf16(ds, ql_, kh_, idesc_sd, acc);
-                    mma_bf16(ds, qh_, kl_, idesc_sd, 1u);
-                    mma_bf16(ds, qh_, kh_, idesc_sd, 1u);
-                    const uint64_t oh_ = kmajor_desc(sDO, BQ, ks);
-                    const uint64_t ol_ = kmajor_desc(sDO + CF::BIG_PLANE, BQ, ks);
-                    const uint64_t vh_ = kmajor_desc(sV, BWD_BLK, ks);
-                    const uint64_t vl_ = kmajor_desc(sV + CF::SMALL_PLANE, BWD_BLK, ks);
-                    mma_bf16(dp, ol_, vh_, idesc_sd, acc);
-                    mma_bf16(dp, oh_, vl_, idesc_sd, 1u);
-                    mma_bf16(dp, oh_, vh_, idesc_sd, 1u);
+                    mma_bf16(ds, desc_add(ql0, ob), desc_add(kh0, sb), idesc_sd, acc);
+                    mma_bf16(dp, desc_add(ol0, ob), desc_add(vh0, sb), idesc_sd, acc);
+                    mma_bf16(ds, desc_add(qh0, ob), desc_add(kl0, sb), idesc_sd, 1u);
+                    mma_bf16(dp, desc_add(oh0, ob), desc_add(vl0, sb), idesc_sd, 1u);
+                    mma_bf16(ds, desc_add(qh0, ob), desc_add(kh0, sb), idesc_sd, 1u);
+                    mma_bf16(dp, desc_add(oh0, ob), desc_add(vh0, sb), idesc_sd, 1u);
                 }
-                mma_commit(&sd_full[j & 1]);
-                mma_commit(&vempty[slot]);
-                if (j >= 1 && !issue_dq(j - 1))
+                mma_commit(&sd_full[j % NBUF]);
+                mma_commit(&vempty[vs_]);
+                if (j >= DQ_LOOKAHEAD && !issue_dq(j - DQ_LOOKAHEAD))
                     ok = false;
             }
-            if (ok && !issue_dq(nblk - 1))
-                ok = false;
+            for (int i = max(0, nblk - DQ_LOOKAHEAD); i < nblk && ok; ++i)
+                if (!issue_dq(i))
+                    ok = false;
             if (!ok)
                 *abort_flag = 1;
+            // fires once every MMA issued has retired (also on abort)
             mma_commit(done);
             mbar_wait(done, 0, 49);
         }
     } else {
         // --------------------------------------------------- softmax / dS
+        const int grp = (warp - 2) >> 2;  // blocks j with j % 2 == grp
         const int quad = warp & 3;
-        const int half = (warp - 2) >> 2;  // key columns [half*16, +16) of each block
         const int r = quad * 32 + lane;
         const int64_t q = q0 + r;
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
         const float lse2 = q < T ? lse[bh * T + q] * LOG2E : 0.0f;
         const float Dq = q < T ? Dv[bh * T + q] : 0.0f;
-        float acc[HH];
-#pragma unroll
-        for (int e = 0; e < HH; ++e)
-            acc[e] = 0.0f;
         bool ok = true;
-        auto fold = [&](int c) -> bool {
-            if (*abort_flag || !mbar_wait(&c_full[c & 1], (c >> 1) & 1, 50))
-                return false;
-            tc_fence_after();
-            float v[HH];
-            load_owned<HD>(tmem + lane_off + CF::ACC_COL + (c & 1) * HD, half, v);
-#pragma unroll
-            for (int e = 0; e < HH; ++e)
-                acc[e] += v[e];
-            tc_fence_before();
-            mbar_arrive(&c_free[c & 1]);
-            return true;
-        };
-        for (int j = 0; j < nblk; ++j) {
-            if (*abort_flag || !mbar_wait(&sd_full[j & 1], (j >> 1) & 1, 51)) {
+        for (int j = grp; j < nblk; j += 2) {
+            const int b = j % NBUF;
+            if (*abort_flag || !mbar_wait(&sd_full[b], (j / NBUF) & 1, 51)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float sv[16], dpv[16];
-            tmem_ld_32x32b_x16(tmem + lane_off + CF::S_COL + (j & 1) * BWD_BLK + half * 16, sv);
-            tmem_ld_32x32b_x16(tmem + lane_off + CF::DP_COL + (j & 1) * BWD_BLK + half * 16, dpv);
+            float sv[32], dpv[32];
+            tmem_ld_32x32b_x32(tmem + lane_off + b * 64, sv);
+            tmem_ld_32x32b_x32(tmem + lane_off + b * 64 + 32, dpv);
             tmem_ld_wait();
-            const int64_t k0 = static_cast<int64_t>(j) * BWD_BLK + half * 16;
+            const int64_t k0 = static_cast<int64_t>(j) * BWD_BLK;
+            const bool diag = k0 + BWD_BLK - 1 > q0;
 #pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const bool live = k0 + e <= q && q < T;
-                const float p = live ? exp2f(fmaf(sv[e], LOG2E, -lse2)) : 0.0f;
+            for (int e = 0; e < 32; ++e) {
+                const bool live = q < T && (!diag || k0 + e <= q);
+                const float p = live ? exp2_approx(fmaf(sv[e], LOG2E, -lse2)) : 0.0f;
                 sv[e] = p * (dpv[e] - Dq);
             }
-            uint32_t hi[8], lo[8];
-            split16(sv, hi, lo);
-            // dS buffer: free once the previous block's dQ MMAs have read it
-            if (j >= 1 && (*abort_flag || !mbar_wait(ds_free, (j - 1) & 1, 52))) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            tmem_st_32x32b_x8(tmem + lane_off + CF::A1_COL + half * 8, hi);
-            tmem_st_32x32b_x8(tmem + lane_off + CF::A1_COL + 16 + half * 8, lo);
+            uint32_t hi[16], lo[16];
+            split32(sv, hi, lo);
+            tmem_st_32x32b_x16(tmem + lane_off + b * 64, hi);
+            tmem_st_32x32b_x16(tmem + lane_off + b * 64 + 16, lo);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(ds_full);
-            if (j >= 1 && ((j - 1) % DQ_CHUNK) == DQ_CHUNK - 1 && !fold((j - 1) / DQ_CHUNK)) {
-                ok = false;
-                break;
-            }
+            mbar_arrive(&ds_full[b]);
         }
-        if (ok)
-            ok = fold((nblk - 1) / DQ_CHUNK);
+        if (ok && (*abort_flag || !mbar_wait(done, 0, 52)))
+            ok = false;
         if (!ok) {
             *abort_flag = 1;
-        } else if (q < T) {
-            const int64_t b = bh / H, h = bh % H;
-            store_owned<HD>(acc, dq + ((b * T + q) * H + h) * HD, q, cs, sn, true, scale, half,
-                            accumulate);
+        } else {
+            tc_fence_after();
+            float g[HH];
+            load_owned<HD>(tmem + lane_off + CF::ACC_COL, grp, g);
+            if (q < T) {
+                const int64_t b = bh / H, h = bh % H;
+                store_owned<HD>(g, dq + ((b * T + q) * H + h) * HD, q, cs, sn, true, scale, grp,
+                                accumulate);
+            }
         }
     }
 
@@ -824,19 +813,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 }
 
 // dK, dV: CTA = 128 keys of one (b, h); query blocks of 32 from the diagonal.
-//   S^T_i = K Q_i^T, dP^T_i = V dO_i^T (TMEM, double-buffered); the softmax
-//   warps write P^T and dS^T = P^T (dP^T - D) to TMEM; dV += P^T dO_i and
-//   dK += dS^T Q_i accumulate in TMEM over every query block.
+//   S^T_i = K Q_i^T (buffer cols [0,32)), dP^T_i = V dO_i^T ([32,64)); the
+//   softmax group writes P^T over S^T (hi [0,16), lo [16,32)) and dS^T =
+//   P^T (dP^T - D) over dP^T ([32,48), [48,64)); dV += P^T dO_i, dK += dS^T Q_i.
+//   lse (pre-multiplied by log2 e) and D of each query block arrive with Q_i
+//   by a bulk copy from the padded (lse, D) table `ld` [B*H][T32][2].
 template <int HD>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_bwd_dkv_tc(const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v,
                     const __grid_constant__ CUtensorMap map_q,
-                    const __grid_constant__ CUtensorMap map_do, const float* __restrict__ lse,
-                    const float* __restrict__ Dv, const float* __restrict__ cs,
-                    const float* __restrict__ sn, float* __restrict__ dk, float* __restrict__ dv,
-                    int accumulate, int64_t T, int H) {
-    using CF = BwdCfg<HD>;
+                    const __grid_constant__ CUtensorMap map_do, const float* __restrict__ ld,
+                    int64_t T32, const float* __restrict__ cs, const float* __restrict__ sn,
+                    float* __restrict__ dk, float* __restrict__ dv, int accumulate, int64_t T,
+                    int H) {
+    using CF = BwdCfg<HD, DKV_R1, DKV_R2>;
     constexpr int HH = HD / 2;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -844,13 +835,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CF::OFF_BAR);
     uint64_t* a_full = bars;
     uint64_t* qfull = bars + 1;
-    uint64_t* qempty = qfull + RING;
-    uint64_t* ofull = qempty + RING;
-    uint64_t* oempty = ofull + RING;
-    uint64_t* sd_full = oempty + RING;  // [2]
-    uint64_t* pds_full = sd_full + 2;
-    uint64_t* pds_free = pds_full + 1;
-    uint64_t* acc_full = pds_free + 1;
+    uint64_t* qempty = qfull + DKV_R1;
+    uint64_t* ofull = qempty + DKV_R1;
+    uint64_t* oempty = ofull + DKV_R1;
+    uint64_t* sd_full = oempty + DKV_R1;    // [NBUF]
+    uint64_t* pds_full = sd_full + NBUF;  // [NBUF]
+    uint64_t* done = pds_full + NBUF;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + CF::NBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -862,17 +852,17 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
     if (threadIdx.x == 0) {
         mbar_init(a_full, 1);
-        for (int i = 0; i < RING; ++i) {
+        for (int i = 0; i < DKV_R1; ++i) {
             mbar_init(&qfull[i], 1);
             mbar_init(&qempty[i], 1);
             mbar_init(&ofull[i], 1);
             mbar_init(&oempty[i], 1);
         }
-        for (int b = 0; b < 2; ++b)
+        for (int b = 0; b < NBUF; ++b) {
             mbar_init(&sd_full[b], 1);
-        mbar_init(pds_full, SOFTMAX_THREADS);
-        mbar_init(pds_free, 1);
-        mbar_init(acc_full, 1);
+            mbar_init(&pds_full[b], GROUP_THREADS);
+        }
+        mbar_init(done, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -895,9 +885,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
         if (lane == 0) {
-            int qarmed[RING], oarmed[RING];
+            int qarmed[DKV_R1], oarmed[DKV_R1];
 #pragma unroll
-            for (int i = 0; i < RING; ++i)
+            for (int i = 0; i < DKV_R1; ++i)
                 qarmed[i] = oarmed[i] = -1;
             mbar_arrive_expect_tx(a_full, 2 * CF::BIG_BYTES);
             tma_load_5d(smem, &map_k, a_full, 0, static_cast<int>(k0), 0, static_cast<int>(bh), 0);
@@ -905,16 +895,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         static_cast<int>(bh), 0);
             bool ok = true;
             for (int n = 0; n < nblk && ok; ++n) {
-                const int slot = n % RING;
-                const uint32_t ph = static_cast<uint32_t>((n / RING) & 1);
+                const int slot = n % DKV_R1;
+                const uint32_t ph = static_cast<uint32_t>((n / DKV_R1) & 1);
                 const int row = (i_first + n) * BWD_BLK;
                 if (*abort_flag || !mbar_wait(&qempty[slot], ph ^ 1, 61)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&qfull[slot], CF::SMALL_BYTES);
+                mbar_arrive_expect_tx(&qfull[slot], CF::SMALL_BYTES + LD_BYTES);
                 tma_load_5d(smem + CF::OFF_R1 + slot * CF::SMALL_BYTES, &map_q, &qfull[slot], 0,
                             row, 0, static_cast<int>(bh), 0);
+                bulk_load(smem + CF::OFF_LD + slot * LD_BYTES, ld + (bh * T32 + row) * 2,
+                          LD_BYTES, &qfull[slot]);
                 qarmed[slot] = static_cast<int>(ph);
                 if (*abort_flag || !mbar_wait(&oempty[slot], ph ^ 1, 62)) {
                     ok = false;
@@ -929,7 +921,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 *abort_flag = 1;
                 mbar_wait(a_full, 0, 66);
 #pragma unroll
-                for (int i = 0; i < RING; ++i) {
+                for (int i = 0; i < DKV_R1; ++i) {
                     if (qarmed[i] >= 0)
                         mbar_wait(&qfull[i], static_cast<uint32_t>(qarmed[i]), 66);
                     if (oarmed[i] >= 0)
@@ -942,42 +934,41 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (lane == 0) {
             constexpr uint32_t idesc_sd = umma_idesc_bf16(BQ, BWD_BLK, 0, 0);
             constexpr uint32_t idesc_acc = umma_idesc_bf16(BQ, HD, 0, 1);
-            const uint32_t sK = s_base, sV = s_base + CF::OFF_BIG1;
+            const uint64_t kh0 = kmajor_desc(s_base, BQ, 0);
+            const uint64_t kl0 = kmajor_desc(s_base + CF::BIG_PLANE, BQ, 0);
+            const uint64_t vh0 = kmajor_desc(s_base + CF::OFF_BIG1, BQ, 0);
+            const uint64_t vl0 = kmajor_desc(s_base + CF::OFF_BIG1 + CF::BIG_PLANE, BQ, 0);
+            const uint32_t dV = tmem + CF::ACC_COL, dK = tmem + CF::ACC_COL + HD;
             bool ok = mbar_wait(a_full, 0, 63);
             auto issue_acc = [&](int i) -> bool {
-                if (*abort_flag || !mbar_wait(pds_full, i & 1, 64))
+                const int b = i % NBUF;
+                if (*abort_flag || !mbar_wait(&pds_full[b], (i / NBUF) & 1, 64))
                     return false;
                 tc_fence_after();
-                const int slot = i % RING;
+                const int slot = i % DKV_R1;
                 const uint32_t sQ = s_base + CF::OFF_R1 + slot * CF::SMALL_BYTES;
                 const uint32_t sO = s_base + CF::OFF_R2 + slot * CF::SMALL_BYTES;
-                const uint32_t dV = tmem + CF::ACC_COL, dK = tmem + CF::ACC_COL + HD;
+                const uint64_t qh = small_mn_desc(sQ, 0), ql = small_mn_desc(sQ + CF::SMALL_PLANE, 0);
+                const uint64_t oh = small_mn_desc(sO, 0), ol = small_mn_desc(sO + CF::SMALL_PLANE, 0);
+                const uint32_t p = tmem + b * 64, d = p + 32;
 #pragma unroll
                 for (int ks = 0; ks < BWD_BLK / 16; ++ks) {
                     const uint32_t first = (i == 0 && ks == 0) ? 0u : 1u;
-                    const uint32_t p_hi = tmem + CF::A1_COL + ks * 8;
-                    const uint32_t p_lo = tmem + CF::A1_COL + 16 + ks * 8;
-                    const uint32_t s_hi = tmem + CF::A2_COL + ks * 8;
-                    const uint32_t s_lo = tmem + CF::A2_COL + 16 + ks * 8;
-                    const uint64_t o_hi = small_mn_desc(sO, ks);
-                    const uint64_t o_lo = small_mn_desc(sO + CF::SMALL_PLANE, ks);
-                    const uint64_t q_hi = small_mn_desc(sQ, ks);
-                    const uint64_t q_lo = small_mn_desc(sQ + CF::SMALL_PLANE, ks);
-                    mma_bf16_ta(dV, p_lo, o_hi, idesc_acc, first);
-                    mma_bf16_ta(dK, s_lo, q_hi, idesc_acc, first);
-                    mma_bf16_ta(dV, p_hi, o_lo, idesc_acc, 1u);
-                    mma_bf16_ta(dK, s_hi, q_lo, idesc_acc, 1u);
-                    mma_bf16_ta(dV, p_hi, o_hi, idesc_acc, 1u);
-                    mma_bf16_ta(dK, s_hi, q_hi, idesc_acc, 1u);
+                    const uint32_t o = ks * 1024;
+                    mma_bf16_ta(dV, p + 16 + ks * 8, desc_add(oh, o), idesc_acc, first);
+                    mma_bf16_ta(dK, d + 16 + ks * 8, desc_add(qh, o), idesc_acc, first);
+                    mma_bf16_ta(dV, p + ks * 8, desc_add(ol, o), idesc_acc, 1u);
+                    mma_bf16_ta(dK, d + ks * 8, desc_add(ql, o), idesc_acc, 1u);
+                    mma_bf16_ta(dV, p + ks * 8, desc_add(oh, o), idesc_acc, 1u);
+                    mma_bf16_ta(dK, d + ks * 8, desc_add(qh, o), idesc_acc, 1u);
                 }
-                mma_commit(pds_free);
                 mma_commit(&qempty[slot]);
                 mma_commit(&oempty[slot]);
                 return true;
             };
             for (int n = 0; n < nblk && ok; ++n) {
-                const int slot = n % RING;
-                const uint32_t ph = static_cast<uint32_t>((n / RING) & 1);
+                const int slot = n % DKV_R1;
+                const uint32_t ph = static_cast<uint32_t>((n / DKV_R1) & 1);
                 if (*abort_flag || !mbar_wait(&qfull[slot], ph, 67) ||
                     !mbar_wait(&ofull[slot], ph, 68)) {
                     ok = false;
@@ -986,86 +977,86 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 tc_fence_after();
                 const uint32_t sQ = s_base + CF::OFF_R1 + slot * CF::SMALL_BYTES;
                 const uint32_t sO = s_base + CF::OFF_R2 + slot * CF::SMALL_BYTES;
-                const uint32_t ds = tmem + CF::S_COL + (n & 1) * BWD_BLK;
-                const uint32_t dp = tmem + CF::DP_COL + (n & 1) * BWD_BLK;
+                const uint64_t qh0 = kmajor_desc(sQ, BWD_BLK, 0);
+                const uint64_t ql0 = kmajor_desc(sQ + CF::SMALL_PLANE, BWD_BLK, 0);
+                const uint64_t oh0 = kmajor_desc(sO, BWD_BLK, 0);
+                const uint64_t ol0 = kmajor_desc(sO + CF::SMALL_PLANE, BWD_BLK, 0);
+                const uint32_t ds = tmem + (n % NBUF) * 64, dp = ds + 32;
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ++ks) {
-                    const uint64_t kh_ = kmajor_desc(sK, BQ, ks);
-                    const uint64_t kl_ = kmajor_desc(sK + CF::BIG_PLANE, BQ, ks);
-                    const uint64_t qh_ = kmajor_desc(sQ, BWD_BLK, ks);
-                    const uint64_t ql_ = kmajor_desc(sQ + CF::SMALL_PLANE, BWD_BLK, ks);
+                    const uint32_t bb = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
+                    const uint32_t sb = (ks >> 1) * (BWD_BLK * 64) + (ks & 1) * 32;
                     const uint32_t acc = ks > 0 ? 1u : 0u;
-                    mma_bf16(ds, kl_, qh_, idesc_sd, acc);
-                    mma_bf16(ds, kh_, ql_, idesc_sd, 1u);
-                    mma_bf16(ds, kh_, qh_, idesc_sd, 1u);
-                    const uint64_t vh_ = kmajor_desc(sV, BQ, ks);
-                    const uint64_t vl_ = kmajor_desc(sV + CF::BIG_PLANE, BQ, ks);
-                    const uint64_t oh_ = kmajor_desc(sO, BWD_BLK, ks);
-                    const uint64_t ol_ = kmajor_desc(sO + CF::SMALL_PLANE, BWD_BLK, ks);
-                    mma_bf16(dp, vl_, oh_, idesc_sd, acc);
-                    mma_bf16(dp, vh_, ol_, idesc_sd, 1u);
-                    mma_bf16(dp, vh_, oh_, idesc_sd, 1u);
+                    mma_bf16(ds, desc_add(kl0, bb), desc_add(qh0, sb), idesc_sd, acc);
+                    mma_bf16(dp, desc_add(vl0, bb), desc_add(oh0, sb), idesc_sd, acc);
+                    mma_bf16(ds, desc_add(kh0, bb), desc_add(ql0, sb), idesc_sd, 1u);
+                    mma_bf16(dp, desc_add(vh0, bb), desc_add(ol0, sb), idesc_sd, 1u);
+                    mma_bf16(ds, desc_add(kh0, bb), desc_add(qh0, sb), idesc_sd, 1u);
+                    mma_bf16(dp, desc_add(vh0, bb), desc_add(oh0, sb), idesc_sd, 1u);
                 }
-                mma_commit(&sd_full[n & 1]);
-                if (n >= 1 && !issue_acc(n - 1))
+                mma_commit(&sd_full[n % NBUF]);
+                if (n >= DKV_LOOKAHEAD && !issue_acc(n - DKV_LOOKAHEAD))
                     ok = false;
             }
-            if (ok && !issue_acc(nblk - 1))
-                ok = false;
+            for (int i = max(0, nblk - DKV_LOOKAHEAD); i < nblk && ok; ++i)
+                if (!issue_acc(i))
+                    ok = false;
             if (!ok)
                 *abort_flag = 1;
-            // fires once every MMA issued has retired (also on abort)
-            mma_commit(acc_full);
-            mbar_wait(acc_full, 0, 69);
+            mma_commit(done);
+            mbar_wait(done, 0, 69);
         }
     } else {
         // ------------------------------------------------ P^T, dS^T, epilogue
+        const int grp = (warp - 2) >> 2;  // query blocks n with n % 2 == grp
         const int quad = warp & 3;
-        const int half = (warp - 2) >> 2;  // query columns [half*16, +16) of each block
         const int r = quad * 32 + lane;
         const int64_t key = k0 + r;
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
         bool ok = true;
-        for (int n = 0; n < nblk; ++n) {
-            if (*abort_flag || !mbar_wait(&sd_full[n & 1], (n >> 1) & 1, 70)) {
+        for (int n = grp; n < nblk; n += 2) {
+            const int b = n % NBUF;
+            if (*abort_flag || !mbar_wait(&sd_full[b], (n / NBUF) & 1, 70)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float sv[16], dpv[16];
-            tmem_ld_32x32b_x16(tmem + lane_off + CF::S_COL + (n & 1) * BWD_BLK + half * 16, sv);
-            tmem_ld_32x32b_x16(tmem + lane_off + CF::DP_COL + (n & 1) * BWD_BLK + half * 16, dpv);
+            float sv[32], dpv[32];
+            tmem_ld_32x32b_x32(tmem + lane_off + b * 64, sv);
+            tmem_ld_32x32b_x32(tmem + lane_off + b * 64 + 32, dpv);
             tmem_ld_wait();
-            const int64_t qb = static_cast<int64_t>(i_first + n) * BWD_BLK + half * 16;
-            float pv[16];
-#pragma unroll
-            for (int e = 0; e < 16; ++e) {
-                const int64_t qi = qb + e;
-                const bool live = key <= qi && qi < T;
-                const float l2 = live ? __ldg(lse + bh * T + qi) * LOG2E : 0.0f;
-                const float dd = live ? __ldg(Dv + bh * T + qi) : 0.0f;
-                const float p = live ? exp2f(fmaf(sv[e], LOG2E, -l2)) : 0.0f;
-                pv[e] = p;
-                sv[e] = p * (dpv[e] - dd);
-            }
-            uint32_t phi[8], plo[8], shi[8], slo[8];
-            split16(pv, phi, plo);
-            split16(sv, shi, slo);
-            // P^T / dS^T buffers: free once the previous block's dV/dK MMAs read them
-            if (n >= 1 && (*abort_flag || !mbar_wait(pds_free, (n - 1) & 1, 71))) {
+            // (lse * log2 e, D) of this query block landed with Q_i: observe
+            // that copy's completion here too (already complete; the slot is
+            // refilled only after this block's pds_full).
+            if (*abort_flag || !mbar_wait(&qfull[n % DKV_R1], (n / DKV_R1) & 1, 73)) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            tmem_st_32x32b_x8(tmem + lane_off + CF::A1_COL + half * 8, phi);
-            tmem_st_32x32b_x8(tmem + lane_off + CF::A1_COL + 16 + half * 8, plo);
-            tmem_st_32x32b_x8(tmem + lane_off + CF::A2_COL + half * 8, shi);
-            tmem_st_32x32b_x8(tmem + lane_off + CF::A2_COL + 16 + half * 8, slo);
+            const float2* ldv =
+                reinterpret_cast<const float2*>(smem + CF::OFF_LD + (n % DKV_R1) * LD_BYTES);
+            const int64_t qb = static_cast<int64_t>(i_first + n) * BWD_BLK;
+            const bool diag = qb < k0 + BQ - 1 || qb + BWD_BLK > T;
+            float pv[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                const float2 lv = ldv[e];
+                const bool live = !diag || (key <= qb + e && qb + e < T);
+                const float p = live ? exp2_approx(fmaf(sv[e], LOG2E, -lv.x)) : 0.0f;
+                pv[e] = p;
+                sv[e] = p * (dpv[e] - lv.y);
+            }
+            uint32_t phi[16], plo[16], shi[16], slo[16];
+            split32(pv, phi, plo);
+            split32(sv, shi, slo);
+            tmem_st_32x32b_x16(tmem + lane_off + b * 64, phi);
+            tmem_st_32x32b_x16(tmem + lane_off + b * 64 + 16, plo);
+            tmem_st_32x32b_x16(tmem + lane_off + b * 64 + 32, shi);
+            tmem_st_32x32b_x16(tmem + lane_off + b * 64 + 48, slo);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(pds_full);
+            mbar_arrive(&pds_full[b]);
         }
-        if (ok && (*abort_flag || !mbar_wait(acc_full, 0, 72)))
+        if (ok && (*abort_flag || !mbar_wait(done, 0, 72)))
             ok = false;
         if (!ok) {
             *abort_flag = 1;
@@ -1073,14 +1064,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tc_fence_after();
             float g[HH];
             const int64_t b = bh / H, h = bh % H;
-            load_owned<HD>(tmem + lane_off + CF::ACC_COL, half, g);
+            load_owned<HD>(tmem + lane_off + CF::ACC_COL, grp, g);
             if (key < T)
                 store_owned<HD>(g, dv + ((b * T + key) * H + h) * HD, key, cs, sn, false, 1.0f,
-                                half, accumulate);
-            load_owned<HD>(tmem + lane_off + CF::ACC_COL + HD, half, g);
+                                grp, accumulate);
+            load_owned<HD>(tmem + lane_off + CF::ACC_COL + HD, grp, g);
             if (key < T)
                 store_owned<HD>(g, dk + ((b * T + key) * H + h) * HD, key, cs, sn, true, 1.0f,
-                                half, accumulate);
+                                grp, accumulate);
         }
     }
 
@@ -1091,6 +1082,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tmem_dealloc(tmem, CF::TMEM_COLS);
     }
 }
+
 }  // namespace fatc
 
 // Tensor map over a pair of split planes (hi at `hi`, lo n elements later),
@@ -1149,9 +1141,10 @@ int attention_tc_forward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat
 
 int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat16* kh,
                                const __nv_bfloat16* vh, const __nv_bfloat16* dh,
-                               const float* lse, const float* Dv, const float* cs,
-                               const float* sn, float* dq, float* dk, float* dv, int accumulate,
-                               int64_t B, int64_t T, int64_t H, float scale, cudaStream_t st) {
+                               const float* lse, const float* Dv, const float* ld, int64_t T32,
+                               const float* cs, const float* sn, float* dq, float* dk, float* dv,
+                               int accumulate, int64_t B, int64_t T, int64_t H, float scale,
+                               cudaStream_t st) {
     const int64_t n = B * T * H * hd;
     const int64_t BH = B * H;
     CUtensorMap q128, d128, k32, v32, k128, v128, q32, d32;
@@ -1168,14 +1161,15 @@ int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloa
     dim3 grid(static_cast<unsigned>((T + fatc::BQ - 1) / fatc::BQ), static_cast<unsigned>(BH));
     auto launch = [&](auto hd_tag) -> int {
         constexpr int HD = decltype(hd_tag)::value;
-        const int smem = fatc::BwdCfg<HD>::BYTES;
+        int smem = fatc::BwdCfg<HD, fatc::DKV_R1, fatc::DKV_R2>::BYTES;
         cudaFuncSetAttribute(fatc::attn_bwd_dkv_tc<HD>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         fatc::attn_bwd_dkv_tc<HD><<<grid, fatc::NUM_THREADS, smem, st>>>(
-            k128, v128, q32, d32, lse, Dv, cs, sn, dk, dv, accumulate, T, static_cast<int>(H));
+            k128, v128, q32, d32, ld, T32, cs, sn, dk, dv, accumulate, T, static_cast<int>(H));
         int r = check_launch("attn_bwd_dkv_tc");
         if (r)
             return r;
+        smem = fatc::BwdCfg<HD, fatc::DQ_R1, fatc::DQ_R2>::BYTES;
         cudaFuncSetAttribute(fatc::attn_bwd_dq_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem);
         fatc::attn_bwd_dq_tc<HD><<<grid, fatc::NUM_THREADS, smem, st>>>(

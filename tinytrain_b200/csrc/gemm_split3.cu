@@ -781,6 +781,64 @@ int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_
                                            stream);
 }
 
+// Caller-held operand splits in the current precision: [batch][2][rows][ld]
+// with ld = cols rounded up to 32, which serves both K-major and MN-major use.
+size_t gemm_split_bytes(int64_t batch, int64_t rows, int64_t cols) {
+    if (batch <= 0 || rows <= 0 || cols <= 0)
+        return 0;
+    const int elt = current_prec() == gemm::PREC_TF32X3 ? 4 : 2;
+    return static_cast<size_t>(batch) * 2 * rows * round_up(cols, 32) * elt;
+}
+
+int gemm_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+               int64_t batch, void* dst, cudaStream_t stream) {
+    if (rows < 0 || cols < 0 || batch < 0 || ld < cols)
+        return set_error(TTK_ERR_ARG, "gemm_split: bad geometry");
+    if (rows == 0 || cols == 0 || batch == 0)
+        return TTK_OK;
+    if (!src || !dst || (reinterpret_cast<uintptr_t>(dst) & 15))
+        return set_error(TTK_ERR_ARG, "gemm_split: null or misaligned pointer");
+    const int64_t ld_pad = round_up(cols, 32);
+    if (current_prec() == gemm::PREC_TF32X3)
+        return launch_split<gemm::PREC_TF32X3>(src, rows, cols, ld, bstride, batch, dst, ld_pad,
+                                               stream);
+    return launch_split<gemm::PREC_BF16X3>(src, rows, cols, ld, bstride, batch, dst, ld_pad,
+                                           stream);
+}
+
+int gemm_on_splits(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                   float alpha, const void* a_split, const void* b_split, float beta, float* C,
+                   int64_t ldc, int64_t strideC, cudaStream_t stream) {
+    if (M < 0 || N < 0 || K < 0 || batch < 0)
+        return set_error(TTK_ERR_ARG, "gemm_on_splits: negative size");
+    if (M == 0 || N == 0 || batch == 0)
+        return TTK_OK;
+    if (!C || (K > 0 && (!a_split || !b_split)))
+        return set_error(TTK_ERR_ARG, "gemm_on_splits: null pointer");
+    if (ldc < N)
+        return set_error(TTK_ERR_ARG, "gemm_on_splits: ldc < N");
+    if (K == 0 || alpha == 0.0f) {
+        if (beta == 1.0f)
+            return TTK_OK;
+        const int64_t total = batch * M * N;
+        const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
+        gemm::scale_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(C, batch, M, N, ldc,
+                                                                         strideC, beta);
+        return check_launch("scale_kernel");
+    }
+    if (M > (1ll << 31) / 2 || N > (1ll << 31) / 2 || K > (1ll << 31) / 2)
+        return set_error(TTK_ERR_ARG, "gemm_on_splits: dimension too large");
+    const int64_t lda_pad = round_up(transA ? M : K, 32);
+    const int64_t ldb_pad = round_up(transB ? K : N, 32);
+    if (current_prec() == gemm::PREC_TF32X3)
+        return run_presplit<gemm::PREC_TF32X3>(transA, transB, batch, M, N, K, alpha, a_split,
+                                               lda_pad, b_split, ldb_pad, beta, C, ldc, strideC,
+                                               stream);
+    return run_presplit<gemm::PREC_BF16X3>(transA, transB, batch, M, N, K, alpha, a_split,
+                                           lda_pad, b_split, ldb_pad, beta, C, ldc, strideC,
+                                           stream);
+}
+
 int gemm_tf32x3_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
                          float alpha, const float* a_split, int64_t lda_pad,
                          const float* b_split, int64_t ldb_pad, float beta, float* C,

@@ -100,6 +100,128 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __r
     }
 }
 
+// Row-parallel variants for D a multiple of 256: a row is spread over TPR =
+// D/8 threads holding 8 elements each (two float4 at columns 4t and
+// 4(t + TPR)), so x and dy are read once and kept in registers; row sums meet
+// in shared memory. A block holds RPB = blockDim.x / TPR row slots.
+constexpr int RMS_EPT = 8;
+
+__device__ __forceinline__ float block_row_sum(float v, float* red, int slot, int t, int tpr,
+                                               int parity) {
+    v = warp_sum(v);
+    const int wpr = tpr >> 5;  // warps per row
+    float* rs = red + (parity * 8 + slot) * 32;
+    if ((t & 31) == 0)
+        rs[t >> 5] = v;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int i = 0; i < wpr; ++i)
+        tot += rs[i];
+    return tot;
+}
+
+__global__ void rmsnorm_fwd_rows_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                        float* __restrict__ y, float* __restrict__ rstd,
+                                        int64_t R, int64_t D, float eps) {
+    __shared__ float red[2 * 8 * 32];
+    const int tpr = static_cast<int>(D / RMS_EPT);
+    const int rpb = blockDim.x / tpr;
+    const int slot = threadIdx.x / tpr, t = threadIdx.x % tpr;
+    const int64_t c0 = 4 * static_cast<int64_t>(t), c1 = 4 * static_cast<int64_t>(t + tpr);
+    const float4 w0 = *reinterpret_cast<const float4*>(w + c0);
+    const float4 w1 = *reinterpret_cast<const float4*>(w + c1);
+    int parity = 0;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * rpb; base < R;
+         base += static_cast<int64_t>(gridDim.x) * rpb, parity ^= 1) {
+        const int64_t row = base + slot;
+        const bool ok = row < R;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+        if (ok) {
+            a = *reinterpret_cast<const float4*>(x + row * D + c0);
+            b = *reinterpret_cast<const float4*>(x + row * D + c1);
+        }
+        const float ss = block_row_sum(a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x +
+                                           b.y * b.y + b.z * b.z + b.w * b.w,
+                                       red, slot, t, tpr, parity);
+        if (!ok)
+            continue;
+        const float r = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+        if (t == 0 && rstd)
+            rstd[row] = r;
+        *reinterpret_cast<float4*>(y + row * D + c0) =
+            make_float4(a.x * r * w0.x, a.y * r * w0.y, a.z * r * w0.z, a.w * r * w0.w);
+        *reinterpret_cast<float4*>(y + row * D + c1) =
+            make_float4(b.x * r * w1.x, b.y * r * w1.y, b.z * r * w1.z, b.w * r * w1.w);
+    }
+}
+
+// dx as rmsnorm_bwd_kernel; dw partial per row slot of each block:
+// partial[blockIdx.x * RPB + slot][D] (rows in a fixed order).
+__global__ void rmsnorm_bwd_rows_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                        const float* __restrict__ rstd,
+                                        const float* __restrict__ dy, float* __restrict__ dx,
+                                        int accumulate, float* __restrict__ partial, int64_t R,
+                                        int64_t D) {
+    __shared__ float red[2 * 8 * 32];
+    const int tpr = static_cast<int>(D / RMS_EPT);
+    const int rpb = blockDim.x / tpr;
+    const int slot = threadIdx.x / tpr, t = threadIdx.x % tpr;
+    const int64_t c0 = 4 * static_cast<int64_t>(t), c1 = 4 * static_cast<int64_t>(t + tpr);
+    const float4 w0 = *reinterpret_cast<const float4*>(w + c0);
+    const float4 w1 = *reinterpret_cast<const float4*>(w + c1);
+    const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    float dw[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int parity = 0;
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * rpb; base < R;
+         base += static_cast<int64_t>(gridDim.x) * rpb, parity ^= 1) {
+        const int64_t row = base + slot;
+        const bool ok = row < R;
+        float xv[8] = {}, gv[8] = {};
+        float r = 0.0f;
+        if (ok) {
+            const float4 a = *reinterpret_cast<const float4*>(x + row * D + c0);
+            const float4 b = *reinterpret_cast<const float4*>(x + row * D + c1);
+            const float4 g0 = *reinterpret_cast<const float4*>(dy + row * D + c0);
+            const float4 g1 = *reinterpret_cast<const float4*>(dy + row * D + c1);
+            xv[0] = a.x, xv[1] = a.y, xv[2] = a.z, xv[3] = a.w;
+            xv[4] = b.x, xv[5] = b.y, xv[6] = b.z, xv[7] = b.w;
+            gv[0] = g0.x, gv[1] = g0.y, gv[2] = g0.z, gv[3] = g0.w;
+            gv[4] = g1.x, gv[5] = g1.y, gv[6] = g1.z, gv[7] = g1.w;
+            r = rstd[row];
+        }
+        float dot = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+            dot += gv[e] * wv[e] * xv[e];
+        dot = block_row_sum(dot, red, slot, t, tpr, parity);
+        if (!ok)
+            continue;
+        const float k = r * r * r / static_cast<float>(D) * dot;
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            o[e] = r * (gv[e] * wv[e]) - xv[e] * k;
+            dw[e] += gv[e] * xv[e] * r;
+        }
+        if (dx) {
+            float4* p0 = reinterpret_cast<float4*>(dx + row * D + c0);
+            float4* p1 = reinterpret_cast<float4*>(dx + row * D + c1);
+            if (accumulate) {
+                const float4 q0 = *p0, q1 = *p1;
+                o[0] += q0.x, o[1] += q0.y, o[2] += q0.z, o[3] += q0.w;
+                o[4] += q1.x, o[5] += q1.y, o[6] += q1.z, o[7] += q1.w;
+            }
+            *p0 = make_float4(o[0], o[1], o[2], o[3]);
+            *p1 = make_float4(o[4], o[5], o[6], o[7]);
+        }
+    }
+    if (partial) {
+        float* pr = partial + (static_cast<int64_t>(blockIdx.x) * rpb + slot) * D;
+        *reinterpret_cast<float4*>(pr + c0) = make_float4(dw[0], dw[1], dw[2], dw[3]);
+        *reinterpret_cast<float4*>(pr + c1) = make_float4(dw[4], dw[5], dw[6], dw[7]);
+    }
+}
+
 // dw[c] += sum_b partial[b][c], b ascending.
 __global__ void colsum_kernel(const float* __restrict__ partial, int64_t nb, int64_t D,
                               float* __restrict__ out) {
@@ -565,6 +687,14 @@ static inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
 
 static inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// Row-parallel RMSNorm applies when D is a multiple of 256 (whole warps per
+// row) and a row fits one block of at most 1024 threads.
+static inline bool rms_rows_ok(int64_t D) { return D % 256 == 0 && D / RMS_EPT <= 1024; }
+static inline int rms_block(int64_t D) {  // threads per block: whole rows, up to 256 (or one row)
+    const int tpr = static_cast<int>(D / RMS_EPT);
+    return tpr >= 256 ? tpr : tpr * (256 / tpr);
+}
+
 extern "C" {
 
 int ttk_rmsnorm_fwd(const float* x, const float* w, float* y, float* rstd, int64_t R, int64_t D,
@@ -575,13 +705,30 @@ int ttk_rmsnorm_fwd(const float* x, const float* w, float* y, float* rstd, int64
         return TTK_OK;
     if ((D & 3) == 0 && !(aligned16(x) && aligned16(w) && aligned16(y)))
         return set_error(TTK_ERR_ARG, "rmsnorm_fwd: tensors must be 16-byte aligned");
+    if (rms_rows_ok(D)) {
+        const int tpr = static_cast<int>(D / RMS_EPT), bs = rms_block(D);
+        const int64_t blocks = std::min<int64_t>((R + bs / tpr - 1) / (bs / tpr), 148 * 8);
+        rmsnorm_fwd_rows_kernel<<<static_cast<int>(blocks), bs, 0, S(stream)>>>(x, w, y, rstd, R,
+                                                                                 D, eps);
+        return check_launch("rmsnorm_fwd_rows_kernel");
+    }
     rmsnorm_fwd_kernel<<<grid_for(R, 8), 256, 0, S(stream)>>>(x, w, y, rstd, R, D, eps);
     return check_launch("rmsnorm_fwd_kernel");
 }
 
 static int64_t rms_blocks(int64_t R) { return std::min<int64_t>(std::max<int64_t>(R / 64, 1), 296); }
 
+// Row-parallel backward: blocks and dw partial rows (one per row slot).
+static int64_t rms_rows_blocks(int64_t R, int64_t D) {
+    const int rpb = rms_block(D) / static_cast<int>(D / RMS_EPT);
+    return std::min<int64_t>((R + rpb - 1) / rpb, 148 * 4);
+}
+
 size_t ttk_rmsnorm_bwd_workspace_size(int64_t R, int64_t D) {
+    if (rms_rows_ok(D)) {
+        const int rpb = rms_block(D) / static_cast<int>(D / RMS_EPT);
+        return static_cast<size_t>(rms_rows_blocks(R, D) * rpb * D) * sizeof(float);
+    }
     return static_cast<size_t>(rms_blocks(R) * D) * sizeof(float);
 }
 
@@ -592,14 +739,26 @@ int ttk_rmsnorm_bwd(const float* x, const float* w, const float* rstd, const flo
         return set_error(TTK_ERR_ARG, "rmsnorm_bwd: bad arguments");
     if (R == 0)
         return TTK_OK;
-    const int64_t nb = rms_blocks(R);
-    const int64_t rpb = (R + nb - 1) / nb;
     float* partial = nullptr;
     if (dw) {
         if (!workspace || workspace_bytes < ttk_rmsnorm_bwd_workspace_size(R, D))
             return set_error(TTK_ERR_ARG, "rmsnorm_bwd: workspace too small");
         partial = static_cast<float*>(workspace);
     }
+    if (rms_rows_ok(D) && aligned16(x) && aligned16(w) && aligned16(dy) && (!dx || aligned16(dx))) {
+        const int bs = rms_block(D);
+        const int64_t nbk = rms_rows_blocks(R, D);
+        rmsnorm_bwd_rows_kernel<<<static_cast<int>(nbk), bs, 0, S(stream)>>>(
+            x, w, rstd, dy, dx, accumulate_dx, partial, R, D);
+        int rc = check_launch("rmsnorm_bwd_rows_kernel");
+        if (rc || !dw)
+            return rc;
+        const int64_t nparts = nbk * (bs / static_cast<int>(D / RMS_EPT));
+        colsum_kernel<<<grid_for(D, 256), 256, 0, S(stream)>>>(partial, nparts, D, dw);
+        return check_launch("colsum_kernel");
+    }
+    const int64_t nb = rms_blocks(R);
+    const int64_t rpb = (R + nb - 1) / nb;
     const size_t smem = static_cast<size_t>(8 * D) * sizeof(float);
     if (smem > 200 * 1024)
         return set_error(TTK_ERR_ARG, "rmsnorm_bwd: D too large");

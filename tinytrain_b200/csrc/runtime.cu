@@ -237,6 +237,22 @@ int ttk_gemm(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_
                        beta, C, ldc, strideC, workspace, workspace_bytes, S(stream));
 }
 
+size_t ttk_gemm_split_bytes(int64_t batch, int64_t rows, int64_t cols) {
+    return gemm_split_bytes(batch, rows, cols);
+}
+
+int ttk_gemm_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+                   int64_t batch, void* dst, void* stream) {
+    return gemm_split(src, rows, cols, ld, bstride, batch, dst, S(stream));
+}
+
+int ttk_gemm_splits(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                    float alpha, const void* a_split, const void* b_split, float beta, float* C,
+                    int64_t ldc, int64_t strideC, void* stream) {
+    return gemm_on_splits(transA, transB, batch, M, N, K, alpha, a_split, b_split, beta, C, ldc,
+                          strideC, S(stream));
+}
+
 int ttk_split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
                    int64_t batch, float* dst, int64_t ld_pad, void* stream) {
     if (ld_pad % 16 || ld_pad < cols || rows < 0 || cols < 0 || batch < 0)

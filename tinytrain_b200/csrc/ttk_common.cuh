@@ -125,6 +125,17 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const void* desc, uint64_
         : "memory");
 }
 
+// Untiled bulk copy global -> shared (both addresses 16-byte aligned, bytes a
+// multiple of 16), completing on an mbarrier's transaction count.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // ----------------------------------------------------------------- tcgen05 --
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
@@ -229,6 +240,17 @@ __device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t
         : "memory");
 }
 
+// Thread t of the warp writes lane (lane_base + t), columns [col, col+16).
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+        "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+        "r"(v[15])
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -280,6 +302,28 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N, int a_mn, i
            | (static_cast<uint32_t>(b_mn) << 16)
            | (static_cast<uint32_t>(N >> 3) << 17)
            | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Shared-memory descriptor advanced by `bytes` (a multiple of 16; the start
+// address field cannot overflow for shared-memory addresses below 256 KB).
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) {
+    return d + static_cast<uint64_t>(bytes >> 4);
+}
+
+// 2^x with the hardware approximation (ex2.approx.ftz.f32, relative error
+// about 2^-22; subnormal results flush to zero).
+__device__ __forceinline__ float exp2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Three-term split of a pair (x0, x1): hi = both rounded to bf16, packed with
+// x0 in the low half; lo = the bf16 rounding of each remainder, packed alike.
+__device__ __forceinline__ void split_pair_bf16(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(hi) : "f"(x1), "f"(x0));
+    const float h0 = __uint_as_float(hi << 16), h1 = __uint_as_float(hi & 0xffff0000u);
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(lo) : "f"(x1 - h1), "f"(x0 - h0));
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

@@ -48,6 +48,12 @@ int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_
              const float* A, int64_t lda, int64_t strideA, const float* B, int64_t ldb,
              int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC, void* ws,
              size_t ws_bytes, cudaStream_t stream);
+size_t gemm_split_bytes(int64_t batch, int64_t rows, int64_t cols);
+int gemm_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
+               int64_t batch, void* dst, cudaStream_t stream);
+int gemm_on_splits(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+                   float alpha, const void* a_split, const void* b_split, float beta, float* C,
+                   int64_t ldc, int64_t strideC, cudaStream_t stream);
 int gemm_tf32x3_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
                          float alpha, const float* a_split, int64_t lda_pad,
                          const float* b_split, int64_t ldb_pad, float beta, float* C,
@@ -71,10 +77,13 @@ bool attention_tc_supported(int hd);
 int attention_tc_forward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat16* kh,
                               const __nv_bfloat16* vh, float* o, float* lse, int64_t B, int64_t T,
                               int64_t H, cudaStream_t st);
+// ld: [B*H][T32][2] table of (lse * log2 e, D), T32 = T rounded up to 32,
+// zero in the padding rows.
 int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat16* kh,
                                const __nv_bfloat16* vh, const __nv_bfloat16* dh,
-                               const float* lse, const float* Dv, const float* cs,
-                               const float* sn, float* dq, float* dk, float* dv, int accumulate,
-                               int64_t B, int64_t T, int64_t H, float scale, cudaStream_t st);
+                               const float* lse, const float* Dv, const float* ld, int64_t T32,
+                               const float* cs, const float* sn, float* dq, float* dk, float* dv,
+                               int accumulate, int64_t B, int64_t T, int64_t H, float scale,
+                               cudaStream_t st);
 
 }  // namespace ttk

@@ -7,8 +7,10 @@
 // Gradient writes: a gradient buffer that is still logically zero is
 // overwritten instead of read-modified-written (grad_target), which saves a
 // memset and a read per first contribution.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <memory>
 #include <stdexcept>
 
 #include "internal.h"
@@ -185,14 +187,72 @@ MatOp mat_operand(const ImplPtr& p) {
     return {p, dread(p), 0};
 }
 
-void gemm(int ta, int tb, int64_t batch, int64_t M, int64_t N, int64_t K, const float* A,
-          int64_t lda, int64_t sA, const float* B, int64_t ldb, int64_t sB, float beta, float* C,
-          int64_t ldc, int64_t sC) {
-    const size_t ws = ttk_gemm_workspace_size(ta, tb, batch, M, N, K);
-    Scratch w(ws);
-    check(ttk_gemm(ta, tb, batch, M, N, K, 1.0f, A, lda, sA, B, ldb, sB, beta, C, ldc, sC, w.ptr,
-                   ws, stream()),
+// The split of a GEMM operand stored in `buf` at `ptr` (batch x rows x cols,
+// leading dimension ld, batch stride bs), from the buffer's cache when its
+// contents and the geometry are unchanged since the last split. The same
+// activation is read by the forward GEMM and by dW, the same output gradient
+// by dX and dW, and a weight by every micro-batch until the optimizer writes
+// it; each is split once.
+const void* operand_split(Buffer* buf, const float* ptr, int64_t batch, int64_t rows,
+                          int64_t cols, int64_t ld, int64_t bs) {
+    const int64_t key[7] = {ptr - buf->dev, batch, rows, cols, ld, bs, ttk_gemm_get_precision()};
+    if (buf->split_dev && buf->split_version == buf->version &&
+        std::equal(key, key + 7, buf->split_key))
+        return buf->split_dev;
+    const size_t bytes = ttk_gemm_split_bytes(batch, rows, cols);
+    if (buf->split_bytes < bytes) {
+        ttk_free(buf->split_dev, stream());
+        buf->split_dev = nullptr;
+        buf->split_bytes = 0;
+        check(ttk_malloc(&buf->split_dev, bytes, stream()), "gemm split");
+        buf->split_bytes = bytes;
+    }
+    check(ttk_gemm_split(ptr, rows, cols, ld, bs, batch, buf->split_dev, stream()), "gemm split");
+    buf->split_version = buf->version;
+    std::copy(key, key + 7, buf->split_key);
+    return buf->split_dev;
+}
+
+// GEMM operand: storage buffer, pointer into it, leading dimension and batch
+// stride (elements) of the stored (not transposed) matrix.
+struct GemmArg {
+    Buffer* buf;
+    const float* ptr;
+    int64_t ld, bs;
+};
+
+void gemm(int ta, int tb, int64_t batch, int64_t M, int64_t N, int64_t K, GemmArg A, GemmArg B,
+          float beta, float* C, int64_t ldc, int64_t sC) {
+    if (M == 0 || N == 0 || batch == 0)
+        return;
+    if (K == 0) {
+        check(ttk_gemm(ta, tb, batch, M, N, K, 1.0f, A.ptr, A.ld, A.bs, B.ptr, B.ld, B.bs, beta, C,
+                       ldc, sC, nullptr, 0, stream()),
+              "gemm");
+        return;
+    }
+    const void* sa = operand_split(A.buf, A.ptr, batch, ta ? K : M, ta ? M : K, A.ld, A.bs);
+    const int64_t brows = tb ? N : K, bcols = tb ? K : N;
+    const void* sb = nullptr;
+    std::unique_ptr<Scratch> own;  // both operands in one buffer, other geometry: B uncached
+    const int64_t bkey[7] = {B.ptr - B.buf->dev, batch, brows, bcols, B.ld, B.bs,
+                             ttk_gemm_get_precision()};
+    if (B.buf == A.buf && !std::equal(bkey, bkey + 7, A.buf->split_key)) {
+        own = std::make_unique<Scratch>(ttk_gemm_split_bytes(batch, brows, bcols));
+        check(ttk_gemm_split(B.ptr, brows, bcols, B.ld, B.bs, batch, own->ptr, stream()),
+              "gemm split");
+        sb = own->ptr;
+    } else {
+        sb = operand_split(B.buf, B.ptr, batch, brows, bcols, B.ld, B.bs);
+    }
+    check(ttk_gemm_splits(ta, tb, batch, M, N, K, 1.0f, sa, sb, beta, C, ldc, sC, stream()),
           "gemm");
+}
+
+// The buffer holding an operand's storage: the tensor's data, or a gradient.
+GemmArg data_arg(Tensor::Impl* p, int64_t ld, int64_t bs) {
+    const float* d = dread(p);
+    return {p->data.get(), d, ld, bs};
 }
 
 }  // namespace
@@ -454,8 +514,8 @@ Tensor batched_matmul(const Tensor& a, const Tensor& b, int64_t Bt, int64_t M, i
     Tensor out = make_out(oshape, a.requires_grad() || b.requires_grad());
     MatOp A = mat_operand(a.impl()), Bm = mat_operand(b.impl());
     const int64_t lda = A.trans ? M : K, ldb = Bm.trans ? K : N;
-    gemm(A.trans, Bm.trans, Bt, M, N, K, A.ptr, lda, M * K, Bm.ptr, ldb, K * N, 0.0f, out_ptr(out),
-         N, M * N);
+    gemm(A.trans, Bm.trans, Bt, M, N, K, {A.base->data.get(), A.ptr, lda, M * K},
+         {Bm.base->data.get(), Bm.ptr, ldb, K * N}, 0.0f, out_ptr(out), N, M * N);
     if (out.requires_grad()) {
         auto ao = a.impl(), bo = b.impl();
         Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
@@ -466,18 +526,19 @@ Tensor batched_matmul(const Tensor& a, const Tensor& b, int64_t Bt, int64_t M, i
                 return;
             MatOp A = mat_operand(ao), Bm = mat_operand(bo);
             const int64_t lda = A.trans ? M : K, ldb = Bm.trans ? K : N;
+            const GemmArg ga{oo->grad.get(), g, N, M * N};
+            const GemmArg aa{A.base->data.get(), A.ptr, lda, M * K};
+            const GemmArg ba{Bm.base->data.get(), Bm.ptr, ldb, K * N};
             if (ao->requires_grad) {
                 // dA = g B^T. For a lazy transpose A = X^T the gradient goes
                 // straight into X: dX = B g^T.
                 bool ow = false;
                 if (!A.trans) {
                     float* d = grad_target(ao, ow);
-                    gemm(0, Bm.trans ? 0 : 1, Bt, M, K, N, g, N, M * N, Bm.ptr, ldb, K * N,
-                         ow ? 0.0f : 1.0f, d, K, M * K);
+                    gemm(0, Bm.trans ? 0 : 1, Bt, M, K, N, ga, ba, ow ? 0.0f : 1.0f, d, K, M * K);
                 } else if (A.base->requires_grad) {
                     float* d = grad_target(A.base, ow);
-                    gemm(Bm.trans ? 1 : 0, 1, Bt, K, M, N, Bm.ptr, ldb, K * N, g, N, M * N,
-                         ow ? 0.0f : 1.0f, d, M, M * K);
+                    gemm(Bm.trans ? 1 : 0, 1, Bt, K, M, N, ba, ga, ow ? 0.0f : 1.0f, d, M, M * K);
                 }
             }
             if (bo->requires_grad) {
@@ -485,12 +546,10 @@ Tensor batched_matmul(const Tensor& a, const Tensor& b, int64_t Bt, int64_t M, i
                 bool ow = false;
                 if (!Bm.trans) {
                     float* d = grad_target(bo, ow);
-                    gemm(A.trans ? 0 : 1, 0, Bt, K, N, M, A.ptr, lda, M * K, g, N, M * N,
-                         ow ? 0.0f : 1.0f, d, N, K * N);
+                    gemm(A.trans ? 0 : 1, 0, Bt, K, N, M, aa, ga, ow ? 0.0f : 1.0f, d, N, K * N);
                 } else if (Bm.base->requires_grad) {
                     float* d = grad_target(Bm.base, ow);
-                    gemm(1, A.trans ? 1 : 0, Bt, N, K, M, g, N, M * N, A.ptr, lda, M * K,
-                         ow ? 0.0f : 1.0f, d, K, K * N);
+                    gemm(1, A.trans ? 1 : 0, Bt, N, K, M, ga, aa, ow ? 0.0f : 1.0f, d, K, K * N);
                 }
             }
         };
@@ -526,8 +585,8 @@ Tensor linear(const Tensor& x, const Tensor& weight) {
         throw std::invalid_argument("matmul: inner dims mismatch");
     const int64_t R = x.dim(0), In = x.dim(1), Out = weight.dim(0);
     Tensor out = make_out({R, Out}, x.requires_grad() || weight.requires_grad());
-    gemm(0, 1, 1, R, Out, In, dread(x.impl()), In, 0, dread(weight.impl()), In, 0, 0.0f,
-         out_ptr(out), Out, 0);
+    gemm(0, 1, 1, R, Out, In, data_arg(x.impl().get(), In, 0), data_arg(weight.impl().get(), In, 0),
+         0.0f, out_ptr(out), Out, 0);
     if (out.requires_grad()) {
         auto xo = x.impl(), wo = weight.impl();
         Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
@@ -536,15 +595,18 @@ Tensor linear(const Tensor& x, const Tensor& weight) {
             const float* g = grad_in(oo);
             if (!g)
                 return;
+            const GemmArg ga{oo->grad.get(), g, Out, 0};
             if (xo->requires_grad) {  // dX = g W
                 bool ow = false;
                 float* d = grad_target(xo, ow);
-                gemm(0, 0, 1, R, In, Out, g, Out, 0, dread(wo), In, 0, ow ? 0.0f : 1.0f, d, In, 0);
+                gemm(0, 0, 1, R, In, Out, ga, data_arg(wo.get(), In, 0), ow ? 0.0f : 1.0f, d, In,
+                     0);
             }
             if (wo->requires_grad) {  // dW = g^T X
                 bool ow = false;
                 float* d = grad_target(wo, ow);
-                gemm(1, 0, 1, Out, In, R, g, Out, 0, dread(xo), In, 0, ow ? 0.0f : 1.0f, d, In, 0);
+                gemm(1, 0, 1, Out, In, R, ga, data_arg(xo.get(), In, 0), ow ? 0.0f : 1.0f, d, In,
+                     0);
             }
         };
     }
@@ -952,6 +1014,7 @@ float clip_grad_norm(const std::vector<Tensor*>& params, float max_norm) {
                     check(ttk_binary(2, g, &one, c.as<float>(), &zero, g, &n, 1, stream()),
                           "clip scale");
                     p->impl()->grad->host_valid = false;
+                    p->impl()->grad->touch();
                 }
         }
     }

@@ -94,6 +94,8 @@ Buffer::Buffer(int64_t n_) : n(n_) {}
 Buffer::~Buffer() {
     if (dev && !external)
         ttk_free(dev, g_stream);
+    if (split_dev)
+        ttk_free(split_dev, g_stream);
 }
 
 static void alloc_dev(Buffer& b) {

@@ -20,6 +20,8 @@
 // dQ kernel per query block (loops over earlier key blocks). Both recompute
 // the scores; no atomics, so results are deterministic.
 #include <cuda_runtime.h>
+
+#include <initializer_list>
 #include <stdint.h>
 
 #include <cstdlib>
@@ -521,6 +523,14 @@ static int attn_check(const void* q, const void* k, const void* v, const void* c
     return TTK_OK;
 }
 
+// The tensor-core engines read q, k, v, dO and the RoPE tables as float4.
+static int attn_align_check(std::initializer_list<const void*> ps) {
+    for (const void* p : ps)
+        if (p && (reinterpret_cast<uintptr_t>(p) & 15))
+            return set_error(TTK_ERR_ARG, "attention: tensors must be 16-byte aligned");
+    return TTK_OK;
+}
+
 namespace {
 // 0: tensor cores, tcgen05 forward where the head dim allows (64, 128) and
 //    mma.sync otherwise (default); 1: fp32 FMA kernels; 2: mma.sync only.
@@ -568,6 +578,9 @@ int ttk_attention_fwd(const float* q, const float* k, const float* v, const floa
     if (attn_impl() != 1) {
         if (!workspace || workspace_bytes < ttk_attention_fwd_workspace_size(B, T, H, hd))
             return set_error(TTK_ERR_ARG, "attention_fwd: workspace too small");
+        rc = attn_align_check({q, k, v, cos_t, sin_t, o});
+        if (rc)
+            return rc;
         const bool tc = attn_impl() == 0 && attention_tc_supported(static_cast<int>(hd));
         return attention_mma_forward(static_cast<int>(hd), q, k, v, cos_t, sin_t, o, lse, B, T,
                                      H, scale, workspace, tc, S(stream));
@@ -603,6 +616,9 @@ int ttk_attention_bwd(const float* q, const float* k, const float* v, const floa
     if (!workspace || workspace_bytes < ttk_attention_bwd_workspace_size(B, T, H, hd))
         return set_error(TTK_ERR_ARG, "attention_bwd: workspace too small");
     if (attn_impl() != 1) {
+        rc = attn_align_check({q, k, v, cos_t, sin_t, o, dout, dq, dk, dv});
+        if (rc)
+            return rc;
         const bool tc = attn_impl() == 0 && attention_tc_supported(static_cast<int>(hd));
         return attention_mma_backward(static_cast<int>(hd), q, k, v, cos_t, sin_t, o, lse, dout,
                                       dq, dk, dv, accumulate, B, T, H, scale, workspace, tc,

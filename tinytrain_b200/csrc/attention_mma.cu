@@ -184,33 +184,54 @@ __device__ __forceinline__ void frag_b_cols(uint32_t (&b)[4], uint32_t tile, int
 }
 
 // ------------------------------------------------------------- prep pass --
-// out_hi/out_lo [B,H,T,HD] = split(rope?(x) * mul) for x [B,T,H,HD].
+// out_hi/out_lo [B,H,T,HD] = split(rope?(x) * mul) for x [B,T,H,HD]. Each
+// thread takes 4 consecutive columns d of the first half and their RoPE
+// partners d + HD/2 (float4 loads, 8-byte bf16x4 stores).
+__device__ __forceinline__ void split4(const float (&v)[4], uint2& hi, uint2& lo) {
+    uint32_t h0, h1, l0, l1;
+    split_pair_bf16(v[0], v[1], h0, l0);
+    split_pair_bf16(v[2], v[3], h1, l1);
+    hi = make_uint2(h0, h1);
+    lo = make_uint2(l0, l1);
+}
+
 __global__ void attn_split_kernel(const float* __restrict__ x, const float* __restrict__ cs,
                                   const float* __restrict__ sn, int rope, float mul,
                                   __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo,
                                   int64_t B, int64_t T, int64_t H, int64_t HD) {
-    const int64_t HH = HD / 2;
-    const int64_t total = B * T * H * HH;
+    const int64_t HH = HD / 2, Q = HH / 4;  // column quads per half row
+    const int64_t total = B * T * H * Q;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t d = i % HH;
-        const int64_t h = (i / HH) % H;
-        const int64_t t = (i / (HH * H)) % T;
-        const int64_t b = i / (HH * H * T);
+        const int64_t d = (i % Q) * 4;
+        const int64_t h = (i / Q) % H;
+        const int64_t t = (i / (Q * H)) % T;
+        const int64_t b = i / (Q * H * T);
         const float* src = x + ((b * T + t) * H + h) * HD;
-        float x1 = src[d], x2 = src[d + HH];
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src + d));
+        const float4 c = __ldg(reinterpret_cast<const float4*>(src + d + HH));
+        float x1[4] = {a.x, a.y, a.z, a.w}, x2[4] = {c.x, c.y, c.z, c.w};
         if (rope) {
-            const float c = cs[t * HH + d], s = sn[t * HH + d];
-            const float r1 = x1 * c - x2 * s, r2 = x1 * s + x2 * c;
-            x1 = r1, x2 = r2;
+            const float4 co = __ldg(reinterpret_cast<const float4*>(cs + t * HH + d));
+            const float4 si = __ldg(reinterpret_cast<const float4*>(sn + t * HH + d));
+            const float cv[4] = {co.x, co.y, co.z, co.w}, sv[4] = {si.x, si.y, si.z, si.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float r1 = x1[u] * cv[u] - x2[u] * sv[u], r2 = x1[u] * sv[u] + x2[u] * cv[u];
+                x1[u] = r1, x2[u] = r2;
+            }
         }
-        x1 *= mul, x2 *= mul;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            x1[u] *= mul, x2[u] *= mul;
         const int64_t o = ((b * H + h) * T + t) * HD;
-        const __nv_bfloat16 h1 = __float2bfloat16_rn(x1), h2 = __float2bfloat16_rn(x2);
-        hi[o + d] = h1;
-        hi[o + d + HH] = h2;
-        lo[o + d] = __float2bfloat16_rn(x1 - __bfloat162float(h1));
-        lo[o + d + HH] = __float2bfloat16_rn(x2 - __bfloat162float(h2));
+        uint2 h1, l1, h2, l2;
+        split4(x1, h1, l1);
+        split4(x2, h2, l2);
+        *reinterpret_cast<uint2*>(hi + o + d) = h1;
+        *reinterpret_cast<uint2*>(lo + o + d) = l1;
+        *reinterpret_cast<uint2*>(hi + o + d + HH) = h2;
+        *reinterpret_cast<uint2*>(lo + o + d + HH) = l2;
     }
 }
 
@@ -760,9 +781,9 @@ struct SplitBufs {
 inline int launch_split(const float* x, const float* cs, const float* sn, int rope, float mul,
                         __nv_bfloat16* hi, __nv_bfloat16* lo, int64_t B, int64_t T, int64_t H,
                         int64_t HD, cudaStream_t st) {
-    const int64_t total = B * T * H * (HD / 2);
-    attn_split_kernel<<<grid_for(total, 256), 256, 0, st>>>(x, cs, sn, rope, mul, hi, lo, B, T, H,
-                                                             HD);
+    const int64_t total = B * T * H * (HD / 8);
+    attn_split_kernel<<<grid_for(total, 256, 148 * 32), 256, 0, st>>>(x, cs, sn, rope, mul, hi,
+                                                                        lo, B, T, H, HD);
     return check_launch("attn_split_kernel");
 }
 

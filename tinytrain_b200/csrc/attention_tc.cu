@@ -460,11 +460,10 @@ constexpr int GROUP_THREADS = 128;
 //           dP_j -> 2 slots
 //   dK, dV: Q_i and dO_i held from S^T_i to the accumulation (lookahead 1)
 //           -> 3 slots each
-constexpr int DQ_R1 = 4, DQ_R2 = 2, DQ_LOOKAHEAD = 2;
 constexpr int DKV_R1 = 3, DKV_R2 = 3, DKV_LOOKAHEAD = 1;
 static_assert(DKV_R1 == DKV_R2, "the dK/dV kernel indexes both rings with one slot");
-static_assert(DQ_LOOKAHEAD < NBUF && DKV_LOOKAHEAD < NBUF, "a score buffer is reused after its "
-              "accumulation MMA was issued");
+static_assert(DKV_LOOKAHEAD < NBUF, "a score buffer is reused after its accumulation MMA "
+              "was issued");
 constexpr int LD_BYTES = BWD_BLK * 8;  // (lse * log2 e, D) pairs of one query block
 
 template <int HD, int R1, int R2>
@@ -560,10 +559,39 @@ __device__ __forceinline__ void split32(const float (&x)[32], uint32_t (&hi)[16]
         split_pair_bf16(x[2 * i], x[2 * i + 1], hi[i], lo[i]);
 }
 
-// dQ: CTA = 128 query rows of one (b, h); key blocks of 32 up to the diagonal.
-//   S_j = Q K_j^T (buffer cols [0,32)), dP_j = dO V_j^T ([32,64)); the
-//   softmax group writes dS_j = P (dP - D) split over S_j's columns
-//   (hi [0,16), lo [16,32)); dQ += dS_j K_j.
+// dQ: CTA = 128 query rows of one (b, h); key blocks of 64 up to the diagonal.
+//   S_j = Q K_j^T (buffer cols [0,64)), dP_j = dO V_j^T ([64,128)); N = 64
+//   per MMA, twice the 32-row blocks of dK/dV, which halves the MMA
+//   instructions per key (an instruction costs about the same time at N = 32
+//   and N = 64). Each softmax thread takes its row in two 32-key halves and
+//   writes the split of dS_j over exactly the 32 S columns the half read:
+//   keys 32h..32h+31 -> hi at [32h, 32h+16), lo at [32h+16, 32h+32).
+//   Issue order S_j, dQ_{j-1}, dP_j: the K slot of block j-1 frees one
+//   product earlier, and V_j's copy hides behind S_j and dQ_{j-1}.
+constexpr int DQ_BK = 64;
+
+template <int HD>
+struct DqCfg {
+    static constexpr int NCH = HD / 32;
+    static constexpr int BIG_PLANE = NCH * BQ * 64;      // Q, dO: [NCH][128][64 B]
+    static constexpr int BIG_BYTES = 2 * BIG_PLANE;
+    static constexpr int TILE_PLANE = NCH * DQ_BK * 64;  // K, V: [NCH][64][64 B]
+    static constexpr int TILE_BYTES = 2 * TILE_PLANE;
+    static constexpr int KR = HD == 128 ? 2 : 4;          // ring depths (shared-memory bound)
+    static constexpr int VR = HD == 128 ? 1 : 3;
+    static constexpr int OFF_DO = BIG_BYTES;
+    static constexpr int OFF_K = 2 * BIG_BYTES;
+    static constexpr int OFF_V = OFF_K + KR * TILE_BYTES;
+    static constexpr int OFF_BAR = OFF_V + VR * TILE_BYTES;
+    static constexpr int NBARS = 32;
+    static constexpr int BYTES = OFF_BAR + 8 * NBARS + 16 + 1024;
+    static constexpr int ACC_COL = 256;  // two 128-column block buffers, then dQ
+    static constexpr int TMEM_COLS = 512;
+    static_assert(ACC_COL + HD <= TMEM_COLS, "TMEM budget");
+    static_assert(BYTES <= 232448, "shared memory budget");
+    static_assert(1 + 2 * KR + 2 * VR + 2 + 2 + 1 <= NBARS, "barriers");
+};
+
 template <int HD>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     attn_bwd_dq_tc(const __grid_constant__ CUtensorMap map_q,
@@ -573,20 +601,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    const float* __restrict__ Dv, const float* __restrict__ cs,
                    const float* __restrict__ sn, float* __restrict__ dq, int accumulate,
                    float scale, int64_t T, int H) {
-    using CF = BwdCfg<HD, DQ_R1, DQ_R2>;
-    constexpr int HH = HD / 2;
+    using CF = DqCfg<HD>;
+    constexpr int HH = HD / 2, KR = CF::KR, VR = CF::VR;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + CF::OFF_BAR);
     uint64_t* a_full = bars;
     uint64_t* kfull = bars + 1;
-    uint64_t* kempty = kfull + DQ_R1;
-    uint64_t* vfull = kempty + DQ_R1;
-    uint64_t* vempty = vfull + DQ_R2;
-    uint64_t* sd_full = vempty + DQ_R2;  // [NBUF]
-    uint64_t* ds_full = sd_full + NBUF;  // [NBUF]
-    uint64_t* done = ds_full + NBUF;
+    uint64_t* kempty = kfull + KR;
+    uint64_t* vfull = kempty + KR;
+    uint64_t* vempty = vfull + VR;
+    uint64_t* sd_full = vempty + VR;  // [2]
+    uint64_t* ds_full = sd_full + 2;  // [2]
+    uint64_t* done = ds_full + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + CF::NBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -596,19 +624,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int64_t q0 = static_cast<int64_t>(qt) * BQ;
     const int64_t bh = blockIdx.y;
     const int64_t q_last = min(q0 + BQ, T) - 1;
-    const int nblk = static_cast<int>(q_last / BWD_BLK) + 1;
+    const int nblk = static_cast<int>(q_last / DQ_BK) + 1;
 
     if (threadIdx.x == 0) {
         mbar_init(a_full, 1);
-        for (int i = 0; i < DQ_R1; ++i) {
+        for (int i = 0; i < KR; ++i) {
             mbar_init(&kfull[i], 1);
             mbar_init(&kempty[i], 1);
         }
-        for (int i = 0; i < DQ_R2; ++i) {
+        for (int i = 0; i < VR; ++i) {
             mbar_init(&vfull[i], 1);
             mbar_init(&vempty[i], 1);
         }
-        for (int b = 0; b < NBUF; ++b) {
+        for (int b = 0; b < 2; ++b) {
             mbar_init(&sd_full[b], 1);
             mbar_init(&ds_full[b], GROUP_THREADS);
         }
@@ -635,48 +663,48 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
         if (lane == 0) {
-            int karmed[DQ_R1], varmed[DQ_R2];
+            int karmed[KR], varmed[VR];
 #pragma unroll
-            for (int i = 0; i < DQ_R1; ++i)
+            for (int i = 0; i < KR; ++i)
                 karmed[i] = -1;
 #pragma unroll
-            for (int i = 0; i < DQ_R2; ++i)
+            for (int i = 0; i < VR; ++i)
                 varmed[i] = -1;
             mbar_arrive_expect_tx(a_full, 2 * CF::BIG_BYTES);
             tma_load_5d(smem, &map_q, a_full, 0, static_cast<int>(q0), 0, static_cast<int>(bh), 0);
-            tma_load_5d(smem + CF::OFF_BIG1, &map_do, a_full, 0, static_cast<int>(q0), 0,
+            tma_load_5d(smem + CF::OFF_DO, &map_do, a_full, 0, static_cast<int>(q0), 0,
                         static_cast<int>(bh), 0);
             bool ok = true;
             for (int j = 0; j < nblk && ok; ++j) {
-                const int ks_ = j % DQ_R1, vs_ = j % DQ_R2;
-                const uint32_t kph = static_cast<uint32_t>((j / DQ_R1) & 1);
-                const uint32_t vph = static_cast<uint32_t>((j / DQ_R2) & 1);
+                const int ks_ = j % KR, vs_ = j % VR;
+                const uint32_t kph = static_cast<uint32_t>((j / KR) & 1);
+                const uint32_t vph = static_cast<uint32_t>((j / VR) & 1);
                 if (*abort_flag || !mbar_wait(&kempty[ks_], kph ^ 1, 41)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&kfull[ks_], CF::SMALL_BYTES);
-                tma_load_5d(smem + CF::OFF_R1 + ks_ * CF::SMALL_BYTES, &map_k, &kfull[ks_], 0,
-                            j * BWD_BLK, 0, static_cast<int>(bh), 0);
+                mbar_arrive_expect_tx(&kfull[ks_], CF::TILE_BYTES);
+                tma_load_5d(smem + CF::OFF_K + ks_ * CF::TILE_BYTES, &map_k, &kfull[ks_], 0,
+                            j * DQ_BK, 0, static_cast<int>(bh), 0);
                 karmed[ks_] = static_cast<int>(kph);
                 if (*abort_flag || !mbar_wait(&vempty[vs_], vph ^ 1, 42)) {
                     ok = false;
                     break;
                 }
-                mbar_arrive_expect_tx(&vfull[vs_], CF::SMALL_BYTES);
-                tma_load_5d(smem + CF::OFF_R2 + vs_ * CF::SMALL_BYTES, &map_v, &vfull[vs_], 0,
-                            j * BWD_BLK, 0, static_cast<int>(bh), 0);
+                mbar_arrive_expect_tx(&vfull[vs_], CF::TILE_BYTES);
+                tma_load_5d(smem + CF::OFF_V + vs_ * CF::TILE_BYTES, &map_v, &vfull[vs_], 0,
+                            j * DQ_BK, 0, static_cast<int>(bh), 0);
                 varmed[vs_] = static_cast<int>(vph);
             }
             if (!ok) {
                 *abort_flag = 1;
                 mbar_wait(a_full, 0, 46);
 #pragma unroll
-                for (int i = 0; i < DQ_R1; ++i)
+                for (int i = 0; i < KR; ++i)
                     if (karmed[i] >= 0)
                         mbar_wait(&kfull[i], static_cast<uint32_t>(karmed[i]), 46);
 #pragma unroll
-                for (int i = 0; i < DQ_R2; ++i)
+                for (int i = 0; i < VR; ++i)
                     if (varmed[i] >= 0)
                         mbar_wait(&vfull[i], static_cast<uint32_t>(varmed[i]), 46);
             }
@@ -684,67 +712,79 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else if (warp == 1) {
         // -------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc_sd = umma_idesc_bf16(BQ, BWD_BLK, 0, 0);
+            constexpr uint32_t idesc_sd = umma_idesc_bf16(BQ, DQ_BK, 0, 0);
             constexpr uint32_t idesc_q = umma_idesc_bf16(BQ, HD, 0, 1);
             const uint64_t qh0 = kmajor_desc(s_base, BQ, 0);
             const uint64_t ql0 = kmajor_desc(s_base + CF::BIG_PLANE, BQ, 0);
-            const uint64_t oh0 = kmajor_desc(s_base + CF::OFF_BIG1, BQ, 0);
-            const uint64_t ol0 = kmajor_desc(s_base + CF::OFF_BIG1 + CF::BIG_PLANE, BQ, 0);
+            const uint64_t oh0 = kmajor_desc(s_base + CF::OFF_DO, BQ, 0);
+            const uint64_t ol0 = kmajor_desc(s_base + CF::OFF_DO + CF::BIG_PLANE, BQ, 0);
             const uint32_t dQ = tmem + CF::ACC_COL;
             bool ok = mbar_wait(a_full, 0, 43);
             auto issue_dq = [&](int i) -> bool {
-                const int b = i % NBUF;
-                if (*abort_flag || !mbar_wait(&ds_full[b], (i / NBUF) & 1, 45))
+                const int b = i & 1;
+                if (*abort_flag || !mbar_wait(&ds_full[b], (i >> 1) & 1, 45))
                     return false;
                 tc_fence_after();
-                const uint32_t sK = s_base + CF::OFF_R1 + (i % DQ_R1) * CF::SMALL_BYTES;
-                const uint64_t kh = small_mn_desc(sK, 0), kl = small_mn_desc(sK + CF::SMALL_PLANE, 0);
-                const uint32_t a = tmem + b * 64;
+                const uint32_t sK = s_base + CF::OFF_K + (i % KR) * CF::TILE_BYTES;
+                // MN-major K_i [64 keys][HD]: k-step of 16 keys = 16 rows of 64 B
+                const uint64_t kh = umma_smem_desc(sK, DQ_BK * 64, 512, kSW64);
+                const uint64_t kl = umma_smem_desc(sK + CF::TILE_PLANE, DQ_BK * 64, 512, kSW64);
+                const uint32_t a = tmem + b * 128;
 #pragma unroll
-                for (int ks = 0; ks < BWD_BLK / 16; ++ks) {
+                for (int ks = 0; ks < DQ_BK / 16; ++ks) {
+                    const uint32_t ah = a + (ks >> 1) * 32 + (ks & 1) * 8, al = ah + 16;
                     const uint64_t bh_ = desc_add(kh, ks * 1024), bl_ = desc_add(kl, ks * 1024);
-                    mma_bf16_ta(dQ, a + 16 + ks * 8, bh_, idesc_q, (i == 0 && ks == 0) ? 0u : 1u);
-                    mma_bf16_ta(dQ, a + ks * 8, bl_, idesc_q, 1u);
-                    mma_bf16_ta(dQ, a + ks * 8, bh_, idesc_q, 1u);
+                    mma_bf16_ta(dQ, al, bh_, idesc_q, (i == 0 && ks == 0) ? 0u : 1u);
+                    mma_bf16_ta(dQ, ah, bl_, idesc_q, 1u);
+                    mma_bf16_ta(dQ, ah, bh_, idesc_q, 1u);
                 }
-                mma_commit(&kempty[i % DQ_R1]);
+                mma_commit(&kempty[i % KR]);
                 return true;
             };
             for (int j = 0; j < nblk && ok; ++j) {
-                const int ks_ = j % DQ_R1, vs_ = j % DQ_R2;
-                if (*abort_flag || !mbar_wait(&kfull[ks_], (j / DQ_R1) & 1, 47) ||
-                    !mbar_wait(&vfull[vs_], (j / DQ_R2) & 1, 48)) {
+                const int ks_ = j % KR, vs_ = j % VR;
+                if (*abort_flag || !mbar_wait(&kfull[ks_], (j / KR) & 1, 47)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t sK = s_base + CF::OFF_R1 + ks_ * CF::SMALL_BYTES;
-                const uint32_t sV = s_base + CF::OFF_R2 + vs_ * CF::SMALL_BYTES;
-                const uint64_t kh0 = kmajor_desc(sK, BWD_BLK, 0);
-                const uint64_t kl0 = kmajor_desc(sK + CF::SMALL_PLANE, BWD_BLK, 0);
-                const uint64_t vh0 = kmajor_desc(sV, BWD_BLK, 0);
-                const uint64_t vl0 = kmajor_desc(sV + CF::SMALL_PLANE, BWD_BLK, 0);
-                const uint32_t ds = tmem + (j % NBUF) * 64, dp = ds + 32;
+                const uint32_t sK = s_base + CF::OFF_K + ks_ * CF::TILE_BYTES;
+                const uint64_t kh0 = kmajor_desc(sK, DQ_BK, 0);
+                const uint64_t kl0 = kmajor_desc(sK + CF::TILE_PLANE, DQ_BK, 0);
+                const uint32_t ds = tmem + (j & 1) * 128, dp = ds + 64;
 #pragma unroll
                 for (int ks = 0; ks < HD / 16; ++ks) {
                     const uint32_t ob = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
-                    const uint32_t sb = (ks >> 1) * (BWD_BLK * 64) + (ks & 1) * 32;
-                    const uint32_t acc = ks > 0 ? 1u : 0u;
-                    mma_bf16(ds, desc_add(ql0, ob), desc_add(kh0, sb), idesc_sd, acc);
-                    mma_bf16(dp, desc_add(ol0, ob), desc_add(vh0, sb), idesc_sd, acc);
+                    const uint32_t sb = (ks >> 1) * (DQ_BK * 64) + (ks & 1) * 32;
+                    mma_bf16(ds, desc_add(ql0, ob), desc_add(kh0, sb), idesc_sd, ks > 0 ? 1u : 0u);
                     mma_bf16(ds, desc_add(qh0, ob), desc_add(kl0, sb), idesc_sd, 1u);
-                    mma_bf16(dp, desc_add(oh0, ob), desc_add(vl0, sb), idesc_sd, 1u);
                     mma_bf16(ds, desc_add(qh0, ob), desc_add(kh0, sb), idesc_sd, 1u);
+                }
+                if (j >= 1 && !issue_dq(j - 1)) {
+                    ok = false;
+                    break;
+                }
+                if (*abort_flag || !mbar_wait(&vfull[vs_], (j / VR) & 1, 48)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sV = s_base + CF::OFF_V + vs_ * CF::TILE_BYTES;
+                const uint64_t vh0 = kmajor_desc(sV, DQ_BK, 0);
+                const uint64_t vl0 = kmajor_desc(sV + CF::TILE_PLANE, DQ_BK, 0);
+#pragma unroll
+                for (int ks = 0; ks < HD / 16; ++ks) {
+                    const uint32_t ob = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
+                    const uint32_t sb = (ks >> 1) * (DQ_BK * 64) + (ks & 1) * 32;
+                    mma_bf16(dp, desc_add(ol0, ob), desc_add(vh0, sb), idesc_sd, ks > 0 ? 1u : 0u);
+                    mma_bf16(dp, desc_add(oh0, ob), desc_add(vl0, sb), idesc_sd, 1u);
                     mma_bf16(dp, desc_add(oh0, ob), desc_add(vh0, sb), idesc_sd, 1u);
                 }
-                mma_commit(&sd_full[j % NBUF]);
+                mma_commit(&sd_full[j & 1]);
                 mma_commit(&vempty[vs_]);
-                if (j >= DQ_LOOKAHEAD && !issue_dq(j - DQ_LOOKAHEAD))
-                    ok = false;
             }
-            for (int i = max(0, nblk - DQ_LOOKAHEAD); i < nblk && ok; ++i)
-                if (!issue_dq(i))
-                    ok = false;
+            if (ok && !issue_dq(nblk - 1))
+                ok = false;
             if (!ok)
                 *abort_flag = 1;
             // fires once every MMA issued has retired (also on abort)
@@ -753,40 +793,43 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else {
         // --------------------------------------------------- softmax / dS
-        const int grp = (warp - 2) >> 2;  // blocks j with j % 2 == grp
+        const int grp = (warp - 2) >> 2;  // blocks j with j % 2 == grp (TMEM buffer grp)
         const int quad = warp & 3;
         const int r = quad * 32 + lane;
         const int64_t q = q0 + r;
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
         const float lse2 = q < T ? lse[bh * T + q] * LOG2E : 0.0f;
         const float Dq = q < T ? Dv[bh * T + q] : 0.0f;
+        const uint32_t buf = tmem + lane_off + grp * 128;
         bool ok = true;
         for (int j = grp; j < nblk; j += 2) {
-            const int b = j % NBUF;
-            if (*abort_flag || !mbar_wait(&sd_full[b], (j / NBUF) & 1, 51)) {
+            if (*abort_flag || !mbar_wait(&sd_full[grp], (j >> 1) & 1, 51)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            float sv[32], dpv[32];
-            tmem_ld_32x32b_x32(tmem + lane_off + b * 64, sv);
-            tmem_ld_32x32b_x32(tmem + lane_off + b * 64 + 32, dpv);
-            tmem_ld_wait();
-            const int64_t k0 = static_cast<int64_t>(j) * BWD_BLK;
-            const bool diag = k0 + BWD_BLK - 1 > q0;
+            const int64_t k0 = static_cast<int64_t>(j) * DQ_BK;
+            const bool diag = k0 + DQ_BK - 1 > q0;
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+                float sv[32], dpv[32];
+                tmem_ld_32x32b_x32(buf + h * 32, sv);
+                tmem_ld_32x32b_x32(buf + 64 + h * 32, dpv);
+                tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const bool live = q < T && (!diag || k0 + e <= q);
-                const float p = live ? exp2_approx(fmaf(sv[e], LOG2E, -lse2)) : 0.0f;
-                sv[e] = p * (dpv[e] - Dq);
+                for (int e = 0; e < 32; ++e) {
+                    const bool live = q < T && (!diag || k0 + h * 32 + e <= q);
+                    const float p = live ? exp2_approx(fmaf(sv[e], LOG2E, -lse2)) : 0.0f;
+                    sv[e] = p * (dpv[e] - Dq);
+                }
+                uint32_t hi[16], lo[16];
+                split32(sv, hi, lo);
+                tmem_st_32x32b_x16(buf + h * 32, hi);
+                tmem_st_32x32b_x16(buf + h * 32 + 16, lo);
             }
-            uint32_t hi[16], lo[16];
-            split32(sv, hi, lo);
-            tmem_st_32x32b_x16(tmem + lane_off + b * 64, hi);
-            tmem_st_32x32b_x16(tmem + lane_off + b * 64 + 16, lo);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&ds_full[b]);
+            mbar_arrive(&ds_full[grp]);
         }
         if (ok && (*abort_flag || !mbar_wait(done, 0, 52)))
             ok = false;
@@ -1147,11 +1190,11 @@ int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloa
                                cudaStream_t st) {
     const int64_t n = B * T * H * hd;
     const int64_t BH = B * H;
-    CUtensorMap q128, d128, k32, v32, k128, v128, q32, d32;
+    CUtensorMap q128, d128, k64, v64, k128, v128, q32, d32;
     int rc = make_plane_map(&q128, qh, n, BH, T, hd, fatc::BQ);
     if (!rc) rc = make_plane_map(&d128, dh, n, BH, T, hd, fatc::BQ);
-    if (!rc) rc = make_plane_map(&k32, kh, n, BH, T, hd, fatc::BWD_BLK);
-    if (!rc) rc = make_plane_map(&v32, vh, n, BH, T, hd, fatc::BWD_BLK);
+    if (!rc) rc = make_plane_map(&k64, kh, n, BH, T, hd, fatc::DQ_BK);
+    if (!rc) rc = make_plane_map(&v64, vh, n, BH, T, hd, fatc::DQ_BK);
     if (!rc) rc = make_plane_map(&k128, kh, n, BH, T, hd, fatc::BQ);
     if (!rc) rc = make_plane_map(&v128, vh, n, BH, T, hd, fatc::BQ);
     if (!rc) rc = make_plane_map(&q32, qh, n, BH, T, hd, fatc::BWD_BLK);
@@ -1169,11 +1212,11 @@ int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloa
         int r = check_launch("attn_bwd_dkv_tc");
         if (r)
             return r;
-        smem = fatc::BwdCfg<HD, fatc::DQ_R1, fatc::DQ_R2>::BYTES;
+        smem = fatc::DqCfg<HD>::BYTES;
         cudaFuncSetAttribute(fatc::attn_bwd_dq_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem);
         fatc::attn_bwd_dq_tc<HD><<<grid, fatc::NUM_THREADS, smem, st>>>(
-            q128, d128, k32, v32, lse, Dv, cs, sn, dq, accumulate, scale, T, static_cast<int>(H));
+            q128, d128, k64, v64, lse, Dv, cs, sn, dq, accumulate, scale, T, static_cast<int>(H));
         return check_launch("attn_bwd_dq_tc");
     };
     if (hd == 128)

@@ -206,79 +206,78 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else if (warp == 1) {
         // -------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc_s = umma_idesc_bf16(BQ, BKV, 0, 0);
-            constexpr uint32_t idesc_o = umma_idesc_bf16(BQ, HD, 0, 1);
-            const uint32_t sQ = s_base;
-            int it = 0;
-            bool ok = mbar_wait(q_full, 0, 22);
-            auto next_slot = [&](uint32_t& addr) -> bool {
-                const int slot = it % NSLOT;
-                const uint32_t ph = static_cast<uint32_t>((it / NSLOT) & 1);
-                if (*abort_flag || !mbar_wait(&full[slot], ph, 23))
-                    return false;
-                addr = s_base + CF::OFF_SLOT + slot * CF::SLOT_BYTES;
-                ++it;
-                return true;
-            };
-            auto issue_pv = [&](int i) -> bool {
-                uint32_t sV;
-                const int slot = it % NSLOT;
-                if (!next_slot(sV))
-                    return false;
-                if (*abort_flag || !mbar_wait(&p_full[i & 1], (i >> 1) & 1, 24))
-                    return false;
-                if (i >= 2 && (*abort_flag || !mbar_wait(&o_free[i & 1], ((i - 2) >> 1) & 1, 25)))
-                    return false;
-                tc_fence_after();
-                const uint32_t sP = s_base + CF::OFF_P + (i & 1) * CF::P_BYTES;
-                const uint32_t d = tmem + CF::O_COL + (i & 1) * HD;
+        // The whole warp runs this loop (uniform control flow); lane 0 issues.
+        constexpr uint32_t idesc_s = umma_idesc_bf16(BQ, BKV, 0, 0);
+        constexpr uint32_t idesc_o = umma_idesc_bf16(BQ, HD, 0, 1);
+        const uint32_t sQ = s_base;
+        int it = 0;
+        bool ok = mbar_wait(q_full, 0, 22);
+        auto next_slot = [&](uint32_t& addr) -> bool {
+            const int slot = it % NSLOT;
+            const uint32_t ph = static_cast<uint32_t>((it / NSLOT) & 1);
+            if (*abort_flag || !mbar_wait(&full[slot], ph, 23))
+                return false;
+            addr = s_base + CF::OFF_SLOT + slot * CF::SLOT_BYTES;
+            ++it;
+            return true;
+        };
+        auto issue_pv = [&](int i) -> bool {
+            uint32_t sV;
+            const int slot = it % NSLOT;
+            if (!next_slot(sV))
+                return false;
+            if (*abort_flag || !mbar_wait(&p_full[i & 1], (i >> 1) & 1, 24))
+                return false;
+            if (i >= 2 && (*abort_flag || !mbar_wait(&o_free[i & 1], ((i - 2) >> 1) & 1, 25)))
+                return false;
+            tc_fence_after();
+            const uint32_t sP = s_base + CF::OFF_P + (i & 1) * CF::P_BYTES;
+            const uint32_t d = tmem + CF::O_COL + (i & 1) * HD;
 #pragma unroll
-                for (int ks = 0; ks < BKV / 16; ++ks) {
-                    const uint64_t ph_ = kmajor_desc(sP, BQ, ks);
-                    const uint64_t pl_ = kmajor_desc(sP + CF::P_PLANE, BQ, ks);
-                    const uint64_t vh_ = v_desc(sV, ks);
-                    const uint64_t vl_ = v_desc(sV + CF::KV_PLANE, ks);
-                    mma_bf16(d, pl_, vh_, idesc_o, ks > 0 ? 1u : 0u);
-                    mma_bf16(d, ph_, vl_, idesc_o, 1u);
-                    mma_bf16(d, ph_, vh_, idesc_o, 1u);
-                }
-                mma_commit(&o_full[i & 1]);
-                mma_commit(&empty[slot]);
-                return true;
-            };
-            for (int j = 0; j < nblk && ok; ++j) {
-                uint32_t sK;
-                const int slot = it % NSLOT;
-                if (!next_slot(sK)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d = tmem + CF::S_COL + (j & 1) * BKV;
-#pragma unroll
-                for (int ks = 0; ks < HD / 16; ++ks) {
-                    const uint64_t qh_ = kmajor_desc(sQ, BQ, ks);
-                    const uint64_t ql_ = kmajor_desc(sQ + CF::Q_PLANE, BQ, ks);
-                    const uint64_t kh_ = kmajor_desc(sK, BKV, ks);
-                    const uint64_t kl_ = kmajor_desc(sK + CF::KV_PLANE, BKV, ks);
-                    mma_bf16(d, ql_, kh_, idesc_s, ks > 0 ? 1u : 0u);
-                    mma_bf16(d, qh_, kl_, idesc_s, 1u);
-                    mma_bf16(d, qh_, kh_, idesc_s, 1u);
-                }
-                mma_commit(&s_full[j & 1]);
-                mma_commit(&empty[slot]);
-                if (j >= 1 && !issue_pv(j - 1))
-                    ok = false;
+            for (int ks = 0; ks < BKV / 16; ++ks) {
+                const uint64_t ph_ = kmajor_desc(sP, BQ, ks);
+                const uint64_t pl_ = kmajor_desc(sP + CF::P_PLANE, BQ, ks);
+                const uint64_t vh_ = v_desc(sV, ks);
+                const uint64_t vl_ = v_desc(sV + CF::KV_PLANE, ks);
+                mma_bf16_w(d, pl_, vh_, idesc_o, ks > 0 ? 1u : 0u);
+                mma_bf16_w(d, ph_, vl_, idesc_o, 1u);
+                mma_bf16_w(d, ph_, vh_, idesc_o, 1u);
             }
-            if (ok && !issue_pv(nblk - 1))
+            mma_commit_w(&o_full[i & 1]);
+            mma_commit_w(&empty[slot]);
+            return true;
+        };
+        for (int j = 0; j < nblk && ok; ++j) {
+            uint32_t sK;
+            const int slot = it % NSLOT;
+            if (!next_slot(sK)) {
                 ok = false;
-            if (!ok)
-                *abort_flag = 1;
-            // Every MMA issued has retired once this fires (also on abort).
-            mma_commit(done);
-            mbar_wait(done, 0, 27);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d = tmem + CF::S_COL + (j & 1) * BKV;
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+                const uint64_t qh_ = kmajor_desc(sQ, BQ, ks);
+                const uint64_t ql_ = kmajor_desc(sQ + CF::Q_PLANE, BQ, ks);
+                const uint64_t kh_ = kmajor_desc(sK, BKV, ks);
+                const uint64_t kl_ = kmajor_desc(sK + CF::KV_PLANE, BKV, ks);
+                mma_bf16_w(d, ql_, kh_, idesc_s, ks > 0 ? 1u : 0u);
+                mma_bf16_w(d, qh_, kl_, idesc_s, 1u);
+                mma_bf16_w(d, qh_, kh_, idesc_s, 1u);
+            }
+            mma_commit_w(&s_full[j & 1]);
+            mma_commit_w(&empty[slot]);
+            if (j >= 1 && !issue_pv(j - 1))
+                ok = false;
         }
+        if (ok && !issue_pv(nblk - 1))
+            ok = false;
+        if (!ok)
+            *abort_flag = 1;
+        // Every MMA issued has retired once this fires (also on abort).
+        mma_commit_w(done);
+        mbar_wait(done, 0, 27);
     } else {
         // ----------------------------------------------------------- softmax
         const int sw = warp - 2;
@@ -563,9 +562,10 @@ __device__ __forceinline__ void split32(const float (&x)[32], uint32_t (&hi)[16]
 //   S_j = Q K_j^T (buffer cols [0,64)), dP_j = dO V_j^T ([64,128)); N = 64
 //   per MMA, twice the 32-row blocks of dK/dV, which halves the MMA
 //   instructions per key (an instruction costs about the same time at N = 32
-//   and N = 64). Each softmax thread takes its row in two 32-key halves and
-//   writes the split of dS_j over exactly the 32 S columns the half read:
-//   keys 32h..32h+31 -> hi at [32h, 32h+16), lo at [32h+16, 32h+32).
+//   and N = 64). The two softmax warps of a lane quadrant each take 32 keys
+//   (half h) of every block and write the split of dS_j over exactly the 32
+//   S columns they read: keys 32h..32h+31 -> hi at [32h, 32h+16), lo at
+//   [32h+16, 32h+32).
 //   Issue order S_j, dQ_{j-1}, dP_j: the K slot of block j-1 frees one
 //   product earlier, and V_j's copy hides behind S_j and dQ_{j-1}.
 constexpr int DQ_BK = 64;
@@ -638,7 +638,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&sd_full[b], 1);
-            mbar_init(&ds_full[b], GROUP_THREADS);
+            mbar_init(&ds_full[b], SOFTMAX_THREADS);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
@@ -711,125 +711,124 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else if (warp == 1) {
         // -------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc_sd = umma_idesc_bf16(BQ, DQ_BK, 0, 0);
-            constexpr uint32_t idesc_q = umma_idesc_bf16(BQ, HD, 0, 1);
-            const uint64_t qh0 = kmajor_desc(s_base, BQ, 0);
-            const uint64_t ql0 = kmajor_desc(s_base + CF::BIG_PLANE, BQ, 0);
-            const uint64_t oh0 = kmajor_desc(s_base + CF::OFF_DO, BQ, 0);
-            const uint64_t ol0 = kmajor_desc(s_base + CF::OFF_DO + CF::BIG_PLANE, BQ, 0);
-            const uint32_t dQ = tmem + CF::ACC_COL;
-            bool ok = mbar_wait(a_full, 0, 43);
-            auto issue_dq = [&](int i) -> bool {
-                const int b = i & 1;
-                if (*abort_flag || !mbar_wait(&ds_full[b], (i >> 1) & 1, 45))
-                    return false;
-                tc_fence_after();
-                const uint32_t sK = s_base + CF::OFF_K + (i % KR) * CF::TILE_BYTES;
-                // MN-major K_i [64 keys][HD]: k-step of 16 keys = 16 rows of 64 B
-                const uint64_t kh = umma_smem_desc(sK, DQ_BK * 64, 512, kSW64);
-                const uint64_t kl = umma_smem_desc(sK + CF::TILE_PLANE, DQ_BK * 64, 512, kSW64);
-                const uint32_t a = tmem + b * 128;
+        // The whole warp runs this loop (uniform control flow); lane 0 issues.
+        constexpr uint32_t idesc_sd = umma_idesc_bf16(BQ, DQ_BK, 0, 0);
+        constexpr uint32_t idesc_q = umma_idesc_bf16(BQ, HD, 0, 1);
+        const uint64_t qh0 = kmajor_desc(s_base, BQ, 0);
+        const uint64_t ql0 = kmajor_desc(s_base + CF::BIG_PLANE, BQ, 0);
+        const uint64_t oh0 = kmajor_desc(s_base + CF::OFF_DO, BQ, 0);
+        const uint64_t ol0 = kmajor_desc(s_base + CF::OFF_DO + CF::BIG_PLANE, BQ, 0);
+        const uint32_t dQ = tmem + CF::ACC_COL;
+        bool ok = mbar_wait(a_full, 0, 43);
+        auto issue_dq = [&](int i) -> bool {
+            const int b = i & 1;
+            if (*abort_flag || !mbar_wait(&ds_full[b], (i >> 1) & 1, 45))
+                return false;
+            tc_fence_after();
+            const uint32_t sK = s_base + CF::OFF_K + (i % KR) * CF::TILE_BYTES;
+            // MN-major K_i [64 keys][HD]: k-step of 16 keys = 16 rows of 64 B
+            const uint64_t kh = umma_smem_desc(sK, DQ_BK * 64, 512, kSW64);
+            const uint64_t kl = umma_smem_desc(sK + CF::TILE_PLANE, DQ_BK * 64, 512, kSW64);
+            const uint32_t a = tmem + b * 128;
 #pragma unroll
-                for (int ks = 0; ks < DQ_BK / 16; ++ks) {
-                    const uint32_t ah = a + (ks >> 1) * 32 + (ks & 1) * 8, al = ah + 16;
-                    const uint64_t bh_ = desc_add(kh, ks * 1024), bl_ = desc_add(kl, ks * 1024);
-                    mma_bf16_ta(dQ, al, bh_, idesc_q, (i == 0 && ks == 0) ? 0u : 1u);
-                    mma_bf16_ta(dQ, ah, bl_, idesc_q, 1u);
-                    mma_bf16_ta(dQ, ah, bh_, idesc_q, 1u);
-                }
-                mma_commit(&kempty[i % KR]);
-                return true;
-            };
-            for (int j = 0; j < nblk && ok; ++j) {
-                const int ks_ = j % KR, vs_ = j % VR;
-                if (*abort_flag || !mbar_wait(&kfull[ks_], (j / KR) & 1, 47)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t sK = s_base + CF::OFF_K + ks_ * CF::TILE_BYTES;
-                const uint64_t kh0 = kmajor_desc(sK, DQ_BK, 0);
-                const uint64_t kl0 = kmajor_desc(sK + CF::TILE_PLANE, DQ_BK, 0);
-                const uint32_t ds = tmem + (j & 1) * 128, dp = ds + 64;
-#pragma unroll
-                for (int ks = 0; ks < HD / 16; ++ks) {
-                    const uint32_t ob = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
-                    const uint32_t sb = (ks >> 1) * (DQ_BK * 64) + (ks & 1) * 32;
-                    mma_bf16(ds, desc_add(ql0, ob), desc_add(kh0, sb), idesc_sd, ks > 0 ? 1u : 0u);
-                    mma_bf16(ds, desc_add(qh0, ob), desc_add(kl0, sb), idesc_sd, 1u);
-                    mma_bf16(ds, desc_add(qh0, ob), desc_add(kh0, sb), idesc_sd, 1u);
-                }
-                if (j >= 1 && !issue_dq(j - 1)) {
-                    ok = false;
-                    break;
-                }
-                if (*abort_flag || !mbar_wait(&vfull[vs_], (j / VR) & 1, 48)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t sV = s_base + CF::OFF_V + vs_ * CF::TILE_BYTES;
-                const uint64_t vh0 = kmajor_desc(sV, DQ_BK, 0);
-                const uint64_t vl0 = kmajor_desc(sV + CF::TILE_PLANE, DQ_BK, 0);
-#pragma unroll
-                for (int ks = 0; ks < HD / 16; ++ks) {
-                    const uint32_t ob = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
-                    const uint32_t sb = (ks >> 1) * (DQ_BK * 64) + (ks & 1) * 32;
-                    mma_bf16(dp, desc_add(ol0, ob), desc_add(vh0, sb), idesc_sd, ks > 0 ? 1u : 0u);
-                    mma_bf16(dp, desc_add(oh0, ob), desc_add(vl0, sb), idesc_sd, 1u);
-                    mma_bf16(dp, desc_add(oh0, ob), desc_add(vh0, sb), idesc_sd, 1u);
-                }
-                mma_commit(&sd_full[j & 1]);
-                mma_commit(&vempty[vs_]);
+            for (int ks = 0; ks < DQ_BK / 16; ++ks) {
+                const uint32_t ah = a + (ks >> 1) * 32 + (ks & 1) * 8, al = ah + 16;
+                const uint64_t bh_ = desc_add(kh, ks * 1024), bl_ = desc_add(kl, ks * 1024);
+                mma_bf16_ta_w(dQ, al, bh_, idesc_q, (i == 0 && ks == 0) ? 0u : 1u);
+                mma_bf16_ta_w(dQ, ah, bl_, idesc_q, 1u);
+                mma_bf16_ta_w(dQ, ah, bh_, idesc_q, 1u);
             }
-            if (ok && !issue_dq(nblk - 1))
+            mma_commit_w(&kempty[i % KR]);
+            return true;
+        };
+        for (int j = 0; j < nblk && ok; ++j) {
+            const int ks_ = j % KR, vs_ = j % VR;
+            if (*abort_flag || !mbar_wait(&kfull[ks_], (j / KR) & 1, 47)) {
                 ok = false;
-            if (!ok)
-                *abort_flag = 1;
-            // fires once every MMA issued has retired (also on abort)
-            mma_commit(done);
-            mbar_wait(done, 0, 49);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t sK = s_base + CF::OFF_K + ks_ * CF::TILE_BYTES;
+            const uint64_t kh0 = kmajor_desc(sK, DQ_BK, 0);
+            const uint64_t kl0 = kmajor_desc(sK + CF::TILE_PLANE, DQ_BK, 0);
+            const uint32_t ds = tmem + (j & 1) * 128, dp = ds + 64;
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+                const uint32_t ob = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
+                const uint32_t sb = (ks >> 1) * (DQ_BK * 64) + (ks & 1) * 32;
+                mma_bf16_w(ds, desc_add(ql0, ob), desc_add(kh0, sb), idesc_sd, ks > 0 ? 1u : 0u);
+                mma_bf16_w(ds, desc_add(qh0, ob), desc_add(kl0, sb), idesc_sd, 1u);
+                mma_bf16_w(ds, desc_add(qh0, ob), desc_add(kh0, sb), idesc_sd, 1u);
+            }
+            if (j >= 1 && !issue_dq(j - 1)) {
+                ok = false;
+                break;
+            }
+            if (*abort_flag || !mbar_wait(&vfull[vs_], (j / VR) & 1, 48)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t sV = s_base + CF::OFF_V + vs_ * CF::TILE_BYTES;
+            const uint64_t vh0 = kmajor_desc(sV, DQ_BK, 0);
+            const uint64_t vl0 = kmajor_desc(sV + CF::TILE_PLANE, DQ_BK, 0);
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+                const uint32_t ob = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
+                const uint32_t sb = (ks >> 1) * (DQ_BK * 64) + (ks & 1) * 32;
+                mma_bf16_w(dp, desc_add(ol0, ob), desc_add(vh0, sb), idesc_sd, ks > 0 ? 1u : 0u);
+                mma_bf16_w(dp, desc_add(oh0, ob), desc_add(vl0, sb), idesc_sd, 1u);
+                mma_bf16_w(dp, desc_add(oh0, ob), desc_add(vh0, sb), idesc_sd, 1u);
+            }
+            mma_commit_w(&sd_full[j & 1]);
+            mma_commit_w(&vempty[vs_]);
         }
+        if (ok && !issue_dq(nblk - 1))
+            ok = false;
+        if (!ok)
+            *abort_flag = 1;
+        // fires once every MMA issued has retired (also on abort)
+        mma_commit_w(done);
+        mbar_wait(done, 0, 49);
     } else {
         // --------------------------------------------------- softmax / dS
-        const int grp = (warp - 2) >> 2;  // blocks j with j % 2 == grp (TMEM buffer grp)
+        // Every block goes through all eight warps: the two warps of a TMEM
+        // lane quadrant take keys [32h, 32h+32) of their rows (h = half).
+        const int grp = (warp - 2) >> 2;  // column half; also the dQ column owner
         const int quad = warp & 3;
         const int r = quad * 32 + lane;
         const int64_t q = q0 + r;
         const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
         const float lse2 = q < T ? lse[bh * T + q] * LOG2E : 0.0f;
         const float Dq = q < T ? Dv[bh * T + q] : 0.0f;
-        const uint32_t buf = tmem + lane_off + grp * 128;
         bool ok = true;
-        for (int j = grp; j < nblk; j += 2) {
-            if (*abort_flag || !mbar_wait(&sd_full[grp], (j >> 1) & 1, 51)) {
+        for (int j = 0; j < nblk; ++j) {
+            const int b = j & 1;
+            if (*abort_flag || !mbar_wait(&sd_full[b], (j >> 1) & 1, 51)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const int64_t k0 = static_cast<int64_t>(j) * DQ_BK;
-            const bool diag = k0 + DQ_BK - 1 > q0;
-#pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
-                float sv[32], dpv[32];
-                tmem_ld_32x32b_x32(buf + h * 32, sv);
-                tmem_ld_32x32b_x32(buf + 64 + h * 32, dpv);
-                tmem_ld_wait();
+            const uint32_t buf = tmem + lane_off + b * 128 + grp * 32;
+            const int64_t k0 = static_cast<int64_t>(j) * DQ_BK + grp * 32;
+            const bool diag = k0 + 31 > q0;
+            float sv[32], dpv[32];
+            tmem_ld_32x32b_x32(buf, sv);
+            tmem_ld_32x32b_x32(buf + 64, dpv);
+            tmem_ld_wait();
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const bool live = q < T && (!diag || k0 + h * 32 + e <= q);
-                    const float p = live ? exp2_approx(fmaf(sv[e], LOG2E, -lse2)) : 0.0f;
-                    sv[e] = p * (dpv[e] - Dq);
-                }
-                uint32_t hi[16], lo[16];
-                split32(sv, hi, lo);
-                tmem_st_32x32b_x16(buf + h * 32, hi);
-                tmem_st_32x32b_x16(buf + h * 32 + 16, lo);
+            for (int e = 0; e < 32; ++e) {
+                const bool live = q < T && (!diag || k0 + e <= q);
+                const float p = live ? exp2_approx(fmaf(sv[e], LOG2E, -lse2)) : 0.0f;
+                sv[e] = p * (dpv[e] - Dq);
             }
+            uint32_t hi[16], lo[16];
+            split32(sv, hi, lo);
+            tmem_st_32x32b_x16(buf, hi);
+            tmem_st_32x32b_x16(buf + 16, lo);
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&ds_full[grp]);
+            mbar_arrive(&ds_full[b]);
         }
         if (ok && (*abort_flag || !mbar_wait(done, 0, 52)))
             ok = false;
@@ -974,81 +973,80 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
     } else if (warp == 1) {
         // -------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            constexpr uint32_t idesc_sd = umma_idesc_bf16(BQ, BWD_BLK, 0, 0);
-            constexpr uint32_t idesc_acc = umma_idesc_bf16(BQ, HD, 0, 1);
-            const uint64_t kh0 = kmajor_desc(s_base, BQ, 0);
-            const uint64_t kl0 = kmajor_desc(s_base + CF::BIG_PLANE, BQ, 0);
-            const uint64_t vh0 = kmajor_desc(s_base + CF::OFF_BIG1, BQ, 0);
-            const uint64_t vl0 = kmajor_desc(s_base + CF::OFF_BIG1 + CF::BIG_PLANE, BQ, 0);
-            const uint32_t dV = tmem + CF::ACC_COL, dK = tmem + CF::ACC_COL + HD;
-            bool ok = mbar_wait(a_full, 0, 63);
-            auto issue_acc = [&](int i) -> bool {
-                const int b = i % NBUF;
-                if (*abort_flag || !mbar_wait(&pds_full[b], (i / NBUF) & 1, 64))
-                    return false;
-                tc_fence_after();
-                const int slot = i % DKV_R1;
-                const uint32_t sQ = s_base + CF::OFF_R1 + slot * CF::SMALL_BYTES;
-                const uint32_t sO = s_base + CF::OFF_R2 + slot * CF::SMALL_BYTES;
-                const uint64_t qh = small_mn_desc(sQ, 0), ql = small_mn_desc(sQ + CF::SMALL_PLANE, 0);
-                const uint64_t oh = small_mn_desc(sO, 0), ol = small_mn_desc(sO + CF::SMALL_PLANE, 0);
-                const uint32_t p = tmem + b * 64, d = p + 32;
+        // The whole warp runs this loop (uniform control flow); lane 0 issues.
+        constexpr uint32_t idesc_sd = umma_idesc_bf16(BQ, BWD_BLK, 0, 0);
+        constexpr uint32_t idesc_acc = umma_idesc_bf16(BQ, HD, 0, 1);
+        const uint64_t kh0 = kmajor_desc(s_base, BQ, 0);
+        const uint64_t kl0 = kmajor_desc(s_base + CF::BIG_PLANE, BQ, 0);
+        const uint64_t vh0 = kmajor_desc(s_base + CF::OFF_BIG1, BQ, 0);
+        const uint64_t vl0 = kmajor_desc(s_base + CF::OFF_BIG1 + CF::BIG_PLANE, BQ, 0);
+        const uint32_t dV = tmem + CF::ACC_COL, dK = tmem + CF::ACC_COL + HD;
+        bool ok = mbar_wait(a_full, 0, 63);
+        auto issue_acc = [&](int i) -> bool {
+            const int b = i % NBUF;
+            if (*abort_flag || !mbar_wait(&pds_full[b], (i / NBUF) & 1, 64))
+                return false;
+            tc_fence_after();
+            const int slot = i % DKV_R1;
+            const uint32_t sQ = s_base + CF::OFF_R1 + slot * CF::SMALL_BYTES;
+            const uint32_t sO = s_base + CF::OFF_R2 + slot * CF::SMALL_BYTES;
+            const uint64_t qh = small_mn_desc(sQ, 0), ql = small_mn_desc(sQ + CF::SMALL_PLANE, 0);
+            const uint64_t oh = small_mn_desc(sO, 0), ol = small_mn_desc(sO + CF::SMALL_PLANE, 0);
+            const uint32_t p = tmem + b * 64, d = p + 32;
 #pragma unroll
-                for (int ks = 0; ks < BWD_BLK / 16; ++ks) {
-                    const uint32_t first = (i == 0 && ks == 0) ? 0u : 1u;
-                    const uint32_t o = ks * 1024;
-                    mma_bf16_ta(dV, p + 16 + ks * 8, desc_add(oh, o), idesc_acc, first);
-                    mma_bf16_ta(dK, d + 16 + ks * 8, desc_add(qh, o), idesc_acc, first);
-                    mma_bf16_ta(dV, p + ks * 8, desc_add(ol, o), idesc_acc, 1u);
-                    mma_bf16_ta(dK, d + ks * 8, desc_add(ql, o), idesc_acc, 1u);
-                    mma_bf16_ta(dV, p + ks * 8, desc_add(oh, o), idesc_acc, 1u);
-                    mma_bf16_ta(dK, d + ks * 8, desc_add(qh, o), idesc_acc, 1u);
-                }
-                mma_commit(&qempty[slot]);
-                mma_commit(&oempty[slot]);
-                return true;
-            };
-            for (int n = 0; n < nblk && ok; ++n) {
-                const int slot = n % DKV_R1;
-                const uint32_t ph = static_cast<uint32_t>((n / DKV_R1) & 1);
-                if (*abort_flag || !mbar_wait(&qfull[slot], ph, 67) ||
-                    !mbar_wait(&ofull[slot], ph, 68)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t sQ = s_base + CF::OFF_R1 + slot * CF::SMALL_BYTES;
-                const uint32_t sO = s_base + CF::OFF_R2 + slot * CF::SMALL_BYTES;
-                const uint64_t qh0 = kmajor_desc(sQ, BWD_BLK, 0);
-                const uint64_t ql0 = kmajor_desc(sQ + CF::SMALL_PLANE, BWD_BLK, 0);
-                const uint64_t oh0 = kmajor_desc(sO, BWD_BLK, 0);
-                const uint64_t ol0 = kmajor_desc(sO + CF::SMALL_PLANE, BWD_BLK, 0);
-                const uint32_t ds = tmem + (n % NBUF) * 64, dp = ds + 32;
-#pragma unroll
-                for (int ks = 0; ks < HD / 16; ++ks) {
-                    const uint32_t bb = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
-                    const uint32_t sb = (ks >> 1) * (BWD_BLK * 64) + (ks & 1) * 32;
-                    const uint32_t acc = ks > 0 ? 1u : 0u;
-                    mma_bf16(ds, desc_add(kl0, bb), desc_add(qh0, sb), idesc_sd, acc);
-                    mma_bf16(dp, desc_add(vl0, bb), desc_add(oh0, sb), idesc_sd, acc);
-                    mma_bf16(ds, desc_add(kh0, bb), desc_add(ql0, sb), idesc_sd, 1u);
-                    mma_bf16(dp, desc_add(vh0, bb), desc_add(ol0, sb), idesc_sd, 1u);
-                    mma_bf16(ds, desc_add(kh0, bb), desc_add(qh0, sb), idesc_sd, 1u);
-                    mma_bf16(dp, desc_add(vh0, bb), desc_add(oh0, sb), idesc_sd, 1u);
-                }
-                mma_commit(&sd_full[n % NBUF]);
-                if (n >= DKV_LOOKAHEAD && !issue_acc(n - DKV_LOOKAHEAD))
-                    ok = false;
+            for (int ks = 0; ks < BWD_BLK / 16; ++ks) {
+                const uint32_t first = (i == 0 && ks == 0) ? 0u : 1u;
+                const uint32_t o = ks * 1024;
+                mma_bf16_ta_w(dV, p + 16 + ks * 8, desc_add(oh, o), idesc_acc, first);
+                mma_bf16_ta_w(dK, d + 16 + ks * 8, desc_add(qh, o), idesc_acc, first);
+                mma_bf16_ta_w(dV, p + ks * 8, desc_add(ol, o), idesc_acc, 1u);
+                mma_bf16_ta_w(dK, d + ks * 8, desc_add(ql, o), idesc_acc, 1u);
+                mma_bf16_ta_w(dV, p + ks * 8, desc_add(oh, o), idesc_acc, 1u);
+                mma_bf16_ta_w(dK, d + ks * 8, desc_add(qh, o), idesc_acc, 1u);
             }
-            for (int i = max(0, nblk - DKV_LOOKAHEAD); i < nblk && ok; ++i)
-                if (!issue_acc(i))
-                    ok = false;
-            if (!ok)
-                *abort_flag = 1;
-            mma_commit(done);
-            mbar_wait(done, 0, 69);
+            mma_commit_w(&qempty[slot]);
+            mma_commit_w(&oempty[slot]);
+            return true;
+        };
+        for (int n = 0; n < nblk && ok; ++n) {
+            const int slot = n % DKV_R1;
+            const uint32_t ph = static_cast<uint32_t>((n / DKV_R1) & 1);
+            if (*abort_flag || !mbar_wait(&qfull[slot], ph, 67) ||
+                !mbar_wait(&ofull[slot], ph, 68)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t sQ = s_base + CF::OFF_R1 + slot * CF::SMALL_BYTES;
+            const uint32_t sO = s_base + CF::OFF_R2 + slot * CF::SMALL_BYTES;
+            const uint64_t qh0 = kmajor_desc(sQ, BWD_BLK, 0);
+            const uint64_t ql0 = kmajor_desc(sQ + CF::SMALL_PLANE, BWD_BLK, 0);
+            const uint64_t oh0 = kmajor_desc(sO, BWD_BLK, 0);
+            const uint64_t ol0 = kmajor_desc(sO + CF::SMALL_PLANE, BWD_BLK, 0);
+            const uint32_t ds = tmem + (n % NBUF) * 64, dp = ds + 32;
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+                const uint32_t bb = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
+                const uint32_t sb = (ks >> 1) * (BWD_BLK * 64) + (ks & 1) * 32;
+                const uint32_t acc = ks > 0 ? 1u : 0u;
+                mma_bf16_w(ds, desc_add(kl0, bb), desc_add(qh0, sb), idesc_sd, acc);
+                mma_bf16_w(dp, desc_add(vl0, bb), desc_add(oh0, sb), idesc_sd, acc);
+                mma_bf16_w(ds, desc_add(kh0, bb), desc_add(ql0, sb), idesc_sd, 1u);
+                mma_bf16_w(dp, desc_add(vh0, bb), desc_add(ol0, sb), idesc_sd, 1u);
+                mma_bf16_w(ds, desc_add(kh0, bb), desc_add(qh0, sb), idesc_sd, 1u);
+                mma_bf16_w(dp, desc_add(vh0, bb), desc_add(oh0, sb), idesc_sd, 1u);
+            }
+            mma_commit_w(&sd_full[n % NBUF]);
+            if (n >= DKV_LOOKAHEAD && !issue_acc(n - DKV_LOOKAHEAD))
+                ok = false;
         }
+        for (int i = max(0, nblk - DKV_LOOKAHEAD); i < nblk && ok; ++i)
+            if (!issue_acc(i))
+                ok = false;
+        if (!ok)
+            *abort_flag = 1;
+        mma_commit_w(done);
+        mbar_wait(done, 0, 69);
     } else {
         // ------------------------------------------------ P^T, dS^T, epilogue
         const int grp = (warp - 2) >> 2;  // query blocks n with n % 2 == grp

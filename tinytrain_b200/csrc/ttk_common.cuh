@@ -184,6 +184,46 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
         : "memory");
 }
 
+// Warp-uniform issue: the whole warp executes these with identical operands
+// and lane 0 alone performs the operation (predicated inside the asm), so the
+// surrounding loop stays warp-uniform and its operands can live in uniform
+// registers, instead of being moved there for every instruction as inside a
+// lane-0-only branch.
+__device__ __forceinline__ void mma_bf16_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 l;\n\t"
+        "mov.u32 l, %%laneid;\n\t"
+        "setp.eq.u32 e, l, 0;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_ta_w(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                              uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 l;\n\t"
+        "mov.u32 l, %%laneid;\n\t"
+        "setp.eq.u32 e, l, 0;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Commit by lane 0 of a warp-uniform caller (the lane that issued the MMAs).
+__device__ __forceinline__ void mma_commit_w(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b32 l;\n\t"
+        "mov.u32 l, %%laneid;\n\t"
+        "setp.eq.u32 e, l, 0;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+
 // Arrive on an mbarrier once every tcgen05 op issued so far by this thread
 // has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {

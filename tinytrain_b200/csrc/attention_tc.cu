@@ -351,18 +351,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             m_prev = m_cur;
             m_cur = fmaxf(m_cur, mx * LOG2E);
             const float mc = m_cur == -INFINITY ? 0.0f : m_cur;  // all masked so far
-            const float alpha = exp2f(m_prev - mc);              // 0 when m_prev = -inf
+            const float alpha = exp2_approx(m_prev - mc);        // 0 when m_prev = -inf
             float rs = 0.0f;
             uint32_t hi[16], lo[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-                const float p0 = exp2f(fmaf(s[e], LOG2E, -mc));
-                const float p1 = exp2f(fmaf(s[e + 1], LOG2E, -mc));
+                const float p0 = exp2_approx(fmaf(s[e], LOG2E, -mc));
+                const float p1 = exp2_approx(fmaf(s[e + 1], LOG2E, -mc));
                 rs += p0 + p1;
-                const __nv_bfloat16 h0 = __float2bfloat16_rn(p0), h1 = __float2bfloat16_rn(p1);
-                hi[e / 2] = pack_bf16x2(h0, h1);
-                lo[e / 2] = pack_bf16x2(__float2bfloat16_rn(p0 - __bfloat162float(h0)),
-                                        __float2bfloat16_rn(p1 - __bfloat162float(h1)));
+                split_pair_bf16(p0, p1, hi[e / 2], lo[e / 2]);
             }
             l = l * alpha + rs;
             // P_j -> buffer j % 2, row r, key chunk `half` (64 B per plane),
@@ -382,7 +379,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_arrive(&p_full[j & 1]);
             // fold O_{j-1} (computed with max m_prev) into acc (scaled to m_hist)
             if (j >= 1) {
-                const float sc = m_prev == -INFINITY ? 0.0f : exp2f(m_hist - m_prev);
+                const float sc = m_prev == -INFINITY ? 0.0f : exp2_approx(m_hist - m_prev);
                 if (!fold_o(j - 1, sc)) {
                     ok = false;
                     break;
@@ -391,7 +388,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             m_hist = m_prev;
         }
         if (ok) {
-            const float sc = m_cur == -INFINITY ? 0.0f : exp2f(m_hist - m_cur);
+            const float sc = m_cur == -INFINITY ? 0.0f : exp2_approx(m_hist - m_cur);
             ok = fold_o(nblk - 1, sc);
         }
         if (!ok)

@@ -126,13 +126,14 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t plane_addr, int mn_maj
     return umma_smem_desc(plane_addr + ks * 32, 16, 512, kLayoutSW64);
 }
 
+// Issued by the whole MMA warp (warp-uniform loop); lane 0 performs it.
 template <int PREC>
 __device__ __forceinline__ void mma_split(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
                                           uint32_t acc) {
     if (PREC == PREC_TF32X3)
-        mma_tf32(d, a, b, idesc, acc);
+        mma_tf32_w(d, a, b, idesc, acc);
     else
-        mma_bf16(d, a, b, idesc, acc);
+        mma_bf16_w(d, a, b, idesc, acc);
 }
 
 template <int BN, int PREC>
@@ -231,57 +232,56 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
         }
     } else if (warp == 1) {
         // -------------------------------------------------------- MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = PREC == PREC_TF32X3 ? umma_idesc_tf32(BM, BN, p.a_mn, p.b_mn)
-                                                       : umma_idesc_bf16(BM, BN, p.a_mn, p.b_mn);
-            int s = 0;
-            uint32_t ph = 0;
-            int64_t g = 0;  // chunk counter across this CTA's tiles
-            bool ok = true;
-            for (int64_t t = blockIdx.x; t < p.num_tiles && ok && !*abort_flag; t += gridDim.x) {
-                for (int kc = 0; kc < p.num_k && ok; kc += KCHUNK_BLOCKS, ++g) {
-                    const int buf = static_cast<int>(g % NBUF);
-                    const uint32_t cph = static_cast<uint32_t>((g / NBUF) & 1);
-                    if (!mbar_wait(&cempty[buf], cph ^ 1, 2)) {
+        // The whole warp runs this loop (uniform control flow); lane 0 issues.
+        const uint32_t idesc = PREC == PREC_TF32X3 ? umma_idesc_tf32(BM, BN, p.a_mn, p.b_mn)
+                                                   : umma_idesc_bf16(BM, BN, p.a_mn, p.b_mn);
+        int s = 0;
+        uint32_t ph = 0;
+        int64_t g = 0;  // chunk counter across this CTA's tiles
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < p.num_tiles && ok && !*abort_flag; t += gridDim.x) {
+            for (int kc = 0; kc < p.num_k && ok; kc += KCHUNK_BLOCKS, ++g) {
+                const int buf = static_cast<int>(g % NBUF);
+                const uint32_t cph = static_cast<uint32_t>((g / NBUF) & 1);
+                if (!mbar_wait(&cempty[buf], cph ^ 1, 2)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + buf * BN;
+                const int kend = min(p.num_k, kc + KCHUNK_BLOCKS);
+                for (int kb = kc; kb < kend; ++kb) {
+                    if (!mbar_wait(&full[s], ph, 3)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t d_tmem = tmem_base + buf * BN;
-                    const int kend = min(p.num_k, kc + KCHUNK_BLOCKS);
-                    for (int kb = kc; kb < kend; ++kb) {
-                        if (!mbar_wait(&full[s], ph, 3)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint32_t sa = smem_u32(smem + s * CF::STAGE_BYTES);
-                        const uint32_t sb = sa + CF::A_BYTES;
+                    const uint32_t sa = smem_u32(smem + s * CF::STAGE_BYTES);
+                    const uint32_t sb = sa + CF::A_BYTES;
 #pragma unroll
-                        for (int ks = 0; ks < BK / PR::UK; ++ks) {
-                            const uint64_t a_hi = operand_desc<PREC>(sa, p.a_mn, ks);
-                            const uint64_t a_lo = operand_desc<PREC>(sa + CF::A_PLANE, p.a_mn, ks);
-                            const uint64_t b_hi = operand_desc<PREC>(sb, p.b_mn, ks);
-                            const uint64_t b_lo = operand_desc<PREC>(sb + CF::B_PLANE, p.b_mn, ks);
-                            const uint32_t acc = (kb > kc || ks > 0) ? 1u : 0u;
-                            mma_split<PREC>(d_tmem, a_lo, b_hi, idesc, acc);
-                            mma_split<PREC>(d_tmem, a_hi, b_lo, idesc, 1u);
-                            mma_split<PREC>(d_tmem, a_hi, b_hi, idesc, 1u);
-                        }
-                        mma_commit(&empty[s]);
-                        if (++s == STAGES) {
-                            s = 0;
-                            ph ^= 1;
-                        }
+                    for (int ks = 0; ks < BK / PR::UK; ++ks) {
+                        const uint64_t a_hi = operand_desc<PREC>(sa, p.a_mn, ks);
+                        const uint64_t a_lo = operand_desc<PREC>(sa + CF::A_PLANE, p.a_mn, ks);
+                        const uint64_t b_hi = operand_desc<PREC>(sb, p.b_mn, ks);
+                        const uint64_t b_lo = operand_desc<PREC>(sb + CF::B_PLANE, p.b_mn, ks);
+                        const uint32_t acc = (kb > kc || ks > 0) ? 1u : 0u;
+                        mma_split<PREC>(d_tmem, a_lo, b_hi, idesc, acc);
+                        mma_split<PREC>(d_tmem, a_hi, b_lo, idesc, 1u);
+                        mma_split<PREC>(d_tmem, a_hi, b_hi, idesc, 1u);
                     }
-                    // Fires once every MMA issued so far has retired, also on
-                    // abort, so TMEM is quiescent before the epilogue / dealloc.
-                    mma_commit(&cfull[buf]);
+                    mma_commit_w(&empty[s]);
+                    if (++s == STAGES) {
+                        s = 0;
+                        ph ^= 1;
+                    }
                 }
+                // Fires once every MMA issued so far has retired, also on
+                // abort, so TMEM is quiescent before the epilogue / dealloc.
+                mma_commit_w(&cfull[buf]);
             }
-            if (!ok)
-                *abort_flag = 1;
         }
+        if (!ok)
+            *abort_flag = 1;
     } else {
         // ---------------------------------------------------------- epilogue
         const int e = warp - 2;

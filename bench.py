@@ -16,9 +16,11 @@ value: tokens/s with the token ids already in HBM (tt_trainer_step_device),
 timed with CUDA events on the launching stream, max over ranks.
 e2e: the same through the public C ABI with host buffers (tt_trainer_step:
 host ids uploaded and the loss read back inside the timed region).
-roofline: the dominant kernel (the tcgen05 3xTF32 GEMM) timed live over the
-timed region (events around each launch); achieved = algorithmic FLOPs
-(2*M*N*K per GEMM) / kernel time.
+roofline: the dominant kernel (the tcgen05 GEMM with the bf16x3 operand
+split) timed live over the timed region (events around each launch);
+achieved = algorithmic FLOPs (2*M*N*K per GEMM) / kernel time; traffic = the
+average DRAM bytes per GEMM launch of one llama-1b micro-batch step, from the
+ncu capture summarized in profiles/gemm_traffic_llama1b_microbatch.md.
 """
 from __future__ import annotations
 
@@ -33,6 +35,20 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+
+def gemm_traffic(model):
+    """DRAM bytes per GEMM launch from the committed ncu summary (llama-1b)."""
+    if model != "llama-1b":
+        return None
+    try:
+        with open(os.path.join(ROOT, "profiles", "gemm_traffic_llama1b_microbatch.md")) as f:
+            for ln in f:
+                if ln.startswith("traffic_bytes_per_launch:"):
+                    return float(ln.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
 
 WORKLOADS = {
     "llama-1b": dict(model="llama-1b", vocab=32000, dim=2048, layers=16, heads=16, ffn=5632,
@@ -317,7 +333,7 @@ def main():
             "roofline": {
                 "kernel": f"gemm_split3_kernel (tcgen05, {prec} split)", "bound": "tensor",
                 "achieved": gemm_tf, "peak": bf16s, "unit": "TFLOP/s",
-                "frac": gemm_tf / bf16s, "traffic": None,
+                "frac": gemm_tf / bf16s, "traffic": gemm_traffic(w["model"]),
                 "peak_source": f"{src} bf16 sustained (kernel timed inside a long step)",
                 "achieved_is": "algorithmic fp32 FLOP/s (2MNK per GEMM); each useful FMA "
                                f"costs 3 MMAs, so the {prec} ceiling is peak/{int(ceil_div)}",

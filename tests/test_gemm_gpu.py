@@ -74,6 +74,23 @@ def test_accumulate_beta(cuda):
     assert rel_err(C.cpu().numpy(), ref.cpu().numpy()) < TOL
 
 
+@pytest.mark.parametrize("N", [36, 37, 300])
+@pytest.mark.parametrize("beta", [0.0, 1.0])
+def test_batched_edges_and_epilogue_modes(cuda, N, beta):
+    """Batched GEMM whose tiles overhang M and N: the TMA-store / TMA-add
+    epilogue (N = 36, 300: 16-byte rows) and the direct one (N = 37) give the
+    same values, with beta = 0 (overwrite) and beta = 1 (accumulate)."""
+    from tinytrain_b200 import kernels as K
+    gen = torch.Generator(device=cuda).manual_seed(N + int(beta))
+    A = torch.rand(3, 130, 70, device=cuda, generator=gen) * 2 - 1
+    B = torch.rand(3, 70, N, device=cuda, generator=gen) * 2 - 1
+    C0 = torch.rand(3, 130, N, device=cuda, generator=gen) * 2 - 1
+    C = C0.clone()
+    K.gemm(A, B, C_out=C, beta=beta)
+    ref = beta * C0.double() + A.double() @ B.double()
+    assert rel_err(C.cpu().numpy(), ref.cpu().numpy()) < TOL
+
+
 @pytest.mark.parametrize("M,K,N", [(2048, 256, 256), (2048, 256, 32000), (8192, 768, 2048),
                                    (16384, 2048, 5632)])
 def test_sweep_shapes(cuda, M, K, N):

@@ -36,6 +36,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstdlib>
+#include <cstring>
 #include <string>
 #include <stdint.h>
 
@@ -84,12 +85,21 @@ struct Cfg {
     static constexpr int TMEM_COLS = 512;
     static constexpr int EPI_WARPS = 4 * (BN / 128);  // each thread: 1 row x 128 columns
     static constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
-    static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    // per epilogue warp: a 32 x 32 fp32 staging tile for the TMA store (128B swizzle)
+    static constexpr int EPI_STAGE_BYTES = EPI_WARPS * 4096;
+    static constexpr int SMEM_BYTES =
+        STAGES * STAGE_BYTES + EPI_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+    static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
+
+// C write mode of the epilogue: direct stores (any layout, any beta), or a
+// TMA store (beta = 0) / TMA reduce-add (beta = 1) of 32 x 32 staged tiles.
+enum { C_DIRECT = 0, C_TMA_STORE = 1, C_TMA_ADD = 2 };
 
 struct Params {
     int64_t M, N, K, batch;
     int a_mn, b_mn;  // 1: operand is MN-major in its storage
+    int c_mode;
     float alpha, beta;
     float* C;
     int64_t ldc, strideC;
@@ -139,7 +149,8 @@ __device__ __forceinline__ void mma_split(uint32_t d, uint64_t a, uint64_t b, ui
 template <int BN, int PREC>
 __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
     gemm_split3_kernel(const __grid_constant__ CUtensorMap map_a,
-                       const __grid_constant__ CUtensorMap map_b, const Params p) {
+                       const __grid_constant__ CUtensorMap map_b,
+                       const __grid_constant__ CUtensorMap map_c, const Params p) {
     using CF = Cfg<BN>;
     using PR = Prec<PREC>;
     constexpr int BK = PR::BK;
@@ -148,7 +159,8 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * CF::STAGE_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * CF::STAGE_BYTES +
+                                                 CF::EPI_STAGE_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + STAGES;
     uint64_t* cfull = bars + 2 * STAGES;
@@ -284,15 +296,19 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
             *abort_flag = 1;
     } else {
         // ---------------------------------------------------------- epilogue
+        // Waits are taken by lane 0 and broadcast, so every branch below is
+        // warp-uniform and __syncwarp is always reached by the whole warp.
         const int e = warp - 2;
         const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
         const int col_base = (e >> 2) * 128;
         const int row_in_tile = quarter * 32 + lane;
+        uint8_t* stage_c = smem + STAGES * CF::STAGE_BYTES + e * 4096;  // 32 rows x 128 B
         const bool vec_ok = ((p.ldc & 3) == 0) &&
                             ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0) &&
                             ((p.strideC & 3) == 0);
         int64_t g = 0;
         bool ok = true;
+        bool pending = false;  // lane 0 has a bulk store reading stage_c
         for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
             float acc[128];
 #pragma unroll
@@ -301,7 +317,10 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
             for (int kc = 0; kc < p.num_k; kc += KCHUNK_BLOCKS, ++g) {
                 const int buf = static_cast<int>(g % NBUF);
                 const uint32_t cph = static_cast<uint32_t>((g / NBUF) & 1);
-                if (*abort_flag || !mbar_wait(&cfull[buf], cph, 4)) {
+                int got = 0;
+                if (lane == 0)
+                    got = !*abort_flag && mbar_wait(&cfull[buf], cph, 4);
+                if (!__shfl_sync(0xffffffffu, got, 0)) {
                     ok = false;
                     *abort_flag = 1;
                     break;
@@ -325,6 +344,36 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
                 break;
             int b, mt, nt;
             tile_coords(p, t, b, mt, nt);
+            if (p.c_mode != C_DIRECT) {
+                // 4 subtiles of 32 columns: registers -> 128B-swizzled staging
+                // tile -> one TMA store (or reduce-add) per warp; rows and
+                // columns outside C are clipped by the tensor map.
+#pragma unroll
+                for (int qd = 0; qd < 4; ++qd) {
+                    if (lane == 0 && pending)
+                        bulk_wait_read_all();
+                    __syncwarp();
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const int j = qd * 32 + c * 4;
+                        *reinterpret_cast<float4*>(stage_c + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+                            make_float4(p.alpha * acc[j], p.alpha * acc[j + 1], p.alpha * acc[j + 2],
+                                        p.alpha * acc[j + 3]);
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        const int x = nt * BN + col_base + qd * 32, y = mt * BM + quarter * 32;
+                        if (p.c_mode == C_TMA_ADD)
+                            tma_reduce_add_3d(&map_c, stage_c, x, y, b);
+                        else
+                            tma_store_3d(&map_c, stage_c, x, y, b);
+                        bulk_commit_group();
+                        pending = true;
+                    }
+                }
+                continue;
+            }
             const int64_t row = static_cast<int64_t>(mt) * BM + row_in_tile;
             if (row >= p.M)
                 continue;
@@ -356,6 +405,9 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
                 }
             }
         }
+        // Bulk stores complete before the kernel ends.
+        if (lane == 0 && pending)
+            bulk_wait_all();
     }
 
     tc_fence_before();
@@ -546,8 +598,8 @@ Profiler& prof() {
 }
 
 template <int BN, int PREC>
-int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, gemm::Params p,
-                cudaStream_t stream) {
+int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+                gemm::Params p, cudaStream_t stream) {
     using CF = gemm::Cfg<BN>;
     static bool attr_set[64] = {};
     int dev = 0;
@@ -572,7 +624,8 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, gemm::Params p,
         rec.flops = 2.0 * static_cast<double>(p.M) * p.N * p.K * p.batch;
         cudaEventRecord(rec.a, stream);
     }
-    gemm::gemm_split3_kernel<BN, PREC><<<grid, CF::NUM_THREADS, CF::SMEM_BYTES, stream>>>(ma, mb, p);
+    gemm::gemm_split3_kernel<BN, PREC><<<grid, CF::NUM_THREADS, CF::SMEM_BYTES, stream>>>(ma, mb,
+                                                                                          mc, p);
     const int rc = check_launch("gemm_split3_kernel");
     if (pr.on) {
         cudaEventRecord(rec.b, stream);
@@ -662,6 +715,33 @@ int launch_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64
     return check_launch("split_kernel");
 }
 
+// Tensor map over C (fp32 [batch][M][ldc]) for the epilogue's TMA stores:
+// boxes of 32 x 32 in the 128B swizzle. Returns the epilogue mode: a TMA store
+// for beta = 0, a TMA reduce-add (C += tile, one fp32 add per element) for
+// beta = 1, and direct stores otherwise or when C's layout does not satisfy
+// the TMA alignment rules (16-byte base, row and batch strides).
+int c_tensor_map(CUtensorMap* map, float* C, int64_t M, int64_t N, int64_t ldc, int64_t strideC,
+                 int64_t batch, float beta) {
+    if (beta != 0.0f && beta != 1.0f)
+        return gemm::C_DIRECT;
+    const int64_t bstride = batch > 1 ? strideC : M * ldc;
+    if ((reinterpret_cast<uintptr_t>(C) & 15) || (ldc & 3) || (bstride & 3) || N < 1 || M < 1)
+        return gemm::C_DIRECT;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc)
+        return gemm::C_DIRECT;
+    cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(M),
+                          static_cast<cuuint64_t>(batch)};
+    cuuint64_t strides[2] = {static_cast<cuuint64_t>(ldc) * 4, static_cast<cuuint64_t>(bstride) * 4};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    if (enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, C, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return gemm::C_DIRECT;
+    return beta == 0.0f ? gemm::C_TMA_STORE : gemm::C_TMA_ADD;
+}
+
 template <int PREC>
 int run_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
                  float alpha, const void* a_split, int64_t lda_pad, const void* b_split,
@@ -691,15 +771,17 @@ int run_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, in
     const int64_t tiles256 = p.num_m * ((N + 255) / 256) * batch;
     const bool use128 = N <= 128 || tiles256 < num_sms();
     const int bn = use128 ? 128 : 256;
-    CUtensorMap ma, mb;
+    CUtensorMap ma, mb, mc;
     int rc = make_operand_map<PREC>(&ma, a_split, ga, batch, p.a_mn, gemm::BM);
     if (rc)
         return rc;
     rc = make_operand_map<PREC>(&mb, b_split, gb, batch, p.b_mn, bn);
     if (rc)
         return rc;
-    return use128 ? launch_gemm<128, PREC>(ma, mb, p, stream)
-                  : launch_gemm<256, PREC>(ma, mb, p, stream);
+    std::memset(&mc, 0, sizeof(mc));
+    p.c_mode = c_tensor_map(&mc, C, M, N, ldc, strideC, batch, beta);
+    return use128 ? launch_gemm<128, PREC>(ma, mb, mc, p, stream)
+                  : launch_gemm<256, PREC>(ma, mb, mc, p, stream);
 }
 
 }  // namespace

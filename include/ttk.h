@@ -89,6 +89,16 @@ int ttk_event_synchronize(void* event);
  * depend on the choice. */
 int ttk_gemm_set_precision(int prec);
 int ttk_gemm_get_precision(void);
+/* Problems of at most `macs` multiply-adds (batch*M*N*K; default 2^24) run
+ * as an exact fp32 SIMT GEMM, one fused multiply-add per product in
+ * ascending k, with no workspace: below that size the split's extra launches
+ * cost more than the products, and the result carries no split truncation
+ * (finite-difference gradient checks, as in the reference's
+ * tests/test_autograd.cpp, rely on that). 0 sends every size to the tensor
+ * cores. ttk_gemm_uses_fp32 reports the choice for one problem. */
+int ttk_gemm_set_fp32_max_macs(int64_t macs);
+int64_t ttk_gemm_get_fp32_max_macs(void);
+int ttk_gemm_uses_fp32(int64_t batch, int64_t M, int64_t N, int64_t K);
 size_t ttk_gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
                                int64_t K);
 int ttk_gemm(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,

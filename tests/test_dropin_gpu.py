@@ -51,3 +51,20 @@ def test_reference_train_program_on_b200(cuda, tmp_path, extra):
     w_ours = rb.load_checkpoint(c, str(tmp_path / "b200" / "ckpt-final"))
     assert w_ref.shape == w_ours.shape
     assert np.abs(w_ref - w_ours).max() <= 1e-2
+
+
+REF_TESTS_B200 = os.path.join(ROOT, "oracle", "_ref", "ref_tests_b200")
+
+
+def test_reference_unit_tests_on_b200(cuda, tmp_path):
+    """The reference's own unit tests (tests/test_scaffold.cpp,
+    tests/test_autograd.cpp, tests/test_model.cpp: finite-difference
+    gradchecks of every op and of a tiny transformer, AdamW/SGD convergence,
+    the checkpoint format), compiled unmodified against this library on the
+    gtest-compatible harness, pass with every op on the device."""
+    if not os.path.exists(REF_TESTS_B200):
+        pytest.skip("oracle/_ref/ref_tests_b200 not built (it needs the reference sources)")
+    r = subprocess.run([REF_TESTS_B200], capture_output=True, text=True, timeout=600,
+                       cwd=str(tmp_path))
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]
+    assert "[  PASSED  ] 22 tests." in r.stdout, r.stdout[-2000:]

@@ -17,6 +17,18 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-4
 
 
+@pytest.fixture(autouse=True)
+def tensor_cores_at_every_size(cuda):
+    """These tests cover the tcgen05 kernel, its tile edges included: small
+    problems, which ttk_gemm otherwise runs as exact fp32 SIMT, are sent to
+    the tensor cores too (tests/test_gemm_fp32_gpu.py covers that path)."""
+    from tinytrain_b200 import _ttk
+    old = _ttk.call("ttk_gemm_get_fp32_max_macs")
+    _ttk.call("ttk_gemm_set_fp32_max_macs", 0)
+    yield
+    _ttk.call("ttk_gemm_set_fp32_max_macs", old)
+
+
 def t(a, dev):
     return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
 

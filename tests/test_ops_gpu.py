@@ -60,6 +60,64 @@ def test_rmsnorm_sizes(cuda, R, D):
     assert rel_err(n(dw), dwr) < TOL
 
 
+@pytest.mark.parametrize("R,D", [(1000, 2048), (16384, 2048), (37, 256)])
+def test_rmsnorm_bwd_accumulates(cuda, R, D):
+    """dx += and dw += into existing gradients (the residual stream's
+    gradient in a transformer block), row counts that leave the last sweep of
+    the row-parallel kernel partly empty."""
+    from oracle import restate as rs
+    from tinytrain_b200 import kernels as K
+    rng = np.random.default_rng(7 * R + D)
+    x = rng.uniform(-1, 1, (R, D)).astype(np.float32)
+    w = rng.uniform(-1, 1, D).astype(np.float32)
+    gy = rng.uniform(-1, 1, (R, D)).astype(np.float32)
+    dx0 = rng.uniform(-1, 1, (R, D)).astype(np.float32)
+    dw0 = rng.uniform(-1, 1, D).astype(np.float32)
+    _, rstd = K.rmsnorm_fwd(t(x, cuda), t(w, cuda), 1e-5)
+    dx, dw = t(dx0, cuda), t(dw0, cuda)
+    K.rmsnorm_bwd(t(x, cuda), t(w, cuda), rstd, t(gy, cuda), dx=dx, dw=dw, accumulate=True)
+    _, rr = rs.rmsnorm(x, w, 1e-5)
+    dxr, dwr = rs.rmsnorm_bwd(x, w, rr, gy)
+    assert rel_err(n(dx), dxr + dx0) < TOL
+    assert rel_err(n(dw), dwr + dw0) < TOL
+
+
+@pytest.mark.parametrize("shape,bshape,offset", [
+    ((4096,), (4096,), 0), ((1027,), (1027,), 0), ((8, 2048, 64), (8, 2048, 64), 0),
+    ((3, 1, 5), (3, 1, 5), 0), ((4096,), (4096,), 1), ((6, 33), (33,), 0), ((6, 33), (6, 1), 0)])
+def test_binary_paths_bitexact(cuda, shape, bshape, offset):
+    """Elementwise add/sub/mul/div on the vector path (same-shape contiguous,
+    16-byte aligned) and on the strided path (broadcast, or an operand one
+    element off alignment) equal numpy's IEEE results bit for bit."""
+    from tinytrain_b200 import _ttk
+    import ctypes as C
+    rng = np.random.default_rng(len(shape) * 100 + offset)
+    a = rng.uniform(-2, 2, shape).astype(np.float32)
+    b = rng.uniform(0.5, 2, bshape).astype(np.float32)
+    full = np.broadcast_shapes(shape, bshape)
+    bb = np.broadcast_to(b, full)
+    nd = len(full)
+    ext = (C.c_int64 * nd)(*full)
+
+    def strides(arr_shape):
+        pad = (1,) * (nd - len(arr_shape)) + tuple(arr_shape)
+        st, acc = [0] * nd, 1
+        for d in range(nd - 1, -1, -1):
+            st[d] = 0 if pad[d] == 1 and full[d] != 1 else acc
+            acc *= pad[d]
+        return (C.c_int64 * nd)(*st)
+
+    abuf = torch.zeros(a.size + offset, dtype=torch.float32, device=cuda)
+    abuf[offset:] = t(a.ravel(), cuda)
+    da, db = abuf[offset:], t(b.ravel(), cuda)
+    out = torch.empty(int(np.prod(full)), dtype=torch.float32, device=cuda)
+    for op, f in enumerate([np.add, np.subtract, np.multiply, np.divide]):
+        _ttk.call("ttk_binary", op, da.data_ptr(), strides(shape), db.data_ptr(), strides(bshape),
+                  out.data_ptr(), ext, nd, torch.cuda.current_stream().cuda_stream)
+        ref = f(np.broadcast_to(a, full), bb).astype(np.float32).ravel()
+        assert np.array_equal(n(out).view(np.uint32), ref.view(np.uint32)), op
+
+
 def test_swiglu_golden(cuda, golden_ops):
     from tinytrain_b200 import kernels as K
     g = golden_ops

@@ -23,6 +23,17 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-4
 
 
+@pytest.fixture(autouse=True)
+def tensor_cores_at_every_size(cuda):
+    """The cases below are small enough for ttk_gemm's exact fp32 path; send
+    them to the tensor cores so that the split operands use the scratch."""
+    from tinytrain_b200 import _ttk
+    old = _ttk.call("ttk_gemm_get_fp32_max_macs")
+    _ttk.call("ttk_gemm_set_fp32_max_macs", 0)
+    yield
+    _ttk.call("ttk_gemm_set_fp32_max_macs", old)
+
+
 def _gemm_ref(A, B, tA, tB, M, N, K, stream):
     from tinytrain_b200 import _ttk
     Cm = torch.empty(M, N, device=A.device)

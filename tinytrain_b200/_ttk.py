@@ -49,6 +49,9 @@ SIGS = {
     "ttk_event_synchronize": (I32, [P]),
     "ttk_gemm_set_precision": (I32, [I32]),
     "ttk_gemm_get_precision": (I32, []),
+    "ttk_gemm_set_fp32_max_macs": (I32, [I64]),
+    "ttk_gemm_get_fp32_max_macs": (I64, []),
+    "ttk_gemm_uses_fp32": (I32, [I64, I64, I64, I64]),
     "ttk_gemm_workspace_size": (SZ, [I32, I32, I64, I64, I64, I64]),
     "ttk_gemm": (I32, [I32, I32, I64, I64, I64, I64, F32, P, I64, I64, P, I64, I64, F32, P, I64,
                        I64, P, SZ, P]),
@@ -114,7 +117,9 @@ SIGS = {
     "ttk_dist_abort": (I32, [P]),
 }
 
-STATUS_FNS = {k for k, (r, _) in SIGS.items() if r is I32}
+# int-returning functions that return a value, not a status
+VALUE_FNS = {"ttk_gemm_get_precision", "ttk_attention_get_impl", "ttk_gemm_uses_fp32"}
+STATUS_FNS = {k for k, (r, _) in SIGS.items() if r is I32 and k not in VALUE_FNS}
 
 
 class TtkError(RuntimeError):

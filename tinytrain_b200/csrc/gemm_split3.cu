@@ -485,6 +485,72 @@ __global__ void scale_kernel(float* C, int64_t batch, int64_t M, int64_t N, int6
     }
 }
 
+// Exact fp32 GEMM for small problems (at most gemm_fp32_max_macs()
+// multiply-adds): C = alpha * op(A) op(B) + beta * C with one fp32 fused
+// multiply-add per product in ascending k, the reference's sgemm arithmetic
+// (ops.cpp:96-125). A 256-thread block owns a 32 x 32 tile of C (a column
+// per lane, four rows per warp) and stages 32-deep slices of op(A) and op(B)
+// in shared memory, zero outside the matrix. Below this size the operand
+// split's extra launches cost more than the products, and the result is
+// as smooth in the inputs as an fp32 loop: finite-difference gradient checks
+// see no split truncation steps.
+constexpr int F32_T = 32;
+__global__ void __launch_bounds__(256) gemm_fp32_kernel(
+    int ta, int tb, int64_t M, int64_t N, int64_t K, float alpha, const float* __restrict__ A,
+    int64_t lda, int64_t sA, const float* __restrict__ B, int64_t ldb, int64_t sB, float beta,
+    float* __restrict__ C, int64_t ldc, int64_t sC) {
+    __shared__ float as[F32_T][F32_T + 1];  // [m][k]
+    __shared__ float bs[F32_T][F32_T + 1];  // [k][n]
+    const int64_t bat = blockIdx.z;
+    const int64_t m0 = static_cast<int64_t>(blockIdx.y) * F32_T;
+    const int64_t n0 = static_cast<int64_t>(blockIdx.x) * F32_T;
+    A += bat * sA, B += bat * sB, C += bat * sC;
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t k0 = 0; k0 < K; k0 += F32_T) {
+        for (int i = threadIdx.x; i < F32_T * F32_T; i += 256) {
+            const int r = i >> 5, c = i & 31;
+            // op(A)[m][k]: r = m offset, c = k offset (k-contiguous for ta = 0)
+            const int64_t am = m0 + (ta ? c : r), ak = k0 + (ta ? r : c);
+            float av = 0.0f;
+            if (am < M && ak < K)
+                av = ta ? A[ak * lda + am] : A[am * lda + ak];
+            if (ta)
+                as[c][r] = av;
+            else
+                as[r][c] = av;
+            // op(B)[k][n]: r = k offset, c = n offset (n-contiguous for tb = 0)
+            const int64_t bk = k0 + (tb ? c : r), bn = n0 + (tb ? r : c);
+            float bv = 0.0f;
+            if (bk < K && bn < N)
+                bv = tb ? B[bn * ldb + bk] : B[bk * ldb + bn];
+            if (tb)
+                bs[c][r] = bv;
+            else
+                bs[r][c] = bv;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < F32_T; ++kk) {
+            const float bv = bs[kk][lane];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                acc[i] = fmaf(as[wp + 8 * i][kk], bv, acc[i]);
+        }
+        __syncthreads();
+    }
+    const int64_t n = n0 + lane;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int64_t m = m0 + wp + 8 * i;
+        if (m < M && n < N) {
+            float* c = C + m * ldc + n;
+            const float r = alpha * acc[i];
+            *c = beta == 0.0f ? r : r + beta * *c;
+        }
+    }
+}
+
 }  // namespace gemm
 
 // ------------------------------------------------------------- host side --
@@ -795,9 +861,31 @@ int gemm_set_precision(int prec) {
 
 int gemm_get_precision() { return current_prec(); }
 
+namespace {
+int64_t g_fp32_max_macs = int64_t(1) << 24;
+}
+
+int gemm_set_fp32_max_macs(int64_t macs) {
+    if (macs < 0)
+        return set_error(TTK_ERR_ARG, "gemm: fp32 size limit must be >= 0");
+    g_fp32_max_macs = macs;
+    return TTK_OK;
+}
+
+int64_t gemm_fp32_max_macs() { return g_fp32_max_macs; }
+
+bool gemm_uses_fp32(int64_t batch, int64_t M, int64_t N, int64_t K) {
+    if (batch <= 0 || M <= 0 || N <= 0 || K <= 0 || batch > 65535 ||
+        (M + gemm::F32_T - 1) / gemm::F32_T > 65535)
+        return false;
+    // Overflow-safe batch * M * N * K <= limit.
+    double macs = static_cast<double>(batch) * M * N * K;
+    return macs <= static_cast<double>(g_fp32_max_macs);
+}
+
 size_t gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
                            int64_t K) {
-    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0)
+    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || gemm_uses_fp32(batch, M, N, K))
         return 0;
     return plan(current_prec(), transA, transB, batch, M, N, K).total;
 }
@@ -831,12 +919,21 @@ int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_
     }
     if (M > (1ll << 31) / 2 || N > (1ll << 31) / 2 || K > (1ll << 31) / 2)
         return set_error(TTK_ERR_ARG, "gemm: dimension too large");
+    if ((transA ? lda < M : lda < K) || (transB ? ldb < K : ldb < N))
+        return set_error(TTK_ERR_ARG, "gemm: leading dimension too small");
+    if (gemm_uses_fp32(batch, M, N, K)) {
+        const dim3 grid(static_cast<unsigned>((N + gemm::F32_T - 1) / gemm::F32_T),
+                        static_cast<unsigned>((M + gemm::F32_T - 1) / gemm::F32_T),
+                        static_cast<unsigned>(batch));
+        gemm::gemm_fp32_kernel<<<grid, 256, 0, stream>>>(transA, transB, M, N, K, alpha, A, lda,
+                                                         strideA, B, ldb, strideB, beta, C, ldc,
+                                                         strideC);
+        return check_launch("gemm_fp32_kernel");
+    }
     const int prec = current_prec();
     const GemmPlan pl = plan(prec, transA, transB, batch, M, N, K);
     if (!ws || ws_bytes < pl.total)
         return set_error(TTK_ERR_ARG, "gemm: workspace too small");
-    if ((transA ? lda < M : lda < K) || (transB ? ldb < K : ldb < N))
-        return set_error(TTK_ERR_ARG, "gemm: leading dimension too small");
     void* wa = ws;
     void* wb = static_cast<char*>(ws) + pl.off_b;
     if (prec == gemm::PREC_TF32X3) {

@@ -63,6 +63,30 @@ __global__ void binary_kernel(int op, const float* __restrict__ a, const float* 
     }
 }
 
+// Same-shape contiguous operands (the residual adds of a transformer block):
+// 16-byte vector loads and stores, no index decode. Same arithmetic as
+// binary_kernel, element for element.
+template <int OP>
+__global__ void binary_contig_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                     float* __restrict__ out, int64_t n) {
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t n4 = n / 4;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += stride) {
+        const float4 x = reinterpret_cast<const float4*>(a)[i];
+        const float4 y = reinterpret_cast<const float4*>(b)[i];
+        float4 r;
+        r.x = bin_fwd(OP, x.x, y.x);
+        r.y = bin_fwd(OP, x.y, y.y);
+        r.z = bin_fwd(OP, x.z, y.z);
+        r.w = bin_fwd(OP, x.w, y.w);
+        reinterpret_cast<float4*>(out)[i] = r;
+    }
+    for (int64_t i = n4 * 4 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += stride)
+        out[i] = bin_fwd(OP, a[i], b[i]);
+}
+
 __global__ void binary_grad_kernel(int op, int which, const float* __restrict__ a,
                                    const float* __restrict__ b, const float* __restrict__ g,
                                    float* __restrict__ gf, Shape8 s, int64_t total) {
@@ -316,6 +340,26 @@ int ttk_binary(int op, const float* a, const int64_t* a_strides, const float* b,
     int rc = fill_shape(s, shape, ndim, a_strides, b_strides, total);
     if (rc || !total)
         return rc;
+    // Row-major contiguous strides on both inputs (extent-1 dims may carry any
+    // stride) and 16-byte aligned pointers: the vector path.
+    bool contig = ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                    reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+    int64_t expect = 1;
+    for (int d = ndim - 1; d >= 0 && contig; --d) {
+        if (s.n[d] != 1 && (s.sa[d] != expect || s.sb[d] != expect))
+            contig = false;
+        expect *= s.n[d];
+    }
+    if (contig) {
+        const unsigned grid = grid_for(total / 4 + 1, 256);
+        switch (op) {
+            case 0: binary_contig_kernel<0><<<grid, 256, 0, S(stream)>>>(a, b, out, total); break;
+            case 1: binary_contig_kernel<1><<<grid, 256, 0, S(stream)>>>(a, b, out, total); break;
+            case 2: binary_contig_kernel<2><<<grid, 256, 0, S(stream)>>>(a, b, out, total); break;
+            default: binary_contig_kernel<3><<<grid, 256, 0, S(stream)>>>(a, b, out, total); break;
+        }
+        return check_launch("binary_contig_kernel");
+    }
     binary_kernel<<<grid_for(total, 256), 256, 0, S(stream)>>>(op, a, b, out, s, total);
     return check_launch("binary_kernel");
 }

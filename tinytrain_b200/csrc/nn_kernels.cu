@@ -170,50 +170,69 @@ __global__ void rmsnorm_bwd_rows_kernel(const float* __restrict__ x, const float
     const float4 w0 = *reinterpret_cast<const float4*>(w + c0);
     const float4 w1 = *reinterpret_cast<const float4*>(w + c1);
     const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    const bool acc = dx && accumulate;
     float dw[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // One row's operands: x, dy, the dx being accumulated into, and rstd. The
+    // next row's are loaded before this row's reduction, so two rows of loads
+    // are in flight per thread.
+    struct RowIn {
+        float4 x0, x1, g0, g1, q0, q1;
+        float r;
+    };
+    auto load = [&](int64_t row) {
+        RowIn v;
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        v.x0 = v.x1 = v.g0 = v.g1 = v.q0 = v.q1 = z;
+        v.r = 0.0f;
+        if (row < R) {
+            v.x0 = *reinterpret_cast<const float4*>(x + row * D + c0);
+            v.x1 = *reinterpret_cast<const float4*>(x + row * D + c1);
+            v.g0 = *reinterpret_cast<const float4*>(dy + row * D + c0);
+            v.g1 = *reinterpret_cast<const float4*>(dy + row * D + c1);
+            if (acc) {
+                v.q0 = *reinterpret_cast<const float4*>(dx + row * D + c0);
+                v.q1 = *reinterpret_cast<const float4*>(dx + row * D + c1);
+            }
+            v.r = rstd[row];
+        }
+        return v;
+    };
+    const int64_t step = static_cast<int64_t>(gridDim.x) * rpb;
     int parity = 0;
+    RowIn cur = load(static_cast<int64_t>(blockIdx.x) * rpb + slot);
     for (int64_t base = static_cast<int64_t>(blockIdx.x) * rpb; base < R;
-         base += static_cast<int64_t>(gridDim.x) * rpb, parity ^= 1) {
+         base += step, parity ^= 1) {
         const int64_t row = base + slot;
         const bool ok = row < R;
-        float xv[8] = {}, gv[8] = {};
-        float r = 0.0f;
-        if (ok) {
-            const float4 a = *reinterpret_cast<const float4*>(x + row * D + c0);
-            const float4 b = *reinterpret_cast<const float4*>(x + row * D + c1);
-            const float4 g0 = *reinterpret_cast<const float4*>(dy + row * D + c0);
-            const float4 g1 = *reinterpret_cast<const float4*>(dy + row * D + c1);
-            xv[0] = a.x, xv[1] = a.y, xv[2] = a.z, xv[3] = a.w;
-            xv[4] = b.x, xv[5] = b.y, xv[6] = b.z, xv[7] = b.w;
-            gv[0] = g0.x, gv[1] = g0.y, gv[2] = g0.z, gv[3] = g0.w;
-            gv[4] = g1.x, gv[5] = g1.y, gv[6] = g1.z, gv[7] = g1.w;
-            r = rstd[row];
-        }
+        const RowIn nxt = load(row + step);
+        const float xv[8] = {cur.x0.x, cur.x0.y, cur.x0.z, cur.x0.w,
+                             cur.x1.x, cur.x1.y, cur.x1.z, cur.x1.w};
+        const float gv[8] = {cur.g0.x, cur.g0.y, cur.g0.z, cur.g0.w,
+                             cur.g1.x, cur.g1.y, cur.g1.z, cur.g1.w};
+        const float r = cur.r;
         float dot = 0.0f;
 #pragma unroll
         for (int e = 0; e < 8; ++e)
             dot += gv[e] * wv[e] * xv[e];
         dot = block_row_sum(dot, red, slot, t, tpr, parity);
-        if (!ok)
-            continue;
-        const float k = r * r * r / static_cast<float>(D) * dot;
-        float o[8];
+        if (ok) {
+            const float k = r * r * r / static_cast<float>(D) * dot;
+            float o[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            o[e] = r * (gv[e] * wv[e]) - xv[e] * k;
-            dw[e] += gv[e] * xv[e] * r;
-        }
-        if (dx) {
-            float4* p0 = reinterpret_cast<float4*>(dx + row * D + c0);
-            float4* p1 = reinterpret_cast<float4*>(dx + row * D + c1);
-            if (accumulate) {
-                const float4 q0 = *p0, q1 = *p1;
-                o[0] += q0.x, o[1] += q0.y, o[2] += q0.z, o[3] += q0.w;
-                o[4] += q1.x, o[5] += q1.y, o[6] += q1.z, o[7] += q1.w;
+            for (int e = 0; e < 8; ++e) {
+                o[e] = r * (gv[e] * wv[e]) - xv[e] * k;
+                dw[e] += gv[e] * xv[e] * r;
             }
-            *p0 = make_float4(o[0], o[1], o[2], o[3]);
-            *p1 = make_float4(o[4], o[5], o[6], o[7]);
+            if (dx) {
+                if (acc) {
+                    o[0] += cur.q0.x, o[1] += cur.q0.y, o[2] += cur.q0.z, o[3] += cur.q0.w;
+                    o[4] += cur.q1.x, o[5] += cur.q1.y, o[6] += cur.q1.z, o[7] += cur.q1.w;
+                }
+                *reinterpret_cast<float4*>(dx + row * D + c0) = make_float4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<float4*>(dx + row * D + c1) = make_float4(o[4], o[5], o[6], o[7]);
+            }
         }
+        cur = nxt;
     }
     if (partial) {
         float* pr = partial + (static_cast<int64_t>(blockIdx.x) * rpb + slot) * D;
@@ -222,15 +241,34 @@ __global__ void rmsnorm_bwd_rows_kernel(const float* __restrict__ x, const float
     }
 }
 
-// dw[c] += sum_b partial[b][c], b ascending.
+// dw[c] += sum_b partial[b][c] over nb partial rows. A block of 8 warps owns
+// 32 adjacent columns (one per lane, 128-byte row segments); warp w sums rows
+// b = w, w + 8, ... in ascending order and the eight warp sums are added in
+// warp order: a fixed summation order, so the result is deterministic.
+constexpr int COLSUM_THREADS = 256;
 __global__ void colsum_kernel(const float* __restrict__ partial, int64_t nb, int64_t D,
                               float* __restrict__ out) {
-    for (int64_t c = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; c < D;
-         c += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    __shared__ float red[8][32];
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    for (int64_t cb = static_cast<int64_t>(blockIdx.x) * 32; cb < D;
+         cb += static_cast<int64_t>(gridDim.x) * 32) {
+        const int64_t c = cb + lane;
         float s = 0.0f;
-        for (int64_t b = 0; b < nb; ++b)
-            s += partial[b * D + c];
-        out[c] += s;
+        if (c < D) {
+#pragma unroll 4
+            for (int64_t b = wp; b < nb; b += 8)
+                s += partial[b * D + c];
+        }
+        red[wp][lane] = s;
+        __syncthreads();
+        if (wp == 0 && c < D) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                tot += red[i][lane];
+            out[c] += tot;
+        }
+        __syncthreads();
     }
 }
 
@@ -716,6 +754,10 @@ int ttk_rmsnorm_fwd(const float* x, const float* w, float* y, float* rstd, int64
     return check_launch("rmsnorm_fwd_kernel");
 }
 
+static int colsum_grid(int64_t D) {
+    return static_cast<int>(std::min<int64_t>((D + 31) / 32, 148 * 8));
+}
+
 static int64_t rms_blocks(int64_t R) { return std::min<int64_t>(std::max<int64_t>(R / 64, 1), 296); }
 
 // Row-parallel backward: blocks and dw partial rows (one per row slot).
@@ -754,7 +796,7 @@ int ttk_rmsnorm_bwd(const float* x, const float* w, const float* rstd, const flo
         if (rc || !dw)
             return rc;
         const int64_t nparts = nbk * (bs / static_cast<int>(D / RMS_EPT));
-        colsum_kernel<<<grid_for(D, 256), 256, 0, S(stream)>>>(partial, nparts, D, dw);
+        colsum_kernel<<<colsum_grid(D), COLSUM_THREADS, 0, S(stream)>>>(partial, nparts, D, dw);
         return check_launch("colsum_kernel");
     }
     const int64_t nb = rms_blocks(R);
@@ -770,7 +812,7 @@ int ttk_rmsnorm_bwd(const float* x, const float* w, const float* rstd, const flo
     int rc = check_launch("rmsnorm_bwd_kernel");
     if (rc || !dw)
         return rc;
-    colsum_kernel<<<grid_for(D, 256), 256, 0, S(stream)>>>(partial, nb, D, dw);
+    colsum_kernel<<<colsum_grid(D), COLSUM_THREADS, 0, S(stream)>>>(partial, nb, D, dw);
     return check_launch("colsum_kernel");
 }
 

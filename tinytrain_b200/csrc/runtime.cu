@@ -218,6 +218,14 @@ int ttk_gemm_set_precision(int prec) { return gemm_set_precision(prec); }
 
 int ttk_gemm_get_precision(void) { return gemm_get_precision(); }
 
+int ttk_gemm_set_fp32_max_macs(int64_t macs) { return gemm_set_fp32_max_macs(macs); }
+
+int64_t ttk_gemm_get_fp32_max_macs(void) { return gemm_fp32_max_macs(); }
+
+int ttk_gemm_uses_fp32(int64_t batch, int64_t M, int64_t N, int64_t K) {
+    return gemm_uses_fp32(batch, M, N, K) ? 1 : 0;
+}
+
 int ttk_profile_enable(int on) { return gemm_profile_enable(on); }
 
 int ttk_profile_read(double* gemm_ms, double* gemm_flops, int64_t* launches) {

@@ -44,6 +44,9 @@ int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t
                int64_t batch, float* dst, int64_t ld_pad, cudaStream_t stream);
 int gemm_set_precision(int prec);
 int gemm_get_precision();
+int gemm_set_fp32_max_macs(int64_t macs);
+int64_t gemm_fp32_max_macs();
+bool gemm_uses_fp32(int64_t batch, int64_t M, int64_t N, int64_t K);
 int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
              const float* A, int64_t lda, int64_t strideA, const float* B, int64_t ldb,
              int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC, void* ws,

@@ -225,7 +225,9 @@ void gemm(int ta, int tb, int64_t batch, int64_t M, int64_t N, int64_t K, GemmAr
           float beta, float* C, int64_t ldc, int64_t sC) {
     if (M == 0 || N == 0 || batch == 0)
         return;
-    if (K == 0) {
+    // K = 0 (C = beta * C) and small problems (the exact fp32 kernel) take no
+    // operand split.
+    if (K == 0 || ttk_gemm_uses_fp32(batch, M, N, K)) {
         check(ttk_gemm(ta, tb, batch, M, N, K, 1.0f, A.ptr, A.ld, A.bs, B.ptr, B.ld, B.bs, beta, C,
                        ldc, sC, nullptr, 0, stream()),
               "gemm");

@@ -89,6 +89,13 @@ int ttk_event_synchronize(void* event);
  * depend on the choice. */
 int ttk_gemm_set_precision(int prec);
 int ttk_gemm_get_precision(void);
+/* Large bf16-split problems run 256 x 256 tiles on CTA pairs (clusters of two
+ * SMs sharing one M = 256 tcgen05 MMA; each SM loads half the operand tiles
+ * of a 128 x 256 tile). Mode 1 (default): pairs when N > 128 and the 256 x 256
+ * tiles occupy every resident pair; 0: single-CTA tiles only; 2: pairs
+ * whenever N > 128. TTK_GEMM_PAIRS=0|1|2 selects the mode at start-up. */
+int ttk_gemm_set_cta_pairs(int mode);
+int ttk_gemm_get_cta_pairs(void);
 /* Problems of at most `macs` multiply-adds (batch*M*N*K; default 2^24) run
  * as an exact fp32 SIMT GEMM, one fused multiply-add per product in
  * ascending k, with no workspace: below that size the split's extra launches

@@ -103,6 +103,52 @@ def test_batched_edges_and_epilogue_modes(cuda, N, beta):
     assert rel_err(C.cpu().numpy(), ref.cpu().numpy()) < TOL
 
 
+@pytest.fixture
+def pair_mode(cuda):
+    """Sets the CTA-pair mode for one test and restores the previous one."""
+    from tinytrain_b200 import _ttk
+    old = _ttk.call("ttk_gemm_get_cta_pairs")
+
+    def set_mode(m):
+        _ttk.call("ttk_gemm_set_cta_pairs", m)
+    yield set_mode
+    _ttk.call("ttk_gemm_set_cta_pairs", old)
+
+
+@pytest.mark.parametrize("tA,tB", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("batch,M,N,K", [(1, 300, 520, 200), (3, 130, 300, 70),
+                                         (1, 2248, 1000, 1000), (2, 256, 256, 32)])
+def test_cta_pair_tiles(cuda, pair_mode, tA, tB, batch, M, N, K):
+    """256 x 256 tiles on CTA pairs (cta_group::2), forced onto small problems
+    whose last tiles overhang M (a pair's second CTA partly or wholly past the
+    last row) and N, with both operand orientations, several K chunks, and
+    the three epilogue modes (TMA store for beta = 0, TMA reduce-add for
+    beta = 1, direct stores otherwise). Equal to fp64 within the bound, and to
+    the single-CTA kernel bit for bit (the same products summed in the same
+    order)."""
+    from tinytrain_b200 import kernels as Kn
+    gen = torch.Generator(device=cuda).manual_seed(M + N + K + 10 * tA + tB)
+    A = torch.rand((batch, K, M) if tA else (batch, M, K), device=cuda, generator=gen) * 2 - 1
+    B = torch.rand((batch, N, K) if tB else (batch, K, N), device=cuda, generator=gen) * 2 - 1
+    C0 = torch.rand(batch, M, N, device=cuda, generator=gen) * 2 - 1
+    oA = A.double().transpose(1, 2) if tA else A.double()
+    oB = B.double().transpose(1, 2) if tB else B.double()
+    prod = oA @ oB
+    for alpha, beta in [(1.0, 0.0), (1.0, 1.0), (0.5, -2.0)]:
+        out = {}
+        for mode in (2, 0):
+            pair_mode(mode)
+            C = C0.clone()
+            Kn.gemm(A, B, transA=bool(tA), transB=bool(tB), C_out=C, alpha=alpha, beta=beta)
+            torch.cuda.synchronize()
+            out[mode] = C
+        ref = alpha * prod + beta * C0.double()
+        assert rel_err(out[2].cpu().numpy(), ref.cpu().numpy()) < TOL, (alpha, beta)
+        assert torch.equal(out[2], out[0]), (alpha, beta)
+    from tinytrain_b200 import _ttk
+    assert _ttk.device_status() == 0
+
+
 @pytest.mark.parametrize("M,K,N", [(2048, 256, 256), (2048, 256, 32000), (8192, 768, 2048),
                                    (16384, 2048, 5632)])
 def test_sweep_shapes(cuda, M, K, N):

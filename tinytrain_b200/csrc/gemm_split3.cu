@@ -19,6 +19,14 @@
 // Both smem layouts have 64-byte rows per k-slice (BK = 16 fp32 or 32 bf16),
 // so the pipeline geometry is shared.
 //
+// CTA pairs (bf16 split, large problems): a cluster of two CTAs computes a
+// 256 x 256 tile with tcgen05.mma.cta_group::2 (M = 256) issued by rank 0.
+// Each CTA loads its 128 rows of A and 128 of the 256 rows of B into its own
+// shared memory (a 6-stage ring of 32 KB stages), both CTAs' TMA loads complete
+// on rank 0's barrier, the MMA commits arrive on both CTAs' barriers, and each
+// CTA drains its own 128 accumulator rows from its own TMEM. Per SM this halves
+// the B traffic of a 128 x 256 tile; results equal the single-CTA kernel's.
+//
 // Kernel structure (persistent, one CTA per SM, 64 + 32*EPI_WARPS threads):
 //   warp 0      TMA producer: 4-stage ring of {A hi|lo, B hi|lo} K-slices
 //               (64 B rows), one TMA per operand per stage (hi and lo planes
@@ -51,7 +59,6 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int ROW_BYTES = 64;  // one k-slice row of an operand tile (SW64)
-constexpr int STAGES = 4;
 constexpr int GROUP_M = 16;  // tile raster: bands of 16 M-tiles sweep N
 // K extent accumulated inside TMEM before the partial sum is promoted to the
 // epilogue's fp32 registers. The tensor-core accumulator rounds with a bias
@@ -74,13 +81,19 @@ struct Prec {
     static constexpr int MN_ROW_BYTES = 32 * ELT;
 };
 
-template <int BN>
+// PAIR: a CTA pair (cluster of two, cta_group::2) computes a 256 x BN tile
+// with M = 256 MMAs issued by rank 0; each CTA loads its 128 rows of A and
+// BN/2 rows of B (half the operand traffic per SM of a 128 x BN tile) and
+// drains its own 128 accumulator rows.
+template <int BN, bool PAIR = false>
 struct Cfg {
+    static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of B held by one CTA
     static constexpr int A_PLANE = BM * ROW_BYTES;
-    static constexpr int B_PLANE = BN * ROW_BYTES;
+    static constexpr int B_PLANE = B_ROWS * ROW_BYTES;
     static constexpr int A_BYTES = 2 * A_PLANE;  // hi | lo
     static constexpr int B_BYTES = 2 * B_PLANE;
     static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGES = PAIR ? 6 : 4;
     static constexpr int NBUF = 512 / BN;            // TMEM chunk buffers
     static constexpr int TMEM_COLS = 512;
     static constexpr int EPI_WARPS = 4 * (BN / 128);  // each thread: 1 row x 128 columns
@@ -90,6 +103,7 @@ struct Cfg {
     static constexpr int SMEM_BYTES =
         STAGES * STAGE_BYTES + EPI_STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
     static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+    static_assert(!PAIR || BN == 256, "CTA pairs use 256 x 256 tiles");
 };
 
 // C write mode of the epilogue: direct stores (any layout, any beta), or a
@@ -146,16 +160,19 @@ __device__ __forceinline__ void mma_split(uint32_t d, uint64_t a, uint64_t b, ui
         mma_bf16_w(d, a, b, idesc, acc);
 }
 
-template <int BN, int PREC>
-__global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
+template <int BN, int PREC, bool PAIR>
+__global__ void __launch_bounds__(Cfg<BN, PAIR>::NUM_THREADS, 1)
     gemm_split3_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b,
                        const __grid_constant__ CUtensorMap map_c, const Params p) {
-    using CF = Cfg<BN>;
+    using CF = Cfg<BN, PAIR>;
     using PR = Prec<PREC>;
     constexpr int BK = PR::BK;
     constexpr int KCHUNK_BLOCKS = PR::KCHUNK_BLOCKS;
     constexpr int NBUF = CF::NBUF;
+    constexpr int STAGES = CF::STAGES;
+    constexpr int TILE_M = PAIR ? 2 * BM : BM;  // rows of C per tile (per pair)
+    static_assert(!PAIR || PREC == PREC_BF16X3, "CTA pairs run the bf16 split");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -170,6 +187,10 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    // Pair rank (0 issues the MMAs); tiles are dealt per pair.
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+    const int64_t tile0 = PAIR ? (blockIdx.x >> 1) : blockIdx.x;
+    const int64_t tile_step = PAIR ? (gridDim.x >> 1) : gridDim.x;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -178,7 +199,8 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
         }
         for (int b = 0; b < NBUF; ++b) {
             mbar_init(&cfull[b], 1);
-            mbar_init(&cempty[b], 32 * CF::EPI_WARPS);
+            // rank 0's barrier collects both CTAs' epilogue threads
+            mbar_init(&cempty[b], (PAIR ? 2 : 1) * 32 * CF::EPI_WARPS);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -188,11 +210,18 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
         tma_prefetch_desc(&map_b);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, CF::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (PAIR) {
+            tmem_alloc_pair(tmem_slot, CF::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, CF::TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR)
+        cluster_sync();  // the peer's barriers are initialized before any remote use
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -207,9 +236,11 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
 #pragma unroll
             for (int i = 0; i < STAGES; ++i)
                 armed_ph[i] = -1;
-            for (int64_t t = blockIdx.x; t < p.num_tiles && !*abort_flag; t += gridDim.x) {
+            for (int64_t t = tile0; t < p.num_tiles && !*abort_flag; t += tile_step) {
                 int b, mt, nt;
                 tile_coords(p, t, b, mt, nt);
+                const int a_row = mt * TILE_M + static_cast<int>(rank) * BM;
+                const int b_row = nt * BN + static_cast<int>(rank) * CF::B_ROWS;
                 for (int kb = 0; kb < p.num_k; ++kb) {
                     if (!mbar_wait(&empty[s], ph ^ 1, 1)) {
                         *abort_flag = 1;
@@ -217,16 +248,32 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
                     }
                     uint8_t* sa = smem + s * CF::STAGE_BYTES;
                     uint8_t* sb = sa + CF::A_BYTES;
-                    mbar_arrive_expect_tx(&full[s], CF::STAGE_BYTES);
                     const int k0 = kb * BK;
-                    if (p.a_mn)
-                        tma_load_5d(sa, &map_a, &full[s], 0, k0, mt * (BM / 32), 0, b);
-                    else
-                        tma_load_4d(sa, &map_a, &full[s], k0, mt * BM, 0, b);
-                    if (p.b_mn)
-                        tma_load_5d(sb, &map_b, &full[s], 0, k0, nt * (BN / 32), 0, b);
-                    else
-                        tma_load_4d(sb, &map_b, &full[s], k0, nt * BN, 0, b);
+                    if constexpr (PAIR) {
+                        // Rank 0 expects both CTAs' bytes on its barrier; each
+                        // CTA loads its own halves into its own shared memory.
+                        if (rank == 0)
+                            mbar_arrive_expect_tx(&full[s], 2 * CF::STAGE_BYTES);
+                        const uint32_t fb = smem_in_cta(&full[s], 0);
+                        if (p.a_mn)
+                            tma_load_5d_pair(sa, &map_a, fb, 0, k0, a_row / 32, 0, b);
+                        else
+                            tma_load_4d_pair(sa, &map_a, fb, k0, a_row, 0, b);
+                        if (p.b_mn)
+                            tma_load_5d_pair(sb, &map_b, fb, 0, k0, b_row / 32, 0, b);
+                        else
+                            tma_load_4d_pair(sb, &map_b, fb, k0, b_row, 0, b);
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], CF::STAGE_BYTES);
+                        if (p.a_mn)
+                            tma_load_5d(sa, &map_a, &full[s], 0, k0, a_row / 32, 0, b);
+                        else
+                            tma_load_4d(sa, &map_a, &full[s], k0, a_row, 0, b);
+                        if (p.b_mn)
+                            tma_load_5d(sb, &map_b, &full[s], 0, k0, b_row / 32, 0, b);
+                        else
+                            tma_load_4d(sb, &map_b, &full[s], k0, b_row, 0, b);
+                    }
                     armed_ph[s] = static_cast<int>(ph);
                     if (++s == STAGES) {
                         s = 0;
@@ -234,24 +281,26 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
                     }
                 }
             }
-            // On abort, let armed copies land before the CTA's smem is released.
-            if (*abort_flag) {
+            // On abort, let armed copies land before the CTA's smem is
+            // released (rank 0 holds the barriers both CTAs' copies complete on).
+            if (*abort_flag && rank == 0) {
 #pragma unroll
                 for (int i = 0; i < STAGES; ++i)
                     if (armed_ph[i] >= 0)
                         mbar_wait(&full[i], static_cast<uint32_t>(armed_ph[i]), 5);
             }
         }
-    } else if (warp == 1) {
+    } else if (warp == 1 && rank == 0) {
         // -------------------------------------------------------- MMA issuer
         // The whole warp runs this loop (uniform control flow); lane 0 issues.
-        const uint32_t idesc = PREC == PREC_TF32X3 ? umma_idesc_tf32(BM, BN, p.a_mn, p.b_mn)
-                                                   : umma_idesc_bf16(BM, BN, p.a_mn, p.b_mn);
+        const uint32_t idesc = PREC == PREC_TF32X3
+                                   ? umma_idesc_tf32(TILE_M, BN, p.a_mn, p.b_mn)
+                                   : umma_idesc_bf16(TILE_M, BN, p.a_mn, p.b_mn);
         int s = 0;
         uint32_t ph = 0;
         int64_t g = 0;  // chunk counter across this CTA's tiles
         bool ok = true;
-        for (int64_t t = blockIdx.x; t < p.num_tiles && ok && !*abort_flag; t += gridDim.x) {
+        for (int64_t t = tile0; t < p.num_tiles && ok && !*abort_flag; t += tile_step) {
             for (int kc = 0; kc < p.num_k && ok; kc += KCHUNK_BLOCKS, ++g) {
                 const int buf = static_cast<int>(g % NBUF);
                 const uint32_t cph = static_cast<uint32_t>((g / NBUF) & 1);
@@ -277,11 +326,21 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
                         const uint64_t b_hi = operand_desc<PREC>(sb, p.b_mn, ks);
                         const uint64_t b_lo = operand_desc<PREC>(sb + CF::B_PLANE, p.b_mn, ks);
                         const uint32_t acc = (kb > kc || ks > 0) ? 1u : 0u;
-                        mma_split<PREC>(d_tmem, a_lo, b_hi, idesc, acc);
-                        mma_split<PREC>(d_tmem, a_hi, b_lo, idesc, 1u);
-                        mma_split<PREC>(d_tmem, a_hi, b_hi, idesc, 1u);
+                        if constexpr (PAIR) {
+                            mma_bf16_pair_w(d_tmem, a_lo, b_hi, idesc, acc);
+                            mma_bf16_pair_w(d_tmem, a_hi, b_lo, idesc, 1u);
+                            mma_bf16_pair_w(d_tmem, a_hi, b_hi, idesc, 1u);
+                        } else {
+                            mma_split<PREC>(d_tmem, a_lo, b_hi, idesc, acc);
+                            mma_split<PREC>(d_tmem, a_hi, b_lo, idesc, 1u);
+                            mma_split<PREC>(d_tmem, a_hi, b_hi, idesc, 1u);
+                        }
                     }
-                    mma_commit_w(&empty[s]);
+                    // frees the stage in both CTAs of a pair
+                    if constexpr (PAIR)
+                        mma_commit_pair_w(&empty[s]);
+                    else
+                        mma_commit_w(&empty[s]);
                     if (++s == STAGES) {
                         s = 0;
                         ph ^= 1;
@@ -289,12 +348,15 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
                 }
                 // Fires once every MMA issued so far has retired, also on
                 // abort, so TMEM is quiescent before the epilogue / dealloc.
-                mma_commit_w(&cfull[buf]);
+                if constexpr (PAIR)
+                    mma_commit_pair_w(&cfull[buf]);
+                else
+                    mma_commit_w(&cfull[buf]);
             }
         }
         if (!ok)
             *abort_flag = 1;
-    } else {
+    } else if (warp >= 2) {
         // ---------------------------------------------------------- epilogue
         // Waits are taken by lane 0 and broadcast, so every branch below is
         // warp-uniform and __syncwarp is always reached by the whole warp.
@@ -309,7 +371,7 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
         int64_t g = 0;
         bool ok = true;
         bool pending = false;  // lane 0 has a bulk store reading stage_c
-        for (int64_t t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        for (int64_t t = tile0; t < p.num_tiles && ok; t += tile_step) {
             float acc[128];
 #pragma unroll
             for (int j = 0; j < 128; ++j)
@@ -338,12 +400,16 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
                         acc[c * 32 + j] += v[j];
                 }
                 tc_fence_before();
-                mbar_arrive(&cempty[buf]);
+                if constexpr (PAIR)
+                    mbar_arrive_cluster(smem_in_cta(&cempty[buf], 0));
+                else
+                    mbar_arrive(&cempty[buf]);
             }
             if (!ok)
                 break;
             int b, mt, nt;
             tile_coords(p, t, b, mt, nt);
+            const int row0 = mt * TILE_M + static_cast<int>(rank) * BM;  // this CTA's rows
             if (p.c_mode != C_DIRECT) {
                 // 4 subtiles of 32 columns: registers -> 128B-swizzled staging
                 // tile -> one TMA store (or reduce-add) per warp; rows and
@@ -363,7 +429,7 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
                     fence_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        const int x = nt * BN + col_base + qd * 32, y = mt * BM + quarter * 32;
+                        const int x = nt * BN + col_base + qd * 32, y = row0 + quarter * 32;
                         if (p.c_mode == C_TMA_ADD)
                             tma_reduce_add_3d(&map_c, stage_c, x, y, b);
                         else
@@ -374,7 +440,7 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
                 }
                 continue;
             }
-            const int64_t row = static_cast<int64_t>(mt) * BM + row_in_tile;
+            const int64_t row = static_cast<int64_t>(row0) + row_in_tile;
             if (row >= p.M)
                 continue;
             const int64_t col0 = static_cast<int64_t>(nt) * BN + col_base;
@@ -412,9 +478,16 @@ __global__ void __launch_bounds__(Cfg<BN>::NUM_THREADS, 1)
 
     tc_fence_before();
     __syncthreads();
+    // Neither CTA of a pair leaves (or frees TMEM) while the other may still
+    // signal its barriers or read its shared memory.
+    if constexpr (PAIR)
+        cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, CF::TMEM_COLS);
+        if constexpr (PAIR)
+            tmem_dealloc_pair(tmem_base, CF::TMEM_COLS);
+        else
+            tmem_dealloc(tmem_base, CF::TMEM_COLS);
     }
 }
 
@@ -663,25 +736,46 @@ Profiler& prof() {
     return p;
 }
 
-template <int BN, int PREC>
+template <int BN, int PREC, bool PAIR>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
                 gemm::Params p, cudaStream_t stream) {
-    using CF = gemm::Cfg<BN>;
+    using CF = gemm::Cfg<BN, PAIR>;
+    auto kern = gemm::gemm_split3_kernel<BN, PREC, PAIR>;
     static bool attr_set[64] = {};
+    static int max_pairs[64] = {};  // co-resident clusters of two (PAIR)
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64)
         return set_error(TTK_ERR_ARG, "gemm: device ordinal out of range");
+    cudaLaunchAttribute cluster_attr;
+    cluster_attr.id = cudaLaunchAttributeClusterDimension;
+    cluster_attr.val.clusterDim.x = 2;
+    cluster_attr.val.clusterDim.y = 1;
+    cluster_attr.val.clusterDim.z = 1;
     if (!attr_set[dev]) {
-        if (cudaFuncSetAttribute(gemm::gemm_split3_kernel<BN, PREC>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  CF::SMEM_BYTES) != cudaSuccess)
             return set_error(TTK_ERR_CUDA, "cudaFuncSetAttribute(gemm) failed");
+        if (PAIR) {
+            // Persistent grid: as many pairs as can be resident at once (a
+            // cluster's two CTAs share a GPC, so this can be below SMs / 2).
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3(2);
+            q.blockDim = dim3(CF::NUM_THREADS);
+            q.dynamicSmemBytes = CF::SMEM_BYTES;
+            q.attrs = &cluster_attr;
+            q.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, kern, &q) != cudaSuccess || n <= 0) {
+                cudaGetLastError();
+                n = num_sms() / 2;
+            }
+            max_pairs[dev] = std::min(n, num_sms() / 2);
+        }
         attr_set[dev] = true;
     }
     p.num_n = static_cast<int>((p.N + BN - 1) / BN);
     p.num_tiles = static_cast<int64_t>(p.num_m) * p.num_n * p.batch;
-    const int grid = static_cast<int>(std::min<int64_t>(p.num_tiles, num_sms()));
     Profiler& pr = prof();
     ProfRec rec{};
     if (pr.on) {
@@ -690,8 +784,20 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
         rec.flops = 2.0 * static_cast<double>(p.M) * p.N * p.K * p.batch;
         cudaEventRecord(rec.a, stream);
     }
-    gemm::gemm_split3_kernel<BN, PREC><<<grid, CF::NUM_THREADS, CF::SMEM_BYTES, stream>>>(ma, mb,
-                                                                                          mc, p);
+    if (PAIR) {
+        const int pairs = static_cast<int>(std::min<int64_t>(p.num_tiles, max_pairs[dev]));
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * pairs);
+        cfg.blockDim = dim3(CF::NUM_THREADS);
+        cfg.dynamicSmemBytes = CF::SMEM_BYTES;
+        cfg.stream = stream;
+        cfg.attrs = &cluster_attr;
+        cfg.numAttrs = 1;
+        cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p);
+    } else {
+        const int grid = static_cast<int>(std::min<int64_t>(p.num_tiles, num_sms()));
+        kern<<<grid, CF::NUM_THREADS, CF::SMEM_BYTES, stream>>>(ma, mb, mc, p);
+    }
     const int rc = check_launch("gemm_split3_kernel");
     if (pr.on) {
         cudaEventRecord(rec.b, stream);
@@ -753,6 +859,19 @@ namespace {
 // Process-wide precision of ttk_gemm (TTK_GEMM_PRECISION=tf32x3 selects the
 // TF32 split; default bf16x3).
 int g_prec = -1;
+
+// CTA-pair tiles for the bf16 split: 0 never, 1 when the pair tiles occupy
+// every pair (default), 2 whenever N > 128 (covers edge tiles on small
+// problems). TTK_GEMM_PAIRS=0|1|2 sets it at start-up.
+int g_pairs = -1;
+
+int cta_pairs_mode() {
+    if (g_pairs < 0) {
+        const char* e = std::getenv("TTK_GEMM_PAIRS");
+        g_pairs = (e && (e[0] == '0' || e[0] == '2') && e[1] == 0) ? e[0] - '0' : 1;
+    }
+    return g_pairs;
+}
 
 int current_prec() {
     if (g_prec < 0) {
@@ -832,22 +951,34 @@ int run_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, in
     p.C = C, p.ldc = ldc, p.strideC = strideC;
     p.num_m = static_cast<int>((M + gemm::BM - 1) / gemm::BM);
     p.num_k = static_cast<int>((K + PR::BK - 1) / PR::BK);
-    // BN = 256 unless the N extent is small or 256-wide tiles would leave most
-    // SMs idle.
+    // 256 x 256 tiles on CTA pairs (bf16 split) when there are enough of them
+    // to occupy every pair; else 128 x BN tiles on single CTAs, BN = 256 unless
+    // the N extent is small or 256-wide tiles would leave most SMs idle.
+    const int64_t pair_tiles = ((M + 2 * gemm::BM - 1) / (2 * gemm::BM)) * ((N + 255) / 256) * batch;
+    const int pmode = cta_pairs_mode();
+    const bool use_pair = PREC == gemm::PREC_BF16X3 && N > 128 &&
+                          (pmode == 2 || (pmode == 1 && pair_tiles >= num_sms() / 2));
     const int64_t tiles256 = p.num_m * ((N + 255) / 256) * batch;
-    const bool use128 = N <= 128 || tiles256 < num_sms();
+    const bool use128 = !use_pair && (N <= 128 || tiles256 < num_sms());
     const int bn = use128 ? 128 : 256;
     CUtensorMap ma, mb, mc;
     int rc = make_operand_map<PREC>(&ma, a_split, ga, batch, p.a_mn, gemm::BM);
     if (rc)
         return rc;
-    rc = make_operand_map<PREC>(&mb, b_split, gb, batch, p.b_mn, bn);
+    // a CTA of a pair holds half of B's 256 rows
+    rc = make_operand_map<PREC>(&mb, b_split, gb, batch, p.b_mn, use_pair ? bn / 2 : bn);
     if (rc)
         return rc;
     std::memset(&mc, 0, sizeof(mc));
     p.c_mode = c_tensor_map(&mc, C, M, N, ldc, strideC, batch, beta);
-    return use128 ? launch_gemm<128, PREC>(ma, mb, mc, p, stream)
-                  : launch_gemm<256, PREC>(ma, mb, mc, p, stream);
+    if constexpr (PREC == gemm::PREC_BF16X3) {
+        if (use_pair) {
+            p.num_m = static_cast<int>((M + 2 * gemm::BM - 1) / (2 * gemm::BM));
+            return launch_gemm<256, PREC, true>(ma, mb, mc, p, stream);
+        }
+    }
+    return use128 ? launch_gemm<128, PREC, false>(ma, mb, mc, p, stream)
+                  : launch_gemm<256, PREC, false>(ma, mb, mc, p, stream);
 }
 
 }  // namespace
@@ -860,6 +991,15 @@ int gemm_set_precision(int prec) {
 }
 
 int gemm_get_precision() { return current_prec(); }
+
+int gemm_set_cta_pairs(int mode) {
+    if (mode < 0 || mode > 2)
+        return set_error(TTK_ERR_ARG, "gemm: CTA-pair mode must be 0, 1 or 2");
+    g_pairs = mode;
+    return TTK_OK;
+}
+
+int gemm_get_cta_pairs() { return cta_pairs_mode(); }
 
 namespace {
 int64_t g_fp32_max_macs = int64_t(1) << 24;

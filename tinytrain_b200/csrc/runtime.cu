@@ -218,6 +218,10 @@ int ttk_gemm_set_precision(int prec) { return gemm_set_precision(prec); }
 
 int ttk_gemm_get_precision(void) { return gemm_get_precision(); }
 
+int ttk_gemm_set_cta_pairs(int mode) { return gemm_set_cta_pairs(mode); }
+
+int ttk_gemm_get_cta_pairs(void) { return gemm_get_cta_pairs(); }
+
 int ttk_gemm_set_fp32_max_macs(int64_t macs) { return gemm_set_fp32_max_macs(macs); }
 
 int64_t ttk_gemm_get_fp32_max_macs(void) { return gemm_fp32_max_macs(); }

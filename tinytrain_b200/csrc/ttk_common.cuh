@@ -175,6 +175,78 @@ __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ------------------------------------------------- CTA pairs (cta_group::2) --
+// Two CTAs of a cluster of two (ranks 0 and 1) share one MMA of M = 256: each
+// holds its 128 rows of A and half of the N rows of B in shared memory at the
+// same offsets, and its 128 accumulator rows in its own TMEM. Rank 0 issues
+// the MMAs; its barriers gate both CTAs' operand stages.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t smem_in_cta(const void* p, uint32_t rank) {
+    uint32_t a;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+    return a;
+}
+
+// All threads of every CTA in the cluster (release / acquire).
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile(
+        "barrier.cluster.arrive.release.aligned;\n\t"
+        "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (own or peer CTA).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(
+                     bar_cluster_addr)
+                 : "memory");
+}
+
+// TMA tile loads of one CTA of a pair into its own shared memory, completing
+// on the transaction count of the pair's rank-0 barrier (shared::cluster
+// address). Plain loads: no multicast.
+__device__ __forceinline__ void tma_load_4d_pair(void* dst, const void* desc, uint32_t bar_cluster,
+                                                 int c0, int c1, int c2, int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(desc), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d_pair(void* dst, const void* desc, uint32_t bar_cluster,
+                                                 int c0, int c1, int c2, int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(desc), "r"(bar_cluster), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+        : "memory");
+}
+
+// TMEM of a pair: one warp (same warp index) of each CTA executes these; the
+// allocation lands at the same column address in both CTAs.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+
 // ----------------------------------------------------------------- tcgen05 --
 
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
@@ -261,6 +333,33 @@ __device__ __forceinline__ void mma_bf16_ta_w(uint32_t d_tmem, uint32_t a_tmem, 
         "setp.ne.b32 p, %4, 0;\n\t"
         "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// M = 256 MMA of a CTA pair, issued by rank 0 (warp-uniform; lane 0 issues):
+// D rows 0..127 in rank 0's TMEM, 128..255 in rank 1's at the same address.
+__device__ __forceinline__ void mma_bf16_pair_w(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 l;\n\t"
+        "mov.u32 l, %%laneid;\n\t"
+        "setp.eq.u32 e, l, 0;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Commit of a pair's MMAs: arrive once on the mbarrier at this shared-memory
+// offset in both CTAs of the pair (CTA mask 0b11) when they have completed.
+__device__ __forceinline__ void mma_commit_pair_w(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b32 l;\n\t.reg .b16 m;\n\t"
+        "mov.u32 l, %%laneid;\n\t"
+        "setp.eq.u32 e, l, 0;\n\t"
+        "mov.b16 m, 3;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+        " [%0], m;\n\t}" ::"r"(smem_u32(bar))
         : "memory");
 }
 

@@ -44,6 +44,8 @@ int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t
                int64_t batch, float* dst, int64_t ld_pad, cudaStream_t stream);
 int gemm_set_precision(int prec);
 int gemm_get_precision();
+int gemm_set_cta_pairs(int mode);
+int gemm_get_cta_pairs();
 int gemm_set_fp32_max_macs(int64_t macs);
 int64_t gemm_fp32_max_macs();
 bool gemm_uses_fp32(int64_t batch, int64_t M, int64_t N, int64_t K);

@@ -12,13 +12,17 @@ Workloads (fp32, seeded):
              forward + backward at rows = batch * seq of the 13M, 110M and 1B
              configs (2048, 65536 per 64x1024 step in 16-row micro-batches of
              16384, 16384), d / F of the config, vocab 32000 for CE
+  hbm        AdamW + global-norm clip over the 1B model's 887.7M parameters,
+             embedding gather / scatter-add and the residual add at 16384 x 2048
   attention  fused causal attention with RoPE, forward + backward, B 8, H 12,
-             hd 64, S in {128, 512, 1024, 2048}, inputs N(0, 1)
-Each line: median of `--iters` timed launches (CUDA events, after warm-up),
-the algorithmic work (FLOPs, or bytes that must cross HBM), achieved rate and
-fraction of the measured peak (MEASURED_PEAKS.json: bf16 burst for tensor
-work, HBM copy bandwidth for memory-bound kernels). The 3xTF32 GEMM's
-fp32-accurate ceiling is the bf16 peak / 6.
+             hd 64, S in {128, 512, 1024, 2048}, inputs N(0, 1) (--hd 128:
+             H 16, the 1B layer)
+Each line: median of `--iters` timed launches (CUDA events, after warm-up, L2
+flushed by a 256 MB write before each), the algorithmic work (FLOPs, or bytes
+that must cross HBM), achieved rate and fraction of the measured peak
+(MEASURED_PEAKS.json, else the pool's earlier figures: bf16 burst for tensor
+work, HBM copy bandwidth for memory-bound kernels). The bf16x3 GEMM's
+fp32-accurate ceiling is the bf16 peak / 3.
 """
 from __future__ import annotations
 
@@ -46,12 +50,25 @@ def peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+_FLUSH = None
+
+
+def flush_l2():
+    """Writes 256 MB (twice the 126 MB L2) so the next launch starts cold."""
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    _FLUSH.fill_(1.0)
+
+
 def timed(fn, iters, warmup=3):
+    """Median of `iters` CUDA-event timings of fn, L2 flushed before each."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
     ts = []
     for _ in range(iters):
+        flush_l2()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         fn()
@@ -129,6 +146,69 @@ def bench_rows(rows, iters):
         del L, dL
 
 
+def llama1b_param_shapes(d=2048, layers=16, ffn=5632, vocab=32000):
+    """Parameter sizes of the 1B model in parameters() order (tied head)."""
+    sizes = [vocab * d]
+    for _ in range(layers):
+        sizes += [d, d * d, d * d, d * d, d * d, d, ffn * d, ffn * d, d * ffn]
+    return sizes + [d]
+
+
+def bench_hbm(iters):
+    """The remaining bandwidth kernels at the 1B sizes: AdamW with global-norm
+    clipping over all 887.7M parameters (32 B / parameter: the norm reads g;
+    the update reads p, g, m, v and writes p, m, v), the embedding gather and
+    scatter-add (8 B per row element each way) and the residual add (12 B /
+    element)."""
+    hbm, _, src = peaks()
+    sizes = llama1b_param_shapes()
+    n = sum(sizes)
+    flat = [torch.empty(n, device="cuda") for _ in range(4)]
+    for t in flat:
+        t.uniform_(-0.01, 0.01)
+    flat[3].abs_()
+
+    def views(buf):
+        out, off = [], 0
+        for k in sizes:
+            out.append(buf[off:off + k])
+            off += k
+        return out
+    P, G, M, V = (views(b) for b in flat)
+    step = [0]
+
+    def adamw_clip():
+        step[0] += 1
+        acc = K.sumsq(G)
+        K.adamw(P, G, M, V, 3e-4, 0.9, 0.95, 1e-8, 0.1, step[0], sumsq_acc=acc, max_norm=1.0)
+    ms = timed(adamw_clip, iters)
+    emit({"op": "adamw_clip", "params": n, "tensors": len(sizes), "ms": ms,
+          "gbs": 32 * n / ms / 1e6, "frac_hbm": 32 * n / ms / 1e6 / hbm, "peak_src": src})
+    del P, G, M, V, flat
+    R, D, Vv = 16384, 2048, 32000
+    W = torch.randn(Vv, D, device="cuda")
+    idx = torch.randint(0, Vv, (R,), device="cuda", dtype=torch.int64)
+    ms = timed(lambda: K.embedding_fwd(W, idx), iters)
+    emit({"op": "embedding", "pass": "fwd", "rows": R, "d": D, "ms": ms,
+          "gbs": 8 * R * D / ms / 1e6, "frac_hbm": 8 * R * D / ms / 1e6 / hbm})
+    dout = torch.randn(R, D, device="cuda")
+    dW = torch.zeros_like(W)
+    ms = timed(lambda: K.embedding_bwd(dout, idx, dW), iters)
+    emit({"op": "embedding", "pass": "bwd (sort + segmented sum)", "rows": R, "d": D, "ms": ms,
+          "gbs": 8 * R * D / ms / 1e6, "frac_hbm": 8 * R * D / ms / 1e6 / hbm})
+    a, b = torch.randn(R, D, device="cuda"), torch.randn(R, D, device="cuda")
+    out = torch.empty_like(a)
+    shape = _ttk.i64_array([R, D])
+    st = _ttk.i64_array([D, 1])
+
+    def add():
+        _ttk.call("ttk_binary", 0, a.data_ptr(), st, b.data_ptr(), st, out.data_ptr(), shape, 2,
+                  torch.cuda.current_stream().cuda_stream)
+    ms = timed(add, iters)
+    emit({"op": "residual_add", "rows": R, "d": D, "ms": ms,
+          "gbs": 12 * R * D / ms / 1e6, "frac_hbm": 12 * R * D / ms / 1e6 / hbm})
+
+
 def bench_attention(seqs, iters, B=8, H=12, hd=64):
     """Forward + backward; fwd FLOPs 2*B*H*S^2*hd (causal half of 4*B*H*S^2*hd),
     backward counted as 2x forward (dQ, dK, dV; recomputation not credited)."""
@@ -152,7 +232,7 @@ def bench_attention(seqs, iters, B=8, H=12, hd=64):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", choices=["gemm", "rows", "ce", "attention"], default=None)
+    ap.add_argument("--only", choices=["gemm", "rows", "ce", "hbm", "attention"], default=None)
     ap.add_argument("--shape", default=None, help="M,K,N for --only gemm")
     ap.add_argument("--rows", type=int, default=None)
     ap.add_argument("--seq", type=int, default=None)
@@ -167,6 +247,8 @@ def main():
         bench_gemm(shapes, a.iters)
     if a.only in (None, "rows", "ce"):
         bench_rows(rows, a.iters)
+    if a.only in (None, "hbm"):
+        bench_hbm(a.iters)
     if a.only in (None, "attention"):
         bench_attention([a.seq] if a.seq else ATTN_S, a.iters,
                         H=12 if a.hd == 64 else 2048 // a.hd, hd=a.hd)

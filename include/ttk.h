@@ -96,6 +96,17 @@ int ttk_gemm_get_precision(void);
  * whenever N > 128. TTK_GEMM_PAIRS=0|1|2 selects the mode at start-up. */
 int ttk_gemm_set_cta_pairs(int mode);
 int ttk_gemm_get_cta_pairs(void);
+/* Split-K (default on; TTK_GEMM_SPLITK=0 turns it off at start-up): a single
+ * GEMM with a long K whose output tiles would leave many SMs idle in the last
+ * wave (the weight gradients dY^T X: M x N small against K = tokens) runs as
+ * S K-slices that write partial products, then one pass sums them in slice
+ * order (deterministic) into alpha * sum + beta * C. ttk_gemm_workspace_size
+ * includes the partials; ttk_gemm_noalloc never splits. ttk_gemm_split_k_slices
+ * reports S for one problem (1 = not split). */
+int ttk_gemm_set_split_k(int on);
+int ttk_gemm_get_split_k(void);
+int ttk_gemm_split_k_slices(int transA, int transB, int64_t batch, int64_t M, int64_t N,
+                            int64_t K);
 /* Problems of at most `macs` multiply-adds (batch*M*N*K; default 2^24) run
  * as an exact fp32 SIMT GEMM, one fused multiply-add per product in
  * ascending k, with no workspace: below that size the split's extra launches

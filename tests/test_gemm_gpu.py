@@ -173,3 +173,67 @@ def test_rejects_bad_args(cuda):
     with pytest.raises(_ttk.TtkError):
         _ttk.call("ttk_gemm", 0, 0, 1, 4, 4, 4, 1.0, None, 4, 16, None, 4, 16, 0.0, None, 4, 16,
                   None, 0, None)
+
+
+@pytest.fixture
+def split_k(cuda):
+    from tinytrain_b200 import _ttk
+    old = _ttk.call("ttk_gemm_get_split_k")
+
+    def set_on(on):
+        _ttk.call("ttk_gemm_set_split_k", int(on))
+    yield set_on
+    _ttk.call("ttk_gemm_set_split_k", old)
+
+
+def _gemm_on_splits(A, B, tA, tB, M, N, K, alpha, beta, C):
+    """The host path: operands split once (ttk_gemm_split), then ttk_gemm_splits."""
+    from tinytrain_b200 import _ttk
+    st = torch.cuda.current_stream().cuda_stream
+    splits = []
+    for X in (A, B):
+        rows, cols = X.shape
+        buf = torch.empty(_ttk.call("ttk_gemm_split_bytes", 1, rows, cols), dtype=torch.uint8,
+                          device=X.device)
+        _ttk.call("ttk_gemm_split", X.data_ptr(), rows, cols, cols, 0, 1, buf.data_ptr(), st)
+        splits.append(buf)
+    _ttk.call("ttk_gemm_splits", tA, tB, 1, M, N, K, alpha, splits[0].data_ptr(),
+              splits[1].data_ptr(), beta, C.data_ptr(), N, 0, st)
+
+
+@pytest.mark.parametrize("M,N,K,S,orients", [
+    (2048, 2048, 16384, 8, [(1, 0)]),            # attention projection dW = dY^T X
+    (5632, 2048, 16384, 2, [(1, 0)]),            # FFN dW
+    (300, 260, 8192, 16, [(0, 0), (0, 1), (1, 0), (1, 1)])])
+def test_split_k(cuda, split_k, M, N, K, S, orients):
+    """Long-K GEMMs with few output tiles run as S K-slices plus an in-order
+    sum of the partial products: equal to fp64 within the bound through both
+    entry points (caller workspace; cached operand splits with pool-allocated
+    partials), with beta = 0, 1 and other alpha / beta, and close to the
+    unsplit result."""
+    from tinytrain_b200 import _ttk
+    from tinytrain_b200 import kernels as Kn
+    for tA, tB in orients:
+        assert _ttk.call("ttk_gemm_split_k_slices", tA, tB, 1, M, N, K) == S
+        gen = torch.Generator(device=cuda).manual_seed(M + N + K + tA + 2 * tB)
+        A = torch.rand((K, M) if tA else (M, K), device=cuda, generator=gen) * 2 - 1
+        B = torch.rand((N, K) if tB else (K, N), device=cuda, generator=gen) * 2 - 1
+        C0 = torch.rand(M, N, device=cuda, generator=gen) * 2 - 1
+        prod = (A.double().T if tA else A.double()) @ (B.double().T if tB else B.double())
+        for alpha, beta in [(1.0, 0.0), (1.0, 1.0), (0.5, -0.5)]:
+            ref = (alpha * prod + beta * C0.double()).cpu().numpy()
+            split_k(True)
+            C1 = C0.clone()
+            Kn.gemm(A, B, transA=bool(tA), transB=bool(tB), C_out=C1, alpha=alpha, beta=beta)
+            C2 = C0.clone()
+            _gemm_on_splits(A, B, tA, tB, M, N, K, alpha, beta, C2)
+            split_k(False)
+            assert _ttk.call("ttk_gemm_split_k_slices", tA, tB, 1, M, N, K) == 1
+            C3 = C0.clone()
+            Kn.gemm(A, B, transA=bool(tA), transB=bool(tB), C_out=C3, alpha=alpha, beta=beta)
+            torch.cuda.synchronize()
+            for got in (C1, C2):
+                assert rel_err(got.cpu().numpy(), ref) < TOL, (tA, tB, alpha, beta)
+            assert torch.equal(C1, C2)
+            assert rel_err(C1.cpu().numpy(), C3.cpu().numpy()) < 1e-5
+    assert _ttk.device_status() == 0

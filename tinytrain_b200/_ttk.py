@@ -50,6 +50,9 @@ SIGS = {
     "ttk_gemm_set_precision": (I32, [I32]),
     "ttk_gemm_get_precision": (I32, []),
     "ttk_gemm_set_cta_pairs": (I32, [I32]),
+    "ttk_gemm_set_split_k": (I32, [I32]),
+    "ttk_gemm_get_split_k": (I32, []),
+    "ttk_gemm_split_k_slices": (I32, [I32, I32, I64, I64, I64, I64]),
     "ttk_gemm_get_cta_pairs": (I32, []),
     "ttk_gemm_set_fp32_max_macs": (I32, [I64]),
     "ttk_gemm_get_fp32_max_macs": (I64, []),
@@ -121,7 +124,7 @@ SIGS = {
 
 # int-returning functions that return a value, not a status
 VALUE_FNS = {"ttk_gemm_get_precision", "ttk_attention_get_impl", "ttk_gemm_uses_fp32",
-             "ttk_gemm_get_cta_pairs"}
+             "ttk_gemm_get_cta_pairs", "ttk_gemm_get_split_k", "ttk_gemm_split_k_slices"}
 STATUS_FNS = {k for k, (r, _) in SIGS.items() if r is I32 and k not in VALUE_FNS}
 
 

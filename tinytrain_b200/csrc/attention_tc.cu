@@ -33,7 +33,7 @@
 // K-major layout for Q, K and P and the MN-major layout for V.
 // Every wait is bounded; on expiry the kernel flags the device status, lets
 // copies in flight land, waits for issued MMAs, frees TMEM and returns.
-// No load uses .multicast::cluster.
+// Every TMA load has one destination: the issuing CTA's shared memory.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>

@@ -66,7 +66,8 @@ int ttk_gemm_noalloc(int transA, int transB, int64_t batch, int64_t M, int64_t N
                      float alpha, const float* A, int64_t lda, int64_t strideA, const float* B,
                      int64_t ldb, int64_t strideB, float beta, float* C, int64_t ldc,
                      int64_t strideC, void* stream) {
-    const size_t need = ttk::gemm_workspace_size(transA, transB, batch, M, N, K);
+    // No split-K here: its partials would need more scratch than the fixed array.
+    const size_t need = ttk::gemm_workspace_size(transA, transB, batch, M, N, K, false);
     if (need > kNoAllocScratchBytes) {
         const std::string msg = "ttk_gemm_noalloc: these operands need " + std::to_string(need) +
                                 " bytes of scratch, above the fixed limit of " +
@@ -84,7 +85,7 @@ int ttk_gemm_noalloc(int transA, int transB, int64_t batch, int64_t M, int64_t N
     // (padding included), so nothing left by an earlier call needs clearing.
     return ttk::gemm_run(transA, transB, batch, M, N, K, alpha, A, lda, strideA, B, ldb,
                             strideB, beta, C, ldc, strideC, ws, kNoAllocScratchBytes,
-                            static_cast<cudaStream_t>(stream));
+                            static_cast<cudaStream_t>(stream), false);
 }
 
 }  // extern "C"

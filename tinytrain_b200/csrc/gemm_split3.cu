@@ -39,7 +39,7 @@
 //               registers (each thread: one row x 128 columns), free it, and
 //               store the finished tile with alpha/beta; the ring lets the
 //               MMAs of the next chunk / tile run while a chunk is drained
-// Loads never use .multicast::cluster.
+// Every TMA load has one destination: the issuing CTA's shared memory.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -558,6 +558,51 @@ __global__ void scale_kernel(float* C, int64_t batch, int64_t M, int64_t N, int6
     }
 }
 
+// Split-K finish: C = alpha * sum_s W[s] + beta * C over S partial products
+// W[s] (M x N, leading dimension ldw, slices M*ldw apart), s ascending: a
+// fixed summation order, so the result is deterministic.
+__global__ void splitk_reduce_kernel(const float* __restrict__ W, int S, int64_t M, int64_t N,
+                                     int64_t ldw, float alpha, float beta, float* __restrict__ C,
+                                     int64_t ldc) {
+    const int64_t slice = M * ldw;
+    const bool vec = ((N & 3) == 0) && ((ldc & 3) == 0) &&
+                     ((reinterpret_cast<uintptr_t>(C) & 15) == 0);
+    if (vec) {
+        const int64_t n4 = N / 4, total = M * n4;
+        for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+             i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+            const int64_t m = i / n4, c = (i % n4) * 4;
+            const float* w = W + m * ldw + c;
+            float4 acc = *reinterpret_cast<const float4*>(w);
+            for (int s = 1; s < S; ++s) {
+                const float4 v = *reinterpret_cast<const float4*>(w + s * slice);
+                acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
+            }
+            float4* dst = reinterpret_cast<float4*>(C + m * ldc + c);
+            float4 o = make_float4(alpha * acc.x, alpha * acc.y, alpha * acc.z, alpha * acc.w);
+            if (beta != 0.0f) {
+                const float4 ci = *dst;
+                o.x += beta * ci.x, o.y += beta * ci.y, o.z += beta * ci.z, o.w += beta * ci.w;
+            }
+            *dst = o;
+        }
+        return;
+    }
+    const int64_t total = M * N;
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const int64_t m = i / N, c = i % N;
+        float acc = W[m * ldw + c];
+        for (int s = 1; s < S; ++s)
+            acc += W[s * slice + m * ldw + c];
+        float* dst = C + m * ldc + c;
+        float o = alpha * acc;
+        if (beta != 0.0f)
+            o += beta * *dst;
+        *dst = o;
+    }
+}
+
 // Exact fp32 GEMM for small problems (at most gemm_fp32_max_macs()
 // multiply-adds): C = alpha * op(A) op(B) + beta * C with one fp32 fused
 // multiply-add per product in ascending k, the reference's sgemm arithmetic
@@ -660,9 +705,12 @@ struct SplitGeom {
 // MN-major map: dims {32, rows(K), cols/32 chunks, plane, batch},
 //               box {32, BK, tile/32, 2, 1}: tf32 128B swizzle with 32B atoms
 //               (128-byte rows), bf16 64B swizzle (64-byte rows).
+// kslices > 1 (split-K; batch 1): the K extent is cut into kslices equal
+// slices that the map presents as its batch dimension, so batch index s of the
+// kernel reads K range [s*K/kslices, (s+1)*K/kslices).
 template <int PREC>
 int make_operand_map(CUtensorMap* map, const void* base, const SplitGeom& g, int64_t batch,
-                     int mn_major, int tile) {
+                     int mn_major, int tile, int kslices = 1) {
     using PR = gemm::Prec<PREC>;
     EncodeTiledFn enc = encode_fn();
     if (!enc)
@@ -673,19 +721,26 @@ int make_operand_map(CUtensorMap* map, const void* base, const SplitGeom& g, int
     CUresult r;
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
     if (!mn_major) {
-        cuuint64_t dims[4] = {static_cast<cuuint64_t>(g.cols), static_cast<cuuint64_t>(g.rows), 2,
-                              static_cast<cuuint64_t>(batch)};
-        cuuint64_t strides[3] = {static_cast<cuuint64_t>(g.ld_pad * PR::ELT), plane, 2 * plane};
+        // K is the column extent
+        const int64_t kc = g.cols / kslices;
+        cuuint64_t dims[4] = {static_cast<cuuint64_t>(kc), static_cast<cuuint64_t>(g.rows), 2,
+                              static_cast<cuuint64_t>(kslices > 1 ? kslices : batch)};
+        cuuint64_t strides[3] = {static_cast<cuuint64_t>(g.ld_pad * PR::ELT), plane,
+                                 kslices > 1 ? static_cast<cuuint64_t>(kc * PR::ELT) : 2 * plane};
         cuuint32_t box[4] = {PR::BK, static_cast<cuuint32_t>(tile), 2, 1};
         r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     } else {
-        cuuint64_t dims[5] = {32, static_cast<cuuint64_t>(g.rows),
+        // K is the row extent
+        const int64_t kr = g.rows / kslices;
+        cuuint64_t dims[5] = {32, static_cast<cuuint64_t>(kr),
                               static_cast<cuuint64_t>(g.ld_pad / 32), 2,
-                              static_cast<cuuint64_t>(batch)};
+                              static_cast<cuuint64_t>(kslices > 1 ? kslices : batch)};
         cuuint64_t strides[4] = {static_cast<cuuint64_t>(g.ld_pad * PR::ELT),
-                                 static_cast<cuuint64_t>(32 * PR::ELT), plane, 2 * plane};
+                                 static_cast<cuuint64_t>(32 * PR::ELT), plane,
+                                 kslices > 1 ? static_cast<cuuint64_t>(kr * g.ld_pad * PR::ELT)
+                                             : 2 * plane};
         cuuint32_t box[5] = {32, PR::BK, static_cast<cuuint32_t>(tile / 32), 2, 1};
         r = enc(map, dt, 5, const_cast<void*>(base), dims, strides, box, estr,
                 CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -736,9 +791,19 @@ Profiler& prof() {
     return p;
 }
 
+// Second step of a split-K GEMM: C = alpha * sum_s W[s] + beta * C.
+struct SplitKFinish {
+    const float* W;
+    int S;
+    int64_t M, N, ldw;
+    float alpha, beta;
+    float* C;
+    int64_t ldc;
+};
+
 template <int BN, int PREC, bool PAIR>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
-                gemm::Params p, cudaStream_t stream) {
+                gemm::Params p, cudaStream_t stream, const SplitKFinish* fin = nullptr) {
     using CF = gemm::Cfg<BN, PAIR>;
     auto kern = gemm::gemm_split3_kernel<BN, PREC, PAIR>;
     static bool attr_set[64] = {};
@@ -798,7 +863,15 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
         const int grid = static_cast<int>(std::min<int64_t>(p.num_tiles, num_sms()));
         kern<<<grid, CF::NUM_THREADS, CF::SMEM_BYTES, stream>>>(ma, mb, mc, p);
     }
-    const int rc = check_launch("gemm_split3_kernel");
+    int rc = check_launch("gemm_split3_kernel");
+    if (!rc && fin) {
+        const int64_t work = fin->M * ((fin->N & 3) == 0 ? fin->N / 4 : fin->N);
+        const int blocks = static_cast<int>(std::min<int64_t>((work + 255) / 256, 148 * 8));
+        gemm::splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(fin->W, fin->S, fin->M, fin->N,
+                                                             fin->ldw, fin->alpha, fin->beta,
+                                                             fin->C, fin->ldc);
+        rc = check_launch("splitk_reduce_kernel");
+    }
     if (pr.on) {
         cudaEventRecord(rec.b, stream);
         pr.recs.push_back(rec);
@@ -806,12 +879,104 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     return rc;
 }
 
+// CTA-pair tiles for the bf16 split: 0 never, 1 when the pair tiles occupy
+// every pair (default), 2 whenever N > 128 (covers edge tiles on small
+// problems). TTK_GEMM_PAIRS=0|1|2 sets it at start-up.
+int g_pairs = -1;
+
+int cta_pairs_mode() {
+    if (g_pairs < 0) {
+        const char* e = std::getenv("TTK_GEMM_PAIRS");
+        g_pairs = (e && (e[0] == '0' || e[0] == '2') && e[1] == 0) ? e[0] - '0' : 1;
+    }
+    return g_pairs;
+}
+
+// Tile configuration the kernel uses for (batch, M, N): CTA pairs with
+// 256 x 256 tiles, or single CTAs with 128 x BN tiles; `slots` tiles run at
+// once on the persistent grid.
+struct TilePlan {
+    bool pair;
+    int bn;
+    int64_t tiles, slots;
+};
+
+TilePlan tile_plan(int prec, int64_t batch, int64_t M, int64_t N) {
+    const int64_t pair_tiles = ((M + 2 * gemm::BM - 1) / (2 * gemm::BM)) * ((N + 255) / 256) * batch;
+    const int pmode = cta_pairs_mode();
+    if (prec == gemm::PREC_BF16X3 && N > 128 &&
+        (pmode == 2 || (pmode == 1 && pair_tiles >= num_sms() / 2)))
+        return {true, 256, pair_tiles, num_sms() / 2};
+    const int64_t mt = (M + gemm::BM - 1) / gemm::BM;
+    const int64_t tiles256 = mt * ((N + 255) / 256) * batch;
+    const int bn = (N <= 128 || tiles256 < num_sms()) ? 128 : 256;
+    return {false, bn, mt * ((N + bn - 1) / bn) * batch, num_sms()};
+}
+
+// Fraction of the slots busy over the waves needed for `units` tiles.
+double wave_eff(int64_t units, int64_t slots) {
+    const int64_t waves = (units + slots - 1) / slots;
+    return static_cast<double>(units) / static_cast<double>(waves * slots);
+}
+
+// Split-K (TTK_GEMM_SPLITK=0 disables): a single long-K problem whose tiles
+// fill the machine's slots poorly (the weight gradients dW = dY^T X, whose
+// M x N is small against K = tokens) runs as S K-slices, each writing a
+// partial product, and one pass sums the partials in slice order.
+int g_splitk = -1;
+
+bool splitk_enabled() {
+    if (g_splitk < 0) {
+        const char* e = std::getenv("TTK_GEMM_SPLITK");
+        g_splitk = (e && e[0] == '0' && e[1] == 0) ? 0 : 1;
+    }
+    return g_splitk != 0;
+}
+
+constexpr int64_t kSplitKMaxBytes = int64_t(512) << 20;
+
+int64_t splitk_ldw(int64_t N) { return round_up(N, 4); }
+
+size_t splitk_bytes(int S, int64_t M, int64_t N) {
+    return S > 1 ? static_cast<size_t>(S) * M * splitk_ldw(N) * 4 : 0;
+}
+
+// Slices: the smallest S (K divisible by S, slices a multiple of 256 long)
+// that lifts the wave efficiency clearly; 1 when the problem fills the
+// machine already.
+int choose_split_k(int prec, int64_t batch, int64_t M, int64_t N, int64_t K) {
+    if (!splitk_enabled() || batch != 1 || K < 2048)
+        return 1;
+    const TilePlan t1 = tile_plan(prec, 1, M, N);
+    double best = wave_eff(t1.tiles, t1.slots);
+    if (best >= 0.9)
+        return 1;
+    int best_s = 1;
+    for (int S = 2; S <= 16; ++S) {
+        if (K % S || (K / S) % 256)
+            continue;
+        if (static_cast<int64_t>(splitk_bytes(S, M, N)) > kSplitKMaxBytes)
+            break;
+        const TilePlan t = tile_plan(prec, S, M, N);
+        const double e = wave_eff(t.tiles, t.slots);
+        if (e > best + 0.05) {
+            best = e;
+            best_s = S;
+        }
+        if (best >= 0.95)
+            break;
+    }
+    return best_s;
+}
+
 struct GemmPlan {
     SplitGeom ga, gb;
     size_t off_b, total;
+    size_t off_w, w_bytes;  // split-K partials (0 bytes when not split)
 };
 
-GemmPlan plan(int prec, int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K) {
+GemmPlan plan(int prec, int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
+              bool allow_splitk = true) {
     GemmPlan pl;
     const int elt = prec == gemm::PREC_TF32X3 ? 4 : 2;
     // op(A) = A [M,K] (K-major) or A^T with A stored [K,M] (MN-major).
@@ -821,6 +986,11 @@ GemmPlan plan(int prec, int transA, int transB, int64_t batch, int64_t M, int64_
     pl.gb = transB ? SplitGeom{N, K, round_up(K, 16), elt} : SplitGeom{K, N, round_up(N, 32), elt};
     pl.off_b = static_cast<size_t>(round_up(static_cast<int64_t>(pl.ga.bytes(batch)), 256));
     pl.total = pl.off_b + pl.gb.bytes(batch);
+    const int S = allow_splitk ? choose_split_k(prec, batch, M, N, K) : 1;
+    pl.off_w = static_cast<size_t>(round_up(static_cast<int64_t>(pl.total), 256));
+    pl.w_bytes = splitk_bytes(S, M, N);
+    if (pl.w_bytes)
+        pl.total = pl.off_w + pl.w_bytes;
     return pl;
 }
 
@@ -860,18 +1030,6 @@ namespace {
 // TF32 split; default bf16x3).
 int g_prec = -1;
 
-// CTA-pair tiles for the bf16 split: 0 never, 1 when the pair tiles occupy
-// every pair (default), 2 whenever N > 128 (covers edge tiles on small
-// problems). TTK_GEMM_PAIRS=0|1|2 sets it at start-up.
-int g_pairs = -1;
-
-int cta_pairs_mode() {
-    if (g_pairs < 0) {
-        const char* e = std::getenv("TTK_GEMM_PAIRS");
-        g_pairs = (e && (e[0] == '0' || e[0] == '2') && e[1] == 0) ? e[0] - '0' : 1;
-    }
-    return g_pairs;
-}
 
 int current_prec() {
     if (g_prec < 0) {
@@ -927,11 +1085,15 @@ int c_tensor_map(CUtensorMap* map, float* C, int64_t M, int64_t N, int64_t ldc, 
     return beta == 0.0f ? gemm::C_TMA_STORE : gemm::C_TMA_ADD;
 }
 
+// kmode: 0 = no split-K; 1 = split-K partials in the caller's workspace kws
+// (kws_bytes; falls back to one pass if too small); 2 = partials from the
+// stream-ordered pool.
 template <int PREC>
 int run_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
                  float alpha, const void* a_split, int64_t lda_pad, const void* b_split,
                  int64_t ldb_pad, float beta, float* C, int64_t ldc, int64_t strideC,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, int kmode = 0, void* kws = nullptr,
+                 size_t kws_bytes = 0) {
     using PR = gemm::Prec<PREC>;
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0)
         return set_error(TTK_ERR_ARG, "gemm_presplit: sizes must be positive");
@@ -943,42 +1105,67 @@ int run_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, in
     SplitGeom gb = transB ? SplitGeom{N, K, ldb_pad, PR::ELT} : SplitGeom{K, N, ldb_pad, PR::ELT};
     if (ga.ld_pad < ga.cols || gb.ld_pad < gb.cols)
         return set_error(TTK_ERR_ARG, "gemm_presplit: padded leading dimension too small");
+    // Split-K: S slices of K, each a batch entry writing its partial product
+    // to W[s]; the finish step adds them in slice order into C.
+    int S = kmode ? choose_split_k(PREC, batch, M, N, K) : 1;
+    float* W = nullptr;
+    bool own_w = false;
+    if (S > 1) {
+        const size_t need = splitk_bytes(S, M, N);
+        if (kmode == 1) {
+            if (kws && kws_bytes >= need && !(reinterpret_cast<uintptr_t>(kws) & 15))
+                W = static_cast<float*>(kws);
+        } else if (cudaMallocAsync(reinterpret_cast<void**>(&W), need, stream) == cudaSuccess) {
+            own_w = true;
+        } else {
+            cudaGetLastError();
+            W = nullptr;
+        }
+        if (!W)
+            S = 1;
+    }
+    const int64_t kb = K / S, nb = S > 1 ? S : batch;
     gemm::Params p{};
-    p.M = M, p.N = N, p.K = K, p.batch = batch;
+    p.M = M, p.N = N, p.K = kb, p.batch = nb;
     p.a_mn = transA ? 1 : 0;
     p.b_mn = transB ? 0 : 1;
-    p.alpha = alpha, p.beta = beta;
-    p.C = C, p.ldc = ldc, p.strideC = strideC;
     p.num_m = static_cast<int>((M + gemm::BM - 1) / gemm::BM);
-    p.num_k = static_cast<int>((K + PR::BK - 1) / PR::BK);
-    // 256 x 256 tiles on CTA pairs (bf16 split) when there are enough of them
-    // to occupy every pair; else 128 x BN tiles on single CTAs, BN = 256 unless
-    // the N extent is small or 256-wide tiles would leave most SMs idle.
-    const int64_t pair_tiles = ((M + 2 * gemm::BM - 1) / (2 * gemm::BM)) * ((N + 255) / 256) * batch;
-    const int pmode = cta_pairs_mode();
-    const bool use_pair = PREC == gemm::PREC_BF16X3 && N > 128 &&
-                          (pmode == 2 || (pmode == 1 && pair_tiles >= num_sms() / 2));
-    const int64_t tiles256 = p.num_m * ((N + 255) / 256) * batch;
-    const bool use128 = !use_pair && (N <= 128 || tiles256 < num_sms());
-    const int bn = use128 ? 128 : 256;
-    CUtensorMap ma, mb, mc;
-    int rc = make_operand_map<PREC>(&ma, a_split, ga, batch, p.a_mn, gemm::BM);
-    if (rc)
-        return rc;
-    // a CTA of a pair holds half of B's 256 rows
-    rc = make_operand_map<PREC>(&mb, b_split, gb, batch, p.b_mn, use_pair ? bn / 2 : bn);
-    if (rc)
-        return rc;
-    std::memset(&mc, 0, sizeof(mc));
-    p.c_mode = c_tensor_map(&mc, C, M, N, ldc, strideC, batch, beta);
-    if constexpr (PREC == gemm::PREC_BF16X3) {
-        if (use_pair) {
-            p.num_m = static_cast<int>((M + 2 * gemm::BM - 1) / (2 * gemm::BM));
-            return launch_gemm<256, PREC, true>(ma, mb, mc, p, stream);
-        }
+    p.num_k = static_cast<int>((kb + PR::BK - 1) / PR::BK);
+    SplitKFinish fin{};
+    if (S > 1) {
+        const int64_t ldw = splitk_ldw(N);
+        p.alpha = 1.0f, p.beta = 0.0f;
+        p.C = W, p.ldc = ldw, p.strideC = M * ldw;
+        fin = SplitKFinish{W, S, M, N, ldw, alpha, beta, C, ldc};
+    } else {
+        p.alpha = alpha, p.beta = beta;
+        p.C = C, p.ldc = ldc, p.strideC = strideC;
     }
-    return use128 ? launch_gemm<128, PREC, false>(ma, mb, mc, p, stream)
-                  : launch_gemm<256, PREC, false>(ma, mb, mc, p, stream);
+    const TilePlan tp = tile_plan(PREC, nb, M, N);
+    const int bn = tp.bn;
+    CUtensorMap ma, mb, mc;
+    int rc = make_operand_map<PREC>(&ma, a_split, ga, batch, p.a_mn, gemm::BM, S);
+    // a CTA of a pair holds half of B's 256 rows
+    if (!rc)
+        rc = make_operand_map<PREC>(&mb, b_split, gb, batch, p.b_mn, tp.pair ? bn / 2 : bn, S);
+    if (!rc) {
+        std::memset(&mc, 0, sizeof(mc));
+        p.c_mode = c_tensor_map(&mc, p.C, M, N, p.ldc, p.strideC, nb, p.beta);
+        const SplitKFinish* f = S > 1 ? &fin : nullptr;
+        rc = -1;
+        if constexpr (PREC == gemm::PREC_BF16X3) {
+            if (tp.pair) {
+                p.num_m = static_cast<int>((M + 2 * gemm::BM - 1) / (2 * gemm::BM));
+                rc = launch_gemm<256, PREC, true>(ma, mb, mc, p, stream, f);
+            }
+        }
+        if (rc == -1)
+            rc = bn == 128 ? launch_gemm<128, PREC, false>(ma, mb, mc, p, stream, f)
+                           : launch_gemm<256, PREC, false>(ma, mb, mc, p, stream, f);
+    }
+    if (own_w)
+        cudaFreeAsync(W, stream);
+    return rc;
 }
 
 }  // namespace
@@ -1000,6 +1187,20 @@ int gemm_set_cta_pairs(int mode) {
 }
 
 int gemm_get_cta_pairs() { return cta_pairs_mode(); }
+
+int gemm_set_split_k(int on) {
+    g_splitk = on ? 1 : 0;
+    return TTK_OK;
+}
+
+int gemm_get_split_k() { return splitk_enabled() ? 1 : 0; }
+
+int gemm_split_k_slices(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K) {
+    (void)transA, (void)transB;
+    if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || gemm_uses_fp32(batch, M, N, K))
+        return 1;
+    return choose_split_k(current_prec(), batch, M, N, K);
+}
 
 namespace {
 int64_t g_fp32_max_macs = int64_t(1) << 24;
@@ -1024,10 +1225,10 @@ bool gemm_uses_fp32(int64_t batch, int64_t M, int64_t N, int64_t K) {
 }
 
 size_t gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
-                           int64_t K) {
+                           int64_t K, bool allow_splitk) {
     if (M <= 0 || N <= 0 || K <= 0 || batch <= 0 || gemm_uses_fp32(batch, M, N, K))
         return 0;
-    return plan(current_prec(), transA, transB, batch, M, N, K).total;
+    return plan(current_prec(), transA, transB, batch, M, N, K, allow_splitk).total;
 }
 
 int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
@@ -1039,7 +1240,7 @@ int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t
 int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
              const float* A, int64_t lda, int64_t strideA, const float* B, int64_t ldb,
              int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC, void* ws,
-             size_t ws_bytes, cudaStream_t stream) {
+             size_t ws_bytes, cudaStream_t stream, bool allow_splitk) {
     if (M < 0 || N < 0 || K < 0 || batch < 0)
         return set_error(TTK_ERR_ARG, "gemm: negative size");
     if (M == 0 || N == 0 || batch == 0)
@@ -1071,7 +1272,7 @@ int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_
         return check_launch("gemm_fp32_kernel");
     }
     const int prec = current_prec();
-    const GemmPlan pl = plan(prec, transA, transB, batch, M, N, K);
+    const GemmPlan pl = plan(prec, transA, transB, batch, M, N, K, allow_splitk);
     if (!ws || ws_bytes < pl.total)
         return set_error(TTK_ERR_ARG, "gemm: workspace too small");
     void* wa = ws;
@@ -1086,7 +1287,9 @@ int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_
             return rc;
         return run_presplit<gemm::PREC_TF32X3>(transA, transB, batch, M, N, K, alpha, wa,
                                                pl.ga.ld_pad, wb, pl.gb.ld_pad, beta, C, ldc,
-                                               strideC, stream);
+                                               strideC, stream, pl.w_bytes ? 1 : 0,
+                                               static_cast<char*>(ws) + pl.off_w,
+                                               pl.w_bytes ? ws_bytes - pl.off_w : 0);
     }
     int rc = launch_split<gemm::PREC_BF16X3>(A, pl.ga.rows, pl.ga.cols, lda, strideA, batch, wa,
                                              pl.ga.ld_pad, stream);
@@ -1097,7 +1300,9 @@ int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_
         return rc;
     return run_presplit<gemm::PREC_BF16X3>(transA, transB, batch, M, N, K, alpha, wa,
                                            pl.ga.ld_pad, wb, pl.gb.ld_pad, beta, C, ldc, strideC,
-                                           stream);
+                                           stream, pl.w_bytes ? 1 : 0,
+                                           static_cast<char*>(ws) + pl.off_w,
+                                           pl.w_bytes ? ws_bytes - pl.off_w : 0);
 }
 
 // Caller-held operand splits in the current precision: [batch][2][rows][ld]
@@ -1152,10 +1357,10 @@ int gemm_on_splits(int transA, int transB, int64_t batch, int64_t M, int64_t N, 
     if (current_prec() == gemm::PREC_TF32X3)
         return run_presplit<gemm::PREC_TF32X3>(transA, transB, batch, M, N, K, alpha, a_split,
                                                lda_pad, b_split, ldb_pad, beta, C, ldc, strideC,
-                                               stream);
+                                               stream, 2);
     return run_presplit<gemm::PREC_BF16X3>(transA, transB, batch, M, N, K, alpha, a_split,
                                            lda_pad, b_split, ldb_pad, beta, C, ldc, strideC,
-                                           stream);
+                                           stream, 2);
 }
 
 int gemm_tf32x3_presplit(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,

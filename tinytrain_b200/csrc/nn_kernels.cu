@@ -130,28 +130,38 @@ __global__ void rmsnorm_fwd_rows_kernel(const float* __restrict__ x, const float
     const int64_t c0 = 4 * static_cast<int64_t>(t), c1 = 4 * static_cast<int64_t>(t + tpr);
     const float4 w0 = *reinterpret_cast<const float4*>(w + c0);
     const float4 w1 = *reinterpret_cast<const float4*>(w + c1);
-    int parity = 0;
-    for (int64_t base = static_cast<int64_t>(blockIdx.x) * rpb; base < R;
-         base += static_cast<int64_t>(gridDim.x) * rpb, parity ^= 1) {
-        const int64_t row = base + slot;
-        const bool ok = row < R;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
-        if (ok) {
+    // The next row's x is loaded before this row's reduction (two rows of
+    // loads in flight per thread).
+    auto load = [&](int64_t row, float4& a, float4& b) {
+        a = b = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (row < R) {
             a = *reinterpret_cast<const float4*>(x + row * D + c0);
             b = *reinterpret_cast<const float4*>(x + row * D + c1);
         }
+    };
+    const int64_t step = static_cast<int64_t>(gridDim.x) * rpb;
+    int parity = 0;
+    float4 a, b;
+    load(static_cast<int64_t>(blockIdx.x) * rpb + slot, a, b);
+    for (int64_t base = static_cast<int64_t>(blockIdx.x) * rpb; base < R;
+         base += step, parity ^= 1) {
+        const int64_t row = base + slot;
+        const bool ok = row < R;
+        float4 na, nb;
+        load(row + step, na, nb);
         const float ss = block_row_sum(a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w + b.x * b.x +
                                            b.y * b.y + b.z * b.z + b.w * b.w,
                                        red, slot, t, tpr, parity);
-        if (!ok)
-            continue;
-        const float r = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
-        if (t == 0 && rstd)
-            rstd[row] = r;
-        *reinterpret_cast<float4*>(y + row * D + c0) =
-            make_float4(a.x * r * w0.x, a.y * r * w0.y, a.z * r * w0.z, a.w * r * w0.w);
-        *reinterpret_cast<float4*>(y + row * D + c1) =
-            make_float4(b.x * r * w1.x, b.y * r * w1.y, b.z * r * w1.z, b.w * r * w1.w);
+        if (ok) {
+            const float r = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
+            if (t == 0 && rstd)
+                rstd[row] = r;
+            *reinterpret_cast<float4*>(y + row * D + c0) =
+                make_float4(a.x * r * w0.x, a.y * r * w0.y, a.z * r * w0.z, a.w * r * w0.w);
+            *reinterpret_cast<float4*>(y + row * D + c1) =
+                make_float4(b.x * r * w1.x, b.y * r * w1.y, b.z * r * w1.z, b.w * r * w1.w);
+        }
+        a = na, b = nb;
     }
 }
 
@@ -241,22 +251,24 @@ __global__ void rmsnorm_bwd_rows_kernel(const float* __restrict__ x, const float
     }
 }
 
-// dw[c] += sum_b partial[b][c] over nb partial rows. A block of 8 warps owns
+// dw[c] += sum_b partial[b][c] over nb partial rows. A block of 16 warps owns
 // 32 adjacent columns (one per lane, 128-byte row segments); warp w sums rows
-// b = w, w + 8, ... in ascending order and the eight warp sums are added in
-// warp order: a fixed summation order, so the result is deterministic.
-constexpr int COLSUM_THREADS = 256;
-__global__ void colsum_kernel(const float* __restrict__ partial, int64_t nb, int64_t D,
-                              float* __restrict__ out) {
-    __shared__ float red[8][32];
+// b = w, w + 16, ... in ascending order and the sixteen warp sums are added
+// in warp order: a fixed summation order, so the result is deterministic.
+constexpr int COLSUM_THREADS = 512;
+__global__ void __launch_bounds__(COLSUM_THREADS) colsum_kernel(const float* __restrict__ partial,
+                                                                int64_t nb, int64_t D,
+                                                                float* __restrict__ out) {
+    constexpr int NW = COLSUM_THREADS / 32;
+    __shared__ float red[NW][32];
     const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
     for (int64_t cb = static_cast<int64_t>(blockIdx.x) * 32; cb < D;
          cb += static_cast<int64_t>(gridDim.x) * 32) {
         const int64_t c = cb + lane;
         float s = 0.0f;
         if (c < D) {
-#pragma unroll 4
-            for (int64_t b = wp; b < nb; b += 8)
+#pragma unroll 8
+            for (int64_t b = wp; b < nb; b += NW)
                 s += partial[b * D + c];
         }
         red[wp][lane] = s;
@@ -264,7 +276,7 @@ __global__ void colsum_kernel(const float* __restrict__ partial, int64_t nb, int
         if (wp == 0 && c < D) {
             float tot = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+            for (int i = 0; i < NW; ++i)
                 tot += red[i][lane];
             out[c] += tot;
         }
@@ -763,7 +775,7 @@ static int64_t rms_blocks(int64_t R) { return std::min<int64_t>(std::max<int64_t
 // Row-parallel backward: blocks and dw partial rows (one per row slot).
 static int64_t rms_rows_blocks(int64_t R, int64_t D) {
     const int rpb = rms_block(D) / static_cast<int>(D / RMS_EPT);
-    return std::min<int64_t>((R + rpb - 1) / rpb, 148 * 4);
+    return std::min<int64_t>((R + rpb - 1) / rpb, 148 * 2);
 }
 
 size_t ttk_rmsnorm_bwd_workspace_size(int64_t R, int64_t D) {

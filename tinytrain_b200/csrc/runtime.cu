@@ -222,6 +222,15 @@ int ttk_gemm_set_cta_pairs(int mode) { return gemm_set_cta_pairs(mode); }
 
 int ttk_gemm_get_cta_pairs(void) { return gemm_get_cta_pairs(); }
 
+int ttk_gemm_set_split_k(int on) { return gemm_set_split_k(on); }
+
+int ttk_gemm_get_split_k(void) { return gemm_get_split_k(); }
+
+int ttk_gemm_split_k_slices(int transA, int transB, int64_t batch, int64_t M, int64_t N,
+                            int64_t K) {
+    return gemm_split_k_slices(transA, transB, batch, M, N, K);
+}
+
 int ttk_gemm_set_fp32_max_macs(int64_t macs) { return gemm_set_fp32_max_macs(macs); }
 
 int64_t ttk_gemm_get_fp32_max_macs(void) { return gemm_fp32_max_macs(); }

@@ -1,7 +1,8 @@
 // Shared device helpers for the ttk kernels (sm_100a only).
 //
-// Inline-PTX wrappers for mbarriers, TMA (cp.async.bulk.tensor, never with
-// .multicast::cluster), and the tcgen05 family (TMEM alloc, MMA, commit, ld).
+// Inline-PTX wrappers for mbarriers, TMA tile copies (each into the issuing
+// CTA's own shared memory), and the tcgen05 family (TMEM alloc, MMA, commit,
+// ld).
 // Every spin wait is bounded by a wall-clock limit read from %globaltimer;
 // on expiry the waiting thread records an error code in the device status
 // word and the caller unwinds instead of hanging the GPU.
@@ -210,7 +211,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
 
 // TMA tile loads of one CTA of a pair into its own shared memory, completing
 // on the transaction count of the pair's rank-0 barrier (shared::cluster
-// address). Plain loads: no multicast.
+// address). Each copy has the issuing CTA as its only destination.
 __device__ __forceinline__ void tma_load_4d_pair(void* dst, const void* desc, uint32_t bar_cluster,
                                                  int c0, int c1, int c2, int c3) {
     asm volatile(

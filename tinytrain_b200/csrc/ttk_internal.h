@@ -38,21 +38,25 @@ inline int grid_for(int64_t n, int threads, int max_blocks = 148 * 16) {
 // GEMM entry points (gemm_split3.cu), shared with the C ABI wrappers.
 int gemm_profile_enable(int on);
 int gemm_profile_read(double* ms, double* flops, int64_t* launches);
+// allow_splitk: include (and use) split-K partials in the workspace.
 size_t gemm_workspace_size(int transA, int transB, int64_t batch, int64_t M, int64_t N,
-                           int64_t K);
+                           int64_t K, bool allow_splitk = true);
 int split_tf32(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
                int64_t batch, float* dst, int64_t ld_pad, cudaStream_t stream);
 int gemm_set_precision(int prec);
 int gemm_get_precision();
 int gemm_set_cta_pairs(int mode);
 int gemm_get_cta_pairs();
+int gemm_set_split_k(int on);
+int gemm_get_split_k();
+int gemm_split_k_slices(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K);
 int gemm_set_fp32_max_macs(int64_t macs);
 int64_t gemm_fp32_max_macs();
 bool gemm_uses_fp32(int64_t batch, int64_t M, int64_t N, int64_t K);
 int gemm_run(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K, float alpha,
              const float* A, int64_t lda, int64_t strideA, const float* B, int64_t ldb,
              int64_t strideB, float beta, float* C, int64_t ldc, int64_t strideC, void* ws,
-             size_t ws_bytes, cudaStream_t stream);
+             size_t ws_bytes, cudaStream_t stream, bool allow_splitk = true);
 size_t gemm_split_bytes(int64_t batch, int64_t rows, int64_t cols);
 int gemm_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
                int64_t batch, void* dst, cudaStream_t stream);

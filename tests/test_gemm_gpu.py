@@ -214,6 +214,7 @@ def test_split_k(cuda, split_k, M, N, K, S, orients):
     from tinytrain_b200 import _ttk
     from tinytrain_b200 import kernels as Kn
     for tA, tB in orients:
+        split_k(True)
         assert _ttk.call("ttk_gemm_split_k_slices", tA, tB, 1, M, N, K) == S
         gen = torch.Generator(device=cuda).manual_seed(M + N + K + tA + 2 * tB)
         A = torch.rand((K, M) if tA else (M, K), device=cuda, generator=gen) * 2 - 1

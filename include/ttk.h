@@ -233,6 +233,18 @@ int ttk_attention_bwd(const float* q, const float* k, const float* v, const floa
                       float* dq, float* dk, float* dv, int accumulate, int64_t B, int64_t T,
                       int64_t H, int64_t hd, float scale, void* workspace,
                       size_t workspace_bytes, void* stream);
+/* ttk_attention_bwd reusing the forward's operand planes: fwd_workspace is
+ * the workspace of the ttk_attention_fwd call that produced o and lse (same
+ * q, k, v, tables, scale and engine, and q, k, v unchanged since), kept by the
+ * caller. Only dO is split here, and `workspace` needs only
+ * ttk_attention_bwd_ex_workspace_size bytes. A null fwd_workspace (or the
+ * FMA engine, whose forward keeps no planes) runs ttk_attention_bwd. */
+size_t ttk_attention_bwd_ex_workspace_size(int64_t B, int64_t T, int64_t H, int64_t hd);
+int ttk_attention_bwd_ex(const float* q, const float* k, const float* v, const float* cos_t,
+                         const float* sin_t, const float* o, const float* lse, const float* dout,
+                         float* dq, float* dk, float* dv, int accumulate, int64_t B, int64_t T,
+                         int64_t H, int64_t hd, float scale, const void* fwd_workspace,
+                         void* workspace, size_t workspace_bytes, void* stream);
 /* Attention engine (process-wide), all fp32-accurate:
  *   0 = tensor cores (default): tcgen05 forward and backward for head dims
  *       64 and 128, mma.sync m16n8k16 elsewhere, both with the bf16x3

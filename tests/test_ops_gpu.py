@@ -288,6 +288,25 @@ def test_attention_bwd_accumulates(cuda, hd, attn_impl):
     assert status_ok()
 
 
+@pytest.mark.parametrize("hd", [64, 128, 32])
+def test_attention_bwd_reuses_forward_planes(cuda, hd, attn_impl):
+    """ttk_attention_bwd_ex with the forward's workspace (its q, k, v planes)
+    gives the same gradients, bit for bit, as ttk_attention_bwd, which splits
+    q, k, v again."""
+    from tinytrain_b200 import kernels as K
+    B, T, H = 2, 300, 2
+    g = torch.Generator(device=cuda).manual_seed(hd)
+    q, k, v, do = (torch.randn(B, T, H, hd, device=cuda, generator=g) for _ in range(4))
+    cs, sn = K.rope_tables(T, hd, 10000.0, cuda)
+    o, lse, fw = K.attention_fwd(q, k, v, cs, sn, keep_ws=True)
+    ref = K.attention_bwd(q, k, v, cs, sn, o, lse, do)
+    got = K.attention_bwd(q, k, v, cs, sn, o, lse, do, fwd_ws=fw)
+    torch.cuda.synchronize()
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)
+    assert status_ok()
+
+
 def test_adamw_golden(cuda, golden_ops):
     """6 steps of the fused multi-tensor AdamW equal the reference's AdamW."""
     from tinytrain_b200 import kernels as K

@@ -638,4 +638,39 @@ int ttk_attention_bwd(const float* q, const float* k, const float* v, const floa
     }
 }
 
+size_t ttk_attention_bwd_ex_workspace_size(int64_t B, int64_t T, int64_t H, int64_t hd) {
+    const size_t dv = align256(static_cast<size_t>(B * T * H) * sizeof(float));
+    if (attn_impl() == 1)
+        return dv;
+    // dO as bf16 hi|lo, then the (lse, D) table; q, k, v come from the forward
+    return dv + static_cast<size_t>(B * T * H * hd) * 2 * 2 +
+           align256(static_cast<size_t>(B * H * ((T + 31) / 32 * 32)) * 8);
+}
+
+int ttk_attention_bwd_ex(const float* q, const float* k, const float* v, const float* cos_t,
+                         const float* sin_t, const float* o, const float* lse, const float* dout,
+                         float* dq, float* dk, float* dv, int accumulate, int64_t B, int64_t T,
+                         int64_t H, int64_t hd, float scale, const void* fwd_workspace,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+    if (!fwd_workspace || attn_impl() == 1)
+        return ttk_attention_bwd(q, k, v, cos_t, sin_t, o, lse, dout, dq, dk, dv, accumulate, B,
+                                 T, H, hd, scale, workspace, workspace_bytes, stream);
+    int rc = attn_check(q, k, v, cos_t, sin_t, B, T, H, hd);
+    if (rc)
+        return rc;
+    if (!B || !T || !H)
+        return TTK_OK;
+    if (!o || !lse || !dout || !dq || !dk || !dv)
+        return set_error(TTK_ERR_ARG, "attention_bwd: null pointer");
+    if (!workspace || workspace_bytes < ttk_attention_bwd_ex_workspace_size(B, T, H, hd))
+        return set_error(TTK_ERR_ARG, "attention_bwd: workspace too small");
+    rc = attn_align_check({q, k, v, cos_t, sin_t, o, dout, dq, dk, dv, fwd_workspace});
+    if (rc)
+        return rc;
+    const bool tc = attn_impl() == 0 && attention_tc_supported(static_cast<int>(hd));
+    return attention_mma_backward(static_cast<int>(hd), q, k, v, cos_t, sin_t, o, lse, dout, dq,
+                                  dk, dv, accumulate, B, T, H, scale, workspace, tc,
+                                  S(stream), fwd_workspace);
+}
+
 }  // extern "C"

@@ -18,6 +18,7 @@
 //   (backward: attn_bwd_mma_dkv / attn_bwd_mma_dq, below)
 // Shared tiles are [rows][HD] bf16 with the 16-byte chunks of each row XOR
 // swizzled so every ldmatrix phase hits 8 distinct bank groups.
+#include <algorithm>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -195,43 +196,51 @@ __device__ __forceinline__ void split4(const float (&v)[4], uint2& hi, uint2& lo
     lo = make_uint2(l0, l1);
 }
 
+// Launch shape: blockIdx.y strides over the B*H heads, blockIdx.x over time;
+// a block of 256 threads covers 256/Q rows (time steps) of one head per
+// sweep, Q = HD/8 threads per row, each thread one column quad of each half
+// row (the RoPE pair). The head's (b, h) is divided out once per head, not
+// per element.
 __global__ void attn_split_kernel(const float* __restrict__ x, const float* __restrict__ cs,
                                   const float* __restrict__ sn, int rope, float mul,
                                   __nv_bfloat16* __restrict__ hi, __nv_bfloat16* __restrict__ lo,
                                   int64_t B, int64_t T, int64_t H, int64_t HD) {
-    const int64_t HH = HD / 2, Q = HH / 4;  // column quads per half row
-    const int64_t total = B * T * H * Q;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t d = (i % Q) * 4;
-        const int64_t h = (i / Q) % H;
-        const int64_t t = (i / (Q * H)) % T;
-        const int64_t b = i / (Q * H * T);
-        const float* src = x + ((b * T + t) * H + h) * HD;
-        const float4 a = __ldg(reinterpret_cast<const float4*>(src + d));
-        const float4 c = __ldg(reinterpret_cast<const float4*>(src + d + HH));
-        float x1[4] = {a.x, a.y, a.z, a.w}, x2[4] = {c.x, c.y, c.z, c.w};
-        if (rope) {
-            const float4 co = __ldg(reinterpret_cast<const float4*>(cs + t * HH + d));
-            const float4 si = __ldg(reinterpret_cast<const float4*>(sn + t * HH + d));
-            const float cv[4] = {co.x, co.y, co.z, co.w}, sv[4] = {si.x, si.y, si.z, si.w};
+    const int HH = static_cast<int>(HD / 2), Q = HH / 4;  // column quads per half row
+    const int rpb = blockDim.x / Q;
+    const int lr = threadIdx.x / Q, d = (threadIdx.x % Q) * 4;
+    if (lr >= rpb)
+        return;
+    for (int64_t bh = blockIdx.y; bh < B * H; bh += gridDim.y) {
+        const int64_t b = bh / H, h = bh - b * H;
+        for (int64_t t = static_cast<int64_t>(blockIdx.x) * rpb + lr; t < T;
+             t += static_cast<int64_t>(gridDim.x) * rpb) {
+            const float* src = x + ((b * T + t) * H + h) * HD;
+            const float4 a = __ldg(reinterpret_cast<const float4*>(src + d));
+            const float4 c = __ldg(reinterpret_cast<const float4*>(src + d + HH));
+            float x1[4] = {a.x, a.y, a.z, a.w}, x2[4] = {c.x, c.y, c.z, c.w};
+            if (rope) {
+                const float4 co = __ldg(reinterpret_cast<const float4*>(cs + t * HH + d));
+                const float4 si = __ldg(reinterpret_cast<const float4*>(sn + t * HH + d));
+                const float cv[4] = {co.x, co.y, co.z, co.w}, sv[4] = {si.x, si.y, si.z, si.w};
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const float r1 = x1[u] * cv[u] - x2[u] * sv[u], r2 = x1[u] * sv[u] + x2[u] * cv[u];
-                x1[u] = r1, x2[u] = r2;
+                for (int u = 0; u < 4; ++u) {
+                    const float r1 = x1[u] * cv[u] - x2[u] * sv[u],
+                                r2 = x1[u] * sv[u] + x2[u] * cv[u];
+                    x1[u] = r1, x2[u] = r2;
+                }
             }
-        }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-            x1[u] *= mul, x2[u] *= mul;
-        const int64_t o = ((b * H + h) * T + t) * HD;
-        uint2 h1, l1, h2, l2;
-        split4(x1, h1, l1);
-        split4(x2, h2, l2);
-        *reinterpret_cast<uint2*>(hi + o + d) = h1;
-        *reinterpret_cast<uint2*>(lo + o + d) = l1;
-        *reinterpret_cast<uint2*>(hi + o + d + HH) = h2;
-        *reinterpret_cast<uint2*>(lo + o + d + HH) = l2;
+            for (int u = 0; u < 4; ++u)
+                x1[u] *= mul, x2[u] *= mul;
+            const int64_t o = (bh * T + t) * HD;
+            uint2 h1, l1, h2, l2;
+            split4(x1, h1, l1);
+            split4(x2, h2, l2);
+            *reinterpret_cast<uint2*>(hi + o + d) = h1;
+            *reinterpret_cast<uint2*>(lo + o + d) = l1;
+            *reinterpret_cast<uint2*>(hi + o + d + HH) = h2;
+            *reinterpret_cast<uint2*>(lo + o + d + HH) = l2;
+        }
     }
 }
 
@@ -781,9 +790,12 @@ struct SplitBufs {
 inline int launch_split(const float* x, const float* cs, const float* sn, int rope, float mul,
                         __nv_bfloat16* hi, __nv_bfloat16* lo, int64_t B, int64_t T, int64_t H,
                         int64_t HD, cudaStream_t st) {
-    const int64_t total = B * T * H * (HD / 8);
-    attn_split_kernel<<<grid_for(total, 256, 148 * 32), 256, 0, st>>>(x, cs, sn, rope, mul, hi,
-                                                                        lo, B, T, H, HD);
+    if (!B || !T || !H)
+        return TTK_OK;
+    const int64_t rpb = 256 / (HD / 8);  // time steps per block sweep
+    const dim3 grid(static_cast<unsigned>(std::min<int64_t>((T + rpb - 1) / rpb, 1024)),
+                    static_cast<unsigned>(std::min<int64_t>(B * H, 65535)));
+    attn_split_kernel<<<grid, 256, 0, st>>>(x, cs, sn, rope, mul, hi, lo, B, T, H, HD);
     return check_launch("attn_split_kernel");
 }
 
@@ -808,16 +820,21 @@ int fwd(const float* q, const float* k, const float* v, const float* cs, const f
     return check_launch("attn_fwd_mma");
 }
 
+// qkv_ready: s.q*, s.k*, s.v* already hold the forward's splits of q, k, v
+// (same inputs, same scale), so only dO is split here.
 template <int HD>
 int bwd(const float* q, const float* k, const float* v, const float* cs, const float* sn,
         const float* o, const float* lse, const float* dout, float* dq, float* dk, float* dv,
         int accumulate, int64_t B, int64_t T, int64_t H, float scale, SplitBufs s, float* Dv,
-        float* ld, bool tc, cudaStream_t st) {
-    int rc = launch_split(q, cs, sn, 1, scale, s.qh, s.ql, B, T, H, HD, st);
-    if (!rc)
-        rc = launch_split(k, cs, sn, 1, 1.0f, s.kh, s.kl, B, T, H, HD, st);
-    if (!rc)
-        rc = launch_split(v, cs, sn, 0, 1.0f, s.vh, s.vl, B, T, H, HD, st);
+        float* ld, bool tc, cudaStream_t st, bool qkv_ready = false) {
+    int rc = TTK_OK;
+    if (!qkv_ready) {
+        rc = launch_split(q, cs, sn, 1, scale, s.qh, s.ql, B, T, H, HD, st);
+        if (!rc)
+            rc = launch_split(k, cs, sn, 1, 1.0f, s.kh, s.kl, B, T, H, HD, st);
+        if (!rc)
+            rc = launch_split(v, cs, sn, 0, 1.0f, s.vh, s.vl, B, T, H, HD, st);
+    }
     if (!rc)
         rc = launch_split(dout, cs, sn, 0, 1.0f, s.dh, s.dl, B, T, H, HD, st);
     if (rc)
@@ -874,27 +891,41 @@ int attention_mma_forward(int hd, const float* q, const float* k, const float* v
     }
 }
 
+// Workspace: Dv [B*T*H] fp32 (256-byte aligned), then the q, k, v, dO planes
+// (8n bf16), then the tcgen05 path's (lse, D) table. With fwd_ws (the
+// forward's workspace: q, k, v planes, 6n bf16) the q, k, v planes are read
+// from there and ws holds Dv, the dO planes and the table.
 int attention_mma_backward(int hd, const float* q, const float* k, const float* v,
                            const float* cs, const float* sn, const float* o, const float* lse,
                            const float* dout, float* dq, float* dk, float* dv, int accumulate,
                            int64_t B, int64_t T, int64_t H, float scale, void* ws, bool tc,
-                           cudaStream_t st) {
+                           cudaStream_t st, const void* fwd_ws) {
     const int64_t n = B * T * H * hd;
     float* Dv = static_cast<float*>(ws);
     __nv_bfloat16* w = reinterpret_cast<__nv_bfloat16*>(
         static_cast<char*>(ws) + ((B * T * H * 4 + 255) / 256) * 256);
-    fa::SplitBufs s{w, w + n, w + 2 * n, w + 3 * n, w + 4 * n, w + 5 * n, w + 6 * n, w + 7 * n};
-    float* ld = reinterpret_cast<float*>(w + 8 * n);  // 256-byte aligned: n*16 bytes before it
+    fa::SplitBufs s;
+    float* ld;
+    if (fwd_ws) {
+        __nv_bfloat16* f = const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(fwd_ws));
+        s = fa::SplitBufs{f, f + n, f + 2 * n, f + 3 * n, f + 4 * n, f + 5 * n, w, w + n};
+        ld = reinterpret_cast<float*>(w + 2 * n);  // 16-byte aligned: n*4 bytes before it
+    } else {
+        s = fa::SplitBufs{w, w + n, w + 2 * n, w + 3 * n, w + 4 * n, w + 5 * n, w + 6 * n,
+                          w + 7 * n};
+        ld = reinterpret_cast<float*>(w + 8 * n);  // 256-byte aligned: n*16 bytes before it
+    }
+    const bool ready = fwd_ws != nullptr;
     switch (hd) {
         case 32:
             return fa::bwd<32>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                               scale, s, Dv, ld, false, st);
+                               scale, s, Dv, ld, false, st, ready);
         case 64:
             return fa::bwd<64>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                               scale, s, Dv, ld, tc, st);
+                               scale, s, Dv, ld, tc, st, ready);
         default:
             return fa::bwd<128>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                                scale, s, Dv, ld, tc, st);
+                                scale, s, Dv, ld, tc, st, ready);
     }
 }
 

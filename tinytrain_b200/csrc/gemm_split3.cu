@@ -507,42 +507,48 @@ __device__ __forceinline__ void split_one(float x, __nv_bfloat16& hi, __nv_bfloa
     lo = __float2bfloat16_rn(x - __bfloat162float(hi));
 }
 
+// Launch shape: TPR threads per row (a power of two covering the row's
+// 4-element groups, at most the block), 256 / TPR rows per block sweep, rows
+// strided over the grid; the batch index is divided out once per row.
 template <class T>
 __global__ void split_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
                              int64_t ld, int64_t bstride, int64_t batch, T* __restrict__ dst,
-                             int64_t ld_pad) {
+                             int64_t ld_pad, int tpr) {
     const int64_t per_row = ld_pad / 4;  // 4-element groups per padded row
-    const int64_t total = batch * rows * per_row;
+    const int64_t nrows = batch * rows;
     const int64_t plane = rows * ld_pad;
+    const int rpb = blockDim.x / tpr;
+    const int lr = threadIdx.x / tpr, lg = threadIdx.x % tpr;
     const bool vec = ((ld & 3) == 0) && ((bstride & 3) == 0) &&
                      ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int64_t g = i % per_row;
-        const int64_t r = (i / per_row) % rows;
-        const int64_t b = i / (per_row * rows);
-        const int64_t c0 = g * 4;
-        const float* s = src + b * bstride + r * ld + c0;
-        float x[4];
-        if (vec && c0 + 4 <= cols) {
-            float4 t = __ldg(reinterpret_cast<const float4*>(s));
-            x[0] = t.x, x[1] = t.y, x[2] = t.z, x[3] = t.w;
-        } else {
+    for (int64_t row = static_cast<int64_t>(blockIdx.x) * rpb + lr; row < nrows;
+         row += static_cast<int64_t>(gridDim.x) * rpb) {
+        const int64_t b = row / rows, r = row - b * rows;
+        const float* s_row = src + b * bstride + r * ld;
+        T* d_row = dst + b * 2 * plane + r * ld_pad;
+        for (int64_t g = lg; g < per_row; g += tpr) {
+            const int64_t c0 = g * 4;
+            float x[4];
+            if (vec && c0 + 4 <= cols) {
+                const float4 t = __ldg(reinterpret_cast<const float4*>(s_row + c0));
+                x[0] = t.x, x[1] = t.y, x[2] = t.z, x[3] = t.w;
+            } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    x[j] = (c0 + j < cols) ? __ldg(s_row + c0 + j) : 0.0f;
+            }
+            T hi[4], lo[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j)
-                x[j] = (c0 + j < cols) ? __ldg(s + j) : 0.0f;
-        }
-        T hi[4], lo[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-            split_one(x[j], hi[j], lo[j]);
-        T* d = dst + b * 2 * plane + r * ld_pad + c0;
-        if (sizeof(T) == 4) {
-            *reinterpret_cast<float4*>(d) = *reinterpret_cast<const float4*>(hi);
-            *reinterpret_cast<float4*>(d + plane) = *reinterpret_cast<const float4*>(lo);
-        } else {
-            *reinterpret_cast<uint2*>(d) = *reinterpret_cast<const uint2*>(hi);
-            *reinterpret_cast<uint2*>(d + plane) = *reinterpret_cast<const uint2*>(lo);
+                split_one(x[j], hi[j], lo[j]);
+            T* d = d_row + c0;
+            if (sizeof(T) == 4) {
+                *reinterpret_cast<float4*>(d) = *reinterpret_cast<const float4*>(hi);
+                *reinterpret_cast<float4*>(d + plane) = *reinterpret_cast<const float4*>(lo);
+            } else {
+                *reinterpret_cast<uint2*>(d) = *reinterpret_cast<const uint2*>(hi);
+                *reinterpret_cast<uint2*>(d + plane) = *reinterpret_cast<const uint2*>(lo);
+            }
         }
     }
 }
@@ -1044,17 +1050,21 @@ int current_prec() {
 template <int PREC>
 int launch_split(const float* src, int64_t rows, int64_t cols, int64_t ld, int64_t bstride,
                  int64_t batch, void* dst, int64_t ld_pad, cudaStream_t stream) {
-    const int64_t total = batch * rows * (ld_pad / 4);
-    if (total == 0)
+    const int64_t per_row = ld_pad / 4, nrows = batch * rows;
+    if (per_row == 0 || nrows == 0)
         return TTK_OK;
     const int threads = 256;
-    const int64_t blocks = std::min<int64_t>((total + threads - 1) / threads, 148 * 16);
+    int tpr = 1;  // threads per row: a power of two covering the row, at most the block
+    while (tpr < threads && tpr < per_row)
+        tpr <<= 1;
+    const int64_t rpb = threads / tpr;
+    const int64_t blocks = std::min<int64_t>((nrows + rpb - 1) / rpb, 148 * 16);
     if (PREC == gemm::PREC_TF32X3)
         gemm::split_kernel<float><<<static_cast<int>(blocks), threads, 0, stream>>>(
-            src, rows, cols, ld, bstride, batch, static_cast<float*>(dst), ld_pad);
+            src, rows, cols, ld, bstride, batch, static_cast<float*>(dst), ld_pad, tpr);
     else
         gemm::split_kernel<__nv_bfloat16><<<static_cast<int>(blocks), threads, 0, stream>>>(
-            src, rows, cols, ld, bstride, batch, static_cast<__nv_bfloat16*>(dst), ld_pad);
+            src, rows, cols, ld, bstride, batch, static_cast<__nv_bfloat16*>(dst), ld_pad, tpr);
     return check_launch("split_kernel");
 }
 

@@ -78,7 +78,7 @@ int attention_mma_backward(int hd, const float* q, const float* k, const float* 
                            const float* cs, const float* sn, const float* o, const float* lse,
                            const float* dout, float* dq, float* dk, float* dv, int accumulate,
                            int64_t B, int64_t T, int64_t H, float scale, void* ws, bool tc,
-                           cudaStream_t st);
+                           cudaStream_t st, const void* fwd_ws = nullptr);
 
 // tcgen05 attention forward / backward (attention_tc.cu) over split planes
 // written by the mma.sync path's split pass; head dims 64 and 128.

@@ -893,20 +893,31 @@ Tensor causal_attention(const Tensor& q, const Tensor& k, const Tensor& v, const
     const bool rg = q.requires_grad() || k.requires_grad() || v.requires_grad();
     Tensor out = make_out({B, T, H * hd}, rg);
     auto lse = std::make_shared<Buffer>(B * H * T);
-    {
-        const size_t ws = ttk_attention_fwd_workspace_size(B, T, H, hd);
-        Scratch w(ws);
-        check(ttk_attention_fwd(dread(q.impl()), dread(k.impl()), dread(v.impl()),
-                                dread(cos.impl()), dread(sin.impl()), out_ptr(out),
-                                lse->device_for_overwrite(), B, T, H, hd, scale, w.ptr, ws,
-                                stream()),
-              "attention");
-    }
+    // The forward's workspace holds q, k, v split into bf16 planes; it is kept
+    // for the backward, which reuses them while q, k, v are unchanged.
+    const size_t fws = ttk_attention_fwd_workspace_size(B, T, H, hd);
+    auto fw = std::make_shared<Scratch>(fws);
+    check(ttk_attention_fwd(dread(q.impl()), dread(k.impl()), dread(v.impl()), dread(cos.impl()),
+                            dread(sin.impl()), out_ptr(out), lse->device_for_overwrite(), B, T,
+                            H, hd, scale, fw->ptr, fws, stream()),
+          "attention");
+    if (!rg)
+        fw.reset();
     if (rg) {
         auto qo = q.impl(), ko = k.impl(), vo = v.impl(), co = cos.impl(), so = sin.impl();
+        // Contents of q, k, v as the forward read them (buffer versions).
+        auto version_of = [](const ImplPtr& p) -> uint64_t {
+            if (p->data)
+                return p->data->version;
+            if (p->transpose_of && p->transpose_of->data)
+                return p->transpose_of->data->version;
+            return ~0ull;
+        };
+        const uint64_t vq = version_of(qo), vk = version_of(ko), vv = version_of(vo);
         Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
         oo->prev = {qo, ko, vo};
-        oo->backward_fn = [qo, ko, vo, co, so, oo, lse, B, T, H, hd, scale]() {
+        oo->backward_fn = [qo, ko, vo, co, so, oo, lse, B, T, H, hd, scale, fw, vq, vk, vv,
+                           version_of]() mutable {
             const float* g = grad_in(oo);
             if (!g)
                 return;
@@ -932,12 +943,25 @@ Tensor causal_attention(const Tensor& q, const Tensor& k, const Tensor& v, const
                 if (ov)
                     check(ttk_memset(dv, 0, static_cast<size_t>(vo->numel) * 4, stream()), "zero");
             }
-            const size_t ws = ttk_attention_bwd_workspace_size(B, T, H, hd);
-            Scratch w(ws);
-            check(ttk_attention_bwd(dread(qo), dread(ko), dread(vo), dread(co), dread(so),
-                                    dread(oo), lse->device(), g, dq, dk, dv, all_fresh ? 0 : 1, B,
-                                    T, H, hd, scale, w.ptr, ws, stream()),
-                  "attention bwd");
+            const float *qd = dread(qo), *kd = dread(ko), *vd = dread(vo);
+            const bool reuse = fw && fw->ptr && vq != ~0ull && version_of(qo) == vq &&
+                               version_of(ko) == vk && version_of(vo) == vv;
+            if (reuse) {
+                const size_t ws = ttk_attention_bwd_ex_workspace_size(B, T, H, hd);
+                Scratch w(ws);
+                check(ttk_attention_bwd_ex(qd, kd, vd, dread(co), dread(so), dread(oo),
+                                           lse->device(), g, dq, dk, dv, all_fresh ? 0 : 1, B, T,
+                                           H, hd, scale, fw->ptr, w.ptr, ws, stream()),
+                      "attention bwd");
+            } else {
+                const size_t ws = ttk_attention_bwd_workspace_size(B, T, H, hd);
+                Scratch w(ws);
+                check(ttk_attention_bwd(qd, kd, vd, dread(co), dread(so), dread(oo),
+                                        lse->device(), g, dq, dk, dv, all_fresh ? 0 : 1, B, T, H,
+                                        hd, scale, w.ptr, ws, stream()),
+                      "attention bwd");
+            }
+            fw.reset();  // planes no longer needed (stream-ordered free)
         };
     }
     return out;

@@ -164,7 +164,8 @@ def rope_tables(T, hd, theta, device):
             torch.from_numpy(np.sin(ang).astype(np.float32)).to(device))
 
 
-def attention_fwd(q, k, v, cos, sin, scale=None):
+def attention_fwd(q, k, v, cos, sin, scale=None, keep_ws=False):
+    """(o, lse); with keep_ws also the workspace (q, k, v planes) for attention_bwd(fwd_ws=)."""
     B, T, H, hd = q.shape
     scale = float(hd) ** -0.5 if scale is None else scale
     o = torch.empty_like(q)
@@ -172,15 +173,24 @@ def attention_fwd(q, k, v, cos, sin, scale=None):
     ws = workspace(call("ttk_attention_fwd_workspace_size", B, T, H, hd), q.device)
     call("ttk_attention_fwd", _p(q), _p(k), _p(v), _p(cos), _p(sin), _p(o), _p(lse), B, T, H, hd,
          scale, _p(ws), ws.numel(), _s())
-    return o, lse
+    return (o, lse, ws) if keep_ws else (o, lse)
 
 
-def attention_bwd(q, k, v, cos, sin, o, lse, do, scale=None, out=None, accumulate=False):
-    """dq, dk, dv; with `out` = (dq, dk, dv) writes (or, with accumulate, adds) into them."""
+def attention_bwd(q, k, v, cos, sin, o, lse, do, scale=None, out=None, accumulate=False,
+                  fwd_ws=None):
+    """dq, dk, dv; with `out` = (dq, dk, dv) writes (or, with accumulate, adds) into them.
+    fwd_ws: the forward's workspace (attention_fwd(keep_ws=True)), whose q, k, v planes are
+    reused."""
     B, T, H, hd = q.shape
     scale = float(hd) ** -0.5 if scale is None else scale
     dq, dk, dv = out if out is not None else (torch.empty_like(q), torch.empty_like(k),
                                                torch.empty_like(v))
+    if fwd_ws is not None and fwd_ws.numel() > 0:
+        ws = workspace(call("ttk_attention_bwd_ex_workspace_size", B, T, H, hd), q.device)
+        call("ttk_attention_bwd_ex", _p(q), _p(k), _p(v), _p(cos), _p(sin), _p(o), _p(lse),
+             _p(do), _p(dq), _p(dk), _p(dv), int(accumulate), B, T, H, hd, scale, _p(fwd_ws),
+             _p(ws), ws.numel(), _s())
+        return dq, dk, dv
     ws = workspace(call("ttk_attention_bwd_workspace_size", B, T, H, hd), q.device)
     call("ttk_attention_bwd", _p(q), _p(k), _p(v), _p(cos), _p(sin), _p(o), _p(lse), _p(do),
          _p(dq), _p(dk), _p(dv), int(accumulate), B, T, H, hd, scale, _p(ws), ws.numel(), _s())

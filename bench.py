@@ -89,10 +89,14 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
+    _count = 0
+
     def __init__(self, gpus):
         self.gpus = gpus
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        ClockSampler._count += 1
+        self.path = os.path.join(ROOT, "gpurun_out",
+                                 f"clocks_{os.getpid()}_{ClockSampler._count}.csv")
 
     def __enter__(self):
         try:
@@ -306,13 +310,14 @@ def main():
     tr.step(pin_idx[0].numpy(), pin_tgt[0].numpy(), B, T, n_micro, 3e-4)  # warm path
     barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
     loss_e2e = None
-    for i in range(ke):
-        loss_e2e, _ = tr.step(pin_idx[i % n_sets].numpy(), pin_tgt[i % n_sets].numpy(), B, T,
-                              n_micro, 3e-4)
-    f1.record(stream)
-    barrier()
+    with ClockSampler([local] if world == 1 else list(range(world))) as clk_e2e:
+        f0.record(stream)
+        for i in range(ke):
+            loss_e2e, _ = tr.step(pin_idx[i % n_sets].numpy(), pin_tgt[i % n_sets].numpy(), B,
+                                  T, n_micro, 3e-4)
+        f1.record(stream)
+        barrier()
     ms_e2e = max_over_ranks(f0.elapsed_time(f1)) / ke
     e2e = tokens_step / (ms_e2e / 1e3)
     status = _ttk.device_status()
@@ -343,7 +348,7 @@ def main():
             "mfu_fp32_equiv": value * flops_per_token(w) / 1e12 / world,
             "gpu_launches": launches,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * tokens_rank * 8,
-                    "d2h_bytes_per_step": 4, "steps": ke},
+                    "d2h_bytes_per_step": 4, "steps": ke, "clocks": clk_e2e.summary()},
             "clocks": clk.summary(),
             "loss": loss_dev, "loss_e2e": loss_e2e, "device_status": status,
         }

@@ -51,6 +51,9 @@ constexpr int BQ = 128;  // query rows per CTA (MMA M, TMEM lanes)
 constexpr int BKV = 64;  // keys per block
 constexpr int NSLOT = 3;
 constexpr int NUM_THREADS = 320;
+// dK/dV: a second MMA-issuing warp (index 10) after the eight softmax warps.
+constexpr int DKV_MMA_B_WARP = 10;
+constexpr int DKV_THREADS = 352;
 constexpr int SOFTMAX_THREADS = 256;
 constexpr uint32_t kSW64 = 4;
 constexpr float LOG2E = 1.4426950408889634f;
@@ -858,7 +861,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 //   lse (pre-multiplied by log2 e) and D of each query block arrive with Q_i
 //   by a bulk copy from the padded (lse, D) table `ld` [B*H][T32][2].
 template <int HD>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(DKV_THREADS, 1)
     attn_bwd_dkv_tc(const __grid_constant__ CUtensorMap map_k,
                     const __grid_constant__ CUtensorMap map_v,
                     const __grid_constant__ CUtensorMap map_q,
@@ -880,6 +883,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint64_t* sd_full = oempty + DKV_R1;    // [NBUF]
     uint64_t* pds_full = sd_full + NBUF;  // [NBUF]
     uint64_t* done = pds_full + NBUF;
+    uint64_t* bfree = done + 1;  // [NBUF]: a score buffer's accumulation MMAs done
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + CF::NBARS);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -897,11 +901,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&ofull[i], 1);
             mbar_init(&oempty[i], 1);
         }
+        // Two MMA-issuing warps: commits from both complete sd_full, bfree and done.
         for (int b = 0; b < NBUF; ++b) {
-            mbar_init(&sd_full[b], 1);
+            mbar_init(&sd_full[b], 2);
             mbar_init(&pds_full[b], GROUP_THREADS);
+            mbar_init(&bfree[b], 2);
         }
-        mbar_init(done, 1);
+        mbar_init(done, 2);
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -968,16 +974,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 }
             }
         }
-    } else if (warp == 1) {
-        // -------------------------------------------------------- MMA issuer
-        // The whole warp runs this loop (uniform control flow); lane 0 issues.
+    } else if (warp == 1 || warp == DKV_MMA_B_WARP) {
+        // -------------------------------------------------------- MMA issuers
+        // One warp issues at most about one MMA per 64 cycles, so two warps
+        // share the work (each loop warp-uniform; lane 0 issues):
+        //   warp A (1):  S^T = K Q^T  and  dK += dS^T Q   (the Q slot)
+        //   warp B (10): dP^T = V dO^T  and  dV += P^T dO  (the dO slot)
+        // Their MMAs are not ordered against each other, so a score buffer is
+        // rewritten only after both warps' accumulation MMAs on its previous
+        // block completed (bfree).
+        const bool wa = warp == 1;
         constexpr uint32_t idesc_sd = umma_idesc_bf16(BQ, BWD_BLK, 0, 0);
         constexpr uint32_t idesc_acc = umma_idesc_bf16(BQ, HD, 0, 1);
-        const uint64_t kh0 = kmajor_desc(s_base, BQ, 0);
-        const uint64_t kl0 = kmajor_desc(s_base + CF::BIG_PLANE, BQ, 0);
-        const uint64_t vh0 = kmajor_desc(s_base + CF::OFF_BIG1, BQ, 0);
-        const uint64_t vl0 = kmajor_desc(s_base + CF::OFF_BIG1 + CF::BIG_PLANE, BQ, 0);
-        const uint32_t dV = tmem + CF::ACC_COL, dK = tmem + CF::ACC_COL + HD;
+        const uint32_t big = wa ? 0u : static_cast<uint32_t>(CF::OFF_BIG1);  // K | V
+        const uint64_t xh0 = kmajor_desc(s_base + big, BQ, 0);
+        const uint64_t xl0 = kmajor_desc(s_base + big + CF::BIG_PLANE, BQ, 0);
+        const uint32_t ring = wa ? static_cast<uint32_t>(CF::OFF_R1) : static_cast<uint32_t>(CF::OFF_R2);
+        uint64_t* rfull = wa ? qfull : ofull;
+        uint64_t* rempty = wa ? qempty : oempty;
+        const uint32_t acc_d = tmem + CF::ACC_COL + (wa ? HD : 0);  // dK | dV
+        const uint32_t half = wa ? 32u : 0u;  // A operand of the accumulation: dS^T | P^T
         bool ok = mbar_wait(a_full, 0, 63);
         auto issue_acc = [&](int i) -> bool {
             const int b = i % NBUF;
@@ -985,55 +1001,45 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 return false;
             tc_fence_after();
             const int slot = i % DKV_R1;
-            const uint32_t sQ = s_base + CF::OFF_R1 + slot * CF::SMALL_BYTES;
-            const uint32_t sO = s_base + CF::OFF_R2 + slot * CF::SMALL_BYTES;
-            const uint64_t qh = small_mn_desc(sQ, 0), ql = small_mn_desc(sQ + CF::SMALL_PLANE, 0);
-            const uint64_t oh = small_mn_desc(sO, 0), ol = small_mn_desc(sO + CF::SMALL_PLANE, 0);
-            const uint32_t p = tmem + b * 64, d = p + 32;
+            const uint32_t sR = s_base + ring + slot * CF::SMALL_BYTES;
+            const uint64_t rh = small_mn_desc(sR, 0), rl = small_mn_desc(sR + CF::SMALL_PLANE, 0);
+            const uint32_t x = tmem + b * 64 + half;
 #pragma unroll
             for (int ks = 0; ks < BWD_BLK / 16; ++ks) {
                 const uint32_t first = (i == 0 && ks == 0) ? 0u : 1u;
                 const uint32_t o = ks * 1024;
-                mma_bf16_ta_w(dV, p + 16 + ks * 8, desc_add(oh, o), idesc_acc, first);
-                mma_bf16_ta_w(dK, d + 16 + ks * 8, desc_add(qh, o), idesc_acc, first);
-                mma_bf16_ta_w(dV, p + ks * 8, desc_add(ol, o), idesc_acc, 1u);
-                mma_bf16_ta_w(dK, d + ks * 8, desc_add(ql, o), idesc_acc, 1u);
-                mma_bf16_ta_w(dV, p + ks * 8, desc_add(oh, o), idesc_acc, 1u);
-                mma_bf16_ta_w(dK, d + ks * 8, desc_add(qh, o), idesc_acc, 1u);
+                mma_bf16_ta_w(acc_d, x + 16 + ks * 8, desc_add(rh, o), idesc_acc, first);
+                mma_bf16_ta_w(acc_d, x + ks * 8, desc_add(rl, o), idesc_acc, 1u);
+                mma_bf16_ta_w(acc_d, x + ks * 8, desc_add(rh, o), idesc_acc, 1u);
             }
-            mma_commit_w(&qempty[slot]);
-            mma_commit_w(&oempty[slot]);
+            mma_commit_w(&rempty[slot]);
+            mma_commit_w(&bfree[b]);
             return true;
         };
         for (int n = 0; n < nblk && ok; ++n) {
             const int slot = n % DKV_R1;
             const uint32_t ph = static_cast<uint32_t>((n / DKV_R1) & 1);
-            if (*abort_flag || !mbar_wait(&qfull[slot], ph, 67) ||
-                !mbar_wait(&ofull[slot], ph, 68)) {
+            const int b = n % NBUF;
+            if (*abort_flag || !mbar_wait(&rfull[slot], ph, wa ? 67 : 68) ||
+                (n >= NBUF && !mbar_wait(&bfree[b], static_cast<uint32_t>((n / NBUF - 1) & 1), 65))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t sQ = s_base + CF::OFF_R1 + slot * CF::SMALL_BYTES;
-            const uint32_t sO = s_base + CF::OFF_R2 + slot * CF::SMALL_BYTES;
-            const uint64_t qh0 = kmajor_desc(sQ, BWD_BLK, 0);
-            const uint64_t ql0 = kmajor_desc(sQ + CF::SMALL_PLANE, BWD_BLK, 0);
-            const uint64_t oh0 = kmajor_desc(sO, BWD_BLK, 0);
-            const uint64_t ol0 = kmajor_desc(sO + CF::SMALL_PLANE, BWD_BLK, 0);
-            const uint32_t ds = tmem + (n % NBUF) * 64, dp = ds + 32;
+            const uint32_t sR = s_base + ring + slot * CF::SMALL_BYTES;
+            const uint64_t rh0 = kmajor_desc(sR, BWD_BLK, 0);
+            const uint64_t rl0 = kmajor_desc(sR + CF::SMALL_PLANE, BWD_BLK, 0);
+            const uint32_t dst = tmem + b * 64 + (wa ? 0u : 32u);  // S^T | dP^T
 #pragma unroll
             for (int ks = 0; ks < HD / 16; ++ks) {
                 const uint32_t bb = (ks >> 1) * (BQ * 64) + (ks & 1) * 32;
                 const uint32_t sb = (ks >> 1) * (BWD_BLK * 64) + (ks & 1) * 32;
                 const uint32_t acc = ks > 0 ? 1u : 0u;
-                mma_bf16_w(ds, desc_add(kl0, bb), desc_add(qh0, sb), idesc_sd, acc);
-                mma_bf16_w(dp, desc_add(vl0, bb), desc_add(oh0, sb), idesc_sd, acc);
-                mma_bf16_w(ds, desc_add(kh0, bb), desc_add(ql0, sb), idesc_sd, 1u);
-                mma_bf16_w(dp, desc_add(vh0, bb), desc_add(ol0, sb), idesc_sd, 1u);
-                mma_bf16_w(ds, desc_add(kh0, bb), desc_add(qh0, sb), idesc_sd, 1u);
-                mma_bf16_w(dp, desc_add(vh0, bb), desc_add(oh0, sb), idesc_sd, 1u);
+                mma_bf16_w(dst, desc_add(xl0, bb), desc_add(rh0, sb), idesc_sd, acc);
+                mma_bf16_w(dst, desc_add(xh0, bb), desc_add(rl0, sb), idesc_sd, 1u);
+                mma_bf16_w(dst, desc_add(xh0, bb), desc_add(rh0, sb), idesc_sd, 1u);
             }
-            mma_commit_w(&sd_full[n % NBUF]);
+            mma_commit_w(&sd_full[b]);
             if (n >= DKV_LOOKAHEAD && !issue_acc(n - DKV_LOOKAHEAD))
                 ok = false;
         }
@@ -1044,7 +1050,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             *abort_flag = 1;
         mma_commit_w(done);
         mbar_wait(done, 0, 69);
-    } else {
+    } else if (warp >= 2 && warp < 2 + 8) {
         // ------------------------------------------------ P^T, dS^T, epilogue
         const int grp = (warp - 2) >> 2;  // query blocks n with n % 2 == grp
         const int quad = warp & 3;
@@ -1202,7 +1208,7 @@ int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloa
         int smem = fatc::BwdCfg<HD, fatc::DKV_R1, fatc::DKV_R2>::BYTES;
         cudaFuncSetAttribute(fatc::attn_bwd_dkv_tc<HD>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        fatc::attn_bwd_dkv_tc<HD><<<grid, fatc::NUM_THREADS, smem, st>>>(
+        fatc::attn_bwd_dkv_tc<HD><<<grid, fatc::DKV_THREADS, smem, st>>>(
             k128, v128, q32, d32, ld, T32, cs, sn, dk, dv, accumulate, T, static_cast<int>(H));
         int r = check_launch("attn_bwd_dkv_tc");
         if (r)

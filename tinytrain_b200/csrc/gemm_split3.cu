@@ -199,8 +199,8 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::NUM_THREADS, 1)
         }
         for (int b = 0; b < NBUF; ++b) {
             mbar_init(&cfull[b], 1);
-            // rank 0's barrier collects both CTAs' epilogue threads
-            mbar_init(&cempty[b], (PAIR ? 2 : 1) * 32 * CF::EPI_WARPS);
+            // one arrive per epilogue warp; rank 0's barrier collects both CTAs'
+            mbar_init(&cempty[b], (PAIR ? 2 : 1) * CF::EPI_WARPS);
         }
         *abort_flag = 0;
         fence_barrier_init();
@@ -399,11 +399,16 @@ __global__ void __launch_bounds__(Cfg<BN, PAIR>::NUM_THREADS, 1)
                     for (int j = 0; j < 32; ++j)
                         acc[c * 32 + j] += v[j];
                 }
+                // Each thread's TMEM reads are complete (tcgen05.wait::ld) and
+                // fenced; after the warp sync one lane releases the buffer.
                 tc_fence_before();
-                if constexpr (PAIR)
-                    mbar_arrive_cluster(smem_in_cta(&cempty[buf], 0));
-                else
-                    mbar_arrive(&cempty[buf]);
+                __syncwarp();
+                if (lane == 0) {
+                    if constexpr (PAIR)
+                        mbar_arrive_cluster(smem_in_cta(&cempty[buf], 0));
+                    else
+                        mbar_arrive(&cempty[buf]);
+                }
             }
             if (!ok)
                 break;

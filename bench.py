@@ -5,7 +5,7 @@
     python bench.py --impl reference ...      # the reference's CPU build
 
 One step = one AdamW optimizer step over the global batch: n_micro
-micro-batches of 8 x 2048 tokens per rank (gradient accumulation), forward,
+micro-batches of 16 x 2048 tokens per rank (gradient accumulation), forward,
 fused cross-entropy, backward, bucketed NCCL gradient all-reduce overlapped
 with the last backward (N > 1), global-norm clipping folded into the fused
 AdamW kernel. Weights are fp32 ~ N(0, 0.02), tokens uniform in [0, 32000)
@@ -52,7 +52,7 @@ def gemm_traffic(model):
 
 WORKLOADS = {
     "llama-1b": dict(model="llama-1b", vocab=32000, dim=2048, layers=16, heads=16, ffn=5632,
-                     max_seq=2048, global_batch=256, seq=2048, micro=8),
+                     max_seq=2048, global_batch=256, seq=2048, micro=16),
     "llama-110m": dict(model="llama-110m", vocab=32000, dim=768, layers=12, heads=12, ffn=2048,
                        max_seq=1024, global_batch=64, seq=1024, micro=16),
     "llama-13m": dict(model="llama-13m", vocab=32000, dim=256, layers=6, heads=8, ffn=768,
@@ -208,10 +208,15 @@ def main():
     ap.add_argument("--global-batch", type=int, default=None,
                     help="override the config's global batch (sequences), e.g. one "
                          "micro-batch per step for an ncu launch list")
+    ap.add_argument("--micro", type=int, default=None,
+                    help="sequences per micro-batch (gradient accumulation unit); "
+                         "the global batch and so the optimizer step are unchanged")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.config])
     if args.global_batch:
         w["global_batch"] = args.global_batch
+    if args.micro:
+        w["micro"] = args.micro
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -43,6 +43,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -59,7 +60,9 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int ROW_BYTES = 64;  // one k-slice row of an operand tile (SW64)
-constexpr int GROUP_M = 16;  // tile raster: bands of 16 M-tiles sweep N
+// Tile raster: bands of group_m M-tiles sweep the N tiles (Params.group_m,
+// chosen per problem on the host so that a band's A rows stay in L2 while
+// the band's N tiles read them).
 // K extent accumulated inside TMEM before the partial sum is promoted to the
 // epilogue's fp32 registers. The tensor-core accumulator rounds with a bias
 // (its error grows linearly with K), so long sums are built from 256-wide
@@ -119,16 +122,17 @@ struct Params {
     int64_t ldc, strideC;
     int num_m, num_n, num_k;
     int64_t num_tiles;
+    int group_m;
 };
 
 __device__ __forceinline__ void tile_coords(const Params& p, int64_t t, int& b, int& m, int& n) {
     int64_t per_batch = static_cast<int64_t>(p.num_m) * p.num_n;
     b = static_cast<int>(t / per_batch);
     int64_t r = t % per_batch;
-    int64_t band = static_cast<int64_t>(GROUP_M) * p.num_n;
+    int64_t band = static_cast<int64_t>(p.group_m) * p.num_n;
     int64_t g = r / band;
-    int first_m = static_cast<int>(g * GROUP_M);
-    int gsize = min(p.num_m - first_m, GROUP_M);
+    int first_m = static_cast<int>(g * p.group_m);
+    int gsize = min(p.num_m - first_m, p.group_m);
     int64_t rr = r % band;
     m = first_m + static_cast<int>(rr % gsize);
     n = static_cast<int>(rr / gsize);
@@ -812,6 +816,34 @@ struct SplitKFinish {
     int64_t ldc;
 };
 
+// Band height of the tile raster (bands of group_m M tiles, each band sweeping
+// the N tiles with M fastest). Operand bytes per batch entry (hi and lo
+// planes): A = M x K, B = N x K.
+//   B within 48 MB: group 1, rows of N tiles; B stays in L2 and each A block
+//     is read once.
+//   else A <= B: one band over all M tiles (up to 16); the B column tile is
+//     read once and the smaller A is what gets re-read.
+//   else: bands whose A rows total about 48 MB.
+// TTK_GEMM_GROUP_M overrides the choice.
+int raster_group(int tile_m, int num_m, int64_t M, int64_t N, int64_t K, int elt) {
+    static int env = -1;
+    if (env < 0) {
+        const char* e = std::getenv("TTK_GEMM_GROUP_M");
+        env = e ? std::max(0, std::atoi(e)) : 0;
+    }
+    if (env > 0)
+        return env;
+    const double budget = 48.0 * (1 << 20);
+    const double a_total = static_cast<double>(M) * K * 2 * elt;
+    const double b_total = static_cast<double>(N) * K * 2 * elt;
+    if (b_total <= budget)
+        return 1;
+    if (a_total <= b_total)
+        return std::max(1, std::min(16, num_m));
+    const double band_row_bytes = static_cast<double>(tile_m) * K * 2 * elt;
+    return std::max(1, std::min(16, static_cast<int>(budget / band_row_bytes)));
+}
+
 template <int BN, int PREC, bool PAIR>
 int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
                 gemm::Params p, cudaStream_t stream, const SplitKFinish* fin = nullptr) {
@@ -852,6 +884,8 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
     }
     p.num_n = static_cast<int>((p.N + BN - 1) / BN);
     p.num_tiles = static_cast<int64_t>(p.num_m) * p.num_n * p.batch;
+    p.group_m = raster_group(PAIR ? 2 * gemm::BM : gemm::BM, p.num_m, p.M, p.N, p.K,
+                             PREC == gemm::PREC_TF32X3 ? 4 : 2);
     Profiler& pr = prof();
     ProfRec rec{};
     if (pr.on) {

@@ -70,6 +70,44 @@ def test_bucket_plan_host_logic():
     assert end >= sum(sizes)
 
 
+def test_gemm_dispatch_host_logic():
+    """Host-side GEMM planning, which needs no device (148 SMs assumed when
+    none is visible): exact fp32 for problems of at most 2^24 multiply-adds,
+    split-K slice counts for the weight gradients of the 1B layer at 16 x 2048
+    tokens (K = 32768), none for GEMMs that fill the machine, and a workspace
+    that grows by the partial products when split."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("the device's own SM count would apply")
+    from tinytrain_b200 import _ttk
+    assert _ttk.call("ttk_gemm_get_fp32_max_macs") == 1 << 24
+    assert _ttk.call("ttk_gemm_uses_fp32", 1, 4, 5, 3) == 1
+    assert _ttk.call("ttk_gemm_uses_fp32", 1, 32768, 2048, 2048) == 0
+    assert _ttk.call("ttk_gemm_get_split_k") == 1
+    assert _ttk.call("ttk_gemm_get_cta_pairs") == 1
+    # dW = dY^T X: (transA, transB) = (1, 0)
+    assert _ttk.call("ttk_gemm_split_k_slices", 1, 0, 1, 2048, 2048, 32768) == 8
+    assert _ttk.call("ttk_gemm_split_k_slices", 1, 0, 1, 5632, 2048, 32768) == 2
+    assert _ttk.call("ttk_gemm_split_k_slices", 1, 0, 1, 2048, 5632, 32768) == 2
+    assert _ttk.call("ttk_gemm_split_k_slices", 1, 0, 1, 32000, 2048, 32768) == 1
+    # forward / dX: plenty of tiles
+    assert _ttk.call("ttk_gemm_split_k_slices", 0, 1, 1, 32768, 2048, 2048) == 1
+    assert _ttk.call("ttk_gemm_split_k_slices", 0, 0, 1, 32768, 2048, 5632) == 1
+    # batched problems are not split
+    assert _ttk.call("ttk_gemm_split_k_slices", 1, 0, 4, 2048, 2048, 32768) == 1
+    base = 2 * 2 * (2048 * 32768 + 32768 * 2048)  # bf16 hi/lo planes of A and B
+    ws = _ttk.call("ttk_gemm_workspace_size", 1, 0, 1, 2048, 2048, 32768)
+    assert ws >= base + 8 * 2048 * 2048 * 4
+    try:
+        _ttk.call("ttk_gemm_set_split_k", 0)
+        assert _ttk.call("ttk_gemm_split_k_slices", 1, 0, 1, 2048, 2048, 32768) == 1
+        assert _ttk.call("ttk_gemm_workspace_size", 1, 0, 1, 2048, 2048, 32768) < ws
+    finally:
+        _ttk.call("ttk_gemm_set_split_k", 1)
+    with pytest.raises(_ttk.TtkError):
+        _ttk.call("ttk_gemm_set_cta_pairs", 3)
+
+
 def _gxx():
     return shutil.which("g++") and "/usr/bin/g++"
 

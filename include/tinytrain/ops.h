@@ -91,6 +91,10 @@ Tensor embedding(const Tensor& weight, const DeviceIds& idx);
 Tensor cross_entropy(const Tensor& logits, const DeviceIds& targets);
 // silu(a) * b fused (model.cpp:149-151).
 Tensor swiglu(const Tensor& a, const Tensor& b);
+// The SwiGLU feed-forward block linear(swiglu(linear(x, w_gate),
+// linear(x, w_up)), w_down) as one op (model.cpp:148-152), same results.
+Tensor ffn_swiglu(const Tensor& x, const Tensor& w_gate, const Tensor& w_up,
+                  const Tensor& w_down);
 // Global L2 norm of the gradients of `params`; when max_norm > 0 the
 // gradients are scaled by max_norm / (norm + 1e-6) if that is < 1
 // (the conventional rule; the reference has no clipping). Returns the norm.

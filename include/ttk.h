@@ -202,6 +202,17 @@ int ttk_swiglu_fwd(const float* a, const float* b, float* y, int64_t n, void* st
 /* da (+)= dy*b*s*(1+a*(1-s)), db (+)= dy*silu(a) (ops.cpp:325-328, :256). */
 int ttk_swiglu_bwd(const float* a, const float* b, const float* dy, float* da, float* db,
                    int accumulate, int64_t n, void* stream);
+/* SwiGLU forward / backward producing their results only as bf16x3 GEMM
+ * operand planes in the layout of ttk_gemm_split ([2][R][round_up(F, 32)]
+ * bf16, hi then lo, padding zero), for a projection GEMM that consumes them
+ * through ttk_gemm_splits: y = silu(a) * b, and da, db for dy, equal bit for
+ * bit to ttk_swiglu_fwd / ttk_swiglu_bwd followed by ttk_gemm_split, without
+ * the fp32 tensors. a, b, dy are [R, F] row-major with F % 4 == 0; requires
+ * the bf16x3 precision. */
+int ttk_swiglu_fwd_split(const float* a, const float* b, void* y_split, int64_t R, int64_t F,
+                         void* stream);
+int ttk_swiglu_bwd_split(const float* a, const float* b, const float* dy, void* da_split,
+                         void* db_split, int64_t R, int64_t F, void* stream);
 
 /* Fused log_softmax + nll_loss (ops.cpp:840-930) over logits [N,C]:
  * loss_sum[0] (+)= sum_i (lse_i - x[i,t_i]) accumulated in fp64 into

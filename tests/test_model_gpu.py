@@ -139,3 +139,26 @@ def test_train_cfg0_30_steps(cuda, gemm_prec):
     diff = np.abs(np.array(losses) - np.array(rec["losses"]))
     assert diff.max() <= 1e-3, (diff.max(), losses[:3], rec["losses"][:3])
     tr.close()
+
+
+def test_fused_ffn_equals_composed_ops(cuda, monkeypatch):
+    """The fused SwiGLU feed-forward op (activation and its gradients only as
+    bf16x3 operand planes) gives the composed linear / swiglu / linear chain's
+    loss and every gradient bit for bit (projections large enough for the
+    tensor-core GEMM: 2048 rows, d 256, F 768)."""
+    from tinytrain_b200.trainer import Trainer
+    cfg = dict(vocab=32000, dim=256, layers=2, heads=8, ffn=768, max_seq=128)
+    rng = np.random.default_rng(3)
+    B, T = 16, 128
+    idx = rng.integers(0, 32000, B * T, dtype=np.int64)
+    tgt = rng.integers(0, 32000, B * T, dtype=np.int64)
+    out = {}
+    for fused in ("1", "0"):
+        monkeypatch.setenv("TT_FUSED_FFN", fused)
+        tr = Trainer(cfg, seed=7, host_init=False)
+        tr.init_normal(0.02, seed=7)
+        loss, _ = tr.forward_backward(idx, tgt, B, T)
+        out[fused] = (loss, tr.get_grads())
+        tr.close()
+    assert out["1"][0] == out["0"][0]
+    assert np.array_equal(out["1"][1], out["0"][1])

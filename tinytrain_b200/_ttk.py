@@ -76,6 +76,8 @@ SIGS = {
     "ttk_rmsnorm_bwd": (I32, [P, P, P, P, P, I32, P, I64, I64, P, SZ, P]),
     "ttk_swiglu_fwd": (I32, [P, P, P, I64, P]),
     "ttk_swiglu_bwd": (I32, [P, P, P, P, P, I32, I64, P]),
+    "ttk_swiglu_fwd_split": (I32, [P, P, P, I64, I64, P]),
+    "ttk_swiglu_bwd_split": (I32, [P, P, P, P, P, I64, I64, P]),
     "ttk_cross_entropy": (I32, [P, P, I64, I64, P, P, F32, P]),
     "ttk_loss_finalize": (I32, [P, F32, P, P]),
     "ttk_attention_fwd_workspace_size": (SZ, [I64, I64, I64, I64]),

@@ -512,8 +512,7 @@ __device__ __forceinline__ void split_one(float x, float& hi, float& lo) {
 }
 
 __device__ __forceinline__ void split_one(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
-    hi = __float2bfloat16_rn(x);
-    lo = __float2bfloat16_rn(x - __bfloat162float(hi));
+    split_bf16(x, hi, lo);
 }
 
 // Launch shape: TPR threads per row (a power of two covering the row's

@@ -5,6 +5,7 @@
 // read and one write of each tensor where the algorithm allows (the fused
 // cross-entropy keeps its 32000-wide row in registers between the reduction
 // and the gradient write).
+#include <algorithm>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -309,6 +310,44 @@ __device__ __forceinline__ void swiglu_grad(float a, float b, float g, float& da
     db = g * (a / (1.0f + expf(-a)));
 }
 
+// SwiGLU forward / backward writing their results only as bf16x3 GEMM
+// operand planes: [2][R][ldp] bf16 (hi plane, then lo), ldp = F rounded up to
+// 32, columns [F, ldp) zero; the layout of ttk_gemm_split. The fp32 values
+// are computed exactly as swiglu_fwd_kernel / swiglu_bwd_kernel compute them,
+// and split with split_bf16 as the split kernel does, so the planes equal
+// those of the unfused pair bit for bit. Launch shape: TPR threads per row,
+// 256 / TPR rows per block sweep (F % 4 == 0).
+__device__ __forceinline__ void store_split4(__nv_bfloat16* hi, int64_t plane, const float (&v)[4]) {
+    __nv_bfloat16 h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        split_bf16(v[j], h[j], l[j]);
+    *reinterpret_cast<uint2*>(hi) = *reinterpret_cast<const uint2*>(h);
+    *reinterpret_cast<uint2*>(hi + plane) = *reinterpret_cast<const uint2*>(l);
+}
+
+__global__ void swiglu_fwd_split_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                        __nv_bfloat16* __restrict__ ys, int64_t R, int64_t F,
+                                        int64_t ldp, int tpr) {
+    const int rpb = blockDim.x / tpr;
+    const int lr = threadIdx.x / tpr, lg = threadIdx.x % tpr;
+    const int64_t plane = R * ldp;
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * rpb + lr; r < R;
+         r += static_cast<int64_t>(gridDim.x) * rpb) {
+        for (int64_t g = lg; g < ldp / 4; g += tpr) {
+            const int64_t c = g * 4;
+            float y[4] = {0.f, 0.f, 0.f, 0.f};
+            if (c < F) {
+                const float4 av = *reinterpret_cast<const float4*>(a + r * F + c);
+                const float4 bv = *reinterpret_cast<const float4*>(b + r * F + c);
+                y[0] = silu_f(av.x) * bv.x, y[1] = silu_f(av.y) * bv.y;
+                y[2] = silu_f(av.z) * bv.z, y[3] = silu_f(av.w) * bv.w;
+            }
+            store_split4(ys + r * ldp + c, plane, y);
+        }
+    }
+}
+
 __global__ void swiglu_bwd_kernel(const float* __restrict__ a, const float* __restrict__ b,
                                   const float* __restrict__ dy, float* __restrict__ da,
                                   float* __restrict__ db, int accumulate, int64_t n) {
@@ -339,6 +378,34 @@ __global__ void swiglu_bwd_kernel(const float* __restrict__ a, const float* __re
         swiglu_grad(a[i], b[i], dy[i], oa, ob);
         da[i] = accumulate ? da[i] + oa : oa;
         db[i] = accumulate ? db[i] + ob : ob;
+    }
+}
+
+__global__ void swiglu_bwd_split_kernel(const float* __restrict__ a, const float* __restrict__ b,
+                                        const float* __restrict__ dy,
+                                        __nv_bfloat16* __restrict__ das,
+                                        __nv_bfloat16* __restrict__ dbs, int64_t R, int64_t F,
+                                        int64_t ldp, int tpr) {
+    const int rpb = blockDim.x / tpr;
+    const int lr = threadIdx.x / tpr, lg = threadIdx.x % tpr;
+    const int64_t plane = R * ldp;
+    for (int64_t r = static_cast<int64_t>(blockIdx.x) * rpb + lr; r < R;
+         r += static_cast<int64_t>(gridDim.x) * rpb) {
+        for (int64_t g = lg; g < ldp / 4; g += tpr) {
+            const int64_t c = g * 4;
+            float da[4] = {0.f, 0.f, 0.f, 0.f}, db[4] = {0.f, 0.f, 0.f, 0.f};
+            if (c < F) {
+                const float4 av = *reinterpret_cast<const float4*>(a + r * F + c);
+                const float4 bv = *reinterpret_cast<const float4*>(b + r * F + c);
+                const float4 gv = *reinterpret_cast<const float4*>(dy + r * F + c);
+                swiglu_grad(av.x, bv.x, gv.x, da[0], db[0]);
+                swiglu_grad(av.y, bv.y, gv.y, da[1], db[1]);
+                swiglu_grad(av.z, bv.z, gv.z, da[2], db[2]);
+                swiglu_grad(av.w, bv.w, gv.w, da[3], db[3]);
+            }
+            store_split4(das + r * ldp + c, plane, da);
+            store_split4(dbs + r * ldp + c, plane, db);
+        }
     }
 }
 
@@ -850,6 +917,53 @@ int ttk_swiglu_bwd(const float* a, const float* b, const float* dy, float* da, f
     swiglu_bwd_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, S(stream)>>>(a, b, dy, da, db,
                                                                        accumulate, n);
     return check_launch("swiglu_bwd_kernel");
+}
+
+static int split_rows_tpr(int64_t ldp) {
+    int tpr = 1;
+    while (tpr < 256 && tpr < ldp / 4)
+        tpr <<= 1;
+    return tpr;
+}
+
+int ttk_swiglu_fwd_split(const float* a, const float* b, void* y_split, int64_t R, int64_t F,
+                         void* stream) {
+    if (R < 0 || F <= 0 || (F & 3) || (R && (!a || !b || !y_split)))
+        return set_error(TTK_ERR_ARG, "swiglu_fwd_split: bad arguments (F % 4 == 0)");
+    if (ttk_gemm_get_precision() != 0)
+        return set_error(TTK_ERR_ARG, "swiglu_fwd_split: the planes are bf16x3 operands");
+    if (!R)
+        return TTK_OK;
+    if (!(aligned16(a) && aligned16(b) && aligned16(y_split)))
+        return set_error(TTK_ERR_ARG, "swiglu_fwd_split: tensors must be 16-byte aligned");
+    const int64_t ldp = (F + 31) / 32 * 32;
+    const int tpr = split_rows_tpr(ldp);
+    const int64_t rpb = 256 / tpr;
+    const int blocks = static_cast<int>(std::min<int64_t>((R + rpb - 1) / rpb, 148 * 16));
+    swiglu_fwd_split_kernel<<<blocks, 256, 0, S(stream)>>>(
+        a, b, static_cast<__nv_bfloat16*>(y_split), R, F, ldp, tpr);
+    return check_launch("swiglu_fwd_split_kernel");
+}
+
+int ttk_swiglu_bwd_split(const float* a, const float* b, const float* dy, void* da_split,
+                         void* db_split, int64_t R, int64_t F, void* stream) {
+    if (R < 0 || F <= 0 || (F & 3) || (R && (!a || !b || !dy || !da_split || !db_split)))
+        return set_error(TTK_ERR_ARG, "swiglu_bwd_split: bad arguments (F % 4 == 0)");
+    if (ttk_gemm_get_precision() != 0)
+        return set_error(TTK_ERR_ARG, "swiglu_bwd_split: the planes are bf16x3 operands");
+    if (!R)
+        return TTK_OK;
+    if (!(aligned16(a) && aligned16(b) && aligned16(dy) && aligned16(da_split) &&
+          aligned16(db_split)))
+        return set_error(TTK_ERR_ARG, "swiglu_bwd_split: tensors must be 16-byte aligned");
+    const int64_t ldp = (F + 31) / 32 * 32;
+    const int tpr = split_rows_tpr(ldp);
+    const int64_t rpb = 256 / tpr;
+    const int blocks = static_cast<int>(std::min<int64_t>((R + rpb - 1) / rpb, 148 * 16));
+    swiglu_bwd_split_kernel<<<blocks, 256, 0, S(stream)>>>(
+        a, b, dy, static_cast<__nv_bfloat16*>(da_split), static_cast<__nv_bfloat16*>(db_split), R,
+        F, ldp, tpr);
+    return check_launch("swiglu_bwd_split_kernel");
 }
 
 int ttk_cross_entropy(const float* logits, const int64_t* targets, int64_t N, int64_t C,

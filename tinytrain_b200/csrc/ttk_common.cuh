@@ -8,6 +8,7 @@
 // word and the caller unwinds instead of hanging the GPU.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -174,6 +175,13 @@ __device__ __forceinline__ void bulk_wait_all() {
 // Generic-proxy shared-memory writes -> visible to the async proxy (TMA).
 __device__ __forceinline__ void fence_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// bf16x3 operand split of one value: hi = bf16_rn(x), lo = bf16_rn(x - hi).
+// Every producer of split planes uses this, so their planes are identical.
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+    hi = __float2bfloat16_rn(x);
+    lo = __float2bfloat16_rn(x - __bfloat162float(hi));
 }
 
 // ------------------------------------------------- CTA pairs (cta_group::2) --

@@ -175,8 +175,7 @@ Tensor GPTModel::forward(const DeviceIds& idx, int64_t B, int64_t T) {
         x = add(x, att_out);
 
         Tensor hff = rmsnorm(x, b.rms_ffn.weight, b.rms_ffn.eps);
-        Tensor act = swiglu(linear(hff, b.wgate.weight), linear(hff, b.wup.weight));
-        Tensor ffn = linear(act, b.wdown.weight);
+        Tensor ffn = ffn_swiglu(hff, b.wgate.weight, b.wup.weight, b.wdown.weight);
         if (drop)
             ffn = dropout(ffn, cfg_.dropout, ++dropout_seed_);
         x = add(x, ffn);

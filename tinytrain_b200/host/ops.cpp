@@ -9,6 +9,7 @@
 // memset and a read per first contribution.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <stdexcept>
@@ -609,6 +610,111 @@ Tensor linear(const Tensor& x, const Tensor& weight) {
                 float* d = grad_target(wo, ow);
                 gemm(1, 0, 1, Out, In, R, ga, data_arg(xo.get(), In, 0), ow ? 0.0f : 1.0f, d, In,
                      0);
+            }
+        };
+    }
+    return out;
+}
+
+// out = linear(swiglu(linear(x, w_gate), linear(x, w_up)), w_down) with the
+// activation y = silu(x W_g^T) * (x W_u^T) and its gradients dA, dB held only
+// as bf16x3 operand planes (ttk_swiglu_*_split): the projection GEMMs take
+// them through ttk_gemm_splits, and the fp32 y, dA and dB of the composed ops
+// never exist. The planes equal the split of those fp32 tensors, so every
+// result equals the composition's bit for bit. The composition runs instead
+// when the operands are not in the bf16x3 precision, when a projection is
+// small enough for the exact fp32 GEMM, or when TT_FUSED_FFN=0.
+Tensor ffn_swiglu(const Tensor& x, const Tensor& w_gate, const Tensor& w_up,
+                  const Tensor& w_down) {
+    if (x.ndim() != 2 || w_gate.ndim() != 2 || w_up.ndim() != 2 || w_down.ndim() != 2)
+        throw std::invalid_argument("ffn_swiglu: x and weights must be 2D");
+    const int64_t R = x.dim(0), d = x.dim(1), F = w_gate.dim(0);
+    if (w_gate.dim(1) != d || w_up.dim(0) != F || w_up.dim(1) != d || w_down.dim(0) != d ||
+        w_down.dim(1) != F)
+        throw std::invalid_argument("ffn_swiglu: weight shapes do not match");
+    const char* env = std::getenv("TT_FUSED_FFN");
+    const bool fused = !(env && env[0] == '0') && ttk_gemm_get_precision() == 0 && F % 4 == 0 &&
+                       !ttk_gemm_uses_fp32(1, R, F, d) && !ttk_gemm_uses_fp32(1, R, d, F) &&
+                       !ttk_gemm_uses_fp32(1, F, d, R) && !ttk_gemm_uses_fp32(1, d, F, R);
+    if (!fused)
+        return linear(swiglu(linear(x, w_gate), linear(x, w_up)), w_down);
+    const bool rg = x.requires_grad() || w_gate.requires_grad() || w_up.requires_grad() ||
+                    w_down.requires_grad();
+    // a, b: the projections, kept in fp32 for the backward (not graph nodes)
+    Tensor a = make_out({R, F}, false), b = make_out({R, F}, false);
+    gemm(0, 1, 1, R, F, d, data_arg(x.impl().get(), d, 0), data_arg(w_gate.impl().get(), d, 0),
+         0.0f, out_ptr(a), F, 0);
+    gemm(0, 1, 1, R, F, d, data_arg(x.impl().get(), d, 0), data_arg(w_up.impl().get(), d, 0),
+         0.0f, out_ptr(b), F, 0);
+    const size_t split_bytes = ttk_gemm_split_bytes(1, R, F);
+    auto ys = std::make_shared<Scratch>(split_bytes);
+    check(ttk_swiglu_fwd_split(dread(a.impl()), dread(b.impl()), ys->ptr, R, F, stream()),
+          "ffn swiglu");
+    Tensor out = make_out({R, d}, rg);
+    {
+        const GemmArg wd = data_arg(w_down.impl().get(), F, 0);
+        const void* wds = operand_split(wd.buf, wd.ptr, 1, d, F, F, 0);
+        check(ttk_gemm_splits(0, 1, 1, R, d, F, 1.0f, ys->ptr, wds, 0.0f, out_ptr(out), d, 0,
+                              stream()),
+              "ffn down");
+    }
+    if (rg) {
+        auto xo = x.impl(), go = w_gate.impl(), uo = w_up.impl(), wo = w_down.impl();
+        auto ao = a.impl(), bo = b.impl();
+        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
+        oo->prev = {xo, go, uo, wo};
+        oo->backward_fn = [xo, go, uo, wo, ao, bo, oo, ys, R, d, F, split_bytes]() {
+            const float* g = grad_in(oo);
+            if (!g)
+                return;
+            const GemmArg ga{oo->grad.get(), g, d, 0};
+            // dY = dOut W_d  [R, F]
+            Scratch dy(static_cast<size_t>(R * F) * 4);
+            gemm(0, 0, 1, R, F, d, ga, data_arg(wo.get(), F, 0), 0.0f, dy.as<float>(), F, 0);
+            if (wo->requires_grad) {  // dW_d = dOut^T Y  [d, F]
+                bool ow = false;
+                float* gw = grad_target(wo, ow);
+                const void* gs = operand_split(ga.buf, ga.ptr, 1, R, d, d, 0);
+                check(ttk_gemm_splits(1, 0, 1, d, F, R, 1.0f, gs, ys->ptr, ow ? 0.0f : 1.0f, gw,
+                                      F, 0, stream()),
+                      "ffn dW down");
+            }
+            if (!(xo->requires_grad || go->requires_grad || uo->requires_grad))
+                return;
+            Scratch das(split_bytes), dbs(split_bytes);
+            check(ttk_swiglu_bwd_split(dread(ao), dread(bo), dy.as<float>(), das.ptr, dbs.ptr, R,
+                                       F, stream()),
+                  "ffn swiglu bwd");
+            if (xo->requires_grad) {  // dX = dA W_g + dB W_u  [R, d]
+                bool ow = false;
+                float* gx = grad_target(xo, ow);
+                const GemmArg wg = data_arg(go.get(), d, 0), wu = data_arg(uo.get(), d, 0);
+                const void* wgs = operand_split(wg.buf, wg.ptr, 1, F, d, d, 0);
+                check(ttk_gemm_splits(0, 0, 1, R, d, F, 1.0f, das.ptr, wgs, ow ? 0.0f : 1.0f, gx,
+                                      d, 0, stream()),
+                      "ffn dX");
+                const void* wus = operand_split(wu.buf, wu.ptr, 1, F, d, d, 0);
+                check(ttk_gemm_splits(0, 0, 1, R, d, F, 1.0f, dbs.ptr, wus, 1.0f, gx, d, 0,
+                                      stream()),
+                      "ffn dX");
+            }
+            if (go->requires_grad || uo->requires_grad) {  // dW_g = dA^T X, dW_u = dB^T X
+                const GemmArg xa = data_arg(xo.get(), d, 0);
+                const void* xs = operand_split(xa.buf, xa.ptr, 1, R, d, d, 0);
+                if (go->requires_grad) {
+                    bool ow = false;
+                    float* gw = grad_target(go, ow);
+                    check(ttk_gemm_splits(1, 0, 1, F, d, R, 1.0f, das.ptr, xs, ow ? 0.0f : 1.0f,
+                                          gw, d, 0, stream()),
+                          "ffn dW gate");
+                }
+                if (uo->requires_grad) {
+                    bool ow = false;
+                    float* gw = grad_target(uo, ow);
+                    check(ttk_gemm_splits(1, 0, 1, F, d, R, 1.0f, dbs.ptr, xs, ow ? 0.0f : 1.0f,
+                                          gw, d, 0, stream()),
+                          "ffn dW up");
+                }
             }
         };
     }

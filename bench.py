@@ -54,7 +54,7 @@ WORKLOADS = {
     "llama-1b": dict(model="llama-1b", vocab=32000, dim=2048, layers=16, heads=16, ffn=5632,
                      max_seq=2048, global_batch=256, seq=2048, micro=16),
     "llama-110m": dict(model="llama-110m", vocab=32000, dim=768, layers=12, heads=12, ffn=2048,
-                       max_seq=1024, global_batch=64, seq=1024, micro=16),
+                       max_seq=1024, global_batch=64, seq=1024, micro=64),
     "llama-13m": dict(model="llama-13m", vocab=32000, dim=256, layers=6, heads=8, ffn=768,
                       max_seq=256, global_batch=16, seq=128, micro=16),
 }

@@ -307,9 +307,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 float v[32];
                 tmem_ld_32x32b_x32(base + c, v);
                 tmem_ld_wait();
+                // acc = acc * scale + v, two lanes per packed FMA (same rounding)
 #pragma unroll
-                for (int e = 0; e < 32; ++e)
-                    acc[c + e] = fmaf(acc[c + e], scale, v[e]);
+                for (int e = 0; e < 32; e += 2) {
+                    const float2 r = __ffma2_rn(make_float2(acc[c + e], acc[c + e + 1]),
+                                                make_float2(scale, scale),
+                                                make_float2(v[e], v[e + 1]));
+                    acc[c + e] = r.x, acc[c + e + 1] = r.y;
+                }
             }
             tc_fence_before();
             mbar_arrive(&o_free[i & 1]);
@@ -341,16 +346,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         so[e] = -INFINITY;
                 }
             }
-            // Both halves fold the same 64 values in the same order, so they
-            // hold bit-identical maxima.
-            float mx0 = half == 0 ? s[0] : so[0];
-            float mx1 = half == 0 ? so[0] : s[0];
-#pragma unroll
-            for (int e = 1; e < 32; ++e) {
-                mx0 = fmaxf(mx0, half == 0 ? s[e] : so[e]);
-                mx1 = fmaxf(mx1, half == 0 ? so[e] : s[e]);
-            }
-            const float mx = fmaxf(mx0, mx1);
+            // Both halves take the maximum of the same 64 values (exact; the
+            // two 32-column maxima are combined in column order).
+            const float ms = max32(s), mso = max32(so);
+            const float mx = half == 0 ? fmaxf(ms, mso) : fmaxf(mso, ms);
             m_prev = m_cur;
             m_cur = fmaxf(m_cur, mx * LOG2E);
             const float mc = m_cur == -INFINITY ? 0.0f : m_cur;  // all masked so far
@@ -359,8 +358,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             uint32_t hi[16], lo[16];
 #pragma unroll
             for (int e = 0; e < 32; e += 2) {
-                const float p0 = exp2_approx(fmaf(s[e], LOG2E, -mc));
-                const float p1 = exp2_approx(fmaf(s[e + 1], LOG2E, -mc));
+                const float2 t = __ffma2_rn(make_float2(s[e], s[e + 1]), make_float2(LOG2E, LOG2E),
+                                            make_float2(-mc, -mc));
+                const float p0 = exp2_approx(t.x);
+                const float p1 = exp2_approx(t.y);
                 rs += p0 + p1;
                 split_pair_bf16(p0, p1, hi[e / 2], lo[e / 2]);
             }
@@ -816,11 +817,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_ld_32x32b_x32(buf, sv);
             tmem_ld_32x32b_x32(buf + 64, dpv);
             tmem_ld_wait();
+            // p = exp2(s log2e - lse), dS = p (dP - D); two lanes per packed
+            // instruction (the same roundings as the scalar forms)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const bool live = q < T && (!diag || k0 + e <= q);
-                const float p = live ? exp2_approx(fmaf(sv[e], LOG2E, -lse2)) : 0.0f;
-                sv[e] = p * (dpv[e] - Dq);
+            for (int e = 0; e < 32; e += 2) {
+                const float2 t = __ffma2_rn(make_float2(sv[e], sv[e + 1]),
+                                            make_float2(LOG2E, LOG2E), make_float2(-lse2, -lse2));
+                const bool l0 = q < T && (!diag || k0 + e <= q);
+                const bool l1 = q < T && (!diag || k0 + e + 1 <= q);
+                const float2 pp = make_float2(l0 ? exp2_approx(t.x) : 0.0f,
+                                              l1 ? exp2_approx(t.y) : 0.0f);
+                const float2 d = __fadd2_rn(make_float2(dpv[e], dpv[e + 1]), make_float2(-Dq, -Dq));
+                const float2 r = __fmul2_rn(pp, d);
+                sv[e] = r.x, sv[e + 1] = r.y;
             }
             uint32_t hi[16], lo[16];
             split32(sv, hi, lo);
@@ -1081,13 +1090,22 @@ __global__ void __launch_bounds__(DKV_THREADS, 1)
             const int64_t qb = static_cast<int64_t>(i_first + n) * BWD_BLK;
             const bool diag = qb < k0 + BQ - 1 || qb + BWD_BLK > T;
             float pv[32];
+            // P^T = exp2(s log2e - lse), dS^T = P^T (dP^T - D); two lanes per
+            // packed instruction (the same roundings as the scalar forms)
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                const float2 lv = ldv[e];
-                const bool live = !diag || (key <= qb + e && qb + e < T);
-                const float p = live ? exp2_approx(fmaf(sv[e], LOG2E, -lv.x)) : 0.0f;
-                pv[e] = p;
-                sv[e] = p * (dpv[e] - lv.y);
+            for (int e = 0; e < 32; e += 2) {
+                const float2 l0 = ldv[e], l1 = ldv[e + 1];
+                const float2 t = __ffma2_rn(make_float2(sv[e], sv[e + 1]),
+                                            make_float2(LOG2E, LOG2E), make_float2(-l0.x, -l1.x));
+                const bool a0 = !diag || (key <= qb + e && qb + e < T);
+                const bool a1 = !diag || (key <= qb + e + 1 && qb + e + 1 < T);
+                const float2 pp = make_float2(a0 ? exp2_approx(t.x) : 0.0f,
+                                              a1 ? exp2_approx(t.y) : 0.0f);
+                const float2 d = __fadd2_rn(make_float2(dpv[e], dpv[e + 1]),
+                                            make_float2(-l0.y, -l1.y));
+                const float2 r = __fmul2_rn(pp, d);
+                pv[e] = pp.x, pv[e + 1] = pp.y;
+                sv[e] = r.x, sv[e + 1] = r.y;
             }
             uint32_t phi[16], plo[16], shi[16], slo[16];
             split32(pv, phi, plo);

@@ -511,6 +511,23 @@ __device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) {
 
 // 2^x with the hardware approximation (ex2.approx.ftz.f32, relative error
 // about 2^-22; subnormal results flush to zero).
+// max(a, b, c) in one instruction (sm_100 three-input max).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// Maximum of 32 values as a tree of three-input maxima (exact: the result is
+// one of the inputs, whatever the order).
+__device__ __forceinline__ float max32(const float (&v)[32]) {
+    float m = max3(v[0], v[1], v[2]);
+#pragma unroll
+    for (int e = 3; e < 31; e += 2)
+        m = max3(m, v[e], v[e + 1]);
+    return fmaxf(m, v[31]);
+}
+
 __device__ __forceinline__ float exp2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

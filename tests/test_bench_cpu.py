@@ -1,0 +1,34 @@
+"""The reference arm of bench.py (the reference's own CPU build, timed on the
+host) prints one JSON line with the keys the benchmark contract asks for; it
+needs no GPU. Skipped where the reference build (oracle/_ref) is absent."""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_reference_arm_line():
+    if not os.path.exists(os.path.join(ROOT, "oracle", "_ref", "libttref.so")):
+        pytest.skip("oracle/_ref not built (it needs the reference sources)")
+    env = dict(os.environ, OMP_NUM_THREADS="4")
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", "llama-13m",
+                        "--steps", "1", "--warmup", "3"], cwd=ROOT, capture_output=True,
+                       text=True, timeout=600, env=env)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    for k in ("impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+              "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+              "cpu_baseline", "e2e"):
+        assert k in line, k
+    assert line["impl"] == "reference" and line["metric"] == "train tokens/sec"
+    assert line["value"] > 0 and line["higher_is_better"] is True
+    assert line["e2e"]["value"] == line["value"]
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
+    cb = line["cpu_baseline"]
+    assert cb["kind"] == "reference" and cb["cores"] == 4 and cb["value"] == line["value"]
+    assert "after 1 untimed" in cb["sample"]
+    assert line["config"]["workload"].startswith("llama-13m")

@@ -31,6 +31,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -90,17 +91,19 @@ class ClockSampler:
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     _count = 0
+    _dir = None
 
     def __init__(self, gpus):
         self.gpus = gpus
         self.proc = None
         ClockSampler._count += 1
-        self.path = os.path.join(ROOT, "gpurun_out",
+        if ClockSampler._dir is None:
+            ClockSampler._dir = tempfile.mkdtemp(prefix="bench_clocks_")
+        self.path = os.path.join(ClockSampler._dir,
                                  f"clocks_{os.getpid()}_{ClockSampler._count}.csv")
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
@@ -287,6 +290,13 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def max_each_over_ranks(vs):
+        if world == 1:
+            return list(vs)
+        t = torch.tensor(vs, dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return [float(x) for x in t.tolist()]
+
     # ---- warm-up (device-resident ids)
     for i in range(args.warmup):
         tr.step_device(dev_idx[i % n_sets].data_ptr(), dev_tgt[i % n_sets].data_ptr(), B, T,
@@ -296,20 +306,24 @@ def main():
     # ---- timed region: value
     _ttk.call("ttk_profile_enable", 1)
     l0 = trn.kernel_launches()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # One event per step boundary on the launching stream: the first and last
+    # bracket the timed region, the ones between give each step's time.
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    e0, e1 = ev[0], ev[-1]
     with ClockSampler([local] if world == 1 else list(range(world))) as clk:
         barrier()
         e0.record(stream)
         for i in range(args.steps):
             tr.step_device(dev_idx[i % n_sets].data_ptr(), dev_tgt[i % n_sets].data_ptr(), B, T,
                            n_micro, 3e-4)
-        e1.record(stream)
+            ev[i + 1].record(stream)
         barrier()
     launches = trn.kernel_launches() - l0
     gms, gfl, gl = C.c_double(0), C.c_double(0), C.c_int64(0)
     _ttk.call("ttk_profile_enable", 0)
     _ttk.call("ttk_profile_read", C.byref(gms), C.byref(gfl), C.byref(gl))
     ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    step_ms = max_each_over_ranks([ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)])
     loss_dev = tr.last_loss()
     tokens_step = tokens_rank * world
     value = tokens_step / (ms / 1e3)
@@ -318,16 +332,18 @@ def main():
     ke = max(1, args.e2e_steps)
     tr.step(pin_idx[0].numpy(), pin_tgt[0].numpy(), B, T, n_micro, 3e-4)  # warm path
     barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    fe = [torch.cuda.Event(enable_timing=True) for _ in range(ke + 1)]
+    f0, f1 = fe[0], fe[-1]
     loss_e2e = None
     with ClockSampler([local] if world == 1 else list(range(world))) as clk_e2e:
         f0.record(stream)
         for i in range(ke):
             loss_e2e, _ = tr.step(pin_idx[i % n_sets].numpy(), pin_tgt[i % n_sets].numpy(), B,
                                   T, n_micro, 3e-4)
-        f1.record(stream)
+            fe[i + 1].record(stream)
         barrier()
     ms_e2e = max_over_ranks(f0.elapsed_time(f1)) / ke
+    step_ms_e2e = max_each_over_ranks([fe[i].elapsed_time(fe[i + 1]) for i in range(ke)])
     e2e = tokens_step / (ms_e2e / 1e3)
     status = _ttk.device_status()
 
@@ -342,6 +358,7 @@ def main():
             "metric": "train tokens/sec", "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "step_ms": [round(x, 2) for x in step_ms],
             "data": "synthetic (N(0,0.02) weights, uniform tokens)",
             "config": workload_config(w, world),
             "roofline": {
@@ -361,7 +378,8 @@ def main():
             "mfu_fp32_equiv": value * flops_per_token(w) / 1e12 / world,
             "gpu_launches": launches,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * tokens_rank * 8,
-                    "d2h_bytes_per_step": 4, "steps": ke, "clocks": clk_e2e.summary()},
+                    "d2h_bytes_per_step": 4, "steps": ke,
+                    "step_ms": [round(x, 2) for x in step_ms_e2e], "clocks": clk_e2e.summary()},
             "clocks": clk.summary(),
             "loss": loss_dev, "loss_e2e": loss_e2e, "device_status": status,
         }

@@ -136,7 +136,9 @@ int ttk_gemm(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_
  * address; make that first call before any stream capture. All calls share
  * the one array, so calls that overlap on the GPU (different streams, or
  * different host threads, without ordering between them) race on it; the
- * caller must serialize them. Inputs and outputs are as for ttk_gemm. */
+ * caller must serialize them. The looked-up address is cached for the life
+ * of the process: do not call it on a device after cudaDeviceReset there.
+ * Inputs and outputs are as for ttk_gemm. */
 size_t ttk_gemm_noalloc_max_workspace(void);
 int ttk_gemm_noalloc(int transA, int transB, int64_t batch, int64_t M, int64_t N, int64_t K,
                      float alpha, const float* A, int64_t lda, int64_t strideA, const float* B,

@@ -132,10 +132,10 @@ def test_cpp_api_compiles_and_links(tmp_path):
 def test_reference_model_and_train_compile_unchanged(tmp_path):
     """The reference's src/model.cpp and apps/train.cpp, unmodified, against
     this library's headers (compile only; running needs a device)."""
-    ref = "/root/reference"
-    if not os.path.isdir(os.path.join(ref, "src")):
-        pytest.skip("reference sources not present")
-    nl = "/opt/prime-rl/.venv/lib/python3.12/site-packages/include/cudnn_frontend/thirdparty"
+    from oracle import paths
+    ref, nl = paths.reference_dir(), paths.nlohmann_dir()
+    if not ref or not nl:
+        pytest.skip("reference sources or nlohmann/json not present")
     for f in ("src/model.cpp", "apps/train.cpp"):
         r = subprocess.run([_gxx(), "-std=c++20", "-fsyntax-only", "-I" + os.path.join(ROOT, "include"),
                             "-I" + nl, os.path.join(ref, f)], capture_output=True, text=True)

@@ -1,7 +1,7 @@
 """Build recipe for the in-tree shared libraries.
 
     python -m tinytrain_b200.build            # libttk.so + libtinytrain.so
-    python -m tinytrain_b200.build --oracle   # + oracle/_ref (needs the reference sources)
+    python -m tinytrain_b200.build --oracle --reference DIR   # + oracle/_ref (the checker)
 
 Outputs (git-ignored, shipped with the tree):
   tinytrain_b200/lib/libttk.so        CUDA kernels + runtime, C ABI (include/ttk.h)
@@ -118,26 +118,30 @@ def build_host(verbose=False, force=False):
     return out
 
 
-def build_oracle(verbose=False):
-    ref = os.environ.get("TT_REFERENCE", "/root/reference")
-    if not os.path.isdir(os.path.join(ref, "src")):
+def build_oracle(verbose=False, ref=None):
+    """Builds the checker (oracle/_ref) from the reference sources at `ref`
+    (or $TT_REFERENCE); does nothing when neither names the sources."""
+    ref = ref or os.environ.get("TT_REFERENCE")
+    if not ref or not os.path.isdir(os.path.join(ref, "src")):
         return None
     _run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={ref}"], verbose)
     return os.path.join(ROOT, "oracle", "_ref", "libttref.so")
 
 
-def build_all(verbose=False, force=False, oracle=True):
+def build_all(verbose=False, force=False, oracle=True, ref=None):
     build_ttk(verbose, force)
     build_host(verbose, force)
     if oracle:
-        build_oracle(verbose)
+        build_oracle(verbose, ref)
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--oracle", action="store_true")
+    ap.add_argument("--reference", default=None,
+                    help="reference source directory for --oracle (default $TT_REFERENCE)")
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
-    build_all(a.verbose, a.force, a.oracle)
+    build_all(a.verbose, a.force, a.oracle, a.reference)
     print("built:", LIBDIR)

@@ -6,7 +6,8 @@
 // allocations, on a code path that must never fail with out-of-memory after
 // start-up, or in a host program that only has its own fixed buffers. They
 // cannot call cudaMalloc (or torch, or any pool) to obtain the workspace that
-// ttk_gemm needs for its split TF32 operands. This entry point takes the
+// ttk_gemm needs for its split operands (bf16 hi/lo planes under the default
+// bf16x3 precision, fp32 planes under tf32x3). This entry point takes the
 // same arguments as ttk_gemm minus the workspace and uses a fixed scratch
 // array compiled into the library instead.
 //
@@ -15,7 +16,10 @@
 // exits. Operands whose split copies need more than that are rejected with
 // TTK_ERR_ARG. In host code the array's name is only a stand-in, not a device
 // address, so each device's address is looked up once with
-// cudaGetSymbolAddress while that device is current and cached.
+// cudaGetSymbolAddress while that device is current and cached. The cache
+// lives as long as the process: after cudaDeviceReset on a device the cached
+// address is stale, so this entry point must not be called on that device
+// again.
 #include <cuda_runtime.h>
 #include <stdint.h>
 

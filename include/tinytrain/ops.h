@@ -86,6 +86,13 @@ Tensor linear(const Tensor& x, const Tensor& weight);
 // 1/sqrt(hd); returns [B,T,H*hd]. Replaces model.cpp:127-141.
 Tensor causal_attention(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& cos,
                         const Tensor& sin);
+// The reference's own op chain for attention, bmm(q, transpose(k)) [N,T,T]
+// with q, k [N,T,hd] (hd 32, 64 or 128), mul by a full() constant, add of a
+// [T,T] causal mask (0 on/below the diagonal, <= -1e9 above), softmax(-1),
+// bmm(., v), also runs as the fused kernel: the intermediate results are
+// deferred and computed only if something else reads them. Number of chains
+// fused so far:
+int64_t fused_attention_chains();
 Tensor embedding(const Tensor& weight, const DeviceIds& idx);
 // cross_entropy with device-resident, range-checked targets.
 Tensor cross_entropy(const Tensor& logits, const DeviceIds& targets);

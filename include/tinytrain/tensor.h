@@ -21,6 +21,12 @@
 //    (the reference copies); their gradients are still separate.
 //  - a 2-D transpose (and the last-two-dims transpose of a 3-D tensor) is
 //    lazy: matmul/bmm read it as a transposed operand without a copy.
+//  - the attention-score chain of model.cpp:133-138, bmm(q, transpose(k)),
+//    mul by a constant, add of a causal mask, softmax, is deferred: each of
+//    those results keeps a recipe instead of a [B*H, T, T] buffer, and the
+//    closing bmm(probs, v) runs the fused causal attention kernel. A deferred
+//    result read any other way (data(), another op) is computed then, with
+//    the reference's own op sequence, so every value stays observable.
 
 #include <cstdint>
 #include <functional>
@@ -28,6 +34,8 @@
 #include <vector>
 
 namespace tt {
+
+struct Deferred;  // recipe of a deferred result (see Tensor::Impl::deferred)
 
 // Device buffer of fp32 values with a host mirror. Shared between views.
 struct Buffer {
@@ -53,6 +61,10 @@ struct Buffer {
     size_t split_bytes = 0;
     uint64_t split_version = ~0ull;
     int64_t split_key[7] = {};
+    // Whether the contents form a causal attention mask (0 on and below the
+    // diagonal, <= -1e9 above), valid while mask_version == version.
+    uint64_t mask_version = ~0ull;
+    bool causal_mask = false;
 
     float* device();             // make the device copy current, return it
     float* device_for_overwrite();  // caller overwrites everything: skip uploads
@@ -77,6 +89,9 @@ public:
         // Lazy transpose: this tensor is `base` with its last two dims
         // swapped; `data` stays null until someone needs it materialized.
         std::shared_ptr<Impl> transpose_of;
+        // Deferred value: `data` stays null until the recipe is computed
+        // (or an op consumes the recipe without ever computing it).
+        std::shared_ptr<Deferred> deferred;
 
         std::function<void()> backward_fn = [] {};
         std::vector<std::shared_ptr<Impl>> prev;

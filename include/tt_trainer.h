@@ -118,6 +118,10 @@ int tt_plan_buckets(const int64_t* sizes, int n, int64_t bucket_bytes, int64_t* 
                     int* n_buckets);
 /* Number of CUDA kernels this library launched so far (all streams). */
 int64_t tt_kernel_launches(void);
+/* Number of attention-score chains (bmm(q, transpose(k)), * constant,
+ * + causal mask, softmax, bmm(., v): model.cpp:133-138 of the reference)
+ * that ran as the fused causal attention kernel since start-up. */
+int64_t tt_fused_attention_chains(void);
 
 #ifdef __cplusplus
 }

@@ -7,6 +7,7 @@ returns numpy results. See oracle/ref_harness.cpp for the op chains.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes as C
 import os
 
@@ -14,7 +15,11 @@ import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_ref", "libttref.so")
-_lib = None
+# The same harness with the reference's src/model.cpp, compiled against this
+# repository's headers and library (the drop-in on the device).
+LIB_B200_PATH = os.path.join(_HERE, "_ref", "libttref_b200.so")
+_libs = {}
+_active = LIB_PATH
 
 
 class RefCfg(C.Structure):
@@ -23,21 +28,36 @@ class RefCfg(C.Structure):
                 ("norm_eps", C.c_float), ("rope_theta", C.c_float)]
 
 
-def available() -> bool:
-    return os.path.exists(LIB_PATH)
+def available(path=None) -> bool:
+    return os.path.exists(path or LIB_PATH)
 
 
 def lib():
-    global _lib
-    if _lib is None:
-        if not available():
+    path = _active
+    if path not in _libs:
+        if not available(path):
             raise FileNotFoundError(
-                f"{LIB_PATH} missing: build it with `make -C oracle` where the reference sources exist")
-        _lib = C.CDLL(LIB_PATH)
-        _lib.ref_last_error.restype = C.c_char_p
-        _lib.ref_param_count.restype = C.c_int64
-        _lib.ref_param_shapes.restype = C.c_int64
-    return _lib
+                f"{path} missing: build it with `make -C oracle` where the reference sources exist")
+        L = C.CDLL(path)
+        L.ref_last_error.restype = C.c_char_p
+        L.ref_param_count.restype = C.c_int64
+        L.ref_param_shapes.restype = C.c_int64
+        _libs[path] = L
+    return _libs[path]
+
+
+@contextlib.contextmanager
+def on_device():
+    """Inside the block every function of this module runs the harness built
+    against this repository's library (oracle/_ref/libttref_b200.so): the
+    reference's own model.cpp and op chains, unmodified, executing on the
+    device. Not for the oracle's role: its results are what gets checked."""
+    global _active
+    prev, _active = _active, LIB_B200_PATH
+    try:
+        yield
+    finally:
+        _active = prev
 
 
 def _f(a):

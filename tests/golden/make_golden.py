@@ -4,6 +4,8 @@ reference's own CPU library (oracle/_ref/libttref.so, built by
 
     python tests/golden/make_golden.py            # op + tiny-model fixtures
     python tests/golden/make_golden.py --cfg0     # + the 30-step config-0 run (~11 min)
+    python tests/golden/make_golden.py --at-scale # + one micro-step of the 110M and 1B
+                                                  #   models (~40 GB of host memory, ~30 min)
 
 Fixtures:
   ops_small.npz   per-op inputs, outputs and gradients (matmul incl. ragged
@@ -16,6 +18,15 @@ Fixtures:
                   betas 0.9/0.95, wd 0.1, clip 1.0): per-step losses and grad
                   norms; inputs are regenerated from the recorded seeds and
                   checked by the recorded checksums
+  model_llama110m_1x1024.npz, model_llama1b_1x2048.npz
+                  one forward/backward micro-step (batch 1) of the benchmarked
+                  models (110M: dim 768, 12 layers, 12 heads, ffn 2048; 1B: dim
+                  2048, 16 layers, 16 heads, ffn 5632; vocab 32000, tied
+                  embeddings) on weights N(0, 0.02) and tokens regenerated from
+                  the recorded seeds: the loss, 8 full logit rows, and for every
+                  parameter max |grad| over all its entries plus the gradient at
+                  up to 512 recorded positions (its largest entry included).
+                  The full gradients (3.5 GB at 1B) are too large to commit.
 """
 from __future__ import annotations
 
@@ -128,11 +139,67 @@ def train_cfg0(steps=30):
         json.dump(rec, f, indent=1)
 
 
+AT_SCALE = {
+    "llama110m_1x1024": (dict(vocab=32000, dim=768, layers=12, heads=12, ffn=2048, max_seq=1024),
+                         1, 1024),
+    "llama1b_1x2048": (dict(vocab=32000, dim=2048, layers=16, heads=16, ffn=5632, max_seq=2048),
+                       1, 2048),
+}
+
+
+def model_at_scale(name, per_param=512, logit_rows=8):
+    cfg, B, T = AT_SCALE[name]
+    c = rb.cfg(**cfg)
+    shapes = inputs.param_shapes(cfg["vocab"], cfg["dim"], cfg["layers"], cfg["heads"],
+                                 cfg["ffn"])
+    assert shapes == rb.param_shapes(c)
+    w = inputs.make_weights(shapes, seed=101)
+    idx, tgt = inputs.make_tokens(1, B, T, cfg["vocab"], seed=102)
+    t0 = time.time()
+    logits, loss, grads = rb.model_fwd_bwd(c, w, idx[0], tgt[0], B, T)
+    secs = time.time() - t0
+    del w
+    rng = np.random.default_rng(103)
+    offs, gmax, pos, gval = [], [], [], []
+    off = 0
+    for s in shapes:
+        n = int(np.prod(s))
+        g = grads[off:off + n]
+        am = int(np.abs(g).argmax())
+        if n <= per_param:
+            p = np.arange(n)
+        else:
+            p = np.unique(np.concatenate([rng.choice(n, per_param - 1, replace=False), [am]]))
+        offs.append(off)
+        gmax.append(float(np.abs(g).max()))
+        pos.append(p.astype(np.int64) + off)
+        gval.append(g[p])
+        off += n
+    rows = np.sort(rng.choice(B * T, logit_rows, replace=False))
+    np.savez_compressed(
+        os.path.join(HERE, f"model_{name}.npz"),
+        cfg=np.array([cfg[k] for k in ("vocab", "dim", "layers", "heads", "ffn", "max_seq")],
+                     np.int64),
+        B=np.int64(B), T=np.int64(T), weight_seed=np.int64(101), weight_std=np.float32(0.02),
+        token_seed=np.int64(102), idx=idx[0], tgt=tgt[0], loss=np.float32(loss),
+        logit_rows=rows, logits=logits[rows], param_offsets=np.array(offs, np.int64),
+        grad_absmax=np.array(gmax, np.float32), grad_pos=np.concatenate(pos),
+        grad_val=np.concatenate(gval).astype(np.float32), cpu_seconds=np.float64(secs))
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--cfg0", action="store_true")
+    ap.add_argument("--at-scale", action="store_true")
+    ap.add_argument("--only", default=None, help="run only this at-scale fixture")
     a = ap.parse_args()
+    if a.only:
+        model_at_scale(a.only)
+        sys.exit(0)
     ops_small()
     model_tiny()
     if a.cfg0:
         train_cfg0()
+    if a.at_scale:
+        for name in AT_SCALE:
+            model_at_scale(name)

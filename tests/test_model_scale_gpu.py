@@ -1,0 +1,64 @@
+"""Whole-model parity at the benchmarked model sizes.
+
+One forward/backward micro-step of the 110M model (dim 768, 12 layers, 12
+heads of 64, ffn 2048, 1 x 1024 tokens) and of the 1B model (dim 2048, 16
+layers, 16 heads of 128, ffn 5632, 1 x 2048 tokens), vocab 32000 and tied
+embeddings, on weights N(0, 0.02) and tokens regenerated from the seeds the
+fixtures record (tests/golden/inputs.py). The fixtures hold the reference's
+own results (its GPTModel::forward, cross_entropy and backward, model.cpp:
+87-160, run by tests/golden/make_golden.py --at-scale on the reference's CPU
+library). Checked, each as max |ours - ref| / max |ref| <= 1e-4:
+  - the loss;
+  - 8 full logit rows;
+  - every parameter's gradient at up to 512 recorded positions (its largest
+    entry among them), normalised by that parameter's max |grad| over all
+    entries.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-4
+
+
+@pytest.mark.parametrize("name", ["llama110m_1x1024", "llama1b_1x2048"])
+def test_micro_step_matches_reference(cuda, name):
+    import inputs
+    from tinytrain_b200.trainer import Trainer
+    path = os.path.join(GOLDEN, f"model_{name}.npz")
+    if not os.path.exists(path):
+        pytest.skip(f"{path} not generated")
+    z = dict(np.load(path))
+    v, d, L, H, F, ms = (int(x) for x in z["cfg"])
+    cfg = dict(vocab=v, dim=d, layers=L, heads=H, ffn=F, max_seq=ms)
+    B, T = int(z["B"]), int(z["T"])
+    shapes = inputs.param_shapes(v, d, L, H, F)
+    w = inputs.make_weights(shapes, seed=int(z["weight_seed"]), std=float(z["weight_std"]))
+    idx, tgt = inputs.make_tokens(1, B, T, v, seed=int(z["token_seed"]))
+    assert np.array_equal(idx[0], z["idx"]) and np.array_equal(tgt[0], z["tgt"])
+    tr = Trainer(cfg, seed=1, host_init=False)
+    tr.set_params(w)
+    del w
+    loss, logits = tr.forward_backward(idx[0], tgt[0], B, T, want_logits=True)
+    grads = tr.get_grads()
+    tr.close()
+
+    assert abs(loss - float(z["loss"])) <= TOL * abs(float(z["loss"])), (loss, float(z["loss"]))
+    assert rel_err(logits[z["logit_rows"]], z["logits"]) <= TOL
+
+    offs = list(z["param_offsets"]) + [grads.size]
+    pos, val, gmax = z["grad_pos"], z["grad_val"], z["grad_absmax"]
+    worst = (0.0, -1)
+    for i in range(len(gmax)):
+        sel = (pos >= offs[i]) & (pos < offs[i + 1])
+        ours = grads[pos[sel]].astype(np.float64)
+        ref = val[sel].astype(np.float64)
+        assert np.abs(ref).max() == pytest.approx(float(gmax[i]), rel=1e-6)
+        # The reference's largest entry is among the samples; ours must agree.
+        err = float(np.abs(ours - ref).max()) / max(float(gmax[i]), 1e-30)
+        worst = max(worst, (err, i))
+    assert worst[0] <= TOL, f"parameter {worst[1]}: normalised gradient error {worst[0]:.2e}"

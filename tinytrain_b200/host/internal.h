@@ -1,6 +1,7 @@
 // Internals shared by the host translation units of libtinytrain.
 #pragma once
 
+#include <functional>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -66,9 +67,33 @@ struct Scratch {
 // The reference's randn stream (xorshift64* + Box-Muller) on the host.
 void host_randn(float* out, int64_t n, uint64_t seed);
 
-// Materialize a lazy transpose into its own buffer.
+// Give `p` its own data: materializes a lazy transpose or computes a
+// deferred result (no-op when the data exists).
 void materialize(Tensor::Impl* p);
 inline void materialize(const ImplPtr& p) { materialize(p.get()); }
+
+}  // namespace detail
+
+// Recipe of a deferred node of the attention-score chain (model.cpp:133-137):
+// scores = bmm(q, transpose(k)) [N, T, T], then optionally * constant,
+// + causal mask, softmax(-1). `compute` writes the node's value into its
+// (already allocated) buffer with the ordinary kernels; the closing
+// bmm(probs, v) reads q, k, scale instead and never computes it.
+struct Deferred {
+    detail::ImplPtr q, k;         // [N, T, hd] operands of bmm(q, transpose(k))
+    uint64_t vq = 0, vk = 0;      // their buffer versions when the chain began
+    float scale = 1.0f;           // product of the constant factors so far
+    bool masked = false;          // causal mask added
+    bool softmax = false;         // row softmax applied
+    std::function<void(Tensor::Impl*)> compute;
+};
+
+namespace detail {
+
+// The chain recipe of `p` when it is an uncomputed deferred node.
+inline const Deferred* pending_chain(const ImplPtr& p) {
+    return (p && p->deferred && !p->data) ? p->deferred.get() : nullptr;
+}
 
 }  // namespace detail
 }  // namespace tt

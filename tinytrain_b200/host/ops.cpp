@@ -88,7 +88,7 @@ struct Operand {
 
 Operand operand(const ImplPtr& p, const std::vector<int64_t>& out_shape) {
     Operand o;
-    if (!p->transpose_of && p->data->pending_fill) {
+    if (p->data && !p->transpose_of && p->data->pending_fill) {
         o.holder = std::make_shared<Scratch>(16);
         check(ttk_fill(o.holder->as<float>(), p->data->fill_value, 1, stream()), "const");
         o.ptr = o.holder->as<float>();
@@ -112,15 +112,104 @@ void accum_grad(const ImplPtr& dst, const float* src) {
 
 float* out_ptr(Tensor& t) { return t.impl()->data->device_for_overwrite(); }
 
+// ------------------------------------------------- deferred attention chain --
+// bmm(q, transpose(k)) -> mul(., constant) -> add(., causal mask) ->
+// softmax(., -1) -> bmm(., v), the attention of model.cpp:133-138. The first
+// four results are deferred (no [N, T, T] buffer); the closing bmm runs the
+// fused causal attention on q, k, v and the accumulated scale. Any other read
+// of a deferred result computes it with the ordinary kernels.
+
+int64_t g_chains_fused = 0;
+
+// Turns the freshly made `out` into a deferred node computed by `fwd`.
+void defer(Tensor& out, std::shared_ptr<Deferred> d, std::function<void(Tensor::Impl*)> fwd) {
+    d->compute = std::move(fwd);
+    out.impl()->data.reset();
+    out.impl()->deferred = std::move(d);
+}
+
+// A tensor with its own (possibly still lazily filled) storage.
+bool plain(const ImplPtr& p) { return p->data && !p->transpose_of && !p->deferred; }
+
+// Constant tensor: a full() that nobody wrote into since.
+bool constant_value(const ImplPtr& p, float& v) {
+    if (!plain(p) || !p->data->pending_fill || !std::isfinite(p->data->fill_value))
+        return false;
+    v = p->data->fill_value;
+    return true;
+}
+
+// [T, T] (or [1, T, T]) holding 0 on and below the diagonal and <= -1e9
+// above it (model.cpp:97-101). Under it the composite softmax gives every
+// masked entry exactly 0, as the fused kernel's causal skip does. Checked on
+// the host mirror once per buffer version.
+bool causal_mask(const ImplPtr& m, int64_t T) {
+    const auto& sh = m->shape;
+    const bool shape_ok = (sh.size() == 2 && sh[0] == T && sh[1] == T) ||
+                          (sh.size() == 3 && sh[0] == 1 && sh[1] == T && sh[2] == T);
+    if (!shape_ok || !plain(m))
+        return false;
+    Buffer& b = *m->data;
+    if (b.mask_version == b.version)
+        return b.causal_mask;
+    const float* h = b.host_ptr();
+    bool ok = true;
+    for (int64_t i = 0; i < T && ok; ++i)
+        for (int64_t j = 0; j < T; ++j) {
+            const float x = h[i * T + j];
+            if (j <= i ? x != 0.0f : !(x <= -1e9f)) {
+                ok = false;
+                break;
+            }
+        }
+    b.mask_version = b.version;
+    b.causal_mask = ok;
+    return ok;
+}
+
+uint64_t version_of(const ImplPtr& p) {
+    if (p->data)
+        return p->data->version;
+    if (p->transpose_of && p->transpose_of->data)
+        return p->transpose_of->data->version;
+    return ~0ull;
+}
+
+void check_chain_inputs(const Deferred& d) {
+    if (version_of(d.q) != d.vq || version_of(d.k) != d.vk)
+        throw std::logic_error(
+            "attention scores: q or k was modified after bmm(q, transpose(k)) and before its "
+            "result was used");
+}
+
 // --------------------------------------------------------- elementwise --
 
 Tensor elem_binary(const Tensor& a, const Tensor& b, int op) {
     auto shape = broadcast_shape(a.shape(), b.shape());
     Tensor out = make_out(shape, a.requires_grad() || b.requires_grad());
-    Operand oa = operand(a.impl(), shape), ob = operand(b.impl(), shape);
-    check(ttk_binary(op, oa.ptr, oa.strides.data(), ob.ptr, ob.strides.data(), out_ptr(out),
-                     shape.data(), static_cast<int>(shape.size()), stream()),
-          "binary");
+    std::shared_ptr<Deferred> chain;
+    if (const Deferred* d = pending_chain(a.impl());
+        d && !d->masked && !d->softmax && shape == a.shape()) {
+        float c = 0.0f;
+        if (op == 2 && constant_value(b.impl(), c)) {  // scores * scale (model.cpp:134)
+            chain = std::make_shared<Deferred>(*d);
+            chain->scale = d->scale * c;
+        } else if (op == 0 && causal_mask(b.impl(), shape[1])) {  // + mask (model.cpp:135)
+            chain = std::make_shared<Deferred>(*d);
+            chain->masked = true;
+        }
+    }
+    auto fwd = [ai = a.impl(), bi = b.impl(), shape, op](Tensor::Impl* o) {
+        Operand oa = operand(ai, shape), ob = operand(bi, shape);
+        check(ttk_binary(op, oa.ptr, oa.strides.data(), ob.ptr, ob.strides.data(),
+                         o->data->device_for_overwrite(), shape.data(),
+                         static_cast<int>(shape.size()), stream()),
+              "binary");
+    };
+    if (chain)
+        defer(out, chain, fwd);
+    else
+        fwd(out.impl().get());
     if (out.requires_grad()) {
         auto ao = a.impl(), bo = b.impl();
         Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
@@ -510,15 +599,29 @@ Tensor unsqueeze(const Tensor& a, int64_t dim) {
 
 namespace {
 
+Tensor fused_attention(const ImplPtr& qo, const ImplPtr& ko, const ImplPtr& vo, ImplPtr co,
+                       ImplPtr so, int64_t B, int64_t T, int64_t H, int64_t hd, float scale,
+                       std::vector<int64_t> oshape);
+
 // C (batch x [M,N]) = op(A) op(B) and its backward, for matmul and bmm. A is
 // [M,K] (storage [K,M] when A.trans), B is [K,N] (storage [N,K] when B.trans).
 Tensor batched_matmul(const Tensor& a, const Tensor& b, int64_t Bt, int64_t M, int64_t K,
-                      int64_t N, std::vector<int64_t> oshape) {
+                      int64_t N, std::vector<int64_t> oshape,
+                      std::shared_ptr<Deferred> chain = nullptr) {
     Tensor out = make_out(oshape, a.requires_grad() || b.requires_grad());
-    MatOp A = mat_operand(a.impl()), Bm = mat_operand(b.impl());
-    const int64_t lda = A.trans ? M : K, ldb = Bm.trans ? K : N;
-    gemm(A.trans, Bm.trans, Bt, M, N, K, {A.base->data.get(), A.ptr, lda, M * K},
-         {Bm.base->data.get(), Bm.ptr, ldb, K * N}, 0.0f, out_ptr(out), N, M * N);
+    auto fwd = [ai = a.impl(), bi = b.impl(), Bt, M, K, N, chain](Tensor::Impl* o) {
+        if (chain)
+            check_chain_inputs(*chain);
+        MatOp A = mat_operand(ai), Bm = mat_operand(bi);
+        const int64_t lda = A.trans ? M : K, ldb = Bm.trans ? K : N;
+        gemm(A.trans, Bm.trans, Bt, M, N, K, {A.base->data.get(), A.ptr, lda, M * K},
+             {Bm.base->data.get(), Bm.ptr, ldb, K * N}, 0.0f, o->data->device_for_overwrite(),
+             N, M * N);
+    };
+    if (chain)
+        defer(out, chain, fwd);
+    else
+        fwd(out.impl().get());
     if (out.requires_grad()) {
         auto ao = a.impl(), bo = b.impl();
         Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
@@ -578,8 +681,30 @@ Tensor bmm(const Tensor& a, const Tensor& b) {
     if (b.dim(0) != B || b.dim(1) != K)
         throw std::invalid_argument("bmm: batch/inner dims mismatch");
     const int64_t N = b.dim(2);
+    // probs @ v closing a deferred causal chain (model.cpp:138): fused.
+    if (const Deferred* d = pending_chain(a.impl());
+        d && d->masked && d->softmax && plain(b.impl()) && b.shape() == d->q->shape) {
+        check_chain_inputs(*d);
+        ++g_chains_fused;
+        return fused_attention(d->q, d->k, b.impl(), nullptr, nullptr, B, M, 1, N, d->scale,
+                               {B, M, N});
+    }
+    // q @ k^T of an attention block (model.cpp:133): deferred.
+    const ImplPtr& bi = b.impl();
+    if (plain(a.impl()) && bi->transpose_of && !bi->data && plain(bi->transpose_of) &&
+        bi->transpose_of->shape == a.shape() && M == N && (K == 32 || K == 64 || K == 128) &&
+        B <= 65535) {
+        auto d = std::make_shared<Deferred>();
+        d->q = a.impl();
+        d->k = bi->transpose_of;
+        d->vq = version_of(d->q);
+        d->vk = version_of(d->k);
+        return batched_matmul(a, b, B, M, K, N, {B, M, N}, d);
+    }
     return batched_matmul(a, b, B, M, K, N, {B, M, N});
 }
+
+int64_t fused_attention_chains() { return g_chains_fused; }
 
 Tensor linear(const Tensor& x, const Tensor& weight) {
     if (x.ndim() != 2 || weight.ndim() != 2)
@@ -794,7 +919,18 @@ Tensor softmax_impl(const Tensor& a, int64_t dim, int log) {
     }
     const int64_t C = a.dim(a.ndim() - 1), R = a.numel() / C;
     Tensor out = make_out(a.shape(), a.requires_grad());
-    check(ttk_softmax_fwd(dread(a.impl()), out_ptr(out), R, C, log, stream()), "softmax");
+    auto fwd = [ai = a.impl(), R, C, log](Tensor::Impl* o) {
+        check(ttk_softmax_fwd(dread(ai), o->data->device_for_overwrite(), R, C, log, stream()),
+              "softmax");
+    };
+    const Deferred* d = pending_chain(a.impl());
+    if (d && d->masked && !d->softmax && !log) {  // softmax(masked scores) (model.cpp:136)
+        auto chain = std::make_shared<Deferred>(*d);
+        chain->softmax = true;
+        defer(out, chain, fwd);
+    } else {
+        fwd(out.impl().get());
+    }
     if (out.requires_grad()) {
         auto ao = a.impl();
         Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
@@ -988,6 +1124,88 @@ Tensor rope(const Tensor& x, const Tensor& cos, const Tensor& sin) {
 
 // ------------------------------------------------------------ fused ops --
 
+namespace {
+
+// The fused causal attention as one graph node: q, k, v [B,T,H,hd] (any
+// logical shape with that storage), RoPE from the tables co/so (identity
+// when null: the deferred chain's q and k are already rotated), output of
+// shape `oshape` holding [B,T,H*hd].
+Tensor fused_attention(const ImplPtr& qo, const ImplPtr& ko, const ImplPtr& vo, ImplPtr co,
+                       ImplPtr so, int64_t B, int64_t T, int64_t H, int64_t hd, float scale,
+                       std::vector<int64_t> oshape) {
+    if (!co) {
+        co = full({T, hd / 2}, 1.0f).impl();
+        so = full({T, hd / 2}, 0.0f).impl();
+    }
+    const bool rg = qo->requires_grad || ko->requires_grad || vo->requires_grad;
+    Tensor out = make_out(oshape, rg);
+    auto lse = std::make_shared<Buffer>(B * H * T);
+    // The forward's workspace holds q, k, v split into bf16 planes; it is kept
+    // for the backward, which reuses them while q, k, v are unchanged.
+    const size_t fws = ttk_attention_fwd_workspace_size(B, T, H, hd);
+    auto fw = std::make_shared<Scratch>(fws);
+    check(ttk_attention_fwd(dread(qo), dread(ko), dread(vo), dread(co), dread(so), out_ptr(out),
+                            lse->device_for_overwrite(), B, T, H, hd, scale, fw->ptr, fws,
+                            stream()),
+          "attention");
+    if (!rg)
+        return out;
+    // Contents of q, k, v as the forward read them (buffer versions).
+    const uint64_t vq = version_of(qo), vk = version_of(ko), vv = version_of(vo);
+    Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
+    oo->prev = {qo, ko, vo};
+    oo->backward_fn = [qo, ko, vo, co, so, oo, lse, B, T, H, hd, scale, fw, vq, vk,
+                       vv]() mutable {
+        const float* g = grad_in(oo);
+        if (!g)
+            return;
+        // Gradients that are not wanted go to scratch.
+        std::vector<std::unique_ptr<Scratch>> junk;
+        auto dst = [&](const ImplPtr& p, bool& ow) -> float* {
+            if (p->requires_grad)
+                return grad_target(p, ow);
+            junk.emplace_back(new Scratch(static_cast<size_t>(p->numel) * 4));
+            ow = true;
+            return junk.back()->as<float>();
+        };
+        bool oq = false, ok = false, ov = false;
+        float* dq = dst(qo, oq);
+        float* dk = dst(ko, ok);
+        float* dv = dst(vo, ov);
+        const bool all_fresh = oq && ok && ov;
+        if (!all_fresh) {  // one accumulate flag covers all three
+            if (oq)
+                check(ttk_memset(dq, 0, static_cast<size_t>(qo->numel) * 4, stream()), "zero");
+            if (ok)
+                check(ttk_memset(dk, 0, static_cast<size_t>(ko->numel) * 4, stream()), "zero");
+            if (ov)
+                check(ttk_memset(dv, 0, static_cast<size_t>(vo->numel) * 4, stream()), "zero");
+        }
+        const float *qd = dread(qo), *kd = dread(ko), *vd = dread(vo);
+        const bool reuse = fw && fw->ptr && vq != ~0ull && version_of(qo) == vq &&
+                           version_of(ko) == vk && version_of(vo) == vv;
+        if (reuse) {
+            const size_t ws = ttk_attention_bwd_ex_workspace_size(B, T, H, hd);
+            Scratch w(ws);
+            check(ttk_attention_bwd_ex(qd, kd, vd, dread(co), dread(so), dread(oo),
+                                       lse->device(), g, dq, dk, dv, all_fresh ? 0 : 1, B, T, H,
+                                       hd, scale, fw->ptr, w.ptr, ws, stream()),
+                  "attention bwd");
+        } else {
+            const size_t ws = ttk_attention_bwd_workspace_size(B, T, H, hd);
+            Scratch w(ws);
+            check(ttk_attention_bwd(qd, kd, vd, dread(co), dread(so), dread(oo), lse->device(),
+                                    g, dq, dk, dv, all_fresh ? 0 : 1, B, T, H, hd, scale, w.ptr,
+                                    ws, stream()),
+                  "attention bwd");
+        }
+        fw.reset();  // planes no longer needed (stream-ordered free)
+    };
+    return out;
+}
+
+}  // namespace
+
 Tensor causal_attention(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& cos,
                         const Tensor& sin) {
     if (q.ndim() != 4 || q.shape() != k.shape() || q.shape() != v.shape())
@@ -996,81 +1214,8 @@ Tensor causal_attention(const Tensor& q, const Tensor& k, const Tensor& v, const
     if (cos.ndim() != 2 || cos.dim(0) < T || cos.dim(1) != hd / 2 || sin.shape() != cos.shape())
         throw std::invalid_argument("rope: cos/sin shape mismatch");
     const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
-    const bool rg = q.requires_grad() || k.requires_grad() || v.requires_grad();
-    Tensor out = make_out({B, T, H * hd}, rg);
-    auto lse = std::make_shared<Buffer>(B * H * T);
-    // The forward's workspace holds q, k, v split into bf16 planes; it is kept
-    // for the backward, which reuses them while q, k, v are unchanged.
-    const size_t fws = ttk_attention_fwd_workspace_size(B, T, H, hd);
-    auto fw = std::make_shared<Scratch>(fws);
-    check(ttk_attention_fwd(dread(q.impl()), dread(k.impl()), dread(v.impl()), dread(cos.impl()),
-                            dread(sin.impl()), out_ptr(out), lse->device_for_overwrite(), B, T,
-                            H, hd, scale, fw->ptr, fws, stream()),
-          "attention");
-    if (!rg)
-        fw.reset();
-    if (rg) {
-        auto qo = q.impl(), ko = k.impl(), vo = v.impl(), co = cos.impl(), so = sin.impl();
-        // Contents of q, k, v as the forward read them (buffer versions).
-        auto version_of = [](const ImplPtr& p) -> uint64_t {
-            if (p->data)
-                return p->data->version;
-            if (p->transpose_of && p->transpose_of->data)
-                return p->transpose_of->data->version;
-            return ~0ull;
-        };
-        const uint64_t vq = version_of(qo), vk = version_of(ko), vv = version_of(vo);
-        Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
-        oo->prev = {qo, ko, vo};
-        oo->backward_fn = [qo, ko, vo, co, so, oo, lse, B, T, H, hd, scale, fw, vq, vk, vv,
-                           version_of]() mutable {
-            const float* g = grad_in(oo);
-            if (!g)
-                return;
-            // Gradients that are not wanted go to scratch.
-            std::vector<std::unique_ptr<Scratch>> junk;
-            auto dst = [&](const ImplPtr& p, bool& ow) -> float* {
-                if (p->requires_grad)
-                    return grad_target(p, ow);
-                junk.emplace_back(new Scratch(static_cast<size_t>(p->numel) * 4));
-                ow = true;
-                return junk.back()->as<float>();
-            };
-            bool oq = false, ok = false, ov = false;
-            float* dq = dst(qo, oq);
-            float* dk = dst(ko, ok);
-            float* dv = dst(vo, ov);
-            const bool all_fresh = oq && ok && ov;
-            if (!all_fresh) {  // one accumulate flag covers all three
-                if (oq)
-                    check(ttk_memset(dq, 0, static_cast<size_t>(qo->numel) * 4, stream()), "zero");
-                if (ok)
-                    check(ttk_memset(dk, 0, static_cast<size_t>(ko->numel) * 4, stream()), "zero");
-                if (ov)
-                    check(ttk_memset(dv, 0, static_cast<size_t>(vo->numel) * 4, stream()), "zero");
-            }
-            const float *qd = dread(qo), *kd = dread(ko), *vd = dread(vo);
-            const bool reuse = fw && fw->ptr && vq != ~0ull && version_of(qo) == vq &&
-                               version_of(ko) == vk && version_of(vo) == vv;
-            if (reuse) {
-                const size_t ws = ttk_attention_bwd_ex_workspace_size(B, T, H, hd);
-                Scratch w(ws);
-                check(ttk_attention_bwd_ex(qd, kd, vd, dread(co), dread(so), dread(oo),
-                                           lse->device(), g, dq, dk, dv, all_fresh ? 0 : 1, B, T,
-                                           H, hd, scale, fw->ptr, w.ptr, ws, stream()),
-                      "attention bwd");
-            } else {
-                const size_t ws = ttk_attention_bwd_workspace_size(B, T, H, hd);
-                Scratch w(ws);
-                check(ttk_attention_bwd(qd, kd, vd, dread(co), dread(so), dread(oo),
-                                        lse->device(), g, dq, dk, dv, all_fresh ? 0 : 1, B, T, H,
-                                        hd, scale, w.ptr, ws, stream()),
-                      "attention bwd");
-            }
-            fw.reset();  // planes no longer needed (stream-ordered free)
-        };
-    }
-    return out;
+    return fused_attention(q.impl(), k.impl(), v.impl(), cos.impl(), sin.impl(), B, T, H, hd,
+                           scale, {B, T, H * hd});
 }
 
 Tensor swiglu(const Tensor& a, const Tensor& b) {

@@ -167,15 +167,26 @@ Tensor make_view(const Tensor& src, const std::vector<int64_t>& shape, bool requ
     impl->shape = shape;
     impl->strides = row_major(shape);
     impl->numel = numel_of(shape);
-    if (src.impl()->transpose_of)
-        materialize(src.impl());
+    materialize(src.impl());
     impl->data = src.impl()->data;
     impl->requires_grad = requires_grad;
     return Tensor::from_impl(impl);
 }
 
 void materialize(Tensor::Impl* p) {
-    if (!p->transpose_of || p->data)
+    if (p->data)
+        return;
+    if (p->deferred) {
+        // Computed with the ordinary kernels; the recipe stays attached (its
+        // inputs stay alive like graph edges) but no longer fuses: a chain
+        // continues only from uncomputed nodes.
+        auto buf = std::make_shared<Buffer>(p->numel);
+        buf->device_for_overwrite();
+        p->data = buf;
+        p->deferred->compute(p);
+        return;
+    }
+    if (!p->transpose_of)
         return;
     const ImplPtr& base = p->transpose_of;
     const int64_t nd = static_cast<int64_t>(p->shape.size());
@@ -194,13 +205,13 @@ void materialize(Tensor::Impl* p) {
 }
 
 const float* dread(Tensor::Impl* p) {
-    if (p->transpose_of && !p->data)
+    if (!p->data)
         materialize(p);
     return p->data->device();
 }
 
 float* dwrite(Tensor::Impl* p) {
-    if (p->transpose_of && !p->data)
+    if (!p->data)
         materialize(p);
     float* d = p->data->device();
     p->data->host_valid = false;
@@ -281,16 +292,14 @@ Tensor Tensor::from_impl(std::shared_ptr<Impl> impl) {
 }
 
 float* Tensor::data() {
-    if (impl_->transpose_of && !impl_->data)
-        materialize(impl_);
+    materialize(impl_);
     float* h = impl_->data->host_ptr();
     impl_->data->host_written();  // the caller may write through the pointer
     return h;
 }
 
 const float* Tensor::data() const {
-    if (impl_->transpose_of && !impl_->data)
-        materialize(impl_);
+    materialize(impl_);
     return impl_->data->host_ptr();
 }
 
@@ -339,8 +348,7 @@ Tensor Tensor::detach() const {
     impl->shape = impl_->shape;
     impl->strides = impl_->strides;
     impl->numel = impl_->numel;
-    if (impl_->transpose_of && !impl_->data)
-        materialize(impl_);
+    materialize(impl_);
     // The reference copies the storage (tensor.cpp:73-81).
     impl->data = std::make_shared<Buffer>(impl->numel);
     float* dst = impl->data->device_for_overwrite();
@@ -361,8 +369,7 @@ float* Tensor::device_grad() const {
 }
 
 void Tensor::copy_from_host(const float* src) {
-    if (impl_->transpose_of && !impl_->data)
-        materialize(impl_);
+    materialize(impl_);
     float* d = impl_->data->device_for_overwrite();
     check(ttk_memcpy_h2d(d, src, static_cast<size_t>(impl_->numel) * 4, stream()), "upload");
 }

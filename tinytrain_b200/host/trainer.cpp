@@ -321,6 +321,7 @@ extern "C" {
 const char* tt_last_error(void) { return t_err.c_str(); }
 
 int64_t tt_kernel_launches(void) { return ttk_launch_count(); }
+int64_t tt_fused_attention_chains(void) { return tt::fused_attention_chains(); }
 
 int tt_trainer_create(const tt_model_config* c, uint64_t seed, int host_init, void** handle) {
     return guarded([&] {

@@ -55,6 +55,7 @@ _SIGS = {
     "tt_trainer_forward_backward": (C.c_int, [P, P, P, I64, I64, P, P]),
     "tt_trainer_dist_init": (C.c_int, [P, C.c_int, C.c_int, P, I64]),
     "tt_kernel_launches": (I64, []),
+    "tt_fused_attention_chains": (I64, []),
     "tt_plan_buckets": (C.c_int, [P, C.c_int, I64, P, P, P, P, P]),
     "tt_tokens_from_file": (C.c_int, [C.c_char_p, P]),
     "tt_tokens_from_host": (C.c_int, [P, I64, P]),
@@ -92,6 +93,11 @@ def _chk(rc, what):
 
 def kernel_launches() -> int:
     return int(lib().tt_kernel_launches())
+
+
+def fused_attention_chains() -> int:
+    """Attention-score op chains run as the fused kernel since start-up."""
+    return int(lib().tt_fused_attention_chains())
 
 
 def set_stream(stream_handle: int):

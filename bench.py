@@ -59,8 +59,12 @@ WORKLOADS = {
     "llama-13m": dict(model="llama-13m", vocab=32000, dim=256, layers=6, heads=8, ffn=768,
                       max_seq=256, global_batch=16, seq=128, micro=16),
 }
-# CPU sample of the reference per step (tokens), bounded to ~10-30 s of work.
-CPU_SAMPLE = {"llama-1b": (1, 16), "llama-110m": (1, 128), "llama-13m": (16, 128)}
+# The reference's CPU micro-step sample per config (B, T): the config's own
+# sequence length. At 1B one 1 x 2048 micro-step takes ~10 min on 8 cores and
+# more than 62 GB of host memory at full depth, so the sample is taken at
+# depths 1 and 2 of the same width and extrapolated (reference_micro_step).
+CPU_SAMPLE = {"llama-1b": (1, 2048), "llama-110m": (1, 1024), "llama-13m": (16, 128)}
+SAMPLE_DEPTHS = (1, 2)
 
 
 def peaks():
@@ -145,21 +149,68 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_reference_time(w, steps, warmup):
-    """Mean seconds per step of the reference's CPU build on a bounded sample."""
+def reference_micro_step(w):
+    """The reference CPU build's training throughput on the workload, from a
+    bounded sample (oracle/_ref: the reference's src/*.cpp compiled unchanged,
+    all host threads).
+
+    The sample is one micro-step of CPU_SAMPLE tokens at the config's width
+    and sequence length: forward, cross-entropy and backward of the
+    reference's GPTModel, timed at depth 1 and at depth 2. The reference runs
+    its layers one after another with the same ops, so a full-depth micro-step
+    costs rest + L * per_layer with per_layer = t(2) - t(1) and rest = t(1) -
+    per_layer (which also absorbs the first layer's one-time costs: process
+    warm-up, allocator growth). The optimizer step (clip + AdamW, linear in the
+    parameter count) is timed on the depth-2 model, scaled to the full
+    parameter count, and amortized over the micro-steps of one global batch,
+    as gradient accumulation does. Returns a dict with tokens/s and the parts.
+    """
     from oracle import refbind as rb
     if not rb.available():
         return None
     B, T = CPU_SAMPLE[w["model"]]
-    c = rb.cfg(vocab=w["vocab"], dim=w["dim"], layers=w["layers"], heads=w["heads"],
-               ffn=w["ffn"], max_seq=max(w["max_seq"], T))
-    secs = rb.time_train(c, B, T, warmup, steps)
-    return secs, B * T
+    d1, d2 = SAMPLE_DEPTHS
+    t, opt = {}, {}
+    for d in (d1, d2):
+        c = rb.cfg(vocab=w["vocab"], dim=w["dim"], layers=d, heads=w["heads"], ffn=w["ffn"],
+                   max_seq=max(w["max_seq"], T))
+        t[d], opt[d] = rb.time_phases(c, B, T, 0, 1)
+    per_layer = (t[d2] - t[d1]) / (d2 - d1)
+    rest = t[d1] - d1 * per_layer
+    micro = rest + w["layers"] * per_layer
+    w2 = dict(w, layers=d2)
+    opt_full = opt[d2] * n_params(w) / n_params(w2)
+    n_micro = w["global_batch"] * w["seq"] / (B * T)
+    step = n_micro * micro + opt_full
+    tps = w["global_batch"] * w["seq"] / step
+    sample = (f"reference train step at the {w['model']} width, one micro-step of {B} x {T} "
+              f"tokens (forward, cross-entropy, backward) timed at depth {d1} ({t[d1]:.1f} s) and "
+              f"depth {d2} ({t[d2]:.1f} s): {per_layer:.1f} s per layer + {rest:.1f} s rest, "
+              f"{micro:.0f} s per full-depth ({w['layers']} layers) micro-step; clip + AdamW "
+              f"{opt_full:.1f} s (timed at depth {d2}, scaled to {n_params(w)} parameters) "
+              f"amortized over the {n_micro:.0f} micro-steps of a {w['global_batch']} x {w['seq']} "
+              f"global batch; {os.cpu_count()} host threads")
+    return {"tokens_per_s": tps, "micro_s": micro, "per_layer_s": per_layer, "rest_s": rest,
+            "opt_s": opt_full, "sample": sample, "timed": {str(d): t[d] for d in t}}
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    return ln.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
 
 
 def run_reference(args, w, rank, world):
     """--impl reference: the reference's own CPU implementation (oracle/_ref,
-    the reference sources compiled unchanged), all host threads, rank 0 only."""
+    the reference sources compiled unchanged), all host threads, rank 0 only.
+    One full-depth micro-step of the workload takes minutes on the CPU, so the
+    arm times the two depth samples of reference_micro_step (two timed
+    micro-steps whatever --steps asks; "steps" reports them)."""
     if rank != 0:
         return
     os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count()))
@@ -168,25 +219,21 @@ def run_reference(args, w, rank, world):
         print(json.dumps({"impl": "reference",
                           "unavailable": "oracle/_ref/libttref.so was not built"}))
         return
-    B, T = CPU_SAMPLE[w["model"]]
     t0 = time.time()
-    # One untimed step settles a CPU run; a 1B sample step takes ~45 s, so the
-    # rest of the requested warm-up is not repeated.
-    cpu_warmup = min(args.warmup, 1)
-    secs, ntok = cpu_reference_time(w, args.steps, cpu_warmup)
-    tps = ntok / secs
+    r = reference_micro_step(w)
+    tps = r["tokens_per_s"]
     cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count()))
-    sample = f"{B} x {T} tokens per step on the {w['model']} model (reference train step: " \
-             f"forward, cross-entropy, backward, clip, AdamW), {args.steps} timed steps " \
-             f"after {cpu_warmup} untimed"
+    ms_step = w["global_batch"] * w["seq"] / tps * 1e3
     print(json.dumps({
         "impl": "reference", "metric": "train tokens/sec", "value": tps, "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": secs * 1e3, "higher_is_better": True, "scaling": "strong",
+        "n_gpus": world, "steps": 2, "steps_requested": args.steps, "warmup": 0,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": workload_config(w, world),
         "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "reference",
-                         "sample": sample},
+                         "cpu": cpu_model(), "sample": r["sample"]},
+        "reference_parts": {k: r[k] for k in ("micro_s", "per_layer_s", "rest_s", "opt_s",
+                                              "timed")},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "wall_s": time.time() - t0}))
@@ -305,6 +352,8 @@ def main():
 
     # ---- timed region: value
     _ttk.call("ttk_profile_enable", 1)
+    if world > 1:
+        tr.comm_profile(True)
     l0 = trn.kernel_launches()
     # One event per step boundary on the launching stream: the first and last
     # bracket the timed region, the ones between give each step's time.
@@ -319,6 +368,18 @@ def main():
             ev[i + 1].record(stream)
         barrier()
     launches = trn.kernel_launches() - l0
+    comm = None
+    if world > 1:
+        tr.comm_profile(False)
+        busy, tail, n_ar, n_st = tr.comm_stats()
+        busy, tail = max_over_ranks(busy), max_over_ranks(tail)
+        comm = {"allreduce_ms_per_step": busy / args.steps,
+                "exposed_tail_ms_per_step": tail / args.steps,
+                "allreduces_per_step": n_ar / max(n_st, 1),
+                "bytes_per_step": n_params(w) * 4,
+                "is": "gradient all-reduce (NCCL, fp32 sum) on the comm stream: summed "
+                      "duration of the buckets' all-reduces, and the tail by which the last "
+                      "all-reduce ends after the last backward kernel (max over ranks)"}
     gms, gfl, gl = C.c_double(0), C.c_double(0), C.c_int64(0)
     _ttk.call("ttk_profile_enable", 0)
     _ttk.call("ttk_profile_read", C.byref(gms), C.byref(gfl), C.byref(gl))
@@ -377,6 +438,8 @@ def main():
                 "launches": gl.value, "share_of_step": gemm_share},
             "mfu_fp32_equiv": value * flops_per_token(w) / 1e12 / world,
             "gpu_launches": launches,
+            "launches_before_timed": l0,
+            "allreduce": comm,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * tokens_rank * 8,
                     "d2h_bytes_per_step": 4, "steps": ke,
                     "step_ms": [round(x, 2) for x in step_ms_e2e], "clocks": clk_e2e.summary()},
@@ -385,20 +448,15 @@ def main():
         }
         if world == 1 and not args.no_cpu_baseline:
             try:
-                r = cpu_reference_time(w, 1, 0)
+                r = reference_micro_step(w)
             except Exception as ex:  # reported, never fatal
                 r = None
                 line["cpu_baseline_error"] = str(ex)[:200]
             if r:
-                secs, ntok = r
-                Bc, Tc = CPU_SAMPLE[w["model"]]
                 line["cpu_baseline"] = {
-                    "value": ntok / secs, "unit": "tokens/s",
+                    "value": r["tokens_per_s"], "unit": "tokens/s",
                     "cores": int(os.environ.get("OMP_NUM_THREADS", os.cpu_count())),
-                    "kind": "reference",
-                    "sample": f"one reference train step (forward, cross-entropy, backward, "
-                              f"clip, AdamW) of {Bc} x {Tc} tokens on the {w['model']} model, "
-                              f"{secs:.1f} s"}
+                    "kind": "reference", "cpu": cpu_model(), "sample": r["sample"]}
         print(json.dumps(line), flush=True)
 
     tr.close()

@@ -103,6 +103,31 @@ float tt_lr_at(float base_lr, int64_t step, int64_t warmup, int64_t total_steps)
 int tt_trainer_save(void* handle, const char* dir);
 int tt_trainer_load(void* handle, const char* dir);
 
+/* Deadline for a distributed step's collectives (default 300 s). Before each
+ * distributed step the previous one's completion is awaited with this bound
+ * (one step in flight), polling ncclCommGetAsyncError; tt_trainer_step also
+ * awaits its own step before reading the loss. On an asynchronous error or
+ * an overrun (a peer left or hangs) the communicator is aborted
+ * (ncclCommAbort ends its pending collectives), the step fails with the
+ * reason, and later distributed steps are refused. No counterpart in the
+ * reference (which has no distributed code). */
+int tt_trainer_set_collective_timeout(void* handle, double seconds);
+/* Timing of the gradient all-reduce (off by default): with profiling on,
+ * every bucket's all-reduce is bracketed by events on the comm stream, and
+ * each distributed step records the end of its last backward on the compute
+ * stream against the end of its last all-reduce. tt_trainer_comm_stats
+ * returns, since the last read, the summed all-reduce time, the summed
+ * exposed tail (all-reduce end minus backward end, when positive: the time
+ * the optimizer waits for the collective), and the counts; it synchronizes. */
+int tt_trainer_comm_profile(void* handle, int on);
+int tt_trainer_comm_stats(void* handle, double* allreduce_ms, double* tail_ms,
+                          int64_t* n_allreduce, int64_t* n_steps);
+/* The watchdog's wait loop on caller-supplied probes, for testing it without
+ * a communicator: done(ctx) != 0 ends the wait (outcome 0); async_error(ctx)
+ * != 0 calls abort(ctx) once (outcome 1); so does passing timeout_s
+ * (outcome 2). */
+int tt_watchdog_selftest(int (*done)(void*), int (*async_error)(void*), int (*abort)(void*),
+                         void* ctx, double timeout_s, int* outcome);
 /* Data parallelism: join an NCCL communicator (id from rank 0's
  * ttk_dist_unique_id, shared out of band) and reduce gradients in buckets of
  * about bucket_bytes during backward. */

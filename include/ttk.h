@@ -45,6 +45,13 @@ int ttk_current_device(int* device);
  * bit 1: an out-of-range index was skipped). Synchronizes the device. */
 int ttk_device_status(unsigned* bits);
 int ttk_synchronize(void);
+/* Failure-path self test, no counterpart in the reference (whose CPU code has
+ * no device waits): one thread waits on an mbarrier that nothing arrives on,
+ * through the bounded wait every pipeline kernel here uses, with a limit of
+ * limit_ns (at most the pipelines' 2 s). The kernel gives up, sets bit 0 of
+ * the device status word and the wait site (bits 8..15), and returns; the
+ * context stays usable. */
+int ttk_selftest_wait_timeout(unsigned site, uint64_t limit_ns, void* stream);
 /* Number of kernels launched through this library so far (all streams). */
 int64_t ttk_launch_count(void);
 
@@ -70,6 +77,9 @@ int ttk_event_record(void* event, void* stream);
 int ttk_stream_wait_event(void* stream, void* event);
 int ttk_event_elapsed_ms(void* start, void* end, float* ms);
 int ttk_event_synchronize(void* event);
+/* *done = 1 when the work before the event's record has completed, else 0;
+ * never blocks. */
+int ttk_event_query(void* event, int* done);
 
 /* ------------------------------------------------------------ dense algebra */
 

@@ -546,4 +546,51 @@ int ref_time_train(const RefCfg* c, int64_t B, int64_t T, int64_t warmup, int64_
     });
 }
 
+// CPU baseline by phase, on one micro-batch of B x T random tokens: the mean
+// seconds of (zero_grad, forward, cross_entropy, backward) over `steps`
+// micro-steps after `warmup` untimed ones, and of one optimizer step (global
+// -norm clip as restated above, then AdamW::step) timed once after them. The
+// caller amortizes the optimizer over as many micro-batches as a global
+// batch holds, as gradient accumulation does. Model construction is untimed.
+int ref_time_phases(const RefCfg* c, int64_t B, int64_t T, int64_t warmup, int64_t steps,
+                    uint64_t seed, double* fb_secs, double* opt_secs) {
+    return guarded([&] {
+        tt::GPTModel m(to_cfg(c), seed);
+        auto ps = m.parameters();
+        tt::AdamW opt(ps, 3e-4f, 0.9f, 0.95f, 1e-8f, 0.1f);
+        uint64_t s = seed ? seed : 1;
+        auto next = [&]() {
+            s ^= s >> 12;
+            s ^= s << 25;
+            s ^= s >> 27;
+            return s * 0x2545F4914F6CDD1DULL;
+        };
+        std::vector<int64_t> ix(static_cast<size_t>(B * T)), tg(static_cast<size_t>(B * T));
+        double total = 0.0;
+        for (int64_t it = 0; it < warmup + steps; ++it) {
+            for (auto& v : ix)
+                v = static_cast<int64_t>(next() % static_cast<uint64_t>(c->vocab));
+            for (auto& v : tg)
+                v = static_cast<int64_t>(next() % static_cast<uint64_t>(c->vocab));
+            auto t0 = std::chrono::steady_clock::now();
+            opt.zero_grad();
+            tt::Tensor lg = m.forward(ix, B, T);
+            tt::Tensor l = tt::cross_entropy(lg, tg);
+            volatile float lv = l.data()[0];
+            (void)lv;
+            l.backward();
+            auto t1 = std::chrono::steady_clock::now();
+            release_graph(l);
+            if (it >= warmup)
+                total += std::chrono::duration<double>(t1 - t0).count();
+        }
+        *fb_secs = total / static_cast<double>(steps > 0 ? steps : 1);
+        auto t0 = std::chrono::steady_clock::now();
+        clip_grads(ps, 1.0f);
+        opt.step();
+        auto t1 = std::chrono::steady_clock::now();
+        *opt_secs = std::chrono::duration<double>(t1 - t0).count();
+    });
+}
+
 } // extern "C"

@@ -283,3 +283,12 @@ def time_train(c: RefCfg, B, T, warmup, steps, seed=42) -> float:
     _check(lib().ref_time_train(C.byref(c), C.c_int64(B), C.c_int64(T), C.c_int64(warmup),
                                 C.c_int64(steps), C.c_uint64(seed), C.byref(secs)))
     return secs.value
+
+
+def time_phases(c: RefCfg, B, T, warmup, steps, seed=42):
+    """(mean seconds of forward+CE+backward per B x T micro-step, seconds of
+    one clip + AdamW step) of the reference on random tokens."""
+    fb, op = C.c_double(0), C.c_double(0)
+    _check(lib().ref_time_phases(C.byref(c), C.c_int64(B), C.c_int64(T), C.c_int64(warmup),
+                                 C.c_int64(steps), C.c_uint64(seed), C.byref(fb), C.byref(op)))
+    return fb.value, op.value

@@ -30,5 +30,10 @@ def test_reference_arm_line():
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["d2h_bytes_per_step"] == 0
     cb = line["cpu_baseline"]
     assert cb["kind"] == "reference" and cb["cores"] == 4 and cb["value"] == line["value"]
-    assert "after 1 untimed" in cb["sample"]
+    assert "depth 1" in cb["sample"] and "depth 2" in cb["sample"]
+    parts = line["reference_parts"]
+    # full depth = rest + layers * per_layer, with the parts from the two samples
+    assert parts["micro_s"] == pytest.approx(parts["rest_s"] + 6 * parts["per_layer_s"])
+    assert parts["per_layer_s"] == pytest.approx(parts["timed"]["2"] - parts["timed"]["1"])
+    assert line["steps"] == 2 and line["steps_requested"] == 1
     assert line["config"]["workload"].startswith("llama-13m")

@@ -2,7 +2,8 @@
 
 One forward/backward micro-step of the 110M model (dim 768, 12 layers, 12
 heads of 64, ffn 2048, 1 x 1024 tokens) and of the 1B model (dim 2048, 16
-layers, 16 heads of 128, ffn 5632, 1 x 2048 tokens), vocab 32000 and tied
+layers, 16 heads of 128, ffn 5632, 1 x 512 tokens: at 1 x 2048 the
+reference's CPU step needs more than 62 GB of host memory), vocab 32000, tied
 embeddings, on weights N(0, 0.02) and tokens regenerated from the seeds the
 fixtures record (tests/golden/inputs.py). The fixtures hold the reference's
 own results (its GPTModel::forward, cross_entropy and backward, model.cpp:
@@ -25,7 +26,7 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-4
 
 
-@pytest.mark.parametrize("name", ["llama110m_1x1024", "llama1b_1x2048"])
+@pytest.mark.parametrize("name", ["llama110m_1x1024", "llama1b_1x512"])
 def test_micro_step_matches_reference(cuda, name):
     import inputs
     from tinytrain_b200.trainer import Trainer

@@ -28,6 +28,8 @@ SIGS = {
     "ttk_current_device": (I32, [P]),
     "ttk_device_status": (I32, [P]),
     "ttk_synchronize": (I32, []),
+    "ttk_selftest_wait_timeout": (I32, [C.c_uint, C.c_uint64, P]),
+    "ttk_event_query": (I32, [P, P]),
     "ttk_launch_count": (I64, []),
     "ttk_malloc": (I32, [P, SZ, P]),
     "ttk_free": (I32, [P, P]),

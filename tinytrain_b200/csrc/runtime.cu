@@ -97,6 +97,37 @@ int ttk_device_status(unsigned* bits) {
 
 int ttk_synchronize(void) { return check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize"); }
 
+}  // extern "C"
+
+namespace ttk {
+namespace selftest {
+
+// One thread waits on an mbarrier of its own shared memory that nothing
+// arrives on, through the same bounded wait the GEMM and attention pipelines
+// use, with the caller's limit. It gives up after limit_ns, records the site
+// in the device status word and returns: no fault, the context stays usable.
+__global__ void wait_timeout_selftest_kernel(unsigned site, uint64_t limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0)
+        return;
+    ttk::mbar_init(&bar, 1);
+    ttk::fence_barrier_init();
+    (void)ttk::mbar_wait_for(&bar, 0, site, limit_ns);
+}
+
+}  // namespace selftest
+}  // namespace ttk
+
+extern "C" {
+
+int ttk_selftest_wait_timeout(unsigned site, uint64_t limit_ns, void* stream) {
+    if (site > 0xffu || limit_ns == 0 || limit_ns > ttk::kWaitLimitNs)
+        return set_error(TTK_ERR_ARG, "selftest_wait_timeout: site <= 255, 0 < limit <= 2 s");
+    ttk::selftest::wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        site, limit_ns);
+    return check_launch("wait_timeout_selftest_kernel");
+}
+
 int ttk_malloc(void** ptr, size_t bytes, void* stream) {
     if (!ptr)
         return set_error(TTK_ERR_ARG, "ttk_malloc: null out pointer");
@@ -210,6 +241,17 @@ int ttk_event_elapsed_ms(void* start, void* end, float* ms) {
 
 int ttk_event_synchronize(void* event) {
     return check_cuda(cudaEventSynchronize(static_cast<cudaEvent_t>(event)), "event sync");
+}
+
+int ttk_event_query(void* event, int* done) {
+    const cudaError_t e = cudaEventQuery(static_cast<cudaEvent_t>(event));
+    if (e == cudaErrorNotReady) {
+        cudaGetLastError();  // not an error: clear it
+        *done = 0;
+        return TTK_OK;
+    }
+    *done = 1;
+    return check_cuda(e, "event query");
 }
 
 // ------------------------------------------------------------------ GEMM --

@@ -78,8 +78,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete. Returns false
-// (and flags the device status) if the limit expires.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned site = 0) {
+// (and flags the device status with the wait site) if `limit_ns` expires.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, unsigned site,
+                                              uint64_t limit_ns) {
     if (mbar_try_wait(bar, parity))
         return true;
     uint64_t t0 = globaltimer_ns();
@@ -87,11 +88,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
         for (int i = 0; i < 64; ++i)
             if (mbar_try_wait(bar, parity))
                 return true;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        if (globaltimer_ns() - t0 > limit_ns) {
             report(kErrWaitTimeout | ((site & 0xffu) << 8));
             return false;
         }
     }
+}
+
+// The pipelines' wait: bounded at kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned site = 0) {
+    return mbar_wait_for(bar, parity, site, kWaitLimitNs);
 }
 
 // --------------------------------------------------------------------- TMA --

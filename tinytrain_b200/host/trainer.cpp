@@ -12,6 +12,9 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <functional>
+#include <thread>
+#include <chrono>
 #include <filesystem>
 #include <fstream>
 #include <map>
@@ -71,6 +74,36 @@ int64_t plan_arena(const std::vector<int64_t>& sizes, int64_t cap, std::vector<i
     return off;
 }
 
+// Bounded wait for the collectives of a data-parallel step (the reference has
+// no distributed code; this is the failure path of the exchange step). Polls
+// `done` every poll_ms and, while waiting, `async_error` (the communicator's
+// asynchronous error state). On an error, or once timeout_s has passed (a
+// peer that left or hangs never joins the collective), calls `abort` once and
+// returns 1 (error) or 2 (timeout) with the reason in `why`; 0 when done.
+int watch_collectives(const std::function<int()>& done, const std::function<int()>& async_error,
+                      const std::function<void()>& abort, double timeout_s, double poll_ms,
+                      std::string& why) {
+    const auto t0 = std::chrono::steady_clock::now();
+    while (true) {
+        if (done())
+            return 0;
+        if (async_error()) {
+            why = "the communicator reported an asynchronous error; aborted";
+            abort();
+            return 1;
+        }
+        const double waited =
+            std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (waited > timeout_s) {
+            why = "collectives did not complete within " + std::to_string(timeout_s) +
+                  " s (a peer left or hangs); aborted";
+            abort();
+            return 2;
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(static_cast<int64_t>(poll_ms * 1e3)));
+    }
+}
+
 struct Trainer {
     GPTConfig cfg;
     std::unique_ptr<GPTModel> model;
@@ -90,14 +123,50 @@ struct Trainer {
     std::unordered_map<Tensor::Impl*, int> bucket_of;
     std::vector<void*> bucket_events;
     void* done_event = nullptr;
+    // collective watchdog: the end of the last distributed step, its deadline
+    void* step_event = nullptr;
+    bool step_pending = false;
+    double coll_timeout_s = 300.0;
+    std::string dist_error;  // set once the communicator was aborted
+    // Optional timing of the gradient all-reduce: per bucket, events around
+    // its all-reduce on the comm stream; per step, the compute stream's end
+    // of backward against the end of the last all-reduce (the exposed tail).
+    bool comm_prof = false;
+    struct CommRec {
+        void *a, *b;
+    };
+    std::vector<CommRec> comm_recs, tail_recs;
+    std::vector<void*> event_pool;
+    void* pooled_event() {
+        void* e = nullptr;
+        if (!event_pool.empty()) {
+            e = event_pool.back();
+            event_pool.pop_back();
+        } else {
+            check(ttk_event_create(&e), "event");
+        }
+        return e;
+    }
 
     ~Trainer() {
         tt::set_grad_ready_hook(nullptr);
+        try {
+            wait_dist();
+        } catch (const std::exception&) {
+        }
         void* s = stream_if_ready();
         if (s)
             ttk_stream_synchronize(s);
         if (comm)
             ttk_dist_destroy(comm);
+        if (step_event)
+            ttk_event_destroy(step_event);
+        for (auto& r : comm_recs)
+            event_pool.push_back(r.a), event_pool.push_back(r.b);
+        for (auto& r : tail_recs)
+            event_pool.push_back(r.a), event_pool.push_back(r.b);
+        for (void* e : event_pool)
+            ttk_event_destroy(e);
         for (void* e : bucket_events)
             ttk_event_destroy(e);
         if (done_event)
@@ -166,7 +235,16 @@ struct Trainer {
         Bucket& bk = buckets[static_cast<size_t>(b)];
         check(ttk_event_record(bucket_events[static_cast<size_t>(b)], stream()), "record");
         check(ttk_stream_wait_event(comm_stream, bucket_events[static_cast<size_t>(b)]), "wait");
+        CommRec r{nullptr, nullptr};
+        if (comm_prof) {
+            r = {pooled_event(), pooled_event()};
+            check(ttk_event_record(r.a, comm_stream), "record");
+        }
         check(ttk_dist_allreduce_f32(comm, arena + bk.offset, bk.count, comm_stream), "allreduce");
+        if (comm_prof) {
+            check(ttk_event_record(r.b, comm_stream), "record");
+            comm_recs.push_back(r);
+        }
     }
 
     // Runs fwd+bwd over n_micro micro-batches; ids are device pointers.
@@ -200,6 +278,12 @@ struct Trainer {
                     if (buckets[b].pending > 0)
                         launch_bucket(static_cast<int>(b));
                 check(ttk_event_record(done_event, comm_stream), "record");
+                if (comm_prof) {
+                    CommRec r{pooled_event(), pooled_event()};
+                    check(ttk_event_record(r.a, stream()), "record");  // backward done
+                    check(ttk_event_record(r.b, comm_stream), "record");  // all-reduces done
+                    tail_recs.push_back(r);
+                }
                 check(ttk_stream_wait_event(stream(), done_event), "wait");
             }
         }
@@ -219,6 +303,54 @@ struct Trainer {
         opt->set_lr(lr);
         opt->set_grad_scale(1.0f / static_cast<float>(n_micro * world));
         opt->step();
+    }
+
+    // Distributed steps: before a step, the previous one's collectives must
+    // have completed within the deadline (at most one step in flight); after
+    // it, its end is recorded for the next check.
+    void begin_step() {
+        if (!dist_error.empty())
+            throw std::runtime_error("data-parallel step refused: the communicator was aborted (" +
+                                     dist_error + ")");
+        wait_dist();
+    }
+
+    void end_step() {
+        if (!comm)
+            return;
+        if (!step_event)
+            check(ttk_event_create(&step_event), "event");
+        check(ttk_event_record(step_event, stream()), "record");
+        step_pending = true;
+    }
+
+    // Bounded wait for the recorded step end. On an asynchronous NCCL error
+    // or a deadline overrun (a peer left or hangs) the communicator is
+    // aborted, which ends the pending collectives, and the step throws.
+    void wait_dist() {
+        if (!comm || !step_pending)
+            return;
+        std::string why;
+        const int rc = watch_collectives(
+            [&] {
+                int d = 0;
+                check(ttk_event_query(step_event, &d), "event query");
+                return d;
+            },
+            [&] {
+                int e = 0;
+                return ttk_dist_async_error(comm, &e) != TTK_OK || e != 0 ? 1 : 0;
+            },
+            [&] { ttk_dist_abort(comm); }, coll_timeout_s, 1.0, why);
+        step_pending = false;
+        if (rc == 0)
+            return;
+        comm = nullptr;  // freed by the abort
+        dist_error = why;
+        ttk_stream_synchronize(stream());  // the aborted collectives have returned
+        if (comm_stream)
+            ttk_stream_synchronize(comm_stream);
+        throw std::runtime_error("data-parallel step: " + why);
     }
 };
 
@@ -416,9 +548,11 @@ int tt_trainer_step_device(void* h, const int64_t* idx, const int64_t* targets, 
         Trainer* t = T_(h);
         if (B <= 0 || T <= 0 || n_micro <= 0)
             throw std::invalid_argument("step: sizes must be positive");
+        t->begin_step();
         t->zero_grads();
         t->accumulate(idx, targets, B, T, n_micro);
         t->optimizer_step(n_micro, lr);
+        t->end_step();
     });
 }
 
@@ -437,9 +571,12 @@ int tt_trainer_step(void* h, const int64_t* idx, const int64_t* targets, int64_t
         check(ttk_memcpy_h2d(d.ptr, idx, static_cast<size_t>(n) * 8, stream()), "ids");
         check(ttk_memcpy_h2d(d.as<int64_t>() + n, targets, static_cast<size_t>(n) * 8, stream()),
               "ids");
+        t->begin_step();
         t->zero_grads();
         t->accumulate(d.as<int64_t>(), d.as<int64_t>() + n, B, T, n_micro);
         t->optimizer_step(n_micro, lr);
+        t->end_step();
+        t->wait_dist();  // bounded, before the blocking loss read
         if (loss)
             check(ttk_memcpy_d2h(loss, t->loss_out, 4, stream()), "loss read");
         if (grad_norm)
@@ -629,6 +766,56 @@ int tt_plan_buckets(const int64_t* sizes, int n, int64_t bucket_bytes, int64_t* 
             bucket_count[b] = bk[b].count;
         }
         *n_buckets = static_cast<int>(bk.size());
+    });
+}
+
+int tt_trainer_comm_profile(void* h, int on) {
+    return guarded([&] { T_(h)->comm_prof = on != 0; });
+}
+
+int tt_trainer_comm_stats(void* h, double* allreduce_ms, double* tail_ms, int64_t* n_allreduce,
+                          int64_t* n_steps) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        double busy = 0.0, tail = 0.0;
+        for (auto& r : t->comm_recs) {
+            float ms = 0.0f;
+            check(ttk_event_synchronize(r.b), "event sync");
+            check(ttk_event_elapsed_ms(r.a, r.b, &ms), "elapsed");
+            busy += ms;
+            t->event_pool.push_back(r.a), t->event_pool.push_back(r.b);
+        }
+        for (auto& r : t->tail_recs) {
+            float ms = 0.0f;
+            check(ttk_event_synchronize(r.b), "event sync");
+            check(ttk_event_synchronize(r.a), "event sync");
+            check(ttk_event_elapsed_ms(r.a, r.b, &ms), "elapsed");
+            tail += ms > 0.0f ? ms : 0.0;
+            t->event_pool.push_back(r.a), t->event_pool.push_back(r.b);
+        }
+        *allreduce_ms = busy;
+        *tail_ms = tail;
+        *n_allreduce = static_cast<int64_t>(t->comm_recs.size());
+        *n_steps = static_cast<int64_t>(t->tail_recs.size());
+        t->comm_recs.clear();
+        t->tail_recs.clear();
+    });
+}
+
+int tt_trainer_set_collective_timeout(void* h, double seconds) {
+    return guarded([&] {
+        if (!(seconds > 0.0))
+            throw std::invalid_argument("collective timeout must be positive");
+        T_(h)->coll_timeout_s = seconds;
+    });
+}
+
+int tt_watchdog_selftest(int (*done)(void*), int (*async_error)(void*), int (*abort)(void*),
+                         void* ctx, double timeout_s, int* outcome) {
+    return guarded([&] {
+        std::string why;
+        *outcome = watch_collectives([&] { return done(ctx); }, [&] { return async_error(ctx); },
+                                     [&] { abort(ctx); }, timeout_s, 1.0, why);
     });
 }
 

@@ -54,6 +54,10 @@ _SIGS = {
     "tt_trainer_last_loss": (C.c_int, [P, P]),
     "tt_trainer_forward_backward": (C.c_int, [P, P, P, I64, I64, P, P]),
     "tt_trainer_dist_init": (C.c_int, [P, C.c_int, C.c_int, P, I64]),
+    "tt_trainer_set_collective_timeout": (C.c_int, [P, C.c_double]),
+    "tt_trainer_comm_profile": (C.c_int, [P, C.c_int]),
+    "tt_trainer_comm_stats": (C.c_int, [P, P, P, P, P]),
+    "tt_watchdog_selftest": (C.c_int, [P, P, P, P, C.c_double, P]),
     "tt_kernel_launches": (I64, []),
     "tt_fused_attention_chains": (I64, []),
     "tt_plan_buckets": (C.c_int, [P, C.c_int, I64, P, P, P, P, P]),
@@ -98,6 +102,20 @@ def kernel_launches() -> int:
 def fused_attention_chains() -> int:
     """Attention-score op chains run as the fused kernel since start-up."""
     return int(lib().tt_fused_attention_chains())
+
+
+_PROBE = C.CFUNCTYPE(C.c_int, C.c_void_p)
+
+
+def watchdog_selftest(done, async_error, abort, timeout_s):
+    """Runs the collective watchdog's wait loop on Python probes (callables
+    without arguments returning int); returns its outcome (0 done, 1 error,
+    2 timeout)."""
+    cbs = [_PROBE(lambda _c, f=f: int(f())) for f in (done, async_error, abort)]
+    out = C.c_int(-1)
+    _chk(lib().tt_watchdog_selftest(C.cast(cbs[0], P), C.cast(cbs[1], P), C.cast(cbs[2], P),
+                                    None, float(timeout_s), C.byref(out)), "watchdog selftest")
+    return out.value
 
 
 def set_stream(stream_handle: int):
@@ -177,6 +195,22 @@ class Trainer:
             self.h, idx.ctypes.data, targets.ctypes.data, B, T, C.byref(loss),
             None if logits is None else logits.ctypes.data), "forward_backward")
         return loss.value, logits
+
+    def set_collective_timeout(self, seconds):
+        """Deadline for a distributed step's collectives; on an overrun or an
+        asynchronous NCCL error the communicator is aborted and the step fails."""
+        _chk(lib().tt_trainer_set_collective_timeout(self.h, float(seconds)), "collective timeout")
+
+    def comm_profile(self, on=True):
+        _chk(lib().tt_trainer_comm_profile(self.h, int(on)), "comm profile")
+
+    def comm_stats(self):
+        """(all-reduce ms summed over buckets, exposed tail ms summed over
+        steps, all-reduce count, step count) since the last read."""
+        a, t, n, k = C.c_double(0), C.c_double(0), C.c_int64(0), C.c_int64(0)
+        _chk(lib().tt_trainer_comm_stats(self.h, C.byref(a), C.byref(t), C.byref(n), C.byref(k)),
+             "comm stats")
+        return a.value, t.value, n.value, k.value
 
     def dist_init(self, rank, world, uid: bytes, bucket_bytes=64 << 20):
         buf = (C.c_ubyte * 128).from_buffer_copy(uid)

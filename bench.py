@@ -156,14 +156,18 @@ def reference_micro_step(w):
 
     The sample is one micro-step of CPU_SAMPLE tokens at the config's width
     and sequence length: forward, cross-entropy and backward of the
-    reference's GPTModel, timed at depth 1 and at depth 2. The reference runs
-    its layers one after another with the same ops, so a full-depth micro-step
-    costs rest + L * per_layer with per_layer = t(2) - t(1) and rest = t(1) -
-    per_layer (which also absorbs the first layer's one-time costs: process
-    warm-up, allocator growth). The optimizer step (clip + AdamW, linear in the
-    parameter count) is timed on the depth-2 model, scaled to the full
-    parameter count, and amortized over the micro-steps of one global batch,
-    as gradient accumulation does. Returns a dict with tokens/s and the parts.
+    reference's GPTModel, timed at depth 1 and at depth 2, each after one
+    untimed micro-step (the first step of a process pays page faults and
+    allocator growth: 77 s against 51 s warm at depth 1 of the 1B width). The
+    reference runs its layers one after another with the same ops, so a
+    full-depth micro-step costs base + L * per_layer with per_layer = t(2) -
+    t(1) and base = t(1) - per_layer. Measured at the 1B width on 8 cores, a
+    third layer added 53 s against 57 s for the second: the per-layer cost is
+    flat to slightly falling, so the estimate is at most a few percent off. The
+    optimizer step (clip + AdamW, linear in the parameter count) is timed on
+    the depth-2 model, scaled to the full parameter count, and amortized over
+    the micro-steps of one global batch, as gradient accumulation does.
+    Returns a dict with tokens/s and the parts.
     """
     from oracle import refbind as rb
     if not rb.available():
@@ -174,7 +178,7 @@ def reference_micro_step(w):
     for d in (d1, d2):
         c = rb.cfg(vocab=w["vocab"], dim=w["dim"], layers=d, heads=w["heads"], ffn=w["ffn"],
                    max_seq=max(w["max_seq"], T))
-        t[d], opt[d] = rb.time_phases(c, B, T, 0, 1)
+        t[d], opt[d] = rb.time_phases(c, B, T, 1, 1)
     per_layer = (t[d2] - t[d1]) / (d2 - d1)
     rest = t[d1] - d1 * per_layer
     micro = rest + w["layers"] * per_layer
@@ -185,7 +189,8 @@ def reference_micro_step(w):
     tps = w["global_batch"] * w["seq"] / step
     sample = (f"reference train step at the {w['model']} width, one micro-step of {B} x {T} "
               f"tokens (forward, cross-entropy, backward) timed at depth {d1} ({t[d1]:.1f} s) and "
-              f"depth {d2} ({t[d2]:.1f} s): {per_layer:.1f} s per layer + {rest:.1f} s rest, "
+              f"depth {d2} ({t[d2]:.1f} s), each after one untimed micro-step: "
+              f"{per_layer:.1f} s per layer + {rest:.1f} s base, "
               f"{micro:.0f} s per full-depth ({w['layers']} layers) micro-step; clip + AdamW "
               f"{opt_full:.1f} s (timed at depth {d2}, scaled to {n_params(w)} parameters) "
               f"amortized over the {n_micro:.0f} micro-steps of a {w['global_batch']} x {w['seq']} "

@@ -885,7 +885,7 @@ int attention_mma_forward(int hd, const float* q, const float* k, const float* v
     __nv_bfloat16* w = static_cast<__nv_bfloat16*>(ws);
     fa::SplitBufs s{w, w + n, w + 2 * n, w + 3 * n, w + 4 * n, w + 5 * n, nullptr, nullptr};
     switch (hd) {
-        case 32: return fa::fwd<32>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, false, st);
+        case 32: return fa::fwd<32>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st);
         case 64: return fa::fwd<64>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st);
         default: return fa::fwd<128>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st);
     }
@@ -919,7 +919,7 @@ int attention_mma_backward(int hd, const float* q, const float* k, const float* 
     switch (hd) {
         case 32:
             return fa::bwd<32>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                               scale, s, Dv, ld, false, st, ready);
+                               scale, s, Dv, ld, tc, st, ready);
         case 64:
             return fa::bwd<64>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
                                scale, s, Dv, ld, tc, st, ready);

@@ -302,14 +302,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 return false;
             tc_fence_after();
             const uint32_t base = tmem + lane_off + CF::O_COL + (i & 1) * HD + half * OH;
+            constexpr int W = OH < 32 ? OH : 32;  // columns per TMEM load
 #pragma unroll
-            for (int c = 0; c < OH; c += 32) {
-                float v[32];
-                tmem_ld_32x32b_x32(base + c, v);
+            for (int c = 0; c < OH; c += W) {
+                float v[W];
+                if constexpr (W == 32)
+                    tmem_ld_32x32b_x32(base + c, v);
+                else
+                    tmem_ld_32x32b_x16(base + c, v);
                 tmem_ld_wait();
                 // acc = acc * scale + v, two lanes per packed FMA (same rounding)
 #pragma unroll
-                for (int e = 0; e < 32; e += 2) {
+                for (int e = 0; e < W; e += 2) {
                     const float2 r = __ffma2_rn(make_float2(acc[c + e], acc[c + e + 1]),
                                                 make_float2(scale, scale),
                                                 make_float2(v[e], v[e + 1]));
@@ -496,23 +500,22 @@ __device__ __forceinline__ uint64_t small_mn_desc(uint32_t plane, int ks) {
 template <int HD>
 __device__ __forceinline__ void load_owned(uint32_t taddr, int grp, float (&v)[HD / 2]) {
     constexpr int QW = HD / 4, HH = HD / 2;
+    float a[QW], b[QW];
     if constexpr (QW == 32) {
-        float a[32], b[32];
         tmem_ld_32x32b_x32(taddr + grp * QW, a);
         tmem_ld_32x32b_x32(taddr + HH + grp * QW, b);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e)
-            v[e] = a[e], v[QW + e] = b[e];
-    } else {
-        float a[16], b[16];
+    } else if constexpr (QW == 16) {
         tmem_ld_32x32b_x16(taddr + grp * QW, a);
         tmem_ld_32x32b_x16(taddr + HH + grp * QW, b);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-            v[e] = a[e], v[QW + e] = b[e];
+    } else {
+        static_assert(QW == 8, "head dims 32, 64, 128");
+        tmem_ld_32x32b_x8(taddr + grp * QW, a);
+        tmem_ld_32x32b_x8(taddr + HH + grp * QW, b);
     }
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < QW; ++e)
+        v[e] = a[e], v[QW + e] = b[e];
 }
 
 // Store owned columns of one gradient row (scaled; RoPE transpose rotation
@@ -1170,7 +1173,7 @@ static int make_plane_map(CUtensorMap* map, const __nv_bfloat16* hi, int64_t n, 
     return TTK_OK;
 }
 
-bool attention_tc_supported(int hd) { return hd == 64 || hd == 128; }
+bool attention_tc_supported(int hd) { return hd == 32 || hd == 64 || hd == 128; }
 
 int attention_tc_forward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat16* kh,
                               const __nv_bfloat16* vh, float* o, float* lse, int64_t B, int64_t T,
@@ -1185,19 +1188,20 @@ int attention_tc_forward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat
     if (rc)
         return rc;
     dim3 grid(static_cast<unsigned>((T + fatc::BQ - 1) / fatc::BQ), static_cast<unsigned>(B * H));
-    if (hd == 128) {
-        const int smem = fatc::FwdCfg<128>::BYTES;
-        cudaFuncSetAttribute(fatc::attn_fwd_tc<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    auto launch = [&](auto hd_tag) {
+        constexpr int HD = decltype(hd_tag)::value;
+        const int smem = fatc::FwdCfg<HD>::BYTES;
+        cudaFuncSetAttribute(fatc::attn_fwd_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem);
-        fatc::attn_fwd_tc<128><<<grid, fatc::NUM_THREADS, smem, st>>>(mq, mk, mv, o, lse, T,
-                                                                       static_cast<int>(H));
-    } else {
-        const int smem = fatc::FwdCfg<64>::BYTES;
-        cudaFuncSetAttribute(fatc::attn_fwd_tc<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             smem);
-        fatc::attn_fwd_tc<64><<<grid, fatc::NUM_THREADS, smem, st>>>(mq, mk, mv, o, lse, T,
+        fatc::attn_fwd_tc<HD><<<grid, fatc::NUM_THREADS, smem, st>>>(mq, mk, mv, o, lse, T,
                                                                       static_cast<int>(H));
-    }
+    };
+    if (hd == 128)
+        launch(std::integral_constant<int, 128>{});
+    else if (hd == 64)
+        launch(std::integral_constant<int, 64>{});
+    else
+        launch(std::integral_constant<int, 32>{});
     return check_launch("attn_fwd_tc");
 }
 
@@ -1240,7 +1244,9 @@ int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloa
     };
     if (hd == 128)
         return launch(std::integral_constant<int, 128>{});
-    return launch(std::integral_constant<int, 64>{});
+    if (hd == 64)
+        return launch(std::integral_constant<int, 64>{});
+    return launch(std::integral_constant<int, 32>{});
 }
 
 }  // namespace ttk

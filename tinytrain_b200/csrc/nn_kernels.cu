@@ -426,6 +426,12 @@ __global__ void __launch_bounds__(CE_THREADS, 1)
     const bool vec = (C & 3) == 0;
     for (int64_t row = blockIdx.x; row < N; row += gridDim.x) {
         const float* xr = logits + row * C;
+        const int64_t t = targets[row];
+        const bool t_ok = t >= 0 && t < C;
+        // The target's logit is read before the first barrier of the row: no
+        // thread writes the row's gradient before the second one, so the
+        // read sees the logit even when dlogits aliases logits.
+        const float x_t = (threadIdx.x == 0 && t_ok) ? xr[t] : 0.0f;
         float v[IN_REGS ? CE_VEC * 4 : 1];
         float m = -INFINITY;
         if (IN_REGS) {
@@ -471,11 +477,9 @@ __global__ void __launch_bounds__(CE_THREADS, 1)
         s = s_redd[lane];
         s = warp_sum_d(s);
         const float lse = m + static_cast<float>(log(s));
-        const int64_t t = targets[row];
-        const bool t_ok = t >= 0 && t < C;
         if (threadIdx.x == 0) {
             if (t_ok)
-                atomicAdd(loss_acc, static_cast<double>(-(xr[t] - lse)));
+                atomicAdd(loss_acc, static_cast<double>(-(x_t - lse)));
             else
                 report(kErrBadIndex);
         }

@@ -201,6 +201,14 @@ int ttk_profile_read(double* gemm_ms, double* gemm_flops, int64_t* launches);
  * (ops.cpp:932-942). */
 int ttk_rmsnorm_fwd(const float* x, const float* w, float* y, float* rstd, int64_t R, int64_t D,
                     float eps, void* stream);
+/* ttk_rmsnorm_fwd that also writes the bf16x3 GEMM operand planes of y into
+ * `split` (ttk_gemm_split_bytes(1, R, D) bytes, the ttk_gemm_split layout),
+ * equal bit for bit to ttk_gemm_split(y, R, D, D, 0, 1, split): the split
+ * pass before the GEMMs that read y (the q/k/v, gate/up and LM-head
+ * projections of the model) is saved. D a multiple of 256, the bf16x3
+ * precision; no counterpart in the reference. */
+int ttk_rmsnorm_fwd_split(const float* x, const float* w, float* y, float* rstd, int64_t R,
+                          int64_t D, float eps, void* split, void* stream);
 /* dx (+)= rstd*w*dy - x*rstd^3/D*sum(dy*w*x); dw += sum_rows(dy*x*rstd).
  * dx may be NULL. dw (when not NULL) is always accumulated; `workspace`
  * (device) must hold ttk_rmsnorm_bwd_workspace_size(R, D) bytes. */

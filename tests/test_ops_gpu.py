@@ -31,6 +31,23 @@ def status_ok():
     return _ttk.device_status() == 0
 
 
+@pytest.mark.parametrize("R,D", [(4096, 2048), (1000, 768), (333, 256)])
+def test_rmsnorm_fwd_split_planes_bitexact(cuda, R, D):
+    """ttk_rmsnorm_fwd_split: y equals ttk_rmsnorm_fwd's and the planes equal
+    ttk_gemm_split(y), bit for bit."""
+    from tinytrain_b200 import kernels as K
+    g = torch.Generator(device=cuda).manual_seed(R + D)
+    x = torch.randn(R, D, device=cuda, generator=g) * 3
+    w = torch.rand(D, device=cuda, generator=g) + 0.5
+    y0, r0 = K.rmsnorm_fwd(x, w, 1e-5)
+    y1, r1, planes = K.rmsnorm_fwd_split(x, w, 1e-5)
+    ref = K.gemm_split(y1)
+    torch.cuda.synchronize()
+    assert torch.equal(y0, y1) and torch.equal(r0, r1)
+    assert torch.equal(planes, ref)
+    assert status_ok()
+
+
 def test_rmsnorm_golden(cuda, golden_ops):
     from tinytrain_b200 import kernels as K
     g = golden_ops

@@ -74,6 +74,7 @@ SIGS = {
     "ttk_profile_enable": (I32, [I32]),
     "ttk_profile_read": (I32, [P, P, P]),
     "ttk_rmsnorm_fwd": (I32, [P, P, P, P, I64, I64, F32, P]),
+    "ttk_rmsnorm_fwd_split": (I32, [P, P, P, P, I64, I64, F32, P, P]),
     "ttk_rmsnorm_bwd_workspace_size": (SZ, [I64, I64]),
     "ttk_rmsnorm_bwd": (I32, [P, P, P, P, P, I32, P, I64, I64, P, SZ, P]),
     "ttk_swiglu_fwd": (I32, [P, P, P, I64, P]),

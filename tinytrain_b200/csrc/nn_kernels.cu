@@ -121,9 +121,15 @@ __device__ __forceinline__ float block_row_sum(float v, float* red, int slot, in
     return tot;
 }
 
+// With `split` (bf16x3 GEMM operand planes [2][R][D], the ttk_gemm_split
+// layout for D a multiple of 32) the kernel also writes the split of y, with
+// the split kernel's arithmetic (split_bf16), so the planes equal
+// ttk_gemm_split(y) bit for bit and the split pass before the GEMMs that
+// read y is skipped.
 __global__ void rmsnorm_fwd_rows_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                         float* __restrict__ y, float* __restrict__ rstd,
-                                        int64_t R, int64_t D, float eps) {
+                                        int64_t R, int64_t D, float eps,
+                                        __nv_bfloat16* __restrict__ split) {
     __shared__ float red[2 * 8 * 32];
     const int tpr = static_cast<int>(D / RMS_EPT);
     const int rpb = blockDim.x / tpr;
@@ -157,10 +163,28 @@ __global__ void rmsnorm_fwd_rows_kernel(const float* __restrict__ x, const float
             const float r = 1.0f / sqrtf(ss / static_cast<float>(D) + eps);
             if (t == 0 && rstd)
                 rstd[row] = r;
-            *reinterpret_cast<float4*>(y + row * D + c0) =
+            const float4 y0 =
                 make_float4(a.x * r * w0.x, a.y * r * w0.y, a.z * r * w0.z, a.w * r * w0.w);
-            *reinterpret_cast<float4*>(y + row * D + c1) =
+            const float4 y1 =
                 make_float4(b.x * r * w1.x, b.y * r * w1.y, b.z * r * w1.z, b.w * r * w1.w);
+            *reinterpret_cast<float4*>(y + row * D + c0) = y0;
+            *reinterpret_cast<float4*>(y + row * D + c1) = y1;
+            if (split) {
+                const int64_t plane = R * D;
+                const float4 ys[2] = {y0, y1};
+                const int64_t cs[2] = {c0, c1};
+#pragma unroll
+                for (int g = 0; g < 2; ++g) {
+                    const float v[4] = {ys[g].x, ys[g].y, ys[g].z, ys[g].w};
+                    __nv_bfloat16 hi[4], lo[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        split_bf16(v[j], hi[j], lo[j]);
+                    __nv_bfloat16* d = split + row * D + cs[g];
+                    *reinterpret_cast<uint2*>(d) = *reinterpret_cast<const uint2*>(hi);
+                    *reinterpret_cast<uint2*>(d + plane) = *reinterpret_cast<const uint2*>(lo);
+                }
+            }
         }
         a = na, b = nb;
     }
@@ -830,11 +854,30 @@ int ttk_rmsnorm_fwd(const float* x, const float* w, float* y, float* rstd, int64
         const int tpr = static_cast<int>(D / RMS_EPT), bs = rms_block(D);
         const int64_t blocks = std::min<int64_t>((R + bs / tpr - 1) / (bs / tpr), 148 * 8);
         rmsnorm_fwd_rows_kernel<<<static_cast<int>(blocks), bs, 0, S(stream)>>>(x, w, y, rstd, R,
-                                                                                 D, eps);
+                                                                                 D, eps, nullptr);
         return check_launch("rmsnorm_fwd_rows_kernel");
     }
     rmsnorm_fwd_kernel<<<grid_for(R, 8), 256, 0, S(stream)>>>(x, w, y, rstd, R, D, eps);
     return check_launch("rmsnorm_fwd_kernel");
+}
+
+int ttk_rmsnorm_fwd_split(const float* x, const float* w, float* y, float* rstd, int64_t R,
+                          int64_t D, float eps, void* split, void* stream) {
+    if (R < 0 || D <= 0 || !x || !w || !y || !split)
+        return set_error(TTK_ERR_ARG, "rmsnorm_fwd_split: bad arguments");
+    if (!rms_rows_ok(D))
+        return set_error(TTK_ERR_ARG, "rmsnorm_fwd_split: D must be a multiple of 256");
+    if (ttk_gemm_get_precision() != 0)
+        return set_error(TTK_ERR_ARG, "rmsnorm_fwd_split: planes exist for the bf16x3 precision");
+    if (!(aligned16(x) && aligned16(w) && aligned16(y) && aligned16(split)))
+        return set_error(TTK_ERR_ARG, "rmsnorm_fwd_split: tensors must be 16-byte aligned");
+    if (R == 0)
+        return TTK_OK;
+    const int tpr = static_cast<int>(D / RMS_EPT), bs = rms_block(D);
+    const int64_t blocks = std::min<int64_t>((R + bs / tpr - 1) / (bs / tpr), 148 * 8);
+    rmsnorm_fwd_rows_kernel<<<static_cast<int>(blocks), bs, 0, S(stream)>>>(
+        x, w, y, rstd, R, D, eps, static_cast<__nv_bfloat16*>(split));
+    return check_launch("rmsnorm_fwd_rows_kernel");
 }
 
 static int colsum_grid(int64_t D) {

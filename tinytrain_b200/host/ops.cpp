@@ -1047,9 +1047,34 @@ Tensor rmsnorm(const Tensor& a, const Tensor& weight, float eps) {
     const int64_t R = a.numel() / D;
     Tensor out = make_out(a.shape(), a.requires_grad() || weight.requires_grad());
     auto rstd = std::make_shared<Buffer>(R);
-    check(ttk_rmsnorm_fwd(dread(a.impl()), dread(weight.impl()), out_ptr(out),
-                          rstd->device_for_overwrite(), R, D, eps, stream()),
-          "rmsnorm");
+    // Outputs large enough to feed tensor-core GEMMs get their bf16x3 operand
+    // planes from the same kernel, cached on the output buffer as a GEMM
+    // operand split of [R, D] rows (what linear() looks up): the projections
+    // that read the output skip their split pass. Same planes, same results.
+    const bool planes = D % 256 == 0 && R * D >= (1 << 20) && ttk_gemm_get_precision() == 0;
+    if (planes) {
+        float* y = out_ptr(out);
+        Buffer& ob = *out.impl()->data;
+        const size_t bytes = ttk_gemm_split_bytes(1, R, D);
+        if (ob.split_bytes < bytes) {
+            ttk_free(ob.split_dev, stream());
+            ob.split_dev = nullptr;
+            ob.split_bytes = 0;
+            check(ttk_malloc(&ob.split_dev, bytes, stream()), "rmsnorm planes");
+            ob.split_bytes = bytes;
+        }
+        check(ttk_rmsnorm_fwd_split(dread(a.impl()), dread(weight.impl()), y,
+                                    rstd->device_for_overwrite(), R, D, eps, ob.split_dev,
+                                    stream()),
+              "rmsnorm");
+        const int64_t key[7] = {0, 1, R, D, D, 0, 0};
+        ob.split_version = ob.version;
+        std::copy(key, key + 7, ob.split_key);
+    } else {
+        check(ttk_rmsnorm_fwd(dread(a.impl()), dread(weight.impl()), out_ptr(out),
+                              rstd->device_for_overwrite(), R, D, eps, stream()),
+              "rmsnorm");
+    }
     if (out.requires_grad()) {
         auto ao = a.impl(), wo = weight.impl();
         Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle

@@ -70,6 +70,24 @@ def rmsnorm_fwd(x, w, eps):
     return y, rstd
 
 
+def rmsnorm_fwd_split(x, w, eps):
+    """(y, rstd, planes): the forward plus y's bf16x3 GEMM operand planes."""
+    R, D = x.shape
+    y = torch.empty_like(x)
+    rstd = torch.empty(R, dtype=torch.float32, device=x.device)
+    planes = workspace(call("ttk_gemm_split_bytes", 1, R, D), x.device)
+    call("ttk_rmsnorm_fwd_split", _p(x), _p(w), _p(y), _p(rstd), R, D, eps, _p(planes), _s())
+    return y, rstd, planes
+
+
+def gemm_split(x):
+    """bf16x3 operand planes of a 2-D fp32 tensor (ttk_gemm_split)."""
+    R, D = x.shape
+    planes = workspace(call("ttk_gemm_split_bytes", 1, R, D), x.device)
+    call("ttk_gemm_split", _p(x), R, D, D, 0, 1, _p(planes), _s())
+    return planes
+
+
 def rmsnorm_bwd(x, w, rstd, dy, dx=None, dw=None, accumulate=False):
     R, D = x.shape
     if dx is None:

@@ -538,6 +538,109 @@ __global__ void __launch_bounds__(CE_THREADS, 1)
     }
 }
 
+// Rows of at most 32768 logits with C a multiple of 4: the same arithmetic as
+// cross_entropy_kernel<true> (identical results), with the next row streamed
+// into shared memory by one bulk copy while the current row is reduced and
+// its gradient written, so the row reads overlap the gradient writes. One
+// 1024-thread block per SM. Thread 0 waits on the copy's mbarrier with the
+// bounded wait; on expiry the block stops (device status set) after waiting
+// once more for the copy it issued.
+__global__ void __launch_bounds__(CE_THREADS, 1)
+    cross_entropy_bulk_kernel(const float* __restrict__ logits,
+                              const int64_t* __restrict__ targets, int64_t N, int64_t C,
+                              double* __restrict__ loss_acc, float* __restrict__ dlogits,
+                              float grad_scale) {
+    extern __shared__ __align__(16) float srow[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float s_red[32];
+    __shared__ double s_redd[32];
+    __shared__ int s_ok;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t bytes = static_cast<uint32_t>(C) * 4u;
+    int64_t row = blockIdx.x;
+    if (row >= N)
+        return;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+        mbar_arrive_expect_tx(&bar, bytes);
+        bulk_load(srow, logits + row * C, bytes, &bar);
+    }
+    uint32_t phase = 0;
+    for (; row < N; row += gridDim.x) {
+        if (threadIdx.x == 0)
+            s_ok = mbar_wait(&bar, phase, 80) ? 1 : 0;
+        __syncthreads();
+        if (!s_ok) {
+            if (threadIdx.x == 0)
+                mbar_wait(&bar, phase, 81);  // the copy in flight lands before exit
+            return;
+        }
+        phase ^= 1u;
+        const int64_t t = targets[row];
+        const bool t_ok = t >= 0 && t < C;
+        const float x_t = (threadIdx.x == 0 && t_ok) ? srow[t] : 0.0f;
+        float v[CE_VEC * 4];
+        float m = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < CE_VEC; ++j) {
+            const int64_t c = (static_cast<int64_t>(j) * CE_THREADS + threadIdx.x) * 4;
+            float4 t4 = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+            if (c < C)
+                t4 = *reinterpret_cast<const float4*>(srow + c);
+            v[4 * j] = t4.x, v[4 * j + 1] = t4.y, v[4 * j + 2] = t4.z, v[4 * j + 3] = t4.w;
+            m = fmaxf(m, fmaxf(fmaxf(t4.x, t4.y), fmaxf(t4.z, t4.w)));
+        }
+        __syncthreads();  // every thread has its part of the row: the buffer is free
+        if (threadIdx.x == 0 && row + gridDim.x < N) {
+            fence_async_smem();
+            mbar_arrive_expect_tx(&bar, bytes);
+            bulk_load(srow, logits + (row + gridDim.x) * C, bytes, &bar);
+        }
+        m = warp_max(m);
+        if (lane == 0)
+            s_red[warp] = m;
+        __syncthreads();
+        m = s_red[lane];
+        m = warp_max(m);
+        __syncthreads();
+        double sd = 0.0;
+#pragma unroll
+        for (int j = 0; j < CE_VEC * 4; ++j)
+            sd += static_cast<double>(expf(v[j] - m));  // exp(-inf) = 0 for padding
+        sd = warp_sum_d(sd);
+        if (lane == 0)
+            s_redd[warp] = sd;
+        __syncthreads();
+        sd = s_redd[lane];
+        sd = warp_sum_d(sd);
+        const float lse = m + static_cast<float>(log(sd));
+        if (threadIdx.x == 0) {
+            if (t_ok)
+                atomicAdd(loss_acc, static_cast<double>(-(x_t - lse)));
+            else
+                report(kErrBadIndex);
+        }
+        if (dlogits) {
+            float* dr = dlogits + row * C;
+#pragma unroll
+            for (int j = 0; j < CE_VEC; ++j) {
+                const int64_t c = (static_cast<int64_t>(j) * CE_THREADS + threadIdx.x) * 4;
+                if (c < C) {
+                    float o[4];
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const float p = expf(v[4 * j + q] - lse);
+                        o[q] = grad_scale * (c + q == t ? p - 1.0f : p);
+                    }
+                    *reinterpret_cast<float4*>(dr + c) = make_float4(o[0], o[1], o[2], o[3]);
+                }
+            }
+        }
+        __syncthreads();  // s_red / s_redd reused by the next row
+    }
+}
+
 __global__ void loss_finalize_kernel(const double* acc, float scale, float* out) {
     out[0] = static_cast<float>(acc[0] * static_cast<double>(scale));
 }
@@ -1021,6 +1124,15 @@ int ttk_cross_entropy(const float* logits, const int64_t* targets, int64_t N, in
         return TTK_OK;
     if ((C & 3) == 0 && !(aligned16(logits) && (!dlogits || aligned16(dlogits))))
         return set_error(TTK_ERR_ARG, "cross_entropy: tensors must be 16-byte aligned");
+    if ((C & 3) == 0 && C <= static_cast<int64_t>(CE_THREADS) * CE_VEC * 4) {
+        const int smem = static_cast<int>(C * 4);
+        cudaFuncSetAttribute(cross_entropy_bulk_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        const int gb = static_cast<int>(std::min<int64_t>(N, 148));
+        cross_entropy_bulk_kernel<<<gb, CE_THREADS, smem, S(stream)>>>(
+            logits, targets, N, C, loss_acc, dlogits, grad_scale);
+        return check_launch("cross_entropy_bulk_kernel");
+    }
     const int grid = static_cast<int>(std::min<int64_t>(N, 148 * 2));
     if (C <= static_cast<int64_t>(CE_THREADS) * CE_VEC * 4)
         cross_entropy_kernel<true><<<grid, CE_THREADS, 0, S(stream)>>>(logits, targets, N, C,

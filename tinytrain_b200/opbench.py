@@ -16,7 +16,8 @@ Workloads (fp32, seeded):
              embedding gather / scatter-add and the residual add at 16384 x 2048
   attention  fused causal attention with RoPE, forward + backward, B 8, H 12,
              hd 64, S in {128, 512, 1024, 2048}, inputs N(0, 1) (--hd 128:
-             H 16, the 1B layer)
+             B 8, H 16, the 1B layer; --hd 32: B 16, H 8, the 13M default
+             model; --batch / --heads override)
 Each line: median of `--iters` timed launches (CUDA events, after warm-up, L2
 flushed by a 256 MB write before each), the algorithmic work (FLOPs, or bytes
 that must cross HBM), achieved rate and fraction of the measured peak
@@ -221,9 +222,7 @@ def bench_attention(seqs, iters, B=8, H=12, hd=64):
         ms_b = timed(lambda: K.attention_bwd(q, k, v, cs, sn, o, lse, do), iters)
         fl_f = 2 * B * H * S * S * hd  # causal half of 4*B*H*S^2*hd
         fl_b = 2 * fl_f
-        eng = {0: ("tcgen05 fwd + bwd, bf16x3 split" if hd in (64, 128) else
-                   "mma.sync m16n8k16 bf16x3 split"),
-               1: "fp32 FMA (CUDA cores)",
+        eng = {0: "tcgen05 fwd + bwd, bf16x3 split",
                2: "mma.sync m16n8k16 bf16x3 split"}[_ttk.call("ttk_attention_get_impl")]
         emit({"op": "attention", "B": B, "H": H, "hd": hd, "S": S, "ms_fwd": ms_f,
               "ms_bwd": ms_b, "tflops_fwd": fl_f / ms_f / 1e9, "tflops_bwd": fl_b / ms_b / 1e9,
@@ -238,6 +237,8 @@ def main():
     ap.add_argument("--seq", type=int, default=None)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--hd", type=int, default=64)
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--heads", type=int, default=None)
     a = ap.parse_args()
     torch.cuda.set_device(0)
     _ttk.call("ttk_init", 0)
@@ -250,8 +251,9 @@ def main():
     if a.only in (None, "hbm"):
         bench_hbm(a.iters)
     if a.only in (None, "attention"):
-        bench_attention([a.seq] if a.seq else ATTN_S, a.iters,
-                        H=12 if a.hd == 64 else 2048 // a.hd, hd=a.hd)
+        B0, H0 = {64: (8, 12), 128: (8, 16), 32: (16, 8)}.get(a.hd, (8, 2048 // a.hd))
+        bench_attention([a.seq] if a.seq else ATTN_S, a.iters, B=a.batch or B0,
+                        H=a.heads or H0, hd=a.hd)
     assert _ttk.device_status() == 0
 
 

@@ -256,6 +256,15 @@ int ttk_attention_fwd(const float* q, const float* k, const float* v, const floa
                       const float* sin_t, float* o, float* lse, int64_t B, int64_t T, int64_t H,
                       int64_t hd, float scale, void* workspace, size_t workspace_bytes,
                       void* stream);
+/* ttk_attention_fwd that also writes the bf16x3 GEMM operand planes of o,
+ * viewed as [B*T, H*hd] rows, into o_split (ttk_gemm_split_bytes(1, B*T,
+ * H*hd) bytes): equal bit for bit to ttk_gemm_split of o, so the output
+ * projection skips its split pass. bf16x3 precision only; no counterpart in
+ * the reference. */
+int ttk_attention_fwd_split(const float* q, const float* k, const float* v, const float* cos_t,
+                            const float* sin_t, float* o, float* lse, void* o_split, int64_t B,
+                            int64_t T, int64_t H, int64_t hd, float scale, void* workspace,
+                            size_t workspace_bytes, void* stream);
 /* dq, dk, dv (+)= gradients w.r.t. the pre-RoPE q, k and v. `workspace` must
  * hold ttk_attention_bwd_workspace_size(B,T,H,hd) bytes. */
 size_t ttk_attention_bwd_workspace_size(int64_t B, int64_t T, int64_t H, int64_t hd);

@@ -286,6 +286,23 @@ def test_attention_sizes(cuda, B, T, H, hd, attn_impl):
     assert rel_err(n(dv), dvr) < TOL
 
 
+@pytest.mark.parametrize("B,T,H,hd", [(2, 300, 4, 64), (1, 256, 16, 128), (4, 128, 8, 32)])
+def test_attention_fwd_split_planes_bitexact(cuda, B, T, H, hd, attn_impl):
+    """ttk_attention_fwd_split: o and lse equal ttk_attention_fwd's, and the
+    planes equal ttk_gemm_split of o as [B*T, H*hd], bit for bit."""
+    from tinytrain_b200 import kernels as K
+    g = torch.Generator(device=cuda).manual_seed(B * T + hd)
+    q, k, v = (torch.randn(B, T, H, hd, device=cuda, generator=g) for _ in range(3))
+    cs, sn = K.rope_tables(T, hd, 10000.0, cuda)
+    o0, l0 = K.attention_fwd(q, k, v, cs, sn)
+    o1, l1, planes = K.attention_fwd_split(q, k, v, cs, sn)
+    ref = K.gemm_split(o1.view(B * T, H * hd))
+    torch.cuda.synchronize()
+    assert torch.equal(o0, o1) and torch.equal(l0, l1)
+    assert torch.equal(planes, ref)
+    assert status_ok()
+
+
 @pytest.mark.parametrize("hd", [64, 128])
 def test_attention_bwd_accumulates(cuda, hd, attn_impl):
     """accumulate = 1 adds the gradients into dq, dk, dv (the autograd engine's

@@ -85,6 +85,8 @@ SIGS = {
     "ttk_loss_finalize": (I32, [P, F32, P, P]),
     "ttk_attention_fwd_workspace_size": (SZ, [I64, I64, I64, I64]),
     "ttk_attention_fwd": (I32, [P, P, P, P, P, P, P, I64, I64, I64, I64, F32, P, SZ, P]),
+    "ttk_attention_fwd_split": (I32, [P, P, P, P, P, P, P, P, I64, I64, I64, I64, F32, P, SZ,
+                                       P]),
     "ttk_attention_set_impl": (I32, [I32]),
     "ttk_attention_get_impl": (I32, []),
     "ttk_attention_bwd_workspace_size": (SZ, [I64, I64, I64, I64]),

@@ -101,6 +101,31 @@ int ttk_attention_fwd(const float* q, const float* k, const float* v, const floa
                                  scale, workspace, tc, S(stream));
 }
 
+int ttk_attention_fwd_split(const float* q, const float* k, const float* v, const float* cos_t,
+                            const float* sin_t, float* o, float* lse, void* o_split, int64_t B,
+                            int64_t T, int64_t H, int64_t hd, float scale, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+    if (!o_split)
+        return set_error(TTK_ERR_ARG, "attention_fwd_split: null o_split");
+    if (ttk_gemm_get_precision() != 0)
+        return set_error(TTK_ERR_ARG, "attention_fwd_split: planes exist for the bf16x3 precision");
+    int rc = attn_check(q, k, v, cos_t, sin_t, B, T, H, hd);
+    if (rc)
+        return rc;
+    if (!B || !T || !H)
+        return TTK_OK;
+    if (!o || !lse)
+        return set_error(TTK_ERR_ARG, "attention_fwd: null output");
+    if (!workspace || workspace_bytes < ttk_attention_fwd_workspace_size(B, T, H, hd))
+        return set_error(TTK_ERR_ARG, "attention_fwd: workspace too small");
+    rc = attn_align_check({q, k, v, cos_t, sin_t, o, o_split});
+    if (rc)
+        return rc;
+    const bool tc = attn_impl() == 0 && attention_tc_supported(static_cast<int>(hd));
+    return attention_mma_forward(static_cast<int>(hd), q, k, v, cos_t, sin_t, o, lse, B, T, H,
+                                 scale, workspace, tc, S(stream), o_split);
+}
+
 size_t ttk_attention_bwd_workspace_size(int64_t B, int64_t T, int64_t H, int64_t hd) {
     const size_t dv = align256(static_cast<size_t>(B * T * H) * sizeof(float));
     // q, k, v, dO as bf16 hi|lo, then the (lse, D) table of the tcgen05 path

@@ -802,7 +802,7 @@ inline int launch_split(const float* x, const float* cs, const float* sn, int ro
 template <int HD>
 int fwd(const float* q, const float* k, const float* v, const float* cs, const float* sn,
         float* o, float* lse, int64_t B, int64_t T, int64_t H, float scale, SplitBufs s, bool tc,
-        cudaStream_t st) {
+        cudaStream_t st, void* o_split) {
     int rc = launch_split(q, cs, sn, 1, scale, s.qh, s.ql, B, T, H, HD, st);
     if (!rc)
         rc = launch_split(k, cs, sn, 1, 1.0f, s.kh, s.kl, B, T, H, HD, st);
@@ -811,13 +811,17 @@ int fwd(const float* q, const float* k, const float* v, const float* cs, const f
     if (rc)
         return rc;
     if (tc)
-        return attention_tc_forward_core(HD, s.qh, s.kh, s.vh, o, lse, B, T, H, st);
+        return attention_tc_forward_core(HD, s.qh, s.kh, s.vh, o, lse, B, T, H, st,
+                                         static_cast<__nv_bfloat16*>(o_split));
     const int smem = FwdSmem<HD>::BYTES;
     cudaFuncSetAttribute(attn_fwd_mma<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     dim3 grid(static_cast<unsigned>((T + FWD_BQ - 1) / FWD_BQ), static_cast<unsigned>(B * H));
     attn_fwd_mma<HD><<<grid, FWD_THREADS, smem, st>>>(s.qh, s.ql, s.kh, s.kl, s.vh, s.vl, o, lse,
                                                       T, static_cast<int>(H));
-    return check_launch("attn_fwd_mma");
+    rc = check_launch("attn_fwd_mma");
+    if (rc || !o_split)
+        return rc;
+    return gemm_split(o, B * T, H * HD, H * HD, 0, 1, o_split, st);
 }
 
 // qkv_ready: s.q*, s.k*, s.v* already hold the forward's splits of q, k, v
@@ -880,14 +884,15 @@ namespace ttk {
 int attention_mma_forward(int hd, const float* q, const float* k, const float* v,
                           const float* cs, const float* sn, float* o, float* lse, int64_t B,
                           int64_t T, int64_t H, float scale, void* ws, bool tc,
-                          cudaStream_t st) {
+                          cudaStream_t st, void* o_split) {
     const int64_t n = B * T * H * hd;
     __nv_bfloat16* w = static_cast<__nv_bfloat16*>(ws);
     fa::SplitBufs s{w, w + n, w + 2 * n, w + 3 * n, w + 4 * n, w + 5 * n, nullptr, nullptr};
     switch (hd) {
-        case 32: return fa::fwd<32>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st);
-        case 64: return fa::fwd<64>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st);
-        default: return fa::fwd<128>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st);
+        case 32: return fa::fwd<32>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st, o_split);
+        case 64: return fa::fwd<64>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st, o_split);
+        default:
+            return fa::fwd<128>(q, k, v, cs, sn, o, lse, B, T, H, scale, s, tc, st, o_split);
     }
 }
 

@@ -51,6 +51,10 @@ constexpr int BQ = 128;  // query rows per CTA (MMA M, TMEM lanes)
 constexpr int BKV = 64;  // keys per block
 constexpr int NSLOT = 3;
 constexpr int NUM_THREADS = 320;
+// Forward: a second MMA-issuing warp (index 10) issues O_j = P_j V_j while
+// warp 1 issues the score MMAs.
+constexpr int FWD_PV_WARP = 10;
+constexpr int FWD_THREADS = 352;
 // dK/dV: a second MMA-issuing warp (index 10) after the eight softmax warps.
 constexpr int DKV_MMA_B_WARP = 10;
 constexpr int DKV_THREADS = 352;
@@ -103,11 +107,20 @@ __device__ __forceinline__ uint64_t v_desc(uint32_t plane, int ks) {
     return umma_smem_desc(plane + ks * 1024, BKV * 64, 512, kSW64);
 }
 
+// Position of K_j / V_j in the producer's ring order (K0, K1, V0, K2, V1, ...,
+// V_last): n = 0 for K0, 2j - 1 for K_j (j >= 1), 2j + 2 for V_j before the
+// last block and 2 * nblk - 1 for the last V.
+__device__ __forceinline__ int ring_pos_k(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__device__ __forceinline__ int ring_pos_v(int j, int nblk) {
+    return j == nblk - 1 ? 2 * nblk - 1 : 2 * j + 2;
+}
+
 template <int HD>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(FWD_THREADS, 1)
     attn_fwd_tc(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_v, float* __restrict__ o,
-                float* __restrict__ lse, int64_t T, int H) {
+                float* __restrict__ lse, int64_t T, int H, __nv_bfloat16* __restrict__ o_split,
+                int64_t o_plane) {
     using CF = FwdCfg<HD>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -144,7 +157,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             mbar_init(&o_full[b], 1);
             mbar_init(&o_free[b], SOFTMAX_THREADS);
         }
-        mbar_init(done, 1);
+        mbar_init(done, 2);  // both MMA-issuing warps commit
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -207,80 +220,88 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         mbar_wait(&full[i], static_cast<uint32_t>(armed_ph[i]), 26);
             }
         }
-    } else if (warp == 1) {
-        // -------------------------------------------------------- MMA issuer
-        // The whole warp runs this loop (uniform control flow); lane 0 issues.
+    } else if (warp == 1 || warp == FWD_PV_WARP) {
+        // ------------------------------------------------------- MMA issuers
+        // One warp issues at most about one MMA per 64 cycles, so two warps
+        // share the work (each loop warp-uniform; lane 0 issues):
+        //   warp 1:  S_j = Q K_j^T into S[j % 2], once the softmax of block
+        //            j - 2 has read that buffer (p_full);
+        //   warp 10: O_j = P_j V_j into O[j % 2], once P_j is written
+        //            (p_full) and O_{j-2} was folded (o_free).
+        // They touch different TMEM columns and shared-memory tiles; each
+        // frees its ring slots as its MMAs complete.
         constexpr uint32_t idesc_s = umma_idesc_bf16(BQ, BKV, 0, 0);
         constexpr uint32_t idesc_o = umma_idesc_bf16(BQ, HD, 0, 1);
         const uint32_t sQ = s_base;
-        int it = 0;
-        bool ok = mbar_wait(q_full, 0, 22);
-        auto next_slot = [&](uint32_t& addr) -> bool {
-            const int slot = it % NSLOT;
-            const uint32_t ph = static_cast<uint32_t>((it / NSLOT) & 1);
-            if (*abort_flag || !mbar_wait(&full[slot], ph, 23))
+        bool ok = true;
+        auto wait_slot = [&](int n, uint32_t& addr, unsigned site) -> bool {
+            const int slot = n % NSLOT;
+            const uint32_t ph = static_cast<uint32_t>((n / NSLOT) & 1);
+            if (*abort_flag || !mbar_wait(&full[slot], ph, site))
                 return false;
             addr = s_base + CF::OFF_SLOT + slot * CF::SLOT_BYTES;
-            ++it;
             return true;
         };
-        auto issue_pv = [&](int i) -> bool {
-            uint32_t sV;
-            const int slot = it % NSLOT;
-            if (!next_slot(sV))
-                return false;
-            if (*abort_flag || !mbar_wait(&p_full[i & 1], (i >> 1) & 1, 24))
-                return false;
-            if (i >= 2 && (*abort_flag || !mbar_wait(&o_free[i & 1], ((i - 2) >> 1) & 1, 25)))
-                return false;
-            tc_fence_after();
-            const uint32_t sP = s_base + CF::OFF_P + (i & 1) * CF::P_BYTES;
-            const uint32_t d = tmem + CF::O_COL + (i & 1) * HD;
+        if (warp == 1) {
+            ok = mbar_wait(q_full, 0, 22);
+            for (int j = 0; j < nblk && ok; ++j) {
+                const int n = ring_pos_k(j);
+                uint32_t sK;
+                if (!wait_slot(n, sK, 23) ||
+                    (j >= 2 && (*abort_flag ||
+                                !mbar_wait(&p_full[j & 1], ((j - 2) >> 1) & 1, 24)))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem + CF::S_COL + (j & 1) * BKV;
 #pragma unroll
-            for (int ks = 0; ks < BKV / 16; ++ks) {
-                const uint64_t ph_ = kmajor_desc(sP, BQ, ks);
-                const uint64_t pl_ = kmajor_desc(sP + CF::P_PLANE, BQ, ks);
-                const uint64_t vh_ = v_desc(sV, ks);
-                const uint64_t vl_ = v_desc(sV + CF::KV_PLANE, ks);
-                mma_bf16_w(d, pl_, vh_, idesc_o, ks > 0 ? 1u : 0u);
-                mma_bf16_w(d, ph_, vl_, idesc_o, 1u);
-                mma_bf16_w(d, ph_, vh_, idesc_o, 1u);
+                for (int ks = 0; ks < HD / 16; ++ks) {
+                    const uint64_t qh_ = kmajor_desc(sQ, BQ, ks);
+                    const uint64_t ql_ = kmajor_desc(sQ + CF::Q_PLANE, BQ, ks);
+                    const uint64_t kh_ = kmajor_desc(sK, BKV, ks);
+                    const uint64_t kl_ = kmajor_desc(sK + CF::KV_PLANE, BKV, ks);
+                    mma_bf16_w(d, ql_, kh_, idesc_s, ks > 0 ? 1u : 0u);
+                    mma_bf16_w(d, qh_, kl_, idesc_s, 1u);
+                    mma_bf16_w(d, qh_, kh_, idesc_s, 1u);
+                }
+                mma_commit_w(&s_full[j & 1]);
+                mma_commit_w(&empty[n % NSLOT]);
             }
-            mma_commit_w(&o_full[i & 1]);
-            mma_commit_w(&empty[slot]);
-            return true;
-        };
-        for (int j = 0; j < nblk && ok; ++j) {
-            uint32_t sK;
-            const int slot = it % NSLOT;
-            if (!next_slot(sK)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t d = tmem + CF::S_COL + (j & 1) * BKV;
+        } else {
+            for (int i = 0; i < nblk && ok; ++i) {
+                const int n = ring_pos_v(i, nblk);
+                uint32_t sV;
+                if (!wait_slot(n, sV, 25) ||
+                    *abort_flag || !mbar_wait(&p_full[i & 1], (i >> 1) & 1, 26) ||
+                    (i >= 2 && (*abort_flag ||
+                                !mbar_wait(&o_free[i & 1], ((i - 2) >> 1) & 1, 27)))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sP = s_base + CF::OFF_P + (i & 1) * CF::P_BYTES;
+                const uint32_t d = tmem + CF::O_COL + (i & 1) * HD;
 #pragma unroll
-            for (int ks = 0; ks < HD / 16; ++ks) {
-                const uint64_t qh_ = kmajor_desc(sQ, BQ, ks);
-                const uint64_t ql_ = kmajor_desc(sQ + CF::Q_PLANE, BQ, ks);
-                const uint64_t kh_ = kmajor_desc(sK, BKV, ks);
-                const uint64_t kl_ = kmajor_desc(sK + CF::KV_PLANE, BKV, ks);
-                mma_bf16_w(d, ql_, kh_, idesc_s, ks > 0 ? 1u : 0u);
-                mma_bf16_w(d, qh_, kl_, idesc_s, 1u);
-                mma_bf16_w(d, qh_, kh_, idesc_s, 1u);
+                for (int ks = 0; ks < BKV / 16; ++ks) {
+                    const uint64_t ph_ = kmajor_desc(sP, BQ, ks);
+                    const uint64_t pl_ = kmajor_desc(sP + CF::P_PLANE, BQ, ks);
+                    const uint64_t vh_ = v_desc(sV, ks);
+                    const uint64_t vl_ = v_desc(sV + CF::KV_PLANE, ks);
+                    mma_bf16_w(d, pl_, vh_, idesc_o, ks > 0 ? 1u : 0u);
+                    mma_bf16_w(d, ph_, vl_, idesc_o, 1u);
+                    mma_bf16_w(d, ph_, vh_, idesc_o, 1u);
+                }
+                mma_commit_w(&o_full[i & 1]);
+                mma_commit_w(&empty[n % NSLOT]);
             }
-            mma_commit_w(&s_full[j & 1]);
-            mma_commit_w(&empty[slot]);
-            if (j >= 1 && !issue_pv(j - 1))
-                ok = false;
         }
-        if (ok && !issue_pv(nblk - 1))
-            ok = false;
         if (!ok)
             *abort_flag = 1;
-        // Every MMA issued has retired once this fires (also on abort).
+        // Every MMA issued by both warps has retired once this fires (also on
+        // abort).
         mma_commit_w(done);
-        mbar_wait(done, 0, 27);
+        mbar_wait(done, 0, 28);
     } else {
         // ----------------------------------------------------------- softmax
         const int sw = warp - 2;
@@ -414,7 +435,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         tc_fence_after();
         tmem_dealloc(tmem, CF::TMEM_COLS);
     }
-    if (warp >= 2 && !*abort_flag) {
+    if (warp >= 2 && warp < 2 + 8 && !*abort_flag) {
         const int quad = warp & 3, half = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const int64_t q = q0 + r;
@@ -422,12 +443,24 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (q < T) {
             const int64_t b = bh / H, h = bh % H;
             const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
-            float* dst = o + ((b * T + q) * H + h) * HD + half * OH;
+            const int64_t off = ((b * T + q) * H + h) * HD + half * OH;
+            float* dst = o + off;
 #pragma unroll
-            for (int c = 0; c < OH; c += 4)
-                *reinterpret_cast<float4*>(dst + c) = make_float4(
-                    acc[c] * inv, acc[c + 1] * inv, acc[c + 2] * inv,
-                    acc[c + 3] * inv);
+            for (int c = 0; c < OH; c += 4) {
+                const float ov[4] = {acc[c] * inv, acc[c + 1] * inv, acc[c + 2] * inv,
+                                     acc[c + 3] * inv};
+                *reinterpret_cast<float4*>(dst + c) = make_float4(ov[0], ov[1], ov[2], ov[3]);
+                if (o_split) {  // the split kernel's arithmetic (split_bf16)
+                    __nv_bfloat16 hi[4], lo[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        split_bf16(ov[u], hi[u], lo[u]);
+                    *reinterpret_cast<uint2*>(o_split + off + c) =
+                        *reinterpret_cast<const uint2*>(hi);
+                    *reinterpret_cast<uint2*>(o_split + o_plane + off + c) =
+                        *reinterpret_cast<const uint2*>(lo);
+                }
+            }
             if (half == 0)
                 lse[bh * T + q] = m_out * LN2 + logf(lt);
         }
@@ -1177,7 +1210,7 @@ bool attention_tc_supported(int hd) { return hd == 32 || hd == 64 || hd == 128; 
 
 int attention_tc_forward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat16* kh,
                               const __nv_bfloat16* vh, float* o, float* lse, int64_t B, int64_t T,
-                              int64_t H, cudaStream_t st) {
+                              int64_t H, cudaStream_t st, __nv_bfloat16* o_split) {
     const int64_t n = B * T * H * hd;
     CUtensorMap mq, mk, mv;
     int rc = make_plane_map(&mq, qh, n, B * H, T, hd, fatc::BQ);
@@ -1193,8 +1226,8 @@ int attention_tc_forward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat
         const int smem = fatc::FwdCfg<HD>::BYTES;
         cudaFuncSetAttribute(fatc::attn_fwd_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem);
-        fatc::attn_fwd_tc<HD><<<grid, fatc::NUM_THREADS, smem, st>>>(mq, mk, mv, o, lse, T,
-                                                                      static_cast<int>(H));
+        fatc::attn_fwd_tc<HD><<<grid, fatc::FWD_THREADS, smem, st>>>(
+            mq, mk, mv, o, lse, T, static_cast<int>(H), o_split, n);
     };
     if (hd == 128)
         launch(std::integral_constant<int, 128>{});

@@ -70,10 +70,13 @@ int gemm_tf32x3_presplit(int transA, int transB, int64_t batch, int64_t M, int64
 
 // Tensor-core attention (attention_mma.cu); ws sized by the C ABI's
 // workspace functions.
+// o_split (optional): bf16x3 GEMM operand planes of o as [B*T, H*hd] rows
+// (the ttk_gemm_split layout), written by the tcgen05 epilogue or, for the
+// mma.sync engine, by a split pass after it.
 int attention_mma_forward(int hd, const float* q, const float* k, const float* v,
                           const float* cs, const float* sn, float* o, float* lse, int64_t B,
                           int64_t T, int64_t H, float scale, void* ws, bool tc,
-                          cudaStream_t st);
+                          cudaStream_t st, void* o_split = nullptr);
 int attention_mma_backward(int hd, const float* q, const float* k, const float* v,
                            const float* cs, const float* sn, const float* o, const float* lse,
                            const float* dout, float* dq, float* dk, float* dv, int accumulate,
@@ -81,11 +84,11 @@ int attention_mma_backward(int hd, const float* q, const float* k, const float* 
                            cudaStream_t st, const void* fwd_ws = nullptr);
 
 // tcgen05 attention forward / backward (attention_tc.cu) over split planes
-// written by the mma.sync path's split pass; head dims 64 and 128.
+// written by the mma.sync path's split pass; head dims 32, 64 and 128.
 bool attention_tc_supported(int hd);
 int attention_tc_forward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat16* kh,
                               const __nv_bfloat16* vh, float* o, float* lse, int64_t B, int64_t T,
-                              int64_t H, cudaStream_t st);
+                              int64_t H, cudaStream_t st, __nv_bfloat16* o_split = nullptr);
 // ld: [B*H][T32][2] table of (lse * log2 e, D), T32 = T rounded up to 32,
 // zero in the padding rows.
 int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloat16* kh,

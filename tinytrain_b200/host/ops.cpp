@@ -601,7 +601,7 @@ namespace {
 
 Tensor fused_attention(const ImplPtr& qo, const ImplPtr& ko, const ImplPtr& vo, ImplPtr co,
                        ImplPtr so, int64_t B, int64_t T, int64_t H, int64_t hd, float scale,
-                       std::vector<int64_t> oshape);
+                       std::vector<int64_t> oshape, bool planes = false);
 
 // C (batch x [M,N]) = op(A) op(B) and its backward, for matmul and bmm. A is
 // [M,K] (storage [K,M] when A.trans), B is [K,N] (storage [N,K] when B.trans).
@@ -1154,10 +1154,13 @@ namespace {
 // The fused causal attention as one graph node: q, k, v [B,T,H,hd] (any
 // logical shape with that storage), RoPE from the tables co/so (identity
 // when null: the deferred chain's q and k are already rotated), output of
-// shape `oshape` holding [B,T,H*hd].
+// shape `oshape` holding [B,T,H*hd]. With `planes` (and the bf16x3
+// precision, an output big enough for tensor-core GEMMs) the kernel also
+// writes the output's operand planes, cached on the output buffer as the
+// [B*T, H*hd] GEMM operand split that the output projection looks up.
 Tensor fused_attention(const ImplPtr& qo, const ImplPtr& ko, const ImplPtr& vo, ImplPtr co,
                        ImplPtr so, int64_t B, int64_t T, int64_t H, int64_t hd, float scale,
-                       std::vector<int64_t> oshape) {
+                       std::vector<int64_t> oshape, bool planes) {
     if (!co) {
         co = full({T, hd / 2}, 1.0f).impl();
         so = full({T, hd / 2}, 0.0f).impl();
@@ -1169,10 +1172,31 @@ Tensor fused_attention(const ImplPtr& qo, const ImplPtr& ko, const ImplPtr& vo, 
     // for the backward, which reuses them while q, k, v are unchanged.
     const size_t fws = ttk_attention_fwd_workspace_size(B, T, H, hd);
     auto fw = std::make_shared<Scratch>(fws);
-    check(ttk_attention_fwd(dread(qo), dread(ko), dread(vo), dread(co), dread(so), out_ptr(out),
-                            lse->device_for_overwrite(), B, T, H, hd, scale, fw->ptr, fws,
-                            stream()),
-          "attention");
+    const int64_t R = B * T, D = H * hd;
+    if (planes && ttk_gemm_get_precision() == 0 && R * D >= (1 << 20)) {
+        float* o = out_ptr(out);
+        Buffer& ob = *out.impl()->data;
+        const size_t bytes = ttk_gemm_split_bytes(1, R, D);
+        if (ob.split_bytes < bytes) {
+            ttk_free(ob.split_dev, stream());
+            ob.split_dev = nullptr;
+            ob.split_bytes = 0;
+            check(ttk_malloc(&ob.split_dev, bytes, stream()), "attention planes");
+            ob.split_bytes = bytes;
+        }
+        check(ttk_attention_fwd_split(dread(qo), dread(ko), dread(vo), dread(co), dread(so), o,
+                                      lse->device_for_overwrite(), ob.split_dev, B, T, H, hd,
+                                      scale, fw->ptr, fws, stream()),
+              "attention");
+        const int64_t key[7] = {0, 1, R, D, D, 0, 0};
+        ob.split_version = ob.version;
+        std::copy(key, key + 7, ob.split_key);
+    } else {
+        check(ttk_attention_fwd(dread(qo), dread(ko), dread(vo), dread(co), dread(so),
+                                out_ptr(out), lse->device_for_overwrite(), B, T, H, hd, scale,
+                                fw->ptr, fws, stream()),
+              "attention");
+    }
     if (!rg)
         return out;
     // Contents of q, k, v as the forward read them (buffer versions).
@@ -1240,7 +1264,7 @@ Tensor causal_attention(const Tensor& q, const Tensor& k, const Tensor& v, const
         throw std::invalid_argument("rope: cos/sin shape mismatch");
     const float scale = 1.0f / std::sqrt(static_cast<float>(hd));
     return fused_attention(q.impl(), k.impl(), v.impl(), cos.impl(), sin.impl(), B, T, H, hd,
-                           scale, {B, T, H * hd});
+                           scale, {B, T, H * hd}, true);
 }
 
 Tensor swiglu(const Tensor& a, const Tensor& b) {

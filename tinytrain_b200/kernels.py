@@ -194,6 +194,19 @@ def attention_fwd(q, k, v, cos, sin, scale=None, keep_ws=False):
     return (o, lse, ws) if keep_ws else (o, lse)
 
 
+def attention_fwd_split(q, k, v, cos, sin, scale=None):
+    """(o, lse, planes): the forward plus o's bf16x3 operand planes ([B*T, H*hd])."""
+    B, T, H, hd = q.shape
+    scale = float(hd) ** -0.5 if scale is None else scale
+    o = torch.empty_like(q)
+    lse = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
+    ws = workspace(call("ttk_attention_fwd_workspace_size", B, T, H, hd), q.device)
+    planes = workspace(call("ttk_gemm_split_bytes", 1, B * T, H * hd), q.device)
+    call("ttk_attention_fwd_split", _p(q), _p(k), _p(v), _p(cos), _p(sin), _p(o), _p(lse),
+         _p(planes), B, T, H, hd, scale, _p(ws), ws.numel(), _s())
+    return o, lse, planes
+
+
 def attention_bwd(q, k, v, cos, sin, o, lse, do, scale=None, out=None, accumulate=False,
                   fwd_ws=None):
     """dq, dk, dv; with `out` = (dq, dk, dv) writes (or, with accumulate, adds) into them.

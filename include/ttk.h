@@ -285,6 +285,19 @@ int ttk_attention_bwd_ex(const float* q, const float* k, const float* v, const f
                          float* dq, float* dk, float* dv, int accumulate, int64_t B, int64_t T,
                          int64_t H, int64_t hd, float scale, const void* fwd_workspace,
                          void* workspace, size_t workspace_bytes, void* stream);
+/* ttk_attention_bwd_ex (fwd_workspace may be NULL: then as ttk_attention_bwd,
+ * with its workspace size) that also writes the bf16x3 GEMM operand planes of
+ * dq, dk and dv, each viewed as [B*T, H*hd] rows, into dq_split / dk_split /
+ * dv_split (each NULL or ttk_gemm_split_bytes(1, B*T, H*hd) bytes): equal bit
+ * for bit to ttk_gemm_split of the stored gradients (after accumulation), so
+ * the q/k/v projections' backward GEMMs skip their split passes. bf16x3
+ * precision only; no counterpart in the reference. */
+int ttk_attention_bwd_split(const float* q, const float* k, const float* v, const float* cos_t,
+                            const float* sin_t, const float* o, const float* lse,
+                            const float* dout, float* dq, float* dk, float* dv, int accumulate,
+                            int64_t B, int64_t T, int64_t H, int64_t hd, float scale,
+                            const void* fwd_workspace, void* workspace, size_t workspace_bytes,
+                            void* dq_split, void* dk_split, void* dv_split, void* stream);
 /* Attention engine (process-wide), all fp32-accurate:
  *   0 = tensor cores (default): tcgen05 forward and backward for head dims
  *       64 and 128, mma.sync m16n8k16 elsewhere, both with the bf16x3

@@ -303,6 +303,30 @@ def test_attention_fwd_split_planes_bitexact(cuda, B, T, H, hd, attn_impl):
     assert status_ok()
 
 
+@pytest.mark.parametrize("B,T,H,hd", [(2, 300, 4, 64), (1, 256, 16, 128), (4, 128, 8, 32)])
+@pytest.mark.parametrize("accumulate", [False, True])
+def test_attention_bwd_split_planes_bitexact(cuda, B, T, H, hd, accumulate, attn_impl):
+    """ttk_attention_bwd_split: dq, dk, dv equal ttk_attention_bwd_ex's (with
+    and without accumulation into existing gradients), and each plane set
+    equals ttk_gemm_split of the stored gradient as [B*T, H*hd], bit for bit."""
+    from tinytrain_b200 import kernels as K
+    g = torch.Generator(device=cuda).manual_seed(B * T + hd + accumulate)
+    q, k, v, do = (torch.randn(B, T, H, hd, device=cuda, generator=g) for _ in range(4))
+    cs, sn = K.rope_tables(T, hd, 10000.0, cuda)
+    o, lse, fw = K.attention_fwd(q, k, v, cs, sn, keep_ws=True)
+    base = [torch.randn(B, T, H, hd, device=cuda, generator=g) for _ in range(3)]
+    ref = K.attention_bwd(q, k, v, cs, sn, o, lse, do, out=[x.clone() for x in base],
+                          accumulate=accumulate, fwd_ws=fw)
+    *got, planes = K.attention_bwd_split(q, k, v, cs, sn, o, lse, do,
+                                         out=[x.clone() for x in base], accumulate=accumulate,
+                                         fwd_ws=fw)
+    for a, b, p in zip(got, ref, planes):
+        torch.cuda.synchronize()
+        assert torch.equal(a, b)
+        assert torch.equal(p, K.gemm_split(a.view(B * T, H * hd)))
+    assert status_ok()
+
+
 @pytest.mark.parametrize("hd", [64, 128])
 def test_attention_bwd_accumulates(cuda, hd, attn_impl):
     """accumulate = 1 adds the gradients into dq, dk, dv (the autograd engine's

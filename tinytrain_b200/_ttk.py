@@ -94,6 +94,7 @@ SIGS = {
                                 SZ, P]),
     "ttk_attention_bwd_ex_workspace_size": (SZ, [I64] * 4),
     "ttk_attention_bwd_ex": (I32, [P] * 11 + [I32] + [I64] * 4 + [F32, P, P, SZ, P]),
+    "ttk_attention_bwd_split": (I32, [P] * 11 + [I32] + [I64] * 4 + [F32, P, P, SZ, P, P, P, P]),
     "ttk_embedding_fwd": (I32, [P, P, P, I64, I64, I64, P]),
     "ttk_embedding_bwd_workspace_size": (SZ, [I64]),
     "ttk_embedding_bwd": (I32, [P, P, P, I64, I64, I64, P, SZ, P]),

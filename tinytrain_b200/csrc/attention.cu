@@ -188,4 +188,33 @@ int ttk_attention_bwd_ex(const float* q, const float* k, const float* v, const f
                                   S(stream), fwd_workspace);
 }
 
+int ttk_attention_bwd_split(const float* q, const float* k, const float* v, const float* cos_t,
+                            const float* sin_t, const float* o, const float* lse,
+                            const float* dout, float* dq, float* dk, float* dv, int accumulate,
+                            int64_t B, int64_t T, int64_t H, int64_t hd, float scale,
+                            const void* fwd_workspace, void* workspace, size_t workspace_bytes,
+                            void* dq_split, void* dk_split, void* dv_split, void* stream) {
+    if (ttk_gemm_get_precision() != 0)
+        return set_error(TTK_ERR_ARG, "attention_bwd_split: planes exist for the bf16x3 precision");
+    int rc = attn_check(q, k, v, cos_t, sin_t, B, T, H, hd);
+    if (rc)
+        return rc;
+    if (!B || !T || !H)
+        return TTK_OK;
+    if (!o || !lse || !dout || !dq || !dk || !dv)
+        return set_error(TTK_ERR_ARG, "attention_bwd: null pointer");
+    const size_t need = fwd_workspace ? ttk_attention_bwd_ex_workspace_size(B, T, H, hd)
+                                      : ttk_attention_bwd_workspace_size(B, T, H, hd);
+    if (!workspace || workspace_bytes < need)
+        return set_error(TTK_ERR_ARG, "attention_bwd: workspace too small");
+    rc = attn_align_check({q, k, v, cos_t, sin_t, o, dout, dq, dk, dv, fwd_workspace, dq_split,
+                           dk_split, dv_split});
+    if (rc)
+        return rc;
+    const bool tc = attn_impl() == 0 && attention_tc_supported(static_cast<int>(hd));
+    return attention_mma_backward(static_cast<int>(hd), q, k, v, cos_t, sin_t, o, lse, dout, dq,
+                                  dk, dv, accumulate, B, T, H, scale, workspace, tc,
+                                  S(stream), fwd_workspace, dq_split, dk_split, dv_split);
+}
+
 }  // extern "C"

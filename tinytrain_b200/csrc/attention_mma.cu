@@ -830,7 +830,8 @@ template <int HD>
 int bwd(const float* q, const float* k, const float* v, const float* cs, const float* sn,
         const float* o, const float* lse, const float* dout, float* dq, float* dk, float* dv,
         int accumulate, int64_t B, int64_t T, int64_t H, float scale, SplitBufs s, float* Dv,
-        float* ld, bool tc, cudaStream_t st, bool qkv_ready = false) {
+        float* ld, bool tc, cudaStream_t st, bool qkv_ready = false, void* dq_split = nullptr,
+        void* dk_split = nullptr, void* dv_split = nullptr) {
     int rc = TTK_OK;
     if (!qkv_ready) {
         rc = launch_split(q, cs, sn, 1, scale, s.qh, s.ql, B, T, H, HD, st);
@@ -857,7 +858,10 @@ int bwd(const float* q, const float* k, const float* v, const float* cs, const f
         return rc;
     if (tc)
         return attention_tc_backward_core(HD, s.qh, s.kh, s.vh, s.dh, lse, Dv, ld, T32, cs, sn,
-                                          dq, dk, dv, accumulate, B, T, H, scale, st);
+                                          dq, dk, dv, accumulate, B, T, H, scale, st,
+                                          static_cast<__nv_bfloat16*>(dq_split),
+                                          static_cast<__nv_bfloat16*>(dk_split),
+                                          static_cast<__nv_bfloat16*>(dv_split));
     int smem = DkvSmem<HD>::BYTES;
     cudaFuncSetAttribute(attn_bwd_mma_dkv<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     dim3 g1(static_cast<unsigned>((T + DKV_BK - 1) / DKV_BK), static_cast<unsigned>(B * H));
@@ -873,7 +877,15 @@ int bwd(const float* q, const float* k, const float* v, const float* cs, const f
     attn_bwd_mma_dq<HD><<<g2, BWD_THREADS, smem, st>>>(s.qh, s.ql, s.kh, s.kl, s.vh, s.vl, s.dh,
                                                        s.dl, lse, Dv, cs, sn, dq, accumulate,
                                                        scale, T, static_cast<int>(H));
-    return check_launch("attn_bwd_mma_dq");
+    rc = check_launch("attn_bwd_mma_dq");
+    const int64_t R = B * T, D = H * HD;
+    if (!rc && dq_split)
+        rc = gemm_split(dq, R, D, D, 0, 1, dq_split, st);
+    if (!rc && dk_split)
+        rc = gemm_split(dk, R, D, D, 0, 1, dk_split, st);
+    if (!rc && dv_split)
+        rc = gemm_split(dv, R, D, D, 0, 1, dv_split, st);
+    return rc;
 }
 
 }  // namespace fa
@@ -904,7 +916,8 @@ int attention_mma_backward(int hd, const float* q, const float* k, const float* 
                            const float* cs, const float* sn, const float* o, const float* lse,
                            const float* dout, float* dq, float* dk, float* dv, int accumulate,
                            int64_t B, int64_t T, int64_t H, float scale, void* ws, bool tc,
-                           cudaStream_t st, const void* fwd_ws) {
+                           cudaStream_t st, const void* fwd_ws, void* dq_split, void* dk_split,
+                           void* dv_split) {
     const int64_t n = B * T * H * hd;
     float* Dv = static_cast<float*>(ws);
     __nv_bfloat16* w = reinterpret_cast<__nv_bfloat16*>(
@@ -924,13 +937,13 @@ int attention_mma_backward(int hd, const float* q, const float* k, const float* 
     switch (hd) {
         case 32:
             return fa::bwd<32>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                               scale, s, Dv, ld, tc, st, ready);
+                               scale, s, Dv, ld, tc, st, ready, dq_split, dk_split, dv_split);
         case 64:
             return fa::bwd<64>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                               scale, s, Dv, ld, tc, st, ready);
+                               scale, s, Dv, ld, tc, st, ready, dq_split, dk_split, dv_split);
         default:
             return fa::bwd<128>(q, k, v, cs, sn, o, lse, dout, dq, dk, dv, accumulate, B, T, H,
-                                scale, s, Dv, ld, tc, st, ready);
+                                scale, s, Dv, ld, tc, st, ready, dq_split, dk_split, dv_split);
     }
 }
 

@@ -553,11 +553,16 @@ __device__ __forceinline__ void load_owned(uint32_t taddr, int grp, float (&v)[H
 
 // Store owned columns of one gradient row (scaled; RoPE transpose rotation
 // when `rope`), overwriting or adding.
+// With `srow` (the row's place in bf16x3 operand planes, lo `plane` elements
+// after hi) the stored values are also split there (split_bf16, the split
+// kernel's arithmetic), after any accumulation.
 template <int HD>
 __device__ __forceinline__ void store_owned(const float (&g)[HD / 2], float* __restrict__ row,
                                             int64_t t, const float* __restrict__ cs,
                                             const float* __restrict__ sn, bool rope, float scale,
-                                            int grp, int accumulate) {
+                                            int grp, int accumulate,
+                                            __nv_bfloat16* __restrict__ srow = nullptr,
+                                            int64_t plane = 0) {
     constexpr int QW = HD / 4, HH = HD / 2;
 #pragma unroll
     for (int e = 0; e < QW; e += 4) {
@@ -584,6 +589,18 @@ __device__ __forceinline__ void store_owned(const float (&g)[HD / 2], float* __r
         }
         *p1 = make_float4(a[0], a[1], a[2], a[3]);
         *p2 = make_float4(b[0], b[1], b[2], b[3]);
+        if (srow) {
+            __nv_bfloat16 ah[4], al[4], bh[4], bl[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                split_bf16(a[u], ah[u], al[u]);
+                split_bf16(b[u], bh[u], bl[u]);
+            }
+            *reinterpret_cast<uint2*>(srow + d) = *reinterpret_cast<const uint2*>(ah);
+            *reinterpret_cast<uint2*>(srow + plane + d) = *reinterpret_cast<const uint2*>(al);
+            *reinterpret_cast<uint2*>(srow + HH + d) = *reinterpret_cast<const uint2*>(bh);
+            *reinterpret_cast<uint2*>(srow + plane + HH + d) = *reinterpret_cast<const uint2*>(bl);
+        }
     }
 }
 
@@ -637,7 +654,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                    const __grid_constant__ CUtensorMap map_v, const float* __restrict__ lse,
                    const float* __restrict__ Dv, const float* __restrict__ cs,
                    const float* __restrict__ sn, float* __restrict__ dq, int accumulate,
-                   float scale, int64_t T, int H) {
+                   float scale, int64_t T, int H, __nv_bfloat16* __restrict__ dq_split,
+                   int64_t plane) {
     using CF = DqCfg<HD>;
     constexpr int HH = HD / 2, KR = CF::KR, VR = CF::VR;
     extern __shared__ uint8_t smem_raw[];
@@ -885,8 +903,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             load_owned<HD>(tmem + lane_off + CF::ACC_COL, grp, g);
             if (q < T) {
                 const int64_t b = bh / H, h = bh % H;
-                store_owned<HD>(g, dq + ((b * T + q) * H + h) * HD, q, cs, sn, true, scale, grp,
-                                accumulate);
+                const int64_t off = ((b * T + q) * H + h) * HD;
+                store_owned<HD>(g, dq + off, q, cs, sn, true, scale, grp, accumulate,
+                                dq_split ? dq_split + off : nullptr, plane);
             }
         }
     }
@@ -913,7 +932,8 @@ __global__ void __launch_bounds__(DKV_THREADS, 1)
                     const __grid_constant__ CUtensorMap map_do, const float* __restrict__ ld,
                     int64_t T32, const float* __restrict__ cs, const float* __restrict__ sn,
                     float* __restrict__ dk, float* __restrict__ dv, int accumulate, int64_t T,
-                    int H) {
+                    int H, __nv_bfloat16* __restrict__ dk_split,
+                    __nv_bfloat16* __restrict__ dv_split, int64_t plane) {
     using CF = BwdCfg<HD, DKV_R1, DKV_R2>;
     constexpr int HH = HD / 2;
     extern __shared__ uint8_t smem_raw[];
@@ -1162,14 +1182,15 @@ __global__ void __launch_bounds__(DKV_THREADS, 1)
             tc_fence_after();
             float g[HH];
             const int64_t b = bh / H, h = bh % H;
+            const int64_t off = ((b * T + key) * H + h) * HD;
             load_owned<HD>(tmem + lane_off + CF::ACC_COL, grp, g);
             if (key < T)
-                store_owned<HD>(g, dv + ((b * T + key) * H + h) * HD, key, cs, sn, false, 1.0f,
-                                grp, accumulate);
+                store_owned<HD>(g, dv + off, key, cs, sn, false, 1.0f, grp, accumulate,
+                                dv_split ? dv_split + off : nullptr, plane);
             load_owned<HD>(tmem + lane_off + CF::ACC_COL + HD, grp, g);
             if (key < T)
-                store_owned<HD>(g, dk + ((b * T + key) * H + h) * HD, key, cs, sn, true, 1.0f,
-                                grp, accumulate);
+                store_owned<HD>(g, dk + off, key, cs, sn, true, 1.0f, grp, accumulate,
+                                dk_split ? dk_split + off : nullptr, plane);
         }
     }
 
@@ -1243,7 +1264,8 @@ int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloa
                                const float* lse, const float* Dv, const float* ld, int64_t T32,
                                const float* cs, const float* sn, float* dq, float* dk, float* dv,
                                int accumulate, int64_t B, int64_t T, int64_t H, float scale,
-                               cudaStream_t st) {
+                               cudaStream_t st, __nv_bfloat16* dq_split,
+                               __nv_bfloat16* dk_split, __nv_bfloat16* dv_split) {
     const int64_t n = B * T * H * hd;
     const int64_t BH = B * H;
     CUtensorMap q128, d128, k64, v64, k128, v128, q32, d32;
@@ -1264,7 +1286,8 @@ int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloa
         cudaFuncSetAttribute(fatc::attn_bwd_dkv_tc<HD>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         fatc::attn_bwd_dkv_tc<HD><<<grid, fatc::DKV_THREADS, smem, st>>>(
-            k128, v128, q32, d32, ld, T32, cs, sn, dk, dv, accumulate, T, static_cast<int>(H));
+            k128, v128, q32, d32, ld, T32, cs, sn, dk, dv, accumulate, T, static_cast<int>(H),
+            dk_split, dv_split, n);
         int r = check_launch("attn_bwd_dkv_tc");
         if (r)
             return r;
@@ -1272,7 +1295,8 @@ int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloa
         cudaFuncSetAttribute(fatc::attn_bwd_dq_tc<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem);
         fatc::attn_bwd_dq_tc<HD><<<grid, fatc::NUM_THREADS, smem, st>>>(
-            q128, d128, k64, v64, lse, Dv, cs, sn, dq, accumulate, scale, T, static_cast<int>(H));
+            q128, d128, k64, v64, lse, Dv, cs, sn, dq, accumulate, scale, T, static_cast<int>(H),
+            dq_split, n);
         return check_launch("attn_bwd_dq_tc");
     };
     if (hd == 128)

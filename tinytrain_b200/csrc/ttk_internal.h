@@ -77,11 +77,15 @@ int attention_mma_forward(int hd, const float* q, const float* k, const float* v
                           const float* cs, const float* sn, float* o, float* lse, int64_t B,
                           int64_t T, int64_t H, float scale, void* ws, bool tc,
                           cudaStream_t st, void* o_split = nullptr);
+// d*_split (optional, each): bf16x3 operand planes of dq / dk / dv as
+// [B*T, H*hd] rows, written by the tcgen05 epilogues or by split passes.
 int attention_mma_backward(int hd, const float* q, const float* k, const float* v,
                            const float* cs, const float* sn, const float* o, const float* lse,
                            const float* dout, float* dq, float* dk, float* dv, int accumulate,
                            int64_t B, int64_t T, int64_t H, float scale, void* ws, bool tc,
-                           cudaStream_t st, const void* fwd_ws = nullptr);
+                           cudaStream_t st, const void* fwd_ws = nullptr,
+                           void* dq_split = nullptr, void* dk_split = nullptr,
+                           void* dv_split = nullptr);
 
 // tcgen05 attention forward / backward (attention_tc.cu) over split planes
 // written by the mma.sync path's split pass; head dims 32, 64 and 128.
@@ -96,6 +100,8 @@ int attention_tc_backward_core(int hd, const __nv_bfloat16* qh, const __nv_bfloa
                                const float* lse, const float* Dv, const float* ld, int64_t T32,
                                const float* cs, const float* sn, float* dq, float* dk, float* dv,
                                int accumulate, int64_t B, int64_t T, int64_t H, float scale,
-                               cudaStream_t st);
+                               cudaStream_t st, __nv_bfloat16* dq_split = nullptr,
+                               __nv_bfloat16* dk_split = nullptr,
+                               __nv_bfloat16* dv_split = nullptr);
 
 }  // namespace ttk

@@ -462,6 +462,17 @@ Tensor reshape(const Tensor& a, const std::vector<int64_t>& shape) {
             const float* g = grad_in(oo);
             if (!g || !ao->requires_grad)
                 return;
+            // The view's gradient has the input's size and element order: when
+            // the input's gradient is still logically zero, hand over the
+            // buffer itself (with any operand split cached on it) instead of
+            // copying it. The view's own reference is dropped once this node
+            // has run, so the buffer then belongs to the input alone.
+            Buffer* ig = ao->grad.get();
+            const bool fresh = !ig || (ig->pending_fill && ig->fill_value == 0.0f && !ig->external);
+            if (fresh && !oo->grad->external && oo->grad->n == ao->numel) {
+                ao->grad = oo->grad;
+                return;
+            }
             accum_grad(ao, g);
         };
     }
@@ -1203,8 +1214,9 @@ Tensor fused_attention(const ImplPtr& qo, const ImplPtr& ko, const ImplPtr& vo, 
     const uint64_t vq = version_of(qo), vk = version_of(ko), vv = version_of(vo);
     Tensor::Impl* oo = out.impl().get();  // own node: raw, no cycle
     oo->prev = {qo, ko, vo};
-    oo->backward_fn = [qo, ko, vo, co, so, oo, lse, B, T, H, hd, scale, fw, vq, vk,
-                       vv]() mutable {
+    const bool grad_planes = planes && ttk_gemm_get_precision() == 0 && R * D >= (1 << 20);
+    oo->backward_fn = [qo, ko, vo, co, so, oo, lse, B, T, H, hd, scale, fw, vq, vk, vv,
+                       grad_planes]() mutable {
         const float* g = grad_in(oo);
         if (!g)
             return;
@@ -1233,7 +1245,42 @@ Tensor fused_attention(const ImplPtr& qo, const ImplPtr& ko, const ImplPtr& vo, 
         const float *qd = dread(qo), *kd = dread(ko), *vd = dread(vo);
         const bool reuse = fw && fw->ptr && vq != ~0ull && version_of(qo) == vq &&
                            version_of(ko) == vk && version_of(vo) == vv;
-        if (reuse) {
+        if (grad_planes) {
+            // The gradients' operand planes, cached on their buffers as the
+            // [B*T, H*hd] GEMM operand split the projections' backward reads.
+            const int64_t R = B * T, D = H * hd;
+            const size_t bytes = ttk_gemm_split_bytes(1, R, D);
+            auto planes_of = [&](const ImplPtr& p) -> Buffer* {
+                if (!p->requires_grad || !p->grad || p->grad->external)
+                    return nullptr;
+                Buffer& gb = *p->grad;
+                if (gb.split_bytes < bytes) {
+                    ttk_free(gb.split_dev, stream());
+                    gb.split_dev = nullptr;
+                    gb.split_bytes = 0;
+                    check(ttk_malloc(&gb.split_dev, bytes, stream()), "gradient planes");
+                    gb.split_bytes = bytes;
+                }
+                return &gb;
+            };
+            Buffer *pq = planes_of(qo), *pk = planes_of(ko), *pv = planes_of(vo);
+            const size_t ws = reuse ? ttk_attention_bwd_ex_workspace_size(B, T, H, hd)
+                                    : ttk_attention_bwd_workspace_size(B, T, H, hd);
+            Scratch w(ws);
+            check(ttk_attention_bwd_split(qd, kd, vd, dread(co), dread(so), dread(oo),
+                                          lse->device(), g, dq, dk, dv, all_fresh ? 0 : 1, B, T,
+                                          H, hd, scale, reuse ? fw->ptr : nullptr, w.ptr, ws,
+                                          pq ? pq->split_dev : nullptr,
+                                          pk ? pk->split_dev : nullptr,
+                                          pv ? pv->split_dev : nullptr, stream()),
+                  "attention bwd");
+            const int64_t key[7] = {0, 1, R, D, D, 0, 0};
+            for (Buffer* b : {pq, pk, pv})
+                if (b) {
+                    b->split_version = b->version;
+                    std::copy(key, key + 7, b->split_key);
+                }
+        } else if (reuse) {
             const size_t ws = ttk_attention_bwd_ex_workspace_size(B, T, H, hd);
             Scratch w(ws);
             check(ttk_attention_bwd_ex(qd, kd, vd, dread(co), dread(so), dread(oo),

@@ -228,6 +228,25 @@ def attention_bwd(q, k, v, cos, sin, o, lse, do, scale=None, out=None, accumulat
     return dq, dk, dv
 
 
+def attention_bwd_split(q, k, v, cos, sin, o, lse, do, scale=None, out=None, accumulate=False,
+                        fwd_ws=None):
+    """(dq, dk, dv, planes): the backward plus the bf16x3 operand planes of dq,
+    dk, dv, each as [B*T, H*hd] rows."""
+    B, T, H, hd = q.shape
+    scale = float(hd) ** -0.5 if scale is None else scale
+    dq, dk, dv = out if out is not None else (torch.empty_like(q), torch.empty_like(k),
+                                               torch.empty_like(v))
+    reuse = fwd_ws is not None and fwd_ws.numel() > 0
+    ws = workspace(call("ttk_attention_bwd_ex_workspace_size" if reuse else
+                        "ttk_attention_bwd_workspace_size", B, T, H, hd), q.device)
+    pb = call("ttk_gemm_split_bytes", 1, B * T, H * hd)
+    planes = [workspace(pb, q.device) for _ in range(3)]
+    call("ttk_attention_bwd_split", _p(q), _p(k), _p(v), _p(cos), _p(sin), _p(o), _p(lse),
+         _p(do), _p(dq), _p(dk), _p(dv), int(accumulate), B, T, H, hd, scale,
+         _p(fwd_ws) if reuse else None, _p(ws), ws.numel(), *(_p(x) for x in planes), _s())
+    return dq, dk, dv, planes
+
+
 def sumsq(tensors):
     acc = torch.zeros(1, dtype=torch.float64, device=tensors[0].device)
     ptrs = _ttk.ptr_array([t.data_ptr() for t in tensors])

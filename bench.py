@@ -356,6 +356,7 @@ def main():
     barrier()
 
     # ---- timed region: value
+    _ttk.call("ttk_pool_high_water", None, None, 1)
     _ttk.call("ttk_profile_enable", 1)
     if world > 1:
         tr.comm_profile(True)
@@ -373,6 +374,11 @@ def main():
             ev[i + 1].record(stream)
         barrier()
     launches = trn.kernel_launches() - l0
+    rh, uh = C.c_size_t(0), C.c_size_t(0)
+    _ttk.call("ttk_pool_high_water", C.byref(rh), C.byref(uh), 0)
+    free_b, total_b = torch.cuda.mem_get_info()
+    memory = {"pool_reserved_high_gb": rh.value / 1e9, "pool_used_high_gb": uh.value / 1e9,
+              "device_free_gb": free_b / 1e9, "device_total_gb": total_b / 1e9}
     comm = None
     if world > 1:
         tr.comm_profile(False)
@@ -444,6 +450,7 @@ def main():
             "mfu_fp32_equiv": value * flops_per_token(w) / 1e12 / world,
             "gpu_launches": launches,
             "launches_before_timed": l0,
+            "memory": memory,
             "allreduce": comm,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * tokens_rank * 8,
                     "d2h_bytes_per_step": 4, "steps": ke,

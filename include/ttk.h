@@ -60,6 +60,9 @@ int64_t ttk_launch_count(void);
 int ttk_malloc(void** ptr, size_t bytes, void* stream);
 int ttk_free(void* ptr, void* stream);
 int ttk_pool_stats(size_t* reserved, size_t* used);
+/* High-water marks of the device pool's reserved and used bytes since the
+ * last reset (reset != 0 resets them after reading). */
+int ttk_pool_high_water(size_t* reserved_high, size_t* used_high, int reset);
 int ttk_host_alloc(void** ptr, size_t bytes); /* pinned host memory */
 int ttk_host_free(void* ptr);
 

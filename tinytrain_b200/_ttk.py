@@ -34,6 +34,7 @@ SIGS = {
     "ttk_malloc": (I32, [P, SZ, P]),
     "ttk_free": (I32, [P, P]),
     "ttk_pool_stats": (I32, [P, P]),
+    "ttk_pool_high_water": (I32, [P, P, I32]),
     "ttk_host_alloc": (I32, [P, SZ]),
     "ttk_host_free": (I32, [P]),
     "ttk_memcpy_h2d": (I32, [P, P, SZ, P]),

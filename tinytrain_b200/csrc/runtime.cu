@@ -145,6 +145,28 @@ int ttk_free(void* ptr, void* stream) {
     return check_cuda(cudaFreeAsync(ptr, S(stream)), "cudaFreeAsync");
 }
 
+int ttk_pool_high_water(size_t* reserved_high, size_t* used_high, int reset) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaMemPool_t pool;
+    int rc = check_cuda(cudaDeviceGetDefaultMemPool(&pool, dev), "cudaDeviceGetDefaultMemPool");
+    if (rc)
+        return rc;
+    uint64_t r = 0, u = 0;
+    cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemHigh, &r);
+    cudaMemPoolGetAttribute(pool, cudaMemPoolAttrUsedMemHigh, &u);
+    if (reserved_high)
+        *reserved_high = r;
+    if (used_high)
+        *used_high = u;
+    if (reset) {
+        uint64_t z = 0;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReservedMemHigh, &z);
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrUsedMemHigh, &z);
+    }
+    return TTK_OK;
+}
+
 int ttk_pool_stats(size_t* reserved, size_t* used) {
     int dev = 0;
     cudaGetDevice(&dev);

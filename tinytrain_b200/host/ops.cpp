@@ -218,13 +218,28 @@ Tensor elem_binary(const Tensor& a, const Tensor& b, int op) {
             const float* g = grad_in(oo);
             if (!g)
                 return;
+            bool handed = false;  // the output gradient's buffer went to an input
             for (int which = 0; which < 2; ++which) {
                 const ImplPtr& X = which ? bo : ao;
                 if (!X->requires_grad)
                     continue;
                 const bool full = same_shape(X, shape);
                 if (full && (op == 0 || (op == 1 && which == 0))) {
-                    accum_grad(X, g);  // d(a+b)/da = d(a+b)/db = d(a-b)/da = 1
+                    // d(a+b)/da = d(a+b)/db = d(a-b)/da = 1. The first input
+                    // whose gradient is still logically zero takes the output
+                    // gradient's buffer itself (this node is its last reader);
+                    // any other gets a copy or an accumulation.
+                    Buffer* xg = X->grad.get();
+                    const bool fresh =
+                        !xg || (xg->pending_fill && xg->fill_value == 0.0f && !xg->external);
+                    // (numel > 1: never the backward root, whose seed stays.)
+                    if (!handed && fresh && !oo->grad->external && oo->grad->n == X->numel &&
+                        oo->numel > 1) {
+                        X->grad = oo->grad;
+                        handed = true;
+                        continue;
+                    }
+                    accum_grad(X, g);
                     continue;
                 }
                 Operand oa = operand(ao, shape), ob = operand(bo, shape);
@@ -466,10 +481,11 @@ Tensor reshape(const Tensor& a, const std::vector<int64_t>& shape) {
             // the input's gradient is still logically zero, hand over the
             // buffer itself (with any operand split cached on it) instead of
             // copying it. The view's own reference is dropped once this node
-            // has run, so the buffer then belongs to the input alone.
+            // has run, so the buffer then belongs to the input alone (a scalar
+            // view may be the backward root, whose seed stays: copied).
             Buffer* ig = ao->grad.get();
             const bool fresh = !ig || (ig->pending_fill && ig->fill_value == 0.0f && !ig->external);
-            if (fresh && !oo->grad->external && oo->grad->n == ao->numel) {
+            if (fresh && !oo->grad->external && oo->grad->n == ao->numel && oo->numel > 1) {
                 ao->grad = oo->grad;
                 return;
             }

@@ -9,9 +9,9 @@ Workloads (fp32, seeded):
              (M, K, N) in {(2048,256,256), (2048,256,32000), (8192,768,2048),
              (16384,2048,5632)}, inputs U(-1, 1)
   rmsnorm / swiglu / ce
-             forward + backward at rows = batch * seq of the 13M, 110M and 1B
-             configs (2048, 65536 per 64x1024 step in 16-row micro-batches of
-             16384, 16384), d / F of the config, vocab 32000 for CE
+             forward + backward at rows = one micro-batch of the bench's 13M,
+             110M and 1B configs (2048, 65536, 32768), d / F of the config,
+             vocab 32000 for CE
   hbm        AdamW + global-norm clip over the 1B model's 887.7M parameters,
              embedding gather / scatter-add and the residual add at 16384 x 2048
   attention  fused causal attention with RoPE, forward + backward, B 8, H 12,
@@ -39,7 +39,9 @@ from . import _ttk, kernels as K
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 GEMM_SHAPES = [(2048, 256, 256), (2048, 256, 32000), (8192, 768, 2048), (16384, 2048, 5632)]
-ROWS = [(2048, 256, 768), (16384, 768, 2048), (16384, 2048, 5632)]  # (rows, d, F)
+# (rows, d, F): rows = one micro-batch of the bench's configs (13M 16 x 128,
+# 110M 64 x 1024, 1B 16 x 2048)
+ROWS = [(2048, 256, 768), (65536, 768, 2048), (32768, 2048, 5632)]
 ATTN_S = [128, 512, 1024, 2048]
 
 

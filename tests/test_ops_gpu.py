@@ -190,10 +190,13 @@ def test_embedding_golden_bitexact(cuda, golden_ops):
     assert np.array_equal(n(dW), g["emb_dW"])
 
 
-@pytest.mark.parametrize("N,V,D", [(2048, 32000, 256), (16384, 32000, 2048), (3000, 7, 64)])
+@pytest.mark.parametrize("N,V,D", [(2048, 32000, 256), (16384, 32000, 2048), (3000, 7, 64),
+                                   (32768, 32000, 512), (40000, 7, 64)])
 def test_embedding_scatter_bitexact(cuda, N, V, D):
     """Sequential per-row order of ops.cpp:766-771 reproduced bit for bit,
-    including heavy collisions (V = 7) and a non-zero starting gradient."""
+    including heavy collisions (V = 7) and a non-zero starting gradient. Above
+    16384 ids the sort runs in 8192-key shared-memory chunks with the passes
+    across chunks in global memory (the 1B micro-batch has 32768)."""
     from oracle import restate as rs
     from tinytrain_b200 import kernels as K
     rng = np.random.default_rng(N + V)

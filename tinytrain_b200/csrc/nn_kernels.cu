@@ -707,6 +707,48 @@ __global__ void bitonic_smem_kernel(uint64_t* __restrict__ keys, int64_t Npow2) 
         keys[i] = sk[i];
 }
 
+// Stages of a global bitonic sort that stay inside chunks of BITONIC_CHUNK
+// keys, each chunk in one block's shared memory. Directions use the global
+// index (i & k), so the passes are those of the global network:
+//   first = 1: every stage k <= BITONIC_CHUNK (the chunks sorted in
+//              alternating directions);
+//   first = 0: the passes j < BITONIC_CHUNK of stage k (after the global
+//              passes j >= BITONIC_CHUNK of that stage).
+constexpr int64_t BITONIC_CHUNK = 8192;
+
+__global__ void __launch_bounds__(1024)
+    bitonic_chunk_kernel(uint64_t* __restrict__ keys, int64_t k_stage, int first) {
+    extern __shared__ uint64_t ck[];
+    const int64_t base = static_cast<int64_t>(blockIdx.x) * BITONIC_CHUNK;
+    for (int64_t i = threadIdx.x; i < BITONIC_CHUNK; i += blockDim.x)
+        ck[i] = keys[base + i];
+    __syncthreads();
+    auto pass = [&](int64_t k, int64_t j) {
+        for (int64_t i = threadIdx.x; i < BITONIC_CHUNK; i += blockDim.x) {
+            const int64_t p = i ^ j;
+            if (p > i) {
+                const bool up = ((base + i) & k) == 0;
+                const uint64_t a = ck[i], b = ck[p];
+                if ((a > b) == up) {
+                    ck[i] = b;
+                    ck[p] = a;
+                }
+            }
+        }
+        __syncthreads();
+    };
+    if (first) {
+        for (int64_t k = 2; k <= BITONIC_CHUNK; k <<= 1)
+            for (int64_t j = k >> 1; j > 0; j >>= 1)
+                pass(k, j);
+    } else {
+        for (int64_t j = BITONIC_CHUNK >> 1; j > 0; j >>= 1)
+            pass(k_stage, j);
+    }
+    for (int64_t i = threadIdx.x; i < BITONIC_CHUNK; i += blockDim.x)
+        keys[base + i] = ck[i];
+}
+
 // One compare-exchange pass (k, j) of a global-memory bitonic sort.
 __global__ void bitonic_global_kernel(uint64_t* __restrict__ keys, int64_t Npow2, int64_t k,
                                       int64_t j) {
@@ -1197,11 +1239,25 @@ int ttk_embedding_bwd(const float* dout, const int64_t* idx, float* dW, int64_t 
         bitonic_smem_kernel<<<1, 1024, smem, S(stream)>>>(keys, np2);
         rc = check_launch("bitonic_smem_kernel");
     } else {
-        for (int64_t k = 2; k <= np2 && !rc; k <<= 1)
-            for (int64_t j = k >> 1; j > 0 && !rc; j >>= 1) {
+        // np2 > 16384 is a multiple of the chunk: stages up to the chunk size
+        // in shared memory, then per stage the passes across chunks in global
+        // memory and the rest in shared memory again (the same network).
+        const int cs = static_cast<int>(BITONIC_CHUNK * sizeof(uint64_t));
+        cudaFuncSetAttribute(bitonic_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             cs);
+        const unsigned nchunks = static_cast<unsigned>(np2 / BITONIC_CHUNK);
+        bitonic_chunk_kernel<<<nchunks, 1024, cs, S(stream)>>>(keys, 0, 1);
+        rc = check_launch("bitonic_chunk_kernel");
+        for (int64_t k = 2 * BITONIC_CHUNK; k <= np2 && !rc; k <<= 1) {
+            for (int64_t j = k >> 1; j >= BITONIC_CHUNK && !rc; j >>= 1) {
                 bitonic_global_kernel<<<grid_for(np2, 256), 256, 0, S(stream)>>>(keys, np2, k, j);
                 rc = check_launch("bitonic_global_kernel");
             }
+            if (!rc) {
+                bitonic_chunk_kernel<<<nchunks, 1024, cs, S(stream)>>>(keys, k, 0);
+                rc = check_launch("bitonic_chunk_kernel");
+            }
+        }
     }
     if (rc)
         return rc;

@@ -14,8 +14,10 @@ so scaling is strong.
 
 value: tokens/s with the token ids already in HBM (tt_trainer_step_device),
 timed with CUDA events on the launching stream, max over ranks.
-e2e: the same through the public C ABI with host buffers (tt_trainer_step:
-host ids uploaded and the loss read back inside the timed region).
+e2e: the same through the public C ABI with host buffers
+(tt_trainer_step_submit / tt_trainer_step_result: each step's host ids
+uploaded and its loss read back inside the timed region, the next step
+submitted before the previous result is collected).
 roofline: the dominant kernel (the tcgen05 GEMM with the bf16x3 operand
 split) timed live over the timed region (events around each launch);
 achieved = algorithmic FLOPs (2*M*N*K per GEMM) / kernel time; traffic = the
@@ -262,7 +264,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="llama-1b", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--global-batch", type=int, default=None,
                     help="override the config's global batch (sequences), e.g. one "
@@ -400,7 +402,11 @@ def main():
     tokens_step = tokens_rank * world
     value = tokens_step / (ms / 1e3)
 
-    # ---- e2e: public C ABI with host buffers (upload ids, read loss back)
+    # ---- e2e: public C ABI with host buffers (upload ids, read loss back).
+    # tt_trainer_step_submit / _result: each step's ids go host -> device and
+    # its loss device -> host inside the timed region; the host submits step
+    # i + 1 before collecting step i, as a training loop would, so the device
+    # never waits for the host between steps.
     ke = max(1, args.e2e_steps)
     tr.step(pin_idx[0].numpy(), pin_tgt[0].numpy(), B, T, n_micro, 3e-4)  # warm path
     barrier()
@@ -410,9 +416,12 @@ def main():
     with ClockSampler([local] if world == 1 else list(range(world))) as clk_e2e:
         f0.record(stream)
         for i in range(ke):
-            loss_e2e, _ = tr.step(pin_idx[i % n_sets].numpy(), pin_tgt[i % n_sets].numpy(), B,
-                                  T, n_micro, 3e-4)
+            tr.step_submit(pin_idx[i % n_sets].numpy(), pin_tgt[i % n_sets].numpy(), B, T,
+                           n_micro, 3e-4)
             fe[i + 1].record(stream)
+            if i > 0:
+                loss_e2e, _ = tr.step_result()
+        loss_e2e, _ = tr.step_result()
         barrier()
     ms_e2e = max_over_ranks(f0.elapsed_time(f1)) / ke
     step_ms_e2e = max_each_over_ranks([fe[i].elapsed_time(fe[i + 1]) for i in range(ke)])

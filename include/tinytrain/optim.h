@@ -30,6 +30,11 @@ public:
     void set_grad_scale(float s) { grad_scale_ = s; }
     // Norm measured by the last step() with clipping on (reads the device).
     float last_grad_norm() const;
+    // The same without a host read: the device sum of squares behind it
+    // (null before the first clipped step) and the scale it is taken at;
+    // norm = sqrt(sum) * scale.
+    const double* grad_sumsq_device() const { return sumsq_; }
+    float grad_scale() const { return grad_scale_; }
     int64_t step_count() const { return step_; }
     // Optimizer state for checkpoints: first (which = 0) or second (1) moment
     // of parameter i on the device, allocated zeroed if it does not exist yet;

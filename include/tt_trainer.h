@@ -59,6 +59,17 @@ int tt_trainer_step(void* handle, const int64_t* idx, const int64_t* targets, in
 int tt_trainer_step_device(void* handle, const int64_t* idx, const int64_t* targets, int64_t B,
                            int64_t T, int64_t n_micro, float lr);
 int tt_trainer_last_loss(void* handle, float* loss);
+/* tt_trainer_step in two halves, so that the host prepares and enqueues step
+ * i + 1 while the device runs step i. submit copies the host ids into one of
+ * two pinned staging slots of the trainer (the caller may reuse its arrays on
+ * return), uploads them, enqueues the step and the copy of its loss and
+ * gradient norm into pinned memory, and returns without waiting. result waits
+ * for the oldest submitted step and returns its loss and norm (as
+ * tt_trainer_step does). At most two steps are in flight: a third submit
+ * before a result fails. */
+int tt_trainer_step_submit(void* handle, const int64_t* idx, const int64_t* targets, int64_t B,
+                           int64_t T, int64_t n_micro, float lr);
+int tt_trainer_step_result(void* handle, float* loss, float* grad_norm);
 /* Forward + cross-entropy + backward only (gradients accumulate into the
  * parameters' gradients, zeroed first); logits (host, may be NULL) receives
  * [B*T, vocab]. */

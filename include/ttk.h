@@ -68,6 +68,9 @@ int ttk_host_free(void* ptr);
 
 int ttk_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
 int ttk_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+/* Stream-ordered device-to-host copy that returns without waiting (dst
+ * pinned for the copy to be asynchronous); ttk_memcpy_d2h waits for it. */
+int ttk_memcpy_d2h_async(void* dst, const void* src, size_t bytes, void* stream);
 int ttk_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
 int ttk_memset(void* dst, int value, size_t bytes, void* stream);
 

@@ -76,3 +76,32 @@ def test_checkpoint_resume_continues_exactly(cuda, tmp_path):
     c = rb.cfg(vocab=CFG["vocab"], dim=CFG["dim"], layers=CFG["layers"], heads=CFG["heads"],
                ffn=CFG["ffn"], max_seq=CFG["max_seq"])
     assert np.array_equal(rb.load_checkpoint(c, ck), saved)
+
+
+def test_step_submit_result_equals_step(cuda):
+    """The pipelined halves (tt_trainer_step_submit / tt_trainer_step_result,
+    two steps in flight) give every step's loss and gradient norm and the
+    final weights of tt_trainer_step on the same ids, bit for bit; a third
+    submit before a result is refused."""
+    from tinytrain_b200 import trainer as TR
+    rng = np.random.default_rng(9)
+    B, T, n_micro, steps = 2, 64, 2, 4
+    ids = [(rng.integers(0, CFG["vocab"], B * T * n_micro),
+            rng.integers(0, CFG["vocab"], B * T * n_micro)) for _ in range(steps)]
+    a, b = _trainer(3, clip=1.0), _trainer(3, clip=1.0)
+    ref = [a.step(i, t, B, T, n_micro, 1e-3) for i, t in ids]
+    got = []
+    for k, (i, t) in enumerate(ids):
+        b.step_submit(i, t, B, T, n_micro, 1e-3)
+        if k == 1:  # two in flight now
+            with pytest.raises(TR.TrainerError, match="two steps are in flight"):
+                b.step_submit(i, t, B, T, n_micro, 1e-3)
+        if k > 0:
+            got.append(b.step_result())
+    got.append(b.step_result())
+    assert got == ref
+    assert np.array_equal(a.get_params(), b.get_params())
+    with pytest.raises(TR.TrainerError, match="no step in flight"):
+        b.step_result()
+    a.close()
+    b.close()

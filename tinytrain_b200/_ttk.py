@@ -39,6 +39,7 @@ SIGS = {
     "ttk_host_free": (I32, [P]),
     "ttk_memcpy_h2d": (I32, [P, P, SZ, P]),
     "ttk_memcpy_d2h": (I32, [P, P, SZ, P]),
+    "ttk_memcpy_d2h_async": (I32, [P, P, SZ, P]),
     "ttk_memcpy_d2d": (I32, [P, P, SZ, P]),
     "ttk_memset": (I32, [P, I32, SZ, P]),
     "ttk_stream_create": (I32, [P]),

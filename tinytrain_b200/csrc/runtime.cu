@@ -207,6 +207,13 @@ int ttk_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream) {
     return check_cuda(cudaStreamSynchronize(S(stream)), "memcpy d2h sync");
 }
 
+int ttk_memcpy_d2h_async(void* dst, const void* src, size_t bytes, void* stream) {
+    if (!bytes)
+        return TTK_OK;
+    return check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, S(stream)),
+                      "memcpy d2h async");
+}
+
 int ttk_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream) {
     if (!bytes)
         return TTK_OK;

@@ -11,6 +11,7 @@
 // the fused clip + AdamW kernel, which divides by world * n_micro.
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <thread>
@@ -123,9 +124,10 @@ struct Trainer {
     std::unordered_map<Tensor::Impl*, int> bucket_of;
     std::vector<void*> bucket_events;
     void* done_event = nullptr;
-    // collective watchdog: the end of the last distributed step, its deadline
-    void* step_event = nullptr;
-    bool step_pending = false;
+    // collective watchdog: the ends of the distributed steps in flight (at
+    // most two: the host enqueues a step while the previous one runs)
+    std::vector<void*> step_events;  // oldest first
+    std::vector<void*> spare_events;
     double coll_timeout_s = 300.0;
     std::string dist_error;  // set once the communicator was aborted
     // Optional timing of the gradient all-reduce: per bucket, events around
@@ -159,8 +161,17 @@ struct Trainer {
             ttk_stream_synchronize(s);
         if (comm)
             ttk_dist_destroy(comm);
-        if (step_event)
-            ttk_event_destroy(step_event);
+        for (void* e : step_events)
+            ttk_event_destroy(e);
+        for (void* e : spare_events)
+            ttk_event_destroy(e);
+        for (auto& sl : async_slots) {
+            ttk_host_free(sl.ids);
+            ttk_host_free(sl.out);
+            ttk_free(sl.dev, s);
+            if (sl.done)
+                ttk_event_destroy(sl.done);
+        }
         for (auto& r : comm_recs)
             event_pool.push_back(r.a), event_pool.push_back(r.b);
         for (auto& r : tail_recs)
@@ -247,12 +258,29 @@ struct Trainer {
         }
     }
 
+    // TT_TRACE_STEP=1: host-side timestamps of each micro-batch's enqueue
+    // (start of forward, end of backward) on stderr, to tell host stalls
+    // from device time.
+    bool trace = [] {
+        const char* e = std::getenv("TT_TRACE_STEP");
+        return e && e[0] == '1';
+    }();
+    std::chrono::steady_clock::time_point trace_t0;
+    void trace_mark(const char* what, int64_t m) {
+        if (!trace)
+            return;
+        const double ms = std::chrono::duration<double, std::milli>(
+                              std::chrono::steady_clock::now() - trace_t0).count();
+        std::fprintf(stderr, "tt_trace %s %ld %.2f\n", what, static_cast<long>(m), ms);
+    }
+
     // Runs fwd+bwd over n_micro micro-batches; ids are device pointers.
     void accumulate(const int64_t* idx, const int64_t* tgt, int64_t B, int64_t T,
                     int64_t n_micro) {
         check(ttk_memset(loss_acc, 0, 4, stream()), "loss zero");
         const int64_t per = B * T;
         for (int64_t m = 0; m < n_micro; ++m) {
+            trace_mark("fwd", m);
             const bool last = m + 1 == n_micro;
             if (comm && last) {
                 for (auto& bk : buckets)
@@ -269,8 +297,10 @@ struct Trainer {
                 Tensor logits = model->forward(DeviceIds::borrow(idx + m * per, per), B, T);
                 Tensor loss = cross_entropy(logits, DeviceIds::borrow(tgt + m * per, per));
                 check(ttk_axpy(1.0f, loss.device_data(), loss_acc, 1, stream()), "loss acc");
+                trace_mark("bwd", m);
                 loss.backward();
             }
+            trace_mark("done", m);
             if (comm && last) {
                 tt::set_grad_ready_hook(nullptr);
                 // Any bucket whose parameters got no gradient this step.
@@ -305,36 +335,50 @@ struct Trainer {
         opt->step();
     }
 
-    // Distributed steps: before a step, the previous one's collectives must
-    // have completed within the deadline (at most one step in flight); after
-    // it, its end is recorded for the next check.
+    // Distributed steps: before a step, at most one earlier step may still be
+    // running (the host enqueues a step while the previous one executes); an
+    // older one must have completed within the deadline. After a step its
+    // end is recorded for these checks.
     void begin_step() {
         if (!dist_error.empty())
             throw std::runtime_error("data-parallel step refused: the communicator was aborted (" +
                                      dist_error + ")");
-        wait_dist();
+        while (step_events.size() >= 2)
+            wait_oldest();
     }
 
     void end_step() {
         if (!comm)
             return;
-        if (!step_event)
-            check(ttk_event_create(&step_event), "event");
-        check(ttk_event_record(step_event, stream()), "record");
-        step_pending = true;
+        void* e = nullptr;
+        if (!spare_events.empty()) {
+            e = spare_events.back();
+            spare_events.pop_back();
+        } else {
+            check(ttk_event_create(&e), "event");
+        }
+        check(ttk_event_record(e, stream()), "record");
+        step_events.push_back(e);
     }
 
-    // Bounded wait for the recorded step end. On an asynchronous NCCL error
-    // or a deadline overrun (a peer left or hangs) the communicator is
-    // aborted, which ends the pending collectives, and the step throws.
+    // Every recorded step end, each with the bounded wait.
     void wait_dist() {
-        if (!comm || !step_pending)
+        while (comm && !step_events.empty())
+            wait_oldest();
+    }
+
+    // Bounded wait for the oldest recorded step end. On an asynchronous NCCL
+    // error or a deadline overrun (a peer left or hangs) the communicator is
+    // aborted, which ends the pending collectives, and the step throws.
+    void wait_oldest() {
+        if (!comm || step_events.empty())
             return;
+        void* ev = step_events.front();
         std::string why;
         const int rc = watch_collectives(
             [&] {
                 int d = 0;
-                check(ttk_event_query(step_event, &d), "event query");
+                check(ttk_event_query(ev, &d), "event query");
                 return d;
             },
             [&] {
@@ -342,16 +386,36 @@ struct Trainer {
                 return ttk_dist_async_error(comm, &e) != TTK_OK || e != 0 ? 1 : 0;
             },
             [&] { ttk_dist_abort(comm); }, coll_timeout_s, 1.0, why);
-        step_pending = false;
+        step_events.erase(step_events.begin());
+        spare_events.push_back(ev);
         if (rc == 0)
             return;
         comm = nullptr;  // freed by the abort
         dist_error = why;
+        for (void* e : step_events)
+            spare_events.push_back(e);
+        step_events.clear();
         ttk_stream_synchronize(stream());  // the aborted collectives have returned
         if (comm_stream)
             ttk_stream_synchronize(comm_stream);
         throw std::runtime_error("data-parallel step: " + why);
     }
+
+    // Pipelined steps (tt_trainer_step_submit / tt_trainer_step_result): two
+    // slots, each with pinned staging for the ids, device ids, pinned space
+    // for the loss and the squared gradient norm, and a completion event.
+    struct AsyncSlot {
+        int64_t* ids = nullptr;  // pinned: idx then targets
+        int64_t* dev = nullptr;
+        size_t cap = 0;          // ids per slot (idx + targets)
+        double* out = nullptr;   // pinned: [0] loss (as float bits), [1] sum of squares
+        void* done = nullptr;
+        bool pending = false;
+        float scale = 1.0f;      // gradient scale of the step (for the norm)
+        bool has_norm = false;
+    };
+    AsyncSlot async_slots[2];
+    int async_next = 0, async_oldest = 0;
 };
 
 // A token stream resident in device memory (int32, apps/prepare_data.cpp's
@@ -560,6 +624,8 @@ int tt_trainer_step(void* h, const int64_t* idx, const int64_t* targets, int64_t
                     int64_t n_micro, float lr, float* loss, float* grad_norm) {
     return guarded([&] {
         Trainer* t = T_(h);
+        t->trace_t0 = std::chrono::steady_clock::now();
+        t->trace_mark("step", 0);
         const int64_t n = B * T * n_micro;
         if (B <= 0 || T <= 0 || n_micro <= 0)
             throw std::invalid_argument("step: sizes must be positive");
@@ -577,10 +643,84 @@ int tt_trainer_step(void* h, const int64_t* idx, const int64_t* targets, int64_t
         t->optimizer_step(n_micro, lr);
         t->end_step();
         t->wait_dist();  // bounded, before the blocking loss read
+        t->trace_mark("enqueued", 0);
         if (loss)
             check(ttk_memcpy_d2h(loss, t->loss_out, 4, stream()), "loss read");
+        t->trace_mark("loss", 0);
         if (grad_norm)
             *grad_norm = t->ocfg.clip_norm > 0.0f ? t->opt->last_grad_norm() : 0.0f;
+    });
+}
+
+int tt_trainer_step_submit(void* h, const int64_t* idx, const int64_t* targets, int64_t B,
+                           int64_t T, int64_t n_micro, float lr) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        const int64_t n = B * T * n_micro;
+        if (B <= 0 || T <= 0 || n_micro <= 0)
+            throw std::invalid_argument("step: sizes must be positive");
+        Trainer::AsyncSlot& sl = t->async_slots[t->async_next];
+        if (sl.pending)
+            throw std::logic_error(
+                "step_submit: two steps are in flight; collect the oldest with step_result first");
+        for (int64_t i = 0; i < n; ++i)
+            if (idx[i] < 0 || idx[i] >= t->cfg.vocab_size || targets[i] < 0 ||
+                targets[i] >= t->cfg.vocab_size)
+                throw std::invalid_argument("embedding: index out of range");
+        if (sl.cap < static_cast<size_t>(2 * n)) {
+            if (sl.done)
+                check(ttk_event_synchronize(sl.done), "slot reuse");  // no copy still reads it
+            ttk_host_free(sl.ids);
+            ttk_free(sl.dev, stream());
+            sl.ids = nullptr;
+            sl.dev = nullptr;
+            check(ttk_host_alloc(reinterpret_cast<void**>(&sl.ids), static_cast<size_t>(n) * 16),
+                  "pinned ids");
+            check(ttk_malloc(reinterpret_cast<void**>(&sl.dev), static_cast<size_t>(n) * 16,
+                             stream()),
+                  "device ids");
+            sl.cap = static_cast<size_t>(2 * n);
+        }
+        if (!sl.out)
+            check(ttk_host_alloc(reinterpret_cast<void**>(&sl.out), 16), "pinned result");
+        if (!sl.done)
+            check(ttk_event_create(&sl.done), "event");
+        // The slot's previous upload finished before its result was collected,
+        // so the staging memory is free.
+        std::memcpy(sl.ids, idx, static_cast<size_t>(n) * 8);
+        std::memcpy(sl.ids + n, targets, static_cast<size_t>(n) * 8);
+        check(ttk_memcpy_h2d(sl.dev, sl.ids, static_cast<size_t>(n) * 16, stream()), "ids");
+        t->begin_step();
+        t->zero_grads();
+        t->accumulate(sl.dev, sl.dev + n, B, T, n_micro);
+        t->optimizer_step(n_micro, lr);
+        t->end_step();
+        check(ttk_memcpy_d2h_async(sl.out, t->loss_out, 4, stream()), "loss read");
+        const double* ss = t->opt->grad_sumsq_device();
+        sl.has_norm = t->ocfg.clip_norm > 0.0f && ss;
+        sl.scale = t->opt->grad_scale();
+        if (sl.has_norm)
+            check(ttk_memcpy_d2h_async(sl.out + 1, ss, 8, stream()), "norm read");
+        check(ttk_event_record(sl.done, stream()), "record");
+        sl.pending = true;
+        t->async_next ^= 1;
+    });
+}
+
+int tt_trainer_step_result(void* h, float* loss, float* grad_norm) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        Trainer::AsyncSlot& sl = t->async_slots[t->async_oldest];
+        if (!sl.pending)
+            throw std::logic_error("step_result: no step in flight");
+        t->wait_dist();  // bounded wait on the collectives (distributed runs)
+        check(ttk_event_synchronize(sl.done), "step result");
+        sl.pending = false;
+        t->async_oldest ^= 1;
+        if (loss)
+            std::memcpy(loss, sl.out, 4);
+        if (grad_norm)
+            *grad_norm = sl.has_norm ? static_cast<float>(std::sqrt(sl.out[1]) * sl.scale) : 0.0f;
     });
 }
 

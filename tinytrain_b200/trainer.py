@@ -52,6 +52,8 @@ _SIGS = {
     "tt_trainer_step": (C.c_int, [P, P, P, I64, I64, I64, F32, P, P]),
     "tt_trainer_step_device": (C.c_int, [P, P, P, I64, I64, I64, F32]),
     "tt_trainer_last_loss": (C.c_int, [P, P]),
+    "tt_trainer_step_submit": (C.c_int, [P, P, P, I64, I64, I64, F32]),
+    "tt_trainer_step_result": (C.c_int, [P, P, P]),
     "tt_trainer_forward_backward": (C.c_int, [P, P, P, I64, I64, P, P]),
     "tt_trainer_dist_init": (C.c_int, [P, C.c_int, C.c_int, P, I64]),
     "tt_trainer_set_collective_timeout": (C.c_int, [P, C.c_double]),
@@ -175,6 +177,20 @@ class Trainer:
         loss, gn = C.c_float(0), C.c_float(0)
         _chk(lib().tt_trainer_step(self.h, idx.ctypes.data, targets.ctypes.data, B, T, n_micro,
                                    lr, C.byref(loss), C.byref(gn)), "step")
+        return loss.value, gn.value
+
+    def step_submit(self, idx, targets, B, T, n_micro=1, lr=3e-4):
+        """Enqueue one step on host ids and return at once (collect it with
+        step_result; at most two in flight)."""
+        idx = np.ascontiguousarray(idx, np.int64)
+        targets = np.ascontiguousarray(targets, np.int64)
+        _chk(lib().tt_trainer_step_submit(self.h, idx.ctypes.data, targets.ctypes.data, B, T,
+                                          n_micro, lr), "step_submit")
+
+    def step_result(self):
+        """(loss, grad_norm) of the oldest submitted step, waiting for it."""
+        loss, gn = C.c_float(0), C.c_float(0)
+        _chk(lib().tt_trainer_step_result(self.h, C.byref(loss), C.byref(gn)), "step_result")
         return loss.value, gn.value
 
     def step_device(self, idx_ptr, tgt_ptr, B, T, n_micro=1, lr=3e-4):

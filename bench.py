@@ -27,7 +27,9 @@ ncu capture summarized in profiles/gemm_traffic_llama1b_microbatch.md.
 from __future__ import annotations
 
 import argparse
+import atexit
 import ctypes as C
+import datetime
 import json
 import os
 import statistics
@@ -90,65 +92,101 @@ def n_params(w):
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+    """nvidia-smi samples of SM clock and throttle reasons, one process per
+    node (local rank 0) for all of the node's GPUs in the run.
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    The sampler starts a couple of seconds before the first timed region, so
+    nvidia-smi's own start-up (driver queries on every GPU) stays outside the
+    timed steps, and it runs until the last region ends. Each sample carries
+    its timestamp; summary(t0, t1) keeps the samples taken between two
+    instants recorded with now() at a region's start and end."""
+
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    STARTUP_S = 2.0
 
-    _count = 0
-    _dir = None
-
-    def __init__(self, gpus):
+    def __init__(self, gpus, active=True):
         self.gpus = gpus
+        self.active = active
         self.proc = None
-        ClockSampler._count += 1
-        if ClockSampler._dir is None:
-            ClockSampler._dir = tempfile.mkdtemp(prefix="bench_clocks_")
-        self.path = os.path.join(ClockSampler._dir,
-                                 f"clocks_{os.getpid()}_{ClockSampler._count}.csv")
+        self.f = None
+        self.path = None
 
-    def __enter__(self):
+    def start(self):
+        if not self.active:
+            return self
         try:
+            d = tempfile.mkdtemp(prefix="bench_clocks_")
+            self.path = os.path.join(d, f"clocks_{os.getpid()}.csv")
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                  "-lms", "200", "-i", ",".join(str(g) for g in self.gpus)],
                 stdout=self.f, stderr=subprocess.DEVNULL)
+            atexit.register(self.stop)
+            time.sleep(self.STARTUP_S)
         except Exception:
             self.proc = None
         return self
 
-    def __exit__(self, *a):
+    def stop(self):
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+            self.proc = None
+        if self.f:
             self.f.close()
+            self.f = None
 
-    def summary(self):
-        if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+    @staticmethod
+    def now():
+        return datetime.datetime.now()
+
+    @staticmethod
+    def parse(lines, t0, t1):
+        """Median SM clock, max SM clock and the active throttle reasons of
+        the CSV sample lines stamped within [t0, t1]."""
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
+        rows = []
+        for line in lines:
             p = [x.strip() for x in line.split(",")]
-            if len(p) < 9:
+            if len(p) < 10:
                 continue
             try:
-                sm.append(float(p[1]))
-                smax.append(float(p[2]))
+                clk, cmax = float(p[2]), float(p[3])
             except ValueError:
                 continue
-            for n, v in zip(names, p[5:9]):
+            try:
+                ts = datetime.datetime.strptime(p[0], "%Y/%m/%d %H:%M:%S.%f")
+            except ValueError:
+                ts = None
+            rows.append((ts, clk, cmax, p))
+        # Samples whose timestamp does not parse are kept only if none parses
+        # (an unexpected nvidia-smi format then gives the whole run's samples).
+        windowed = any(r[0] is not None for r in rows)
+        for ts, clk, cmax, p in rows:
+            if windowed and (ts is None or ts < t0 or ts > t1):
+                continue
+            sm.append(clk)
+            smax.append(cmax)
+            for n, v in zip(names, p[6:10]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
         if not sm:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+    def summary(self, t0, t1):
+        if not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        with open(self.path) as f:
+            return self.parse(f.readlines(), t0, t1)
 
 
 def reference_micro_step(w):
@@ -367,14 +405,18 @@ def main():
     # bracket the timed region, the ones between give each step's time.
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     e0, e1 = ev[0], ev[-1]
-    with ClockSampler([local] if world == 1 else list(range(world))) as clk:
-        barrier()
-        e0.record(stream)
-        for i in range(args.steps):
-            tr.step_device(dev_idx[i % n_sets].data_ptr(), dev_tgt[i % n_sets].data_ptr(), B, T,
-                           n_micro, 3e-4)
-            ev[i + 1].record(stream)
-        barrier()
+    # One sampler per node (local rank 0) over the node's GPUs of this run,
+    # started before the timed region and stopped after the e2e region.
+    clk = ClockSampler([local] if world == 1 else list(range(world)), active=local == 0).start()
+    barrier()
+    c0 = clk.now()
+    e0.record(stream)
+    for i in range(args.steps):
+        tr.step_device(dev_idx[i % n_sets].data_ptr(), dev_tgt[i % n_sets].data_ptr(), B, T,
+                       n_micro, 3e-4)
+        ev[i + 1].record(stream)
+    barrier()
+    c1 = clk.now()
     launches = trn.kernel_launches() - l0
     rh, uh = C.c_size_t(0), C.c_size_t(0)
     _ttk.call("ttk_pool_high_water", C.byref(rh), C.byref(uh), 0)
@@ -413,16 +455,18 @@ def main():
     fe = [torch.cuda.Event(enable_timing=True) for _ in range(ke + 1)]
     f0, f1 = fe[0], fe[-1]
     loss_e2e = None
-    with ClockSampler([local] if world == 1 else list(range(world))) as clk_e2e:
-        f0.record(stream)
-        for i in range(ke):
-            tr.step_submit(pin_idx[i % n_sets].numpy(), pin_tgt[i % n_sets].numpy(), B, T,
-                           n_micro, 3e-4)
-            fe[i + 1].record(stream)
-            if i > 0:
-                loss_e2e, _ = tr.step_result()
-        loss_e2e, _ = tr.step_result()
-        barrier()
+    c2 = clk.now()
+    f0.record(stream)
+    for i in range(ke):
+        tr.step_submit(pin_idx[i % n_sets].numpy(), pin_tgt[i % n_sets].numpy(), B, T,
+                       n_micro, 3e-4)
+        fe[i + 1].record(stream)
+        if i > 0:
+            loss_e2e, _ = tr.step_result()
+    loss_e2e, _ = tr.step_result()
+    barrier()
+    c3 = clk.now()
+    clk.stop()
     ms_e2e = max_over_ranks(f0.elapsed_time(f1)) / ke
     step_ms_e2e = max_each_over_ranks([fe[i].elapsed_time(fe[i + 1]) for i in range(ke)])
     e2e = tokens_step / (ms_e2e / 1e3)
@@ -463,8 +507,8 @@ def main():
             "allreduce": comm,
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": 2 * tokens_rank * 8,
                     "d2h_bytes_per_step": 4, "steps": ke,
-                    "step_ms": [round(x, 2) for x in step_ms_e2e], "clocks": clk_e2e.summary()},
-            "clocks": clk.summary(),
+                    "step_ms": [round(x, 2) for x in step_ms_e2e], "clocks": clk.summary(c2, c3)},
+            "clocks": clk.summary(c0, c1),
             "loss": loss_dev, "loss_e2e": loss_e2e, "device_status": status,
         }
         if world == 1 and not args.no_cpu_baseline:

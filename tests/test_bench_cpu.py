@@ -37,3 +37,26 @@ def test_reference_arm_line():
     assert parts["per_layer_s"] == pytest.approx(parts["timed"]["2"] - parts["timed"]["1"])
     assert line["steps"] == 2 and line["steps_requested"] == 1
     assert line["config"]["workload"].startswith("llama-13m")
+
+
+def test_clock_samples_windowed_by_timestamp():
+    """The clock summary keeps only the samples stamped inside the timed
+    region, so nvidia-smi's start-up and the idle seconds before the region do
+    not count; the throttle reasons come from the samples inside it."""
+    import datetime
+    sys.path.insert(0, ROOT)
+    import bench
+
+    def row(ts, mhz, cap):
+        return (f"2026/12/02 10:00:{ts:06.3f}, 0, {mhz}, 1965, 900.0, 0x4, Not Active, "
+                f"Not Active, Not Active, {'Active' if cap else 'Not Active'}")
+    lines = [row(1.0, 300, False), row(2.0, 300, False),  # before the region: idle
+             row(3.0, 1450, True), row(3.2, 1460, True), row(3.4, 1440, False),
+             row(5.0, 1965, False), "garbage line", ""]
+    t0 = datetime.datetime(2026, 12, 2, 10, 0, 2, 500000)
+    t1 = datetime.datetime(2026, 12, 2, 10, 0, 4, 0)
+    s = bench.ClockSampler.parse(lines, t0, t1)
+    assert s["samples"] == 3 and s["sm_mhz"] == 1450.0 and s["sm_max_mhz"] == 1965.0
+    assert s["reasons"] == ["sw_power_cap"]
+    empty = bench.ClockSampler.parse(lines, t1, t1)
+    assert empty["sm_mhz"] is None and empty["reasons"] == ["no samples"]

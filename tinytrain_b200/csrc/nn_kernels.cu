@@ -985,6 +985,38 @@ static inline int rms_block(int64_t D) {  // threads per block: whole rows, up t
     return tpr >= 256 ? tpr : tpr * (256 / tpr);
 }
 
+// Blocks of `kernel` (bs threads, static shared memory only) that are
+// resident at once on all SMs of the current device: the row kernels loop
+// over rows with a grid stride, so a grid of exactly one resident wave keeps
+// every SM busy to the end (a grid of 1.6 waves left 40% of the SMs idle for
+// the second wave's duration). Cached per device and block size.
+template <class Kernel>
+static int64_t resident_grid(Kernel kernel, int bs, int slot) {
+    constexpr int kDevs = 16, kSlots = 2, kSizes = 33;
+    static int cache[kDevs][kSlots][kSizes] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess)
+        dev = 0;
+    const int bi = bs / 32;
+    int* c = (dev < kDevs && slot < kSlots && bi < kSizes && bs % 32 == 0) ? &cache[dev][slot][bi]
+                                                                          : nullptr;
+    if (c && *c > 0)
+        return *c;
+    int sms = 0, per = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        sms <= 0)
+        sms = 148;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, bs, 0) != cudaSuccess ||
+        per <= 0) {
+        cudaGetLastError();
+        per = 2;
+    }
+    const int n = sms * per;
+    if (c)
+        *c = n;
+    return n;
+}
+
 extern "C" {
 
 int ttk_rmsnorm_fwd(const float* x, const float* w, float* y, float* rstd, int64_t R, int64_t D,
@@ -997,7 +1029,8 @@ int ttk_rmsnorm_fwd(const float* x, const float* w, float* y, float* rstd, int64
         return set_error(TTK_ERR_ARG, "rmsnorm_fwd: tensors must be 16-byte aligned");
     if (rms_rows_ok(D)) {
         const int tpr = static_cast<int>(D / RMS_EPT), bs = rms_block(D);
-        const int64_t blocks = std::min<int64_t>((R + bs / tpr - 1) / (bs / tpr), 148 * 8);
+        const int64_t blocks = std::min<int64_t>((R + bs / tpr - 1) / (bs / tpr),
+                                                 resident_grid(rmsnorm_fwd_rows_kernel, bs, 0));
         rmsnorm_fwd_rows_kernel<<<static_cast<int>(blocks), bs, 0, S(stream)>>>(x, w, y, rstd, R,
                                                                                  D, eps, nullptr);
         return check_launch("rmsnorm_fwd_rows_kernel");
@@ -1019,7 +1052,8 @@ int ttk_rmsnorm_fwd_split(const float* x, const float* w, float* y, float* rstd,
     if (R == 0)
         return TTK_OK;
     const int tpr = static_cast<int>(D / RMS_EPT), bs = rms_block(D);
-    const int64_t blocks = std::min<int64_t>((R + bs / tpr - 1) / (bs / tpr), 148 * 8);
+    const int64_t blocks = std::min<int64_t>((R + bs / tpr - 1) / (bs / tpr),
+                                             resident_grid(rmsnorm_fwd_rows_kernel, bs, 0));
     rmsnorm_fwd_rows_kernel<<<static_cast<int>(blocks), bs, 0, S(stream)>>>(
         x, w, y, rstd, R, D, eps, static_cast<__nv_bfloat16*>(split));
     return check_launch("rmsnorm_fwd_rows_kernel");
@@ -1031,10 +1065,12 @@ static int colsum_grid(int64_t D) {
 
 static int64_t rms_blocks(int64_t R) { return std::min<int64_t>(std::max<int64_t>(R / 64, 1), 296); }
 
-// Row-parallel backward: blocks and dw partial rows (one per row slot).
+// Row-parallel backward: blocks (one resident wave) and dw partial rows (one
+// per row slot).
 static int64_t rms_rows_blocks(int64_t R, int64_t D) {
-    const int rpb = rms_block(D) / static_cast<int>(D / RMS_EPT);
-    return std::min<int64_t>((R + rpb - 1) / rpb, 148 * 2);
+    const int bs = rms_block(D);
+    const int rpb = bs / static_cast<int>(D / RMS_EPT);
+    return std::min<int64_t>((R + rpb - 1) / rpb, resident_grid(rmsnorm_bwd_rows_kernel, bs, 1));
 }
 
 size_t ttk_rmsnorm_bwd_workspace_size(int64_t R, int64_t D) {

@@ -95,16 +95,15 @@ class ClockSampler:
     """nvidia-smi samples of SM clock and throttle reasons, one process per
     node (local rank 0) for all of the node's GPUs in the run.
 
-    The sampler starts a couple of seconds before the first timed region, so
-    nvidia-smi's own start-up (driver queries on every GPU) stays outside the
-    timed steps, and it runs until the last region ends. Each sample carries
-    its timestamp; summary(t0, t1) keeps the samples taken between two
-    instants recorded with now() at a region's start and end."""
+    The sampler starts before the warm-up steps, so nvidia-smi's own start-up
+    (driver queries on every GPU) overlaps the warm-up and leaves the device
+    busy, and it runs until the last region ends. Each sample carries its
+    timestamp; summary(t0, t1) keeps the samples taken between two instants
+    recorded with now() at a region's start and end."""
 
     Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
-    STARTUP_S = 2.0
 
     def __init__(self, gpus, active=True):
         self.gpus = gpus
@@ -125,7 +124,6 @@ class ClockSampler:
                  "-lms", "200", "-i", ",".join(str(g) for g in self.gpus)],
                 stdout=self.f, stderr=subprocess.DEVNULL)
             atexit.register(self.stop)
-            time.sleep(self.STARTUP_S)
         except Exception:
             self.proc = None
         return self
@@ -389,11 +387,21 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return [float(x) for x in t.tolist()]
 
-    # ---- warm-up (device-resident ids)
+    # One clock sampler per node (local rank 0) over the node's GPUs of this
+    # run, started before the warm-up and stopped after the e2e region.
+    clk = ClockSampler([local] if world == 1 else list(range(world)), active=local == 0).start()
+
+    # ---- warm-up (device-resident ids). The last warm-up step runs with the
+    # GEMM timing on, so the timed steps find its CUDA events already
+    # created: creating the ~10k events of a first timed step cost 0.4 s of
+    # device time (9.40 s against 8.99 s for the next steps).
     for i in range(args.warmup):
+        if i == args.warmup - 1:
+            _ttk.call("ttk_profile_enable", 1)
         tr.step_device(dev_idx[i % n_sets].data_ptr(), dev_tgt[i % n_sets].data_ptr(), B, T,
                        n_micro, 3e-4)
     barrier()
+    _ttk.call("ttk_profile_read", None, None, None)  # discard; returns the events to the pool
 
     # ---- timed region: value
     _ttk.call("ttk_pool_high_water", None, None, 1)
@@ -405,9 +413,6 @@ def main():
     # bracket the timed region, the ones between give each step's time.
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
     e0, e1 = ev[0], ev[-1]
-    # One sampler per node (local rank 0) over the node's GPUs of this run,
-    # started before the timed region and stopped after the e2e region.
-    clk = ClockSampler([local] if world == 1 else list(range(world)), active=local == 0).start()
     barrier()
     c0 = clk.now()
     e0.record(stream)
@@ -450,7 +455,12 @@ def main():
     # i + 1 before collecting step i, as a training loop would, so the device
     # never waits for the host between steps.
     ke = max(1, args.e2e_steps)
-    tr.step(pin_idx[0].numpy(), pin_tgt[0].numpy(), B, T, n_micro, 3e-4)  # warm path
+    # warm path: both submission slots (their pinned staging is allocated on
+    # first use)
+    for i in range(2):
+        tr.step_submit(pin_idx[i].numpy(), pin_tgt[i].numpy(), B, T, n_micro, 3e-4)
+    for i in range(2):
+        tr.step_result()
     barrier()
     fe = [torch.cuda.Event(enable_timing=True) for _ in range(ke + 1)]
     f0, f1 = fe[0], fe[-1]

@@ -306,12 +306,12 @@ int ttk_attention_bwd_split(const float* q, const float* k, const float* v, cons
                             void* dq_split, void* dk_split, void* dv_split, void* stream);
 /* Attention engine (process-wide), all fp32-accurate:
  *   0 = tensor cores (default): tcgen05 forward and backward for head dims
- *       64 and 128, mma.sync m16n8k16 elsewhere, both with the bf16x3
+ *       32, 64 and 128, mma.sync m16n8k16 elsewhere, both with the bf16x3
  *       operand split;
- *   1 = fp32 FMA kernels;
  *   2 = mma.sync m16n8k16 kernels only.
- * The environment variable TTK_ATTENTION=fma | mma selects 1 | 2 at start-up.
- * Workspace sizes depend on the choice. */
+ * Engine 1 (scalar fp32 FMA kernels) was removed; asking for it fails with
+ * TTK_ERR_ARG. The environment variable TTK_ATTENTION=mma selects 2 at
+ * start-up. Workspace sizes depend on the choice. */
 int ttk_attention_set_impl(int impl);
 int ttk_attention_get_impl(void);
 

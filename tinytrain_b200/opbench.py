@@ -114,39 +114,54 @@ def bench_gemm(shapes, iters):
                   "includes": "operand split (hi/lo) + tcgen05 kernel"})
 
 
-def bench_rows(rows, iters):
+def bench_rows(rows, iters, ops=("rmsnorm", "swiglu", "ce")):
     hbm, _, src = peaks()
     for (R, D, F) in rows:
-        x = torch.rand(R, D, device="cuda") * 2 - 1
-        w = torch.rand(D, device="cuda")
-        dy = torch.rand(R, D, device="cuda") * 2 - 1
-        y, rstd = K.rmsnorm_fwd(x, w, 1e-5)
-        ms = timed(lambda: K.rmsnorm_fwd(x, w, 1e-5), iters)
-        emit({"op": "rmsnorm", "pass": "fwd", "rows": R, "d": D, "ms": ms,
-              "gbs": 8 * R * D / ms / 1e6, "frac_hbm": 8 * R * D / ms / 1e6 / hbm,
-              "peak_src": src})
-        dx, dw = torch.empty_like(x), torch.zeros_like(w)
-        ms = timed(lambda: K.rmsnorm_bwd(x, w, rstd, dy, dx=dx, dw=dw), iters)
-        emit({"op": "rmsnorm", "pass": "bwd", "rows": R, "d": D, "ms": ms,
-              "gbs": 12 * R * D / ms / 1e6, "frac_hbm": 12 * R * D / ms / 1e6 / hbm})
-        a = torch.rand(R, F, device="cuda") * 8 - 4
-        b = torch.rand(R, F, device="cuda") * 2 - 1
-        g = torch.rand(R, F, device="cuda") * 2 - 1
-        ms = timed(lambda: K.swiglu_fwd(a, b), iters)
-        emit({"op": "swiglu", "pass": "fwd", "rows": R, "F": F, "ms": ms,
-              "gbs": 12 * R * F / ms / 1e6, "frac_hbm": 12 * R * F / ms / 1e6 / hbm})
-        da, db = torch.empty_like(a), torch.empty_like(b)
-        ms = timed(lambda: K.swiglu_bwd(a, b, g, da=da, db=db), iters)
-        emit({"op": "swiglu", "pass": "bwd", "rows": R, "F": F, "ms": ms,
-              "gbs": 20 * R * F / ms / 1e6, "frac_hbm": 20 * R * F / ms / 1e6 / hbm})
-        V = 32000
-        L = torch.randn(R, V, device="cuda") * 3
-        t = torch.randint(0, V, (R,), device="cuda", dtype=torch.int64)
-        dL = torch.empty_like(L)
-        ms = timed(lambda: K.cross_entropy(L, t, dlogits=dL), iters)
-        emit({"op": "cross_entropy", "pass": "fwd+bwd fused", "rows": R, "vocab": V, "ms": ms,
-              "gbs": 8 * R * V / ms / 1e6, "frac_hbm": 8 * R * V / ms / 1e6 / hbm})
-        del L, dL
+        if "rmsnorm" in ops:
+            bench_rmsnorm(R, D, iters, hbm, src)
+        if "swiglu" in ops:
+            bench_swiglu(R, F, iters, hbm)
+        if "ce" in ops:
+            bench_ce(R, iters, hbm)
+
+
+def bench_rmsnorm(R, D, iters, hbm, src):
+    x = torch.rand(R, D, device="cuda") * 2 - 1
+    w = torch.rand(D, device="cuda")
+    dy = torch.rand(R, D, device="cuda") * 2 - 1
+    y, rstd = K.rmsnorm_fwd(x, w, 1e-5)
+    ms = timed(lambda: K.rmsnorm_fwd(x, w, 1e-5), iters)
+    emit({"op": "rmsnorm", "pass": "fwd", "rows": R, "d": D, "ms": ms,
+          "gbs": 8 * R * D / ms / 1e6, "frac_hbm": 8 * R * D / ms / 1e6 / hbm,
+          "peak_src": src})
+    dx, dw = torch.empty_like(x), torch.zeros_like(w)
+    ms = timed(lambda: K.rmsnorm_bwd(x, w, rstd, dy, dx=dx, dw=dw), iters)
+    emit({"op": "rmsnorm", "pass": "bwd", "rows": R, "d": D, "ms": ms,
+          "gbs": 12 * R * D / ms / 1e6, "frac_hbm": 12 * R * D / ms / 1e6 / hbm})
+
+
+def bench_swiglu(R, F, iters, hbm):
+    a = torch.rand(R, F, device="cuda") * 8 - 4
+    b = torch.rand(R, F, device="cuda") * 2 - 1
+    g = torch.rand(R, F, device="cuda") * 2 - 1
+    ms = timed(lambda: K.swiglu_fwd(a, b), iters)
+    emit({"op": "swiglu", "pass": "fwd", "rows": R, "F": F, "ms": ms,
+          "gbs": 12 * R * F / ms / 1e6, "frac_hbm": 12 * R * F / ms / 1e6 / hbm})
+    da, db = torch.empty_like(a), torch.empty_like(b)
+    ms = timed(lambda: K.swiglu_bwd(a, b, g, da=da, db=db), iters)
+    emit({"op": "swiglu", "pass": "bwd", "rows": R, "F": F, "ms": ms,
+          "gbs": 20 * R * F / ms / 1e6, "frac_hbm": 20 * R * F / ms / 1e6 / hbm})
+
+
+def bench_ce(R, iters, hbm):
+    V = 32000
+    L = torch.randn(R, V, device="cuda") * 3
+    t = torch.randint(0, V, (R,), device="cuda", dtype=torch.int64)
+    dL = torch.empty_like(L)
+    ms = timed(lambda: K.cross_entropy(L, t, dlogits=dL), iters)
+    emit({"op": "cross_entropy", "pass": "fwd+bwd fused", "rows": R, "vocab": V, "ms": ms,
+          "gbs": 8 * R * V / ms / 1e6, "frac_hbm": 8 * R * V / ms / 1e6 / hbm})
+    del L, dL
 
 
 def llama1b_param_shapes(d=2048, layers=16, ffn=5632, vocab=32000):
@@ -236,6 +251,10 @@ def main():
     ap.add_argument("--only", choices=["gemm", "rows", "ce", "hbm", "attention"], default=None)
     ap.add_argument("--shape", default=None, help="M,K,N for --only gemm")
     ap.add_argument("--rows", type=int, default=None)
+    ap.add_argument("--dims", default=None,
+                    help="R,D,F: one row shape for --only rows (e.g. a capture-sized case)")
+    ap.add_argument("--ops", default="rmsnorm,swiglu,ce",
+                    help="row kernels for --only rows: any of rmsnorm, swiglu, ce")
     ap.add_argument("--seq", type=int, default=None)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--hd", type=int, default=64)
@@ -246,10 +265,13 @@ def main():
     _ttk.call("ttk_init", 0)
     shapes = [tuple(int(x) for x in a.shape.split(","))] if a.shape else GEMM_SHAPES
     rows = [r for r in ROWS if a.rows is None or r[0] == a.rows] or ROWS
+    if a.dims:
+        rows = [tuple(int(x) for x in a.dims.split(","))]
     if a.only in (None, "gemm"):
         bench_gemm(shapes, a.iters)
     if a.only in (None, "rows", "ce"):
-        bench_rows(rows, a.iters)
+        ops = ("ce",) if a.only == "ce" else tuple(a.ops.split(","))
+        bench_rows(rows, a.iters, ops)
     if a.only in (None, "hbm"):
         bench_hbm(a.iters)
     if a.only in (None, "attention"):

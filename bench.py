@@ -212,13 +212,23 @@ def reference_micro_step(w):
         return None
     B, T = CPU_SAMPLE[w["model"]]
     d1, d2 = SAMPLE_DEPTHS
-    t, opt = {}, {}
+    t, opt, reps = {}, {}, {}
     for d in (d1, d2):
         c = rb.cfg(vocab=w["vocab"], dim=w["dim"], layers=d, heads=w["heads"], ffn=w["ffn"],
                    max_seq=max(w["max_seq"], T))
         t[d], opt[d] = rb.time_phases(c, B, T, 1, 1)
+        reps[d] = 1
+        if t[d] < 1.0:
+            # A small model's micro-step is short against timer and load
+            # noise: average enough of them for about two seconds.
+            reps[d] = min(20, int(2.0 / max(t[d], 1e-3)) + 1)
+            t[d], opt[d] = rb.time_phases(c, B, T, 1, reps[d])
     per_layer = (t[d2] - t[d1]) / (d2 - d1)
-    rest = t[d1] - d1 * per_layer
+    if per_layer <= 0.0:
+        # Noise larger than a layer's cost (tiny models only): charge the
+        # whole depth-d2 time to its layers.
+        per_layer = t[d2] / d2
+    rest = max(t[d1] - d1 * per_layer, 0.0)
     micro = rest + w["layers"] * per_layer
     w2 = dict(w, layers=d2)
     opt_full = opt[d2] * n_params(w) / n_params(w2)
@@ -227,7 +237,8 @@ def reference_micro_step(w):
     tps = w["global_batch"] * w["seq"] / step
     sample = (f"reference train step at the {w['model']} width, one micro-step of {B} x {T} "
               f"tokens (forward, cross-entropy, backward) timed at depth {d1} ({t[d1]:.1f} s) and "
-              f"depth {d2} ({t[d2]:.1f} s), each after one untimed micro-step: "
+              f"depth {d2} ({t[d2]:.1f} s), each after one untimed micro-step"
+              f"{' (means over %d and %d micro-steps)' % (reps[d1], reps[d2]) if reps[d1] > 1 or reps[d2] > 1 else ''}: "
               f"{per_layer:.1f} s per layer + {rest:.1f} s base, "
               f"{micro:.0f} s per full-depth ({w['layers']} layers) micro-step; clip + AdamW "
               f"{opt_full:.1f} s (timed at depth {d2}, scaled to {n_params(w)} parameters) "

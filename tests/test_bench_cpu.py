@@ -34,7 +34,10 @@ def test_reference_arm_line():
     parts = line["reference_parts"]
     # full depth = rest + layers * per_layer, with the parts from the two samples
     assert parts["micro_s"] == pytest.approx(parts["rest_s"] + 6 * parts["per_layer_s"])
-    assert parts["per_layer_s"] == pytest.approx(parts["timed"]["2"] - parts["timed"]["1"])
+    # per layer = t(2) - t(1), or t(2) / 2 when timing noise makes the difference <= 0
+    assert parts["per_layer_s"] > 0 and parts["rest_s"] >= 0
+    assert parts["per_layer_s"] in (pytest.approx(parts["timed"]["2"] - parts["timed"]["1"]),
+                                    pytest.approx(parts["timed"]["2"] / 2))
     assert line["steps"] == 2 and line["steps_requested"] == 1
     assert line["config"]["workload"].startswith("llama-13m")
 

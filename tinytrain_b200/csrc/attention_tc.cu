@@ -436,33 +436,50 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         tmem_dealloc(tmem, CF::TMEM_COLS);
     }
     if (warp >= 2 && warp < 2 + 8 && !*abort_flag) {
+        // Epilogue in two phases. (1) Each thread scales its half row of O
+        // and puts it in a shared-memory tile [BQ][HD + 4] over the K/V ring
+        // (free: every MMA that read it has completed). (2) The eight warps
+        // store the tile row by row, HD / 4 lanes per row with one float4
+        // each, so a warp's stores (and those of the bf16x3 planes) cover
+        // whole contiguous rows instead of 32 rows 4 KB apart.
+        constexpr int LD = HD + 4;  // row pitch in floats: conflict-free float4 stores
+        static_assert(BQ * LD * 4 <= NSLOT * CF::SLOT_BYTES, "epilogue tile fits the ring");
+        float* tile = reinterpret_cast<float*>(smem + CF::OFF_SLOT);
         const int quad = warp & 3, half = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const int64_t q = q0 + r;
         const float lt = l_own + red[(half ^ 1) * BQ + r];
-        if (q < T) {
-            const int64_t b = bh / H, h = bh % H;
-            const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
-            const int64_t off = ((b * T + q) * H + h) * HD + half * OH;
-            float* dst = o + off;
+        const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
+        float* trow = tile + r * LD + half * OH;
 #pragma unroll
-            for (int c = 0; c < OH; c += 4) {
-                const float ov[4] = {acc[c] * inv, acc[c + 1] * inv, acc[c + 2] * inv,
-                                     acc[c + 3] * inv};
-                *reinterpret_cast<float4*>(dst + c) = make_float4(ov[0], ov[1], ov[2], ov[3]);
-                if (o_split) {  // the split kernel's arithmetic (split_bf16)
-                    __nv_bfloat16 hi[4], lo[4];
+        for (int c = 0; c < OH; c += 4)
+            *reinterpret_cast<float4*>(trow + c) =
+                make_float4(acc[c] * inv, acc[c + 1] * inv, acc[c + 2] * inv, acc[c + 3] * inv);
+        if (q < T && half == 0)
+            lse[bh * T + q] = m_out * LN2 + logf(lt);
+        asm volatile("bar.sync 1, %0;" ::"n"(SOFTMAX_THREADS) : "memory");
+        constexpr int LPR = HD / 4;     // lanes per row
+        constexpr int RPI = 32 / LPR;   // rows per warp instruction
+        const int sw = warp - 2;
+        const int c = (lane % LPR) * 4;
+        const int64_t b = bh / H, h = bh % H;
+        for (int rr = sw * RPI + lane / LPR; rr < BQ; rr += 8 * RPI) {
+            const int64_t qq = q0 + rr;
+            if (qq >= T)
+                break;
+            const float4 v = *reinterpret_cast<const float4*>(tile + rr * LD + c);
+            const int64_t off = ((b * T + qq) * H + h) * HD + c;
+            *reinterpret_cast<float4*>(o + off) = v;
+            if (o_split) {  // the split kernel's arithmetic (split_bf16)
+                const float ov[4] = {v.x, v.y, v.z, v.w};
+                __nv_bfloat16 hi[4], lo[4];
 #pragma unroll
-                    for (int u = 0; u < 4; ++u)
-                        split_bf16(ov[u], hi[u], lo[u]);
-                    *reinterpret_cast<uint2*>(o_split + off + c) =
-                        *reinterpret_cast<const uint2*>(hi);
-                    *reinterpret_cast<uint2*>(o_split + o_plane + off + c) =
-                        *reinterpret_cast<const uint2*>(lo);
-                }
+                for (int u = 0; u < 4; ++u)
+                    split_bf16(ov[u], hi[u], lo[u]);
+                *reinterpret_cast<uint2*>(o_split + off) = *reinterpret_cast<const uint2*>(hi);
+                *reinterpret_cast<uint2*>(o_split + o_plane + off) =
+                    *reinterpret_cast<const uint2*>(lo);
             }
-            if (half == 0)
-                lse[bh * T + q] = m_out * LN2 + logf(lt);
         }
     }
 }
@@ -551,18 +568,21 @@ __device__ __forceinline__ void load_owned(uint32_t taddr, int grp, float (&v)[H
         v[e] = a[e], v[QW + e] = b[e];
 }
 
-// Store owned columns of one gradient row (scaled; RoPE transpose rotation
-// when `rope`), overwriting or adding.
-// With `srow` (the row's place in bf16x3 operand planes, lo `plane` elements
-// after hi) the stored values are also split there (split_bf16, the split
-// kernel's arithmetic), after any accumulation.
+// Epilogues stage a 128-row gradient tile in shared memory ([BQ][HD + 4]
+// floats: the pitch makes each thread's float4 stores conflict-free) so that
+// the global stores cover whole rows per warp.
 template <int HD>
-__device__ __forceinline__ void store_owned(const float (&g)[HD / 2], float* __restrict__ row,
+__host__ __device__ constexpr int tile_ld() {
+    return HD + 4;
+}
+
+// Phase 1: this thread's owned columns of one gradient row, scaled, with the
+// RoPE transpose rotation when `rope`, into its tile row.
+template <int HD>
+__device__ __forceinline__ void stage_owned(const float (&g)[HD / 2], float* __restrict__ trow,
                                             int64_t t, const float* __restrict__ cs,
                                             const float* __restrict__ sn, bool rope, float scale,
-                                            int grp, int accumulate,
-                                            __nv_bfloat16* __restrict__ srow = nullptr,
-                                            int64_t plane = 0) {
+                                            int grp) {
     constexpr int QW = HD / 4, HH = HD / 2;
 #pragma unroll
     for (int e = 0; e < QW; e += 4) {
@@ -580,28 +600,69 @@ __device__ __forceinline__ void store_owned(const float (&g)[HD / 2], float* __r
             a[u] = rope ? g1 * cc[u] + g2 * ss[u] : g1;
             b[u] = rope ? -g1 * ss[u] + g2 * cc[u] : g2;
         }
-        float4* p1 = reinterpret_cast<float4*>(row + d);
-        float4* p2 = reinterpret_cast<float4*>(row + HH + d);
+        *reinterpret_cast<float4*>(trow + d) = make_float4(a[0], a[1], a[2], a[3]);
+        *reinterpret_cast<float4*>(trow + HH + d) = make_float4(b[0], b[1], b[2], b[3]);
+    }
+}
+
+// Phase 2: the eight epilogue warps (sw = 0..7) store the tile's rows row0 +
+// rr (rows at or past T skipped), HD / 4 lanes per row with one float4 each,
+// into out [B,T,H,HD] for head bh: added to the stored values when
+// `accumulate`, and split into bf16x3 planes at `split` (lo `plane` elements
+// after hi) after the addition, with the split kernel's arithmetic
+// (split_bf16).
+template <int HD>
+__device__ __forceinline__ void store_rows(const float* __restrict__ tile, float* __restrict__ out,
+                                           __nv_bfloat16* __restrict__ split, int64_t plane,
+                                           int64_t row0, int64_t T, int H, int64_t bh,
+                                           int accumulate, int sw, int lane) {
+    constexpr int LD = tile_ld<HD>();
+    constexpr int LPR = HD / 4;    // lanes per row
+    constexpr int RPI = 32 / LPR;  // rows per warp instruction
+    const int c = (lane % LPR) * 4;
+    const int64_t b = bh / H, h = bh % H;
+    for (int rr = sw * RPI + lane / LPR; rr < BQ; rr += 8 * RPI) {
+        const int64_t t = row0 + rr;
+        if (t >= T)
+            break;
+        float4 v = *reinterpret_cast<const float4*>(tile + rr * LD + c);
+        const int64_t off = ((b * T + t) * H + h) * HD + c;
+        float4* p = reinterpret_cast<float4*>(out + off);
         if (accumulate) {
-            const float4 o1 = *p1, o2 = *p2;
-            a[0] += o1.x, a[1] += o1.y, a[2] += o1.z, a[3] += o1.w;
-            b[0] += o2.x, b[1] += o2.y, b[2] += o2.z, b[3] += o2.w;
+            const float4 o = *p;
+            v.x += o.x, v.y += o.y, v.z += o.z, v.w += o.w;
         }
-        *p1 = make_float4(a[0], a[1], a[2], a[3]);
-        *p2 = make_float4(b[0], b[1], b[2], b[3]);
-        if (srow) {
-            __nv_bfloat16 ah[4], al[4], bh[4], bl[4];
+        *p = v;
+        if (split) {
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+            __nv_bfloat16 hi[4], lo[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                split_bf16(a[u], ah[u], al[u]);
-                split_bf16(b[u], bh[u], bl[u]);
-            }
-            *reinterpret_cast<uint2*>(srow + d) = *reinterpret_cast<const uint2*>(ah);
-            *reinterpret_cast<uint2*>(srow + plane + d) = *reinterpret_cast<const uint2*>(al);
-            *reinterpret_cast<uint2*>(srow + HH + d) = *reinterpret_cast<const uint2*>(bh);
-            *reinterpret_cast<uint2*>(srow + plane + HH + d) = *reinterpret_cast<const uint2*>(bl);
+            for (int u = 0; u < 4; ++u)
+                split_bf16(vv[u], hi[u], lo[u]);
+            *reinterpret_cast<uint2*>(split + off) = *reinterpret_cast<const uint2*>(hi);
+            *reinterpret_cast<uint2*>(split + plane + off) = *reinterpret_cast<const uint2*>(lo);
         }
     }
+}
+
+// Barrier 1 over the 256 softmax / epilogue threads, returning whether `ok`
+// holds in all of them (every one of them reaches it: their waits are
+// bounded), so that they take the epilogue or the abort path together.
+__device__ __forceinline__ bool softmax_all(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(ok)), "n"(SOFTMAX_THREADS)
+        : "memory");
+    return r != 0;
+}
+
+__device__ __forceinline__ void softmax_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(SOFTMAX_THREADS) : "memory");
 }
 
 // Packed bf16 hi|lo of 32 values: hi[i], lo[i] hold elements 2i, 2i+1.
@@ -895,18 +956,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         }
         if (ok && (*abort_flag || !mbar_wait(done, 0, 52)))
             ok = false;
-        if (!ok) {
+        if (!softmax_all(ok)) {
             *abort_flag = 1;
         } else {
+            // dQ tile staged over the Q / dO tiles (every MMA has completed),
+            // then stored row by row.
+            static_assert(BQ * tile_ld<HD>() * 4 <= 2 * CF::BIG_BYTES, "dQ tile fits");
+            float* tile = reinterpret_cast<float*>(smem);
             tc_fence_after();
             float g[HH];
             load_owned<HD>(tmem + lane_off + CF::ACC_COL, grp, g);
-            if (q < T) {
-                const int64_t b = bh / H, h = bh % H;
-                const int64_t off = ((b * T + q) * H + h) * HD;
-                store_owned<HD>(g, dq + off, q, cs, sn, true, scale, grp, accumulate,
-                                dq_split ? dq_split + off : nullptr, plane);
-            }
+            if (q < T)
+                stage_owned<HD>(g, tile + r * tile_ld<HD>(), q, cs, sn, true, scale, grp);
+            softmax_sync();
+            store_rows<HD>(tile, dq, dq_split, plane, q0, T, H, bh, accumulate, warp - 2, lane);
         }
     }
 
@@ -1176,21 +1239,26 @@ __global__ void __launch_bounds__(DKV_THREADS, 1)
         }
         if (ok && (*abort_flag || !mbar_wait(done, 0, 72)))
             ok = false;
-        if (!ok) {
+        if (!softmax_all(ok)) {
             *abort_flag = 1;
         } else {
+            // dV and dK tiles staged over the K / V tiles and the first ring
+            // (every MMA and copy has completed), then stored row by row.
+            constexpr int TILE = BQ * tile_ld<HD>();
+            static_assert(2 * TILE * 4 <= CF::OFF_BAR, "dK/dV tiles fit");
+            float* tile_v = reinterpret_cast<float*>(smem);
+            float* tile_k = tile_v + TILE;
             tc_fence_after();
             float g[HH];
-            const int64_t b = bh / H, h = bh % H;
-            const int64_t off = ((b * T + key) * H + h) * HD;
             load_owned<HD>(tmem + lane_off + CF::ACC_COL, grp, g);
             if (key < T)
-                store_owned<HD>(g, dv + off, key, cs, sn, false, 1.0f, grp, accumulate,
-                                dv_split ? dv_split + off : nullptr, plane);
+                stage_owned<HD>(g, tile_v + r * tile_ld<HD>(), key, cs, sn, false, 1.0f, grp);
             load_owned<HD>(tmem + lane_off + CF::ACC_COL + HD, grp, g);
             if (key < T)
-                store_owned<HD>(g, dk + off, key, cs, sn, true, 1.0f, grp, accumulate,
-                                dk_split ? dk_split + off : nullptr, plane);
+                stage_owned<HD>(g, tile_k + r * tile_ld<HD>(), key, cs, sn, true, 1.0f, grp);
+            softmax_sync();
+            store_rows<HD>(tile_v, dv, dv_split, plane, k0, T, H, bh, accumulate, warp - 2, lane);
+            store_rows<HD>(tile_k, dk, dk_split, plane, k0, T, H, bh, accumulate, warp - 2, lane);
         }
     }
 

@@ -406,13 +406,18 @@ def main():
     # GEMM timing on, so the timed steps find its CUDA events already
     # created: creating the ~10k events of a first timed step cost 0.4 s of
     # device time (9.40 s against 8.99 s for the next steps).
+    # The all-reduce timing events (N > 1) are warmed the same way.
     for i in range(args.warmup):
         if i == args.warmup - 1:
             _ttk.call("ttk_profile_enable", 1)
+            if world > 1:
+                tr.comm_profile(True)
         tr.step_device(dev_idx[i % n_sets].data_ptr(), dev_tgt[i % n_sets].data_ptr(), B, T,
                        n_micro, 3e-4)
     barrier()
     _ttk.call("ttk_profile_read", None, None, None)  # discard; returns the events to the pool
+    if world > 1:
+        tr.comm_stats()  # discard, likewise
 
     # ---- timed region: value
     _ttk.call("ttk_pool_high_water", None, None, 1)

@@ -16,6 +16,7 @@
 #include <functional>
 #include <thread>
 #include <chrono>
+#include <unistd.h>
 #include <filesystem>
 #include <fstream>
 #include <map>
@@ -269,9 +270,12 @@ struct Trainer {
     void trace_mark(const char* what, int64_t m) {
         if (!trace)
             return;
-        const double ms = std::chrono::duration<double, std::milli>(
-                              std::chrono::steady_clock::now() - trace_t0).count();
-        std::fprintf(stderr, "tt_trace %s %ld %.2f\n", what, static_cast<long>(m), ms);
+        const auto now = std::chrono::steady_clock::now();
+        const double ms = std::chrono::duration<double, std::milli>(now - trace_t0).count();
+        const double abs_ms =
+            std::chrono::duration<double, std::milli>(now.time_since_epoch()).count();
+        std::fprintf(stderr, "tt_trace %d %s %ld %.2f %.2f\n", static_cast<int>(getpid()), what,
+                     static_cast<long>(m), ms, abs_ms);
     }
 
     // Runs fwd+bwd over n_micro micro-batches; ids are device pointers.
@@ -612,11 +616,14 @@ int tt_trainer_step_device(void* h, const int64_t* idx, const int64_t* targets, 
         Trainer* t = T_(h);
         if (B <= 0 || T <= 0 || n_micro <= 0)
             throw std::invalid_argument("step: sizes must be positive");
+        t->trace_t0 = std::chrono::steady_clock::now();
+        t->trace_mark("step", 0);
         t->begin_step();
         t->zero_grads();
         t->accumulate(idx, targets, B, T, n_micro);
         t->optimizer_step(n_micro, lr);
         t->end_step();
+        t->trace_mark("enqueued", 0);
     });
 }
 

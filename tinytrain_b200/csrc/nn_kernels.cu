@@ -6,6 +6,7 @@
 // cross-entropy keeps its 32000-wide row in registers between the reduction
 // and the gradient write).
 #include <algorithm>
+#include <atomic>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -993,15 +994,19 @@ static inline int rms_block(int64_t D) {  // threads per block: whole rows, up t
 template <class Kernel>
 static int64_t resident_grid(Kernel kernel, int bs, int slot) {
     constexpr int kDevs = 16, kSlots = 2, kSizes = 33;
-    static int cache[kDevs][kSlots][kSizes] = {};
+    static std::atomic<int> cache[kDevs][kSlots][kSizes];  // zero-initialized (static)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess)
         dev = 0;
     const int bi = bs / 32;
-    int* c = (dev < kDevs && slot < kSlots && bi < kSizes && bs % 32 == 0) ? &cache[dev][slot][bi]
-                                                                          : nullptr;
-    if (c && *c > 0)
-        return *c;
+    std::atomic<int>* c =
+        (dev < kDevs && slot < kSlots && bi < kSizes && bs % 32 == 0) ? &cache[dev][slot][bi]
+                                                                      : nullptr;
+    if (c) {
+        const int v = c->load(std::memory_order_relaxed);
+        if (v > 0)
+            return v;
+    }
     int sms = 0, per = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
         sms <= 0)
@@ -1013,7 +1018,7 @@ static int64_t resident_grid(Kernel kernel, int bs, int slot) {
     }
     const int n = sms * per;
     if (c)
-        *c = n;
+        c->store(n, std::memory_order_relaxed);
     return n;
 }
 

@@ -319,6 +319,9 @@ def main():
     ap.add_argument("--micro", type=int, default=None,
                     help="sequences per micro-batch (gradient accumulation unit); "
                          "the global batch and so the optimizer step are unchanged")
+    ap.add_argument("--graph", action="store_true",
+                    help="also time the step replayed from a CUDA graph (one GPU; reported "
+                         "under 'graph', after the e2e region)")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.config])
     if args.global_batch:
@@ -492,10 +495,38 @@ def main():
     loss_e2e, _ = tr.step_result()
     barrier()
     c3 = clk.now()
-    clk.stop()
     ms_e2e = max_over_ranks(f0.elapsed_time(f1)) / ke
     step_ms_e2e = max_each_over_ranks([fe[i].elapsed_time(fe[i + 1]) for i in range(ke)])
     e2e = tokens_step / (ms_e2e / 1e3)
+
+    # ---- optional: the same step replayed from a CUDA graph (one GPU). The
+    # graph reads each step's ids from two fixed device buffers, filled by a
+    # device copy before each launch (inside the timed region).
+    graph = None
+    if args.graph and world == 1:
+        gi, gt = torch.empty_like(dev_idx[0]), torch.empty_like(dev_tgt[0])
+        for i in range(2):  # an eager step, then the recording + first launch
+            gi.copy_(dev_idx[i % n_sets])
+            gt.copy_(dev_tgt[i % n_sets])
+            tr.step_graph(gi.data_ptr(), gt.data_ptr(), B, T, n_micro, 3e-4)
+        barrier()
+        ge = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        c4 = clk.now()
+        ge[0].record(stream)
+        for i in range(args.steps):
+            gi.copy_(dev_idx[i % n_sets])
+            gt.copy_(dev_tgt[i % n_sets])
+            tr.step_graph(gi.data_ptr(), gt.data_ptr(), B, T, n_micro, 3e-4)
+            ge[i + 1].record(stream)
+        barrier()
+        c5 = clk.now()
+        ms_g = ge[0].elapsed_time(ge[-1]) / args.steps
+        graph = {"value": tokens_step / (ms_g / 1e3), "unit": "tokens/s", "ms_per_step": ms_g,
+                 "step_ms": [round(ge[i].elapsed_time(ge[i + 1]), 3) for i in range(args.steps)],
+                 "loss": tr.last_loss(), "clocks": clk.summary(c4, c5),
+                 "is": "tt_trainer_step_graph: the step recorded once in a CUDA graph and "
+                       "replayed (ids copied into fixed device buffers before each launch)"}
+    clk.stop()
     status = _ttk.device_status()
 
     if rank == 0:
@@ -536,6 +567,7 @@ def main():
                     "step_ms": [round(x, 2) for x in step_ms_e2e], "clocks": clk.summary(c2, c3)},
             "clocks": clk.summary(c0, c1),
             "loss": loss_dev, "loss_e2e": loss_e2e, "device_status": status,
+            **({"graph": graph} if graph else {}),
         }
         if world == 1 and not args.no_cpu_baseline:
             try:

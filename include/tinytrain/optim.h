@@ -41,6 +41,11 @@ public:
     // and the step counter behind the bias correction.
     float* moment(size_t i, int which);
     void set_step_count(int64_t t) { step_ = t; }
+    // Learning rate and bias-corrected rate read from the device ({lr,
+    // lr_t} at `sched`, written by ttk_adamw_sched_set) instead of passed
+    // with the launch: for a step recorded in a CUDA graph and replayed.
+    // nullptr returns to the host values.
+    void set_device_schedule(const float* sched) { sched_ = sched; }
 
 private:
     std::vector<Tensor*> params_;
@@ -50,6 +55,7 @@ private:
     // per-parameter state, allocated lazily on the device, keyed by index
     std::vector<float*> m_, v_;
     double* sumsq_ = nullptr;
+    const float* sched_ = nullptr;
 };
 
 // SGD with optional momentum and weight decay.

@@ -58,6 +58,20 @@ int tt_trainer_step(void* handle, const int64_t* idx, const int64_t* targets, in
  * (read it with tt_trainer_last_loss) so no host synchronization happens. */
 int tt_trainer_step_device(void* handle, const int64_t* idx, const int64_t* targets, int64_t B,
                            int64_t T, int64_t n_micro, float lr);
+/* tt_trainer_step_device replayed from a CUDA graph (single GPU; no
+ * counterpart in the reference, whose step is host code). The first call
+ * with given id pointers and sizes runs an ordinary step; the second records
+ * a step into a graph and launches it; later calls with the same pointers
+ * and sizes launch the graph again, after writing that step's learning rate
+ * and AdamW bias correction to the device. Each call is one optimizer step
+ * with the same arithmetic as tt_trainer_step_device (identical results).
+ * The caller puts each step's ids into the same two device buffers before
+ * the call (stream-ordered). Other pointers or sizes drop the graph and
+ * start over. Recording returns the device pool's unused memory first: the
+ * graph allocates its activations from its own pool. Fails on a trainer
+ * with a communicator. */
+int tt_trainer_step_graph(void* handle, const int64_t* idx, const int64_t* targets, int64_t B,
+                          int64_t T, int64_t n_micro, float lr);
 int tt_trainer_last_loss(void* handle, float* loss);
 /* tt_trainer_step in two halves, so that the host prepares and enqueues step
  * i + 1 while the device runs step i. submit copies the host ids into one of

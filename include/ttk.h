@@ -87,6 +87,19 @@ int ttk_event_synchronize(void* event);
  * never blocks. */
 int ttk_event_query(void* event, int* done);
 
+/* CUDA graphs (no counterpart in the reference, which has no device):
+ * ttk_stream_begin_capture starts recording `stream` (not the legacy default
+ * stream) in thread-local mode; ttk_stream_end_capture ends it and returns an
+ * instantiated graph (memory the graph allocates and leaves allocated is
+ * freed at its next launch); ttk_graph_launch replays it on any stream;
+ * ttk_graph_destroy releases it. ttk_pool_trim waits for `stream` and
+ * returns the device pool's unused memory to the device. */
+int ttk_stream_begin_capture(void* stream);
+int ttk_stream_end_capture(void* stream, void** graph_exec);
+int ttk_graph_launch(void* graph_exec, void* stream);
+int ttk_graph_destroy(void* graph_exec);
+int ttk_pool_trim(void* stream);
+
 /* ------------------------------------------------------------ dense algebra */
 
 /* C[b] = alpha * op(A[b]) @ op(B[b]) + beta * C[b] on the tcgen05 tensor
@@ -381,6 +394,18 @@ int ttk_adamw_multi(float* const* params, const float* const* grads, float* cons
                     float* const* v, const int64_t* sizes, int n_tensors, float lr, float beta1,
                     float beta2, float eps, float weight_decay, int64_t step,
                     const double* sumsq, float max_norm, float grad_scale, void* stream);
+/* The same step taking the learning rate and the bias-corrected rate from
+ * the device (sched = {lr, lr_t}, read when the kernel starts), so a step
+ * recorded once in a CUDA graph can be replayed with each step's values;
+ * ttk_adamw_sched_set writes them for a 1-based step count (the arithmetic
+ * of ttk_adamw_multi, so both give the same update). No counterpart in the
+ * reference. */
+int ttk_adamw_multi_sched(float* const* params, const float* const* grads, float* const* m,
+                          float* const* v, const int64_t* sizes, int n_tensors, float beta1,
+                          float beta2, float eps, float weight_decay, const float* sched,
+                          const double* sumsq, float max_norm, float grad_scale, void* stream);
+int ttk_adamw_sched_set(float* sched, float lr, float beta1, float beta2, int64_t step,
+                        void* stream);
 /* SGD with momentum / L2 decay (optim.cpp:58-82) on one tensor. */
 int ttk_sgd(float* p, const float* g, float* vel, int64_t n, float lr, float momentum,
             float weight_decay, void* stream);

@@ -30,6 +30,11 @@ SIGS = {
     "ttk_synchronize": (I32, []),
     "ttk_selftest_wait_timeout": (I32, [C.c_uint, C.c_uint64, P]),
     "ttk_event_query": (I32, [P, P]),
+    "ttk_stream_begin_capture": (I32, [P]),
+    "ttk_stream_end_capture": (I32, [P, P]),
+    "ttk_graph_launch": (I32, [P, P]),
+    "ttk_graph_destroy": (I32, [P]),
+    "ttk_pool_trim": (I32, [P]),
     "ttk_launch_count": (I64, []),
     "ttk_malloc": (I32, [P, SZ, P]),
     "ttk_free": (I32, [P, P]),
@@ -113,6 +118,8 @@ SIGS = {
     "ttk_softmax_bwd": (I32, [P, P, P, I32, I64, I64, I32, P]),
     "ttk_sumsq_multi": (I32, [P, P, I32, P, P]),
     "ttk_adamw_multi": (I32, [P, P, P, P, P, I32, F32, F32, F32, F32, F32, I64, P, F32, F32, P]),
+    "ttk_adamw_multi_sched": (I32, [P, P, P, P, P, I32, F32, F32, F32, F32, P, P, F32, F32, P]),
+    "ttk_adamw_sched_set": (I32, [P, F32, F32, F32, I64, P]),
     "ttk_sgd": (I32, [P, P, P, I64, F32, F32, F32, P]),
     "ttk_binary": (I32, [I32, P, P, P, P, P, P, I32, P]),
     "ttk_binary_bwd": (I32, [I32, I32, P, P, P, P, P, P, P, I32, P]),

@@ -887,7 +887,12 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
                              PREC == gemm::PREC_TF32X3 ? 4 : 2);
     Profiler& pr = prof();
     ProfRec rec{};
-    if (pr.on) {
+    // No timing events inside a stream capture: a replayed graph would not
+    // add records, and the recorded pair would be read as a launch.
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    const bool timed = pr.on && cudaStreamIsCapturing(stream, &cap) == cudaSuccess &&
+                       cap == cudaStreamCaptureStatusNone;
+    if (timed) {
         rec.a = pr.get();
         rec.b = pr.get();
         rec.flops = 2.0 * static_cast<double>(p.M) * p.N * p.K * p.batch;
@@ -916,7 +921,7 @@ int launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap&
                                                              fin->C, fin->ldc);
         rc = check_launch("splitk_reduce_kernel");
     }
-    if (pr.on) {
+    if (timed) {
         cudaEventRecord(rec.b, stream);
         pr.recs.push_back(rec);
     }

@@ -71,7 +71,23 @@ __global__ void sumsq_kernel(TensorList L, double* __restrict__ acc) {
 struct AdamArgs {
     float lr, b1, b2, eps, wd, lr_t, grad_scale, max_norm;
     const double* sumsq;
+    // Device schedule {lr, lr_t} read at kernel start when set (a step
+    // replayed from a CUDA graph takes its learning rate and bias correction
+    // from here instead of from the launch arguments recorded once).
+    const float* sched;
 };
+
+// lr_t of optim.cpp:22-24 in float, as the reference computes it.
+static float adam_lr_t(float lr, float beta1, float beta2, int64_t step) {
+    const float bc1 = 1.0f - std::pow(beta1, static_cast<float>(step));
+    const float bc2 = 1.0f - std::pow(beta2, static_cast<float>(step));
+    return lr * std::sqrt(bc2) / bc1;
+}
+
+__global__ void adam_sched_kernel(float* __restrict__ sched, float lr, float lr_t) {
+    sched[0] = lr;
+    sched[1] = lr_t;
+}
 
 // One element of optim.cpp:36-45, gradient pre-multiplied by the clip
 // coefficient and grad_scale.
@@ -84,6 +100,10 @@ __device__ __forceinline__ void adam_elem(float& d, float gi, float& m, float& v
 }
 
 __global__ void adamw_kernel(TensorList L, AdamArgs a) {
+    if (a.sched) {
+        a.lr = a.sched[0];
+        a.lr_t = a.sched[1];
+    }
     float coef = a.grad_scale;
     if (a.sumsq && a.max_norm > 0.0f) {
         // coef = max_norm / (||g|| + 1e-6), applied when < 1 (the norm is of
@@ -177,21 +197,20 @@ int ttk_sumsq_multi(const float* const* ptrs, const int64_t* sizes, int n_tensor
     return TTK_OK;
 }
 
-int ttk_adamw_multi(float* const* params, const float* const* grads, float* const* m,
-                    float* const* v, const int64_t* sizes, int n_tensors, float lr, float beta1,
-                    float beta2, float eps, float weight_decay, int64_t step,
-                    const double* sumsq, float max_norm, float grad_scale, void* stream) {
+static int adamw_multi(float* const* params, const float* const* grads, float* const* m,
+                       float* const* v, const int64_t* sizes, int n_tensors, float lr, float beta1,
+                       float beta2, float eps, float weight_decay, int64_t step,
+                       const double* sumsq, float max_norm, float grad_scale, const float* sched,
+                       void* stream) {
     if (n_tensors < 0 || step < 1)
         return set_error(TTK_ERR_ARG, "adamw_multi: bad arguments");
     AdamArgs a;
     a.lr = lr, a.b1 = beta1, a.b2 = beta2, a.eps = eps, a.wd = weight_decay;
-    // optim.cpp:22-24, in float like the reference.
-    const float bc1 = 1.0f - std::pow(beta1, static_cast<float>(step));
-    const float bc2 = 1.0f - std::pow(beta2, static_cast<float>(step));
-    a.lr_t = lr * std::sqrt(bc2) / bc1;
+    a.lr_t = adam_lr_t(lr, beta1, beta2, step);
     a.grad_scale = grad_scale;
     a.max_norm = max_norm;
     a.sumsq = sumsq;
+    a.sched = sched;
     for (int base = 0; base < n_tensors; base += kMaxTensors) {
         TensorList L{};
         L.count = std::min(kMaxTensors, n_tensors - base);
@@ -213,6 +232,33 @@ int ttk_adamw_multi(float* const* params, const float* const* grads, float* cons
             return rc;
     }
     return TTK_OK;
+}
+
+int ttk_adamw_multi(float* const* params, const float* const* grads, float* const* m,
+                    float* const* v, const int64_t* sizes, int n_tensors, float lr, float beta1,
+                    float beta2, float eps, float weight_decay, int64_t step,
+                    const double* sumsq, float max_norm, float grad_scale, void* stream) {
+    return adamw_multi(params, grads, m, v, sizes, n_tensors, lr, beta1, beta2, eps, weight_decay,
+                       step, sumsq, max_norm, grad_scale, nullptr, stream);
+}
+
+int ttk_adamw_multi_sched(float* const* params, const float* const* grads, float* const* m,
+                          float* const* v, const int64_t* sizes, int n_tensors, float beta1,
+                          float beta2, float eps, float weight_decay, const float* sched,
+                          const double* sumsq, float max_norm, float grad_scale, void* stream) {
+    if (!sched)
+        return set_error(TTK_ERR_ARG, "adamw_multi_sched: null schedule");
+    // lr and step are placeholders: the kernel reads lr and lr_t from sched.
+    return adamw_multi(params, grads, m, v, sizes, n_tensors, 0.0f, beta1, beta2, eps,
+                       weight_decay, 1, sumsq, max_norm, grad_scale, sched, stream);
+}
+
+int ttk_adamw_sched_set(float* sched, float lr, float beta1, float beta2, int64_t step,
+                        void* stream) {
+    if (!sched || step < 1)
+        return set_error(TTK_ERR_ARG, "adamw_sched_set: bad arguments");
+    adam_sched_kernel<<<1, 1, 0, S(stream)>>>(sched, lr, adam_lr_t(lr, beta1, beta2, step));
+    return check_launch("adam_sched_kernel");
 }
 
 int ttk_sgd(float* p, const float* g, float* vel, int64_t n, float lr, float momentum,

@@ -283,6 +283,65 @@ int ttk_event_query(void* event, int* done) {
     return check_cuda(e, "event query");
 }
 
+// ---------------------------------------------------------- CUDA graphs --
+// Capture of one stream's work into a graph (thread-local capture mode: an
+// API call of this thread that is not allowed while capturing fails instead
+// of silently breaking the capture), instantiation with auto-free on launch
+// (memory a launch allocates and does not free is released at the next
+// launch), replay, and release.
+
+int ttk_stream_begin_capture(void* stream) {
+    return check_cuda(cudaStreamBeginCapture(S(stream), cudaStreamCaptureModeThreadLocal),
+                      "stream begin capture");
+}
+
+int ttk_stream_end_capture(void* stream, void** graph_exec) {
+    *graph_exec = nullptr;
+    cudaGraph_t g = nullptr;
+    int rc = check_cuda(cudaStreamEndCapture(S(stream), &g), "stream end capture");
+    if (rc) {
+        if (g)
+            cudaGraphDestroy(g);
+        return rc;
+    }
+    cudaGraphExec_t e = nullptr;
+    rc = check_cuda(cudaGraphInstantiateWithFlags(&e, g, cudaGraphInstantiateFlagAutoFreeOnLaunch),
+                    "graph instantiate");
+    cudaGraphDestroy(g);
+    if (!rc)
+        *graph_exec = e;
+    return rc;
+}
+
+int ttk_graph_launch(void* graph_exec, void* stream) {
+    if (!graph_exec)
+        return set_error(TTK_ERR_ARG, "graph launch: null graph");
+    return check_cuda(cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph_exec), S(stream)),
+                      "graph launch");
+}
+
+int ttk_graph_destroy(void* graph_exec) {
+    if (!graph_exec)
+        return TTK_OK;
+    return check_cuda(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph_exec)),
+                      "graph destroy");
+}
+
+int ttk_pool_trim(void* stream) {
+    int dev = 0;
+    int rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    if (rc)
+        return rc;
+    rc = check_cuda(cudaStreamSynchronize(S(stream)), "pool trim sync");
+    if (rc)
+        return rc;
+    cudaMemPool_t pool;
+    rc = check_cuda(cudaDeviceGetDefaultMemPool(&pool, dev), "cudaDeviceGetDefaultMemPool");
+    if (rc)
+        return rc;
+    return check_cuda(cudaMemPoolTrimTo(pool, 0), "cudaMemPoolTrimTo");
+}
+
 // ------------------------------------------------------------------ GEMM --
 
 int ttk_gemm_set_precision(int prec) { return gemm_set_precision(prec); }

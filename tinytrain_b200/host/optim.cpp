@@ -77,10 +77,16 @@ void AdamW::step() {
               "sumsq");
         ss = sumsq_;
     }
-    check(ttk_adamw_multi(ps.data(), gs.data(), ms.data(), vs.data(), ns.data(),
-                          static_cast<int>(ps.size()), lr_, beta1_, beta2_, eps_, weight_decay_,
-                          step_, ss, clip_, grad_scale_, stream()),
-          "adamw");
+    if (sched_)
+        check(ttk_adamw_multi_sched(ps.data(), gs.data(), ms.data(), vs.data(), ns.data(),
+                                    static_cast<int>(ps.size()), beta1_, beta2_, eps_,
+                                    weight_decay_, sched_, ss, clip_, grad_scale_, stream()),
+              "adamw");
+    else
+        check(ttk_adamw_multi(ps.data(), gs.data(), ms.data(), vs.data(), ns.data(),
+                              static_cast<int>(ps.size()), lr_, beta1_, beta2_, eps_,
+                              weight_decay_, step_, ss, clip_, grad_scale_, stream()),
+              "adamw");
 }
 
 float* AdamW::moment(size_t i, int which) {

@@ -13,6 +13,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <exception>
 #include <functional>
 #include <thread>
 #include <chrono>
@@ -183,6 +184,10 @@ struct Trainer {
             ttk_event_destroy(e);
         if (done_event)
             ttk_event_destroy(done_event);
+        ttk_graph_destroy(graph_exec);
+        if (capture_stream)
+            ttk_stream_destroy(capture_stream);
+        ttk_free(sched, s);
         if (comm_stream)
             ttk_stream_destroy(comm_stream);
         opt.reset();
@@ -420,6 +425,67 @@ struct Trainer {
     };
     AsyncSlot async_slots[2];
     int async_next = 0, async_oldest = 0;
+
+    // Steps replayed from a CUDA graph (tt_trainer_step_graph). The graph
+    // holds one recorded step for fixed id pointers and sizes; the AdamW
+    // kernel in it reads {lr, lr_t} from `sched`, written before each launch.
+    struct GraphKey {
+        const int64_t* idx = nullptr;
+        const int64_t* tgt = nullptr;
+        int64_t B = 0, T = 0, n_micro = 0;
+        bool operator==(const GraphKey& o) const {
+            return idx == o.idx && tgt == o.tgt && B == o.B && T == o.T && n_micro == o.n_micro;
+        }
+    };
+    GraphKey graph_key, warm_key;
+    bool warm_valid = false;
+    void* graph_exec = nullptr;
+    void* capture_stream = nullptr;
+    float* sched = nullptr;
+
+    // Records one training step on the capture stream (nothing runs while
+    // recording; the host-side state advances by one step, as for an eager
+    // step) and instantiates it. The pool's unused memory is returned to the
+    // device first: the graph allocates its activations from its own pool.
+    void capture_step(const GraphKey& key, float lr) {
+        if (!capture_stream)
+            check(ttk_stream_create(&capture_stream), "capture stream");
+        if (!sched)
+            check(ttk_malloc(reinterpret_cast<void**>(&sched), 16, stream()), "schedule");
+        void* user = stream();
+        check(ttk_pool_trim(user), "pool trim");
+        tt::set_stream(capture_stream);
+        opt->set_device_schedule(sched);
+        std::exception_ptr err;
+        int rc = ttk_stream_begin_capture(capture_stream);
+        if (!rc) {
+            try {
+                begin_step();
+                zero_grads();
+                accumulate(key.idx, key.tgt, key.B, key.T, key.n_micro);
+                optimizer_step(key.n_micro, lr);
+                end_step();
+            } catch (...) {
+                err = std::current_exception();
+            }
+            void* exec = nullptr;
+            const int rc_end = ttk_stream_end_capture(capture_stream, &exec);
+            if (!rc_end && !err) {
+                graph_exec = exec;
+                graph_key = key;
+            } else {
+                ttk_graph_destroy(exec);
+                rc = rc_end;
+            }
+        }
+        const std::string msg = rc ? ttk_last_error() : "";
+        opt->set_device_schedule(nullptr);
+        tt::set_stream(user);
+        if (err)
+            std::rethrow_exception(err);
+        if (rc)
+            throw std::runtime_error("step_graph: capture failed: " + msg);
+    }
 };
 
 // A token stream resident in device memory (int32, apps/prepare_data.cpp's
@@ -624,6 +690,46 @@ int tt_trainer_step_device(void* h, const int64_t* idx, const int64_t* targets, 
         t->optimizer_step(n_micro, lr);
         t->end_step();
         t->trace_mark("enqueued", 0);
+    });
+}
+
+int tt_trainer_step_graph(void* h, const int64_t* idx, const int64_t* targets, int64_t B,
+                          int64_t T, int64_t n_micro, float lr) {
+    return guarded([&] {
+        Trainer* t = T_(h);
+        if (B <= 0 || T <= 0 || n_micro <= 0 || !idx || !targets)
+            throw std::invalid_argument("step: sizes must be positive");
+        if (t->comm)
+            throw std::logic_error(
+                "step_graph: data-parallel steps are not recorded in a graph; use step_device");
+        const Trainer::GraphKey key{idx, targets, B, T, n_micro};
+        if (t->graph_exec && !(t->graph_key == key)) {
+            check(ttk_stream_synchronize(stream()), "graph release");
+            ttk_graph_destroy(t->graph_exec);
+            t->graph_exec = nullptr;
+        }
+        if (!t->graph_exec) {
+            if (!t->warm_valid || !(t->warm_key == key)) {
+                // The first step with these ids and sizes runs eagerly: it
+                // allocates the state (moments, cached weight splits) that
+                // the recorded step then finds in place.
+                t->begin_step();
+                t->zero_grads();
+                t->accumulate(idx, targets, B, T, n_micro);
+                t->optimizer_step(n_micro, lr);
+                t->end_step();
+                t->warm_key = key;
+                t->warm_valid = true;
+                return;
+            }
+            t->capture_step(key, lr);  // the optimizer's step count advanced by one
+        } else {
+            t->opt->set_step_count(t->opt->step_count() + 1);
+        }
+        check(ttk_adamw_sched_set(t->sched, lr, t->ocfg.beta1, t->ocfg.beta2,
+                                  t->opt->step_count(), stream()),
+              "schedule");
+        check(ttk_graph_launch(t->graph_exec, stream()), "graph launch");
     });
 }
 

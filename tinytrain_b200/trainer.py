@@ -51,6 +51,7 @@ _SIGS = {
     "tt_trainer_set_optimizer": (C.c_int, [P, P]),
     "tt_trainer_step": (C.c_int, [P, P, P, I64, I64, I64, F32, P, P]),
     "tt_trainer_step_device": (C.c_int, [P, P, P, I64, I64, I64, F32]),
+    "tt_trainer_step_graph": (C.c_int, [P, P, P, I64, I64, I64, F32]),
     "tt_trainer_last_loss": (C.c_int, [P, P]),
     "tt_trainer_step_submit": (C.c_int, [P, P, P, I64, I64, I64, F32]),
     "tt_trainer_step_result": (C.c_int, [P, P, P]),
@@ -196,6 +197,14 @@ class Trainer:
     def step_device(self, idx_ptr, tgt_ptr, B, T, n_micro=1, lr=3e-4):
         _chk(lib().tt_trainer_step_device(self.h, idx_ptr, tgt_ptr, B, T, n_micro, lr),
              "step_device")
+
+    def step_graph(self, idx_ptr, tgt_ptr, B, T, n_micro=1, lr=3e-4):
+        """step_device replayed from a CUDA graph (one GPU): the first call with
+        these pointers and sizes runs eagerly, the second records and launches the
+        graph, later ones launch it. The ids must be in the same device buffers
+        each call."""
+        _chk(lib().tt_trainer_step_graph(self.h, idx_ptr, tgt_ptr, B, T, n_micro, lr),
+             "step_graph")
 
     def last_loss(self):
         v = C.c_float(0)

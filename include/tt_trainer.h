@@ -67,7 +67,10 @@ int tt_trainer_step_device(void* handle, const int64_t* idx, const int64_t* targ
  * with the same arithmetic as tt_trainer_step_device (identical results).
  * The caller puts each step's ids into the same two device buffers before
  * the call (stream-ordered). Other pointers or sizes drop the graph and
- * start over. Recording returns the device pool's unused memory first: the
+ * start over, as do tt_trainer_set_params, tt_trainer_init_normal,
+ * tt_trainer_load, tt_trainer_set_optimizer and tt_trainer_dist_init (they
+ * rewrite or replace state the graph reads). A failed recording leaves the
+ * step count as it was. Recording returns the device pool's unused memory first: the
  * graph allocates its activations from its own pool. Fails on a trainer
  * with a communicator. */
 int tt_trainer_step_graph(void* handle, const int64_t* idx, const int64_t* targets, int64_t B,

@@ -83,3 +83,29 @@ def test_graph_then_eager_step(cuda):
     assert np.array_equal(a.get_params(), b.get_params())
     a.close()
     b.close()
+
+
+def test_graph_dropped_when_params_written(cuda):
+    """Parameters written from the host between replays (set_params) drop the
+    recorded step: the next call runs eagerly, which uploads the new values,
+    and the results stay equal to eager steps."""
+    batches = _batches(6)
+    a, b = _trainer(), _trainer()
+    bi = torch.empty_like(batches[0][0])
+    bt = torch.empty_like(batches[0][1])
+    fresh = (np.random.default_rng(5).standard_normal(a.get_params().size) * 0.02).astype(
+        np.float32)
+    for step, (ids, tgt) in enumerate(batches):
+        if step == 3:
+            torch.cuda.synchronize()
+            a.set_params(fresh)
+            b.set_params(fresh)
+        a.step_device(ids.data_ptr(), tgt.data_ptr(), B, T, NM, LRS[step])
+        torch.cuda.synchronize()
+        bi.copy_(ids)
+        bt.copy_(tgt)
+        b.step_graph(bi.data_ptr(), bt.data_ptr(), B, T, NM, LRS[step])
+    torch.cuda.synchronize()
+    assert np.array_equal(a.get_params(), b.get_params())
+    a.close()
+    b.close()

@@ -443,6 +443,20 @@ struct Trainer {
     void* capture_stream = nullptr;
     float* sched = nullptr;
 
+    // Drops the recorded step: anything that replaces or rewrites the state
+    // a graph reads (parameters written from the host, a new optimizer,
+    // loaded checkpoints, a communicator) calls this, so the next
+    // tt_trainer_step_graph runs eagerly (uploading host-side writes) and
+    // records again.
+    void drop_graph() {
+        if (graph_exec) {
+            check(ttk_stream_synchronize(stream()), "graph release");
+            ttk_graph_destroy(graph_exec);
+            graph_exec = nullptr;
+        }
+        warm_valid = false;
+    }
+
     // Records one training step on the capture stream (nothing runs while
     // recording; the host-side state advances by one step, as for an eager
     // step) and instantiates it. The pool's unused memory is returned to the
@@ -456,6 +470,7 @@ struct Trainer {
         check(ttk_pool_trim(user), "pool trim");
         tt::set_stream(capture_stream);
         opt->set_device_schedule(sched);
+        const int64_t step0 = opt->step_count();
         std::exception_ptr err;
         int rc = ttk_stream_begin_capture(capture_stream);
         if (!rc) {
@@ -481,6 +496,11 @@ struct Trainer {
         const std::string msg = rc ? ttk_last_error() : "";
         opt->set_device_schedule(nullptr);
         tt::set_stream(user);
+        if (err || rc) {
+            // nothing ran: the step count stays; the next call runs eagerly
+            opt->set_step_count(step0);
+            warm_valid = false;
+        }
         if (err)
             std::rethrow_exception(err);
         if (rc)
@@ -627,13 +647,17 @@ int64_t tt_trainer_param_count(void* h) {
 }
 
 int tt_trainer_init_normal(void* h, float std, uint64_t seed) {
-    return guarded([&] { T_(h)->model->init_normal_(std, seed); });
+    return guarded([&] {
+        T_(h)->drop_graph();
+        T_(h)->model->init_normal_(std, seed);
+    });
 }
 
 int tt_trainer_set_params(void* h, const float* host, int64_t n) {
     return guarded([&] {
         if (n != tt_trainer_param_count(h))
             throw std::invalid_argument("set_params: size mismatch");
+        T_(h)->drop_graph();
         int64_t off = 0;
         for (Tensor* p : T_(h)->params) {
             p->copy_from_host(host + off);
@@ -670,6 +694,7 @@ int tt_trainer_get_grads(void* h, float* host, int64_t n) {
 int tt_trainer_set_optimizer(void* h, const tt_adamw_config* c) {
     return guarded([&] {
         Trainer* t = T_(h);
+        t->drop_graph();
         t->ocfg = *c;
         t->opt.reset(new AdamW(t->params, c->lr, c->beta1, c->beta2, c->eps, c->weight_decay));
         t->opt->set_clip_norm(c->clip_norm);
@@ -703,11 +728,8 @@ int tt_trainer_step_graph(void* h, const int64_t* idx, const int64_t* targets, i
             throw std::logic_error(
                 "step_graph: data-parallel steps are not recorded in a graph; use step_device");
         const Trainer::GraphKey key{idx, targets, B, T, n_micro};
-        if (t->graph_exec && !(t->graph_key == key)) {
-            check(ttk_stream_synchronize(stream()), "graph release");
-            ttk_graph_destroy(t->graph_exec);
-            t->graph_exec = nullptr;
-        }
+        if (t->graph_exec && !(t->graph_key == key))
+            t->drop_graph();
         if (!t->graph_exec) {
             if (!t->warm_valid || !(t->warm_key == key)) {
                 // The first step with these ids and sizes runs eagerly: it
@@ -968,6 +990,7 @@ int tt_trainer_save(void* h, const char* dir) {
 int tt_trainer_load(void* h, const char* dir) {
     return guarded([&] {
         Trainer* t = T_(h);
+        t->drop_graph();
         t->model->load_checkpoint(dir);
         const std::string path = std::string(dir) + "/optimizer.safetensors";
         std::ifstream f(path, std::ios::binary);
@@ -1076,6 +1099,7 @@ int tt_trainer_dist_init(void* h, int rank, int world, const unsigned char id[12
                          int64_t bucket_bytes) {
     return guarded([&] {
         Trainer* t = T_(h);
+        t->drop_graph();  // the bucket plan below moves the gradient arena's layout
         check(ttk_dist_init(rank, world, id, &t->comm), "dist init");
         t->rank = rank;
         t->world = world;

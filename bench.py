@@ -23,6 +23,8 @@ split) timed live over the timed region (events around each launch);
 achieved = algorithmic FLOPs (2*M*N*K per GEMM) / kernel time; traffic = the
 average DRAM bytes per GEMM launch of one llama-1b micro-batch step, from the
 ncu capture summarized in profiles/gemm_traffic_llama1b_microbatch.md.
+graph (--graph, one GPU): the same step replayed from a CUDA graph
+(tt_trainer_step_graph), timed after the e2e region.
 """
 from __future__ import annotations
 
@@ -184,7 +186,15 @@ class ClockSampler:
         if not self.path:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         with open(self.path) as f:
-            return self.parse(f.readlines(), t0, t1)
+            lines = f.readlines()
+        r = self.parse(lines, t0, t1)
+        if r["sm_mhz"] is None:
+            # a region shorter than the 200 ms sampling period: the samples
+            # within half a second of it
+            pad = datetime.timedelta(seconds=0.5)
+            r = self.parse(lines, t0 - pad, t1 + pad)
+            r["window"] = "region +- 0.5 s (region shorter than the sampling period)"
+        return r
 
 
 def reference_micro_step(w):

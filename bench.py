@@ -360,6 +360,11 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
     stream = torch.cuda.current_stream()
     trn.set_stream(stream.cuda_stream)
+    # Freed blocks are handed back out by the library instead of returning
+    # to the device pool: a training loop repeats its allocation pattern
+    # every step, and without the cache the pool's map / unmap calls into
+    # the driver stalled the host for 0.5-2 s at the start of some steps.
+    _ttk.call("ttk_set_block_cache", 1)
 
     if w["global_batch"] % world:
         raise SystemExit("global batch must split evenly across ranks")

@@ -99,6 +99,16 @@ int ttk_stream_end_capture(void* stream, void** graph_exec);
 int ttk_graph_launch(void* graph_exec, void* stream);
 int ttk_graph_destroy(void* graph_exec);
 int ttk_pool_trim(void* stream);
+/* Host-side cache of freed device blocks over the pool (on != 0; off by
+ * default): a block that ttk_free returns on a stream is handed out again by
+ * a later ttk_malloc of the same size on the same device and stream (stream
+ * order makes the reuse safe), so a training loop's repeating pattern of
+ * allocations stops reaching the pool. Allocations made while a stream is
+ * being captured into a graph bypass it; when a ttk_malloc finds the device
+ * out of memory the cached blocks are returned to the pool and it retries;
+ * ttk_pool_trim and turning the cache off return them too. No counterpart in
+ * the reference. */
+int ttk_set_block_cache(int on);
 
 /* ------------------------------------------------------------ dense algebra */
 

@@ -35,6 +35,7 @@ SIGS = {
     "ttk_graph_launch": (I32, [P, P]),
     "ttk_graph_destroy": (I32, [P]),
     "ttk_pool_trim": (I32, [P]),
+    "ttk_set_block_cache": (I32, [I32]),
     "ttk_launch_count": (I64, []),
     "ttk_malloc": (I32, [P, SZ, P]),
     "ttk_free": (I32, [P, P]),

@@ -11,7 +11,11 @@
 #include <atomic>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <string>
+#include <unordered_map>
+#include <vector>
 
 #include "ttk_common.cuh"
 #include "ttk_internal.h"
@@ -118,6 +122,78 @@ __global__ void wait_timeout_selftest_kernel(unsigned site, uint64_t limit_ns) {
 }  // namespace selftest
 }  // namespace ttk
 
+namespace {
+
+// Host-side cache of freed device blocks, off by default (ttk_set_block_cache).
+// A block that ttk_free gives back on stream s is handed out again, for the
+// same size on the same device and stream, by a later ttk_malloc: stream
+// order makes that safe (the new user's work runs after the old user's).
+// The pool underneath then sees no frees and no re-allocations once a
+// training step's pattern of sizes repeats. Blocks allocated while a stream
+// is captured into a graph bypass it.
+struct BlockCache {
+    struct Key {
+        int dev;
+        void* stream;
+        size_t bytes;
+        bool operator<(const Key& o) const {
+            if (dev != o.dev)
+                return dev < o.dev;
+            if (stream != o.stream)
+                return stream < o.stream;
+            return bytes < o.bytes;
+        }
+    };
+    std::mutex mu;
+    std::atomic<bool> enabled{false};
+    std::unordered_map<void*, size_t> live;  // blocks from ttk_malloc while enabled
+    std::map<Key, std::vector<void*>> free;
+    size_t cached_bytes = 0;
+};
+
+BlockCache& block_cache() {
+    static BlockCache c;
+    return c;
+}
+
+bool capturing(cudaStream_t s) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    return cudaStreamIsCapturing(s, &st) == cudaSuccess && st != cudaStreamCaptureStatusNone;
+}
+
+// Returns every cached block to the pool (after the device is idle: the
+// blocks' last users ran on streams that may since have been destroyed).
+int release_cached() {
+    BlockCache& c = block_cache();
+    std::map<BlockCache::Key, std::vector<void*>> blocks;
+    {
+        std::lock_guard<std::mutex> lock(c.mu);
+        blocks.swap(c.free);
+        c.cached_bytes = 0;
+    }
+    if (blocks.empty())
+        return TTK_OK;
+    int cur = 0;
+    cudaGetDevice(&cur);
+    int rc = TTK_OK;
+    for (auto& kv : blocks) {
+        if (cudaSetDevice(kv.first.dev) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+            rc = check_cuda(cudaGetLastError(), "block cache release");
+            continue;
+        }
+        // The device is idle: free in the order of the legacy stream.
+        for (void* p : kv.second)
+            if (cudaFreeAsync(p, nullptr) != cudaSuccess)
+                rc = check_cuda(cudaGetLastError(), "block cache release");
+        if (cudaStreamSynchronize(nullptr) != cudaSuccess)
+            rc = check_cuda(cudaGetLastError(), "block cache release");
+    }
+    cudaSetDevice(cur);
+    return rc;
+}
+
+}  // namespace
+
 extern "C" {
 
 int ttk_selftest_wait_timeout(unsigned site, uint64_t limit_ns, void* stream) {
@@ -136,13 +212,72 @@ int ttk_malloc(void** ptr, size_t bytes, void* stream) {
         return TTK_OK;
     // 256-byte granularity keeps every allocation TMA- and vector-aligned.
     bytes = (bytes + 255) & ~static_cast<size_t>(255);
-    return check_cuda(cudaMallocAsync(ptr, bytes, S(stream)), "cudaMallocAsync");
+    BlockCache& c = block_cache();
+    const bool cache = c.enabled.load(std::memory_order_relaxed) && !capturing(S(stream));
+    int dev = 0;
+    if (cache) {
+        cudaGetDevice(&dev);
+        std::lock_guard<std::mutex> lock(c.mu);
+        auto it = c.free.find(BlockCache::Key{dev, stream, bytes});
+        if (it != c.free.end() && !it->second.empty()) {
+            *ptr = it->second.back();
+            it->second.pop_back();
+            c.cached_bytes -= bytes;
+            c.live[*ptr] = bytes;
+            return TTK_OK;
+        }
+    }
+    cudaError_t e = cudaMallocAsync(ptr, bytes, S(stream));
+    if (e == cudaErrorMemoryAllocation && cache) {
+        cudaGetLastError();  // not sticky: give the cached blocks back and retry
+        release_cached();
+        e = cudaMallocAsync(ptr, bytes, S(stream));
+    }
+    int rc = check_cuda(e, "cudaMallocAsync");
+    if (!rc && cache) {
+        std::lock_guard<std::mutex> lock(c.mu);
+        c.live[*ptr] = bytes;
+    }
+    return rc;
 }
 
 int ttk_free(void* ptr, void* stream) {
     if (!ptr)
         return TTK_OK;
+    BlockCache& c = block_cache();
+    size_t bytes = 0;
+    {
+        std::lock_guard<std::mutex> lock(c.mu);
+        auto it = c.live.find(ptr);
+        if (it != c.live.end()) {
+            bytes = it->second;
+            c.live.erase(it);
+        }
+    }
+    if (bytes) {
+        if (capturing(S(stream))) {
+            // A block from before a stream capture, freed inside it: the
+            // recorded graph uses it up to this point of every replay, so it
+            // is neither handed out again nor freed.
+            return TTK_OK;
+        }
+        if (c.enabled.load(std::memory_order_relaxed)) {
+            int dev = 0;
+            cudaGetDevice(&dev);
+            std::lock_guard<std::mutex> lock(c.mu);
+            c.free[BlockCache::Key{dev, stream, bytes}].push_back(ptr);
+            c.cached_bytes += bytes;
+            return TTK_OK;
+        }
+    }
     return check_cuda(cudaFreeAsync(ptr, S(stream)), "cudaFreeAsync");
+}
+
+int ttk_set_block_cache(int on) {
+    block_cache().enabled.store(on != 0, std::memory_order_relaxed);
+    if (!on)
+        return release_cached();
+    return TTK_OK;
 }
 
 int ttk_pool_high_water(size_t* reserved_high, size_t* used_high, int reset) {
@@ -333,6 +468,9 @@ int ttk_pool_trim(void* stream) {
     if (rc)
         return rc;
     rc = check_cuda(cudaStreamSynchronize(S(stream)), "pool trim sync");
+    if (rc)
+        return rc;
+    rc = release_cached();
     if (rc)
         return rc;
     cudaMemPool_t pool;

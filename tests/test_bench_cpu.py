@@ -63,3 +63,22 @@ def test_clock_samples_windowed_by_timestamp():
     assert s["reasons"] == ["sw_power_cap"]
     empty = bench.ClockSampler.parse(lines, t1, t1)
     assert empty["sm_mhz"] is None and empty["reasons"] == ["no samples"]
+
+
+def test_clock_summary_of_a_short_region_uses_neighbouring_samples(tmp_path):
+    """A region shorter than the 200 ms sampling period holds no sample; its
+    summary then takes the samples within half a second of it."""
+    import datetime
+    sys.path.insert(0, ROOT)
+    import bench
+    path = tmp_path / "clocks.csv"
+    path.write_text("".join(
+        f"2026/12/02 10:00:{s:06.3f}, 0, {mhz}, 1965, 900.0, 0x4, Not Active, Not Active, "
+        f"Not Active, Active\n" for s, mhz in ((1.0, 1400), (1.2, 1500), (3.0, 1600))))
+    c = bench.ClockSampler([0], active=False)
+    c.path = str(path)
+    t0 = datetime.datetime(2026, 12, 2, 10, 0, 1, 50000)
+    t1 = datetime.datetime(2026, 12, 2, 10, 0, 1, 100000)
+    s = c.summary(t0, t1)
+    assert s["samples"] == 2 and s["sm_mhz"] == 1450.0 and "window" in s
+    assert s["reasons"] == ["sw_power_cap"]
